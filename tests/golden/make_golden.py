@@ -1,0 +1,400 @@
+"""Generate golden vectors by running the unmodified einjax reference.
+
+Run in a container where the reference source tree is available (pass its
+path with ``--reference``; it is read, never written). The reference needs
+``jax``; the stand-in under ``tests/golden/_jaxstub`` maps ``jax.numpy`` onto
+numpy so the reference's own functions run unchanged:
+
+* ``tensor/sparse.py``             SparseTensor, to_relation, _extract_coo
+* ``execution/sparse_dispatch.py`` coordinate_join, kernel_einsum, segment_sum,
+                                   execute_sparse, execute_sharded_sparse, ...
+* ``kernels/pallas_matmul.py``, ``kernels/pallas_gather.py``
+* ``autodiff/custom_vjp.py``       sparse_einsum_raw forward and backward rule
+* ``sharding/partition.py``        tile_shape_to_partition_spec
+
+Cases: the inputs of the reference's own hot-path unit tests, seeded random
+relations over several kernel strings, and scaled-down instances of the five
+benchmark configurations. Outputs go to ``tests/golden/*.npz`` (keys
+``<case>__<field>``, with a JSON ``<case>__meta``).
+
+Usage:  python tests/golden/make_golden.py --reference <path-to-einjax>
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import sys
+import types
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def load_reference(root: str):
+    sys.path.insert(0, os.path.join(HERE, "_jaxstub"))
+    import jax  # noqa: F401  (the stand-in)
+    pkg = types.ModuleType("einjax")
+    pkg.__path__ = [root]
+    sys.modules["einjax"] = pkg
+    for sub in ("core", "tensor", "execution", "kernels", "autodiff", "sharding"):
+        m = types.ModuleType(f"einjax.{sub}")
+        m.__path__ = [os.path.join(root, sub)]
+        sys.modules[f"einjax.{sub}"] = m
+    mods = {}
+    for name in ("tensor.sparse", "execution.sparse_dispatch", "kernels.pallas_matmul",
+                 "kernels.pallas_gather", "kernels.registry", "autodiff.custom_vjp",
+                 "sharding.partition"):
+        mods[name] = importlib.import_module(f"einjax.{name}")
+    return mods
+
+
+class Store:
+    def __init__(self):
+        self.arrays = {}
+
+    def put(self, case: str, meta: dict, **arrays):
+        assert case not in {k.split("__")[0] for k in self.arrays}, case
+        self.arrays[f"{case}__meta"] = np.array(json.dumps(meta))
+        for k, v in arrays.items():
+            self.arrays[f"{case}__{k}"] = np.asarray(v)
+
+    def save(self, path):
+        np.savez_compressed(path, **self.arrays)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True)
+    args = ap.parse_args()
+    mods = load_reference(os.path.abspath(args.reference))
+    import jax
+    sp_mod = mods["tensor.sparse"]
+    sd = mods["execution.sparse_dispatch"]
+    pm = mods["kernels.pallas_matmul"]
+    pg = mods["kernels.pallas_gather"]
+    cv = mods["autodiff.custom_vjp"]
+    part = mods["sharding.partition"]
+    STR = sp_mod.SparseTensorRelation
+
+    def rel_from_dense(dense, tile):
+        return sp_mod.SparseTensor("t", dense).to_relation(tile)
+
+    def rel_arrays(prefix, rel, vdtype=None):
+        vals = rel.values if vdtype is None else rel.values.astype(vdtype)
+        return {f"{prefix}_coords": rel.coords, f"{prefix}_values": vals,
+                f"{prefix}_shape": np.array(rel.shape, dtype=np.int64),
+                f"{prefix}_tile": np.array(rel.tile_shape, dtype=np.int64)}
+
+    # ------------------------------------------------------------------ unit cases
+    st = Store()
+
+    # to_relation (tests/test_sparse.py:219-295, tests/test_rigorous.py:438-463)
+    d44 = np.zeros((4, 4)); d44[0, 0] = 1.0
+    d3 = np.zeros((4, 4, 4)); d3[0, 0, 0] = 1.0; d3[3, 3, 3] = 2.0
+    rt = np.array([[1.0, 0, 0, 2], [0, 3, 0, 0], [0, 0, 4, 0], [5, 0, 0, 6]])
+    trel_cases = {
+        "identity": (np.array([[1.0, 0.0], [0.0, 2.0]]), (2, 2)),
+        "diagonal": (np.diag([1.0, 2.0, 3.0, 4.0]), (2, 2)),
+        "skip_empty": (d44, (2, 2)),
+        "roundtrip": (rt, (2, 2)),
+        "empty": (np.zeros((4, 4)), (2, 2)),
+        "three_d": (d3, (2, 2, 2)),
+        "element_tiling": (np.eye(3), (1, 1)),
+        "one_d": (np.array([0.0, 1.0, 0.0, 3.0, 0.0, 0.0, 7.0, 0.0]), (2,)),
+    }
+    rng = np.random.default_rng(7)
+    for i, (shape, tile, dens) in enumerate([((16, 16), (4, 4), 0.1), ((12, 18), (3, 6), 0.3),
+                                              ((8, 8, 8), (2, 4, 2), 0.05), ((64, 32), (16, 8), 0.01)]):
+        d = rng.standard_normal(shape) * (rng.random(shape) < dens)
+        trel_cases[f"random{i}"] = (d, tile)
+    for name, (dense, tile) in trel_cases.items():
+        idx, val, shape = sp_mod._extract_coo(dense)
+        rel = sp_mod.SparseTensor("t", dense).to_relation(tile)
+        st.put(f"torel_{name}", {"kind": "to_relation", "tile": list(tile), "shape": list(shape)},
+               indices=idx, values=val, out_coords=rel.coords, out_values=rel.values)
+    # duplicates through scipy COO: the last entry in input order survives
+    import scipy.sparse as ssp
+    rows = np.array([0, 1, 0, 3, 0, 2, 3]); cols = np.array([1, 2, 1, 3, 1, 0, 3])
+    vals = np.array([1.0, 2.0, 3.0, 4.0, 5.0, 0.0, -6.0])
+    coo = ssp.coo_matrix((vals, (rows, cols)), shape=(4, 4))
+    idx, val, shape = sp_mod._extract_coo(coo)
+    rel = sp_mod.SparseTensor("dup", coo).to_relation((2, 2))
+    st.put("torel_duplicates", {"kind": "to_relation", "tile": [2, 2], "shape": [4, 4]},
+           indices=idx, values=val, out_coords=rel.coords, out_values=rel.values)
+
+    # joins (tests/test_sparse_dispatch.py:43-129, tests/test_pallas.py:232-338,
+    #        tests/test_rigorous.py:884-933, 1275-1300)
+    join_cases = {
+        "matmul": (np.array([[0, 0], [0, 1]]), np.array([[0, 0], [1, 0]]), [(1, 0)]),
+        "cross": (np.array([[0, 0], [1, 1]]), np.array([[0, 0], [1, 1]]), []),
+        "nomatch": (np.array([[0, 0]]), np.array([[1, 0]]), [(1, 0)]),
+        "multi": (np.array([[0, 0], [1, 0]]), np.array([[0, 0]]), [(1, 0)]),
+        "empty": (np.zeros((0, 2)), np.zeros((0, 2)), [(1, 0)]),
+        "pallas_matmul": (np.array([[0, 0], [0, 1], [1, 0]]), np.array([[0, 0], [1, 0]]), [(1, 0)]),
+        "pallas_cross": (np.array([[0], [1]]), np.array([[0], [1], [2]]), []),
+        "same_dim": (np.array([[0, 0], [1, 1]]), np.array([[0, 0], [1, 1]]), [(0, 0), (1, 1)]),
+        "many_to_many": (np.array([[0, 0], [0, 1]]), np.array([[0, 0], [0, 1]]), [(0, 0)]),
+        "multi_sorted": (np.array([[0, 0], [1, 0]]), np.array([[0, 0], [0, 1]]), [(1, 0)]),
+        "consistency": (np.array([[0, 0], [0, 1], [1, 0]]), np.array([[0, 0], [1, 0], [1, 1]]), [(1, 0)]),
+    }
+    r42 = np.random.RandomState(42)
+    join_cases["hash_vs_sorted50"] = (r42.randint(0, 5, size=(50, 2)), r42.randint(0, 5, size=(50, 2)), [(1, 0)])
+    rng = np.random.default_rng(11)
+    for i, (nl, nr, ndl, ndr, keys, hi) in enumerate([
+            (200, 150, 2, 2, [(1, 0)], 12), (300, 300, 3, 2, [(2, 0)], 20),
+            (100, 120, 3, 3, [(0, 0), (2, 1)], 6), (64, 64, 2, 2, [(0, 1), (1, 0)], 8),
+            (1, 500, 2, 2, [(1, 0)], 3), (400, 1, 2, 2, [(1, 1)], 4)]):
+        join_cases[f"random{i}"] = (rng.integers(0, hi, (nl, ndl)), rng.integers(0, hi, (nr, ndr)), keys)
+    for name, (lc, rc, keys) in join_cases.items():
+        lc = np.asarray(lc, dtype=np.int32); rc = np.asarray(rc, dtype=np.int32)
+        L = STR(coords=lc, values=np.zeros((lc.shape[0], 1)), shape=(1,) * lc.shape[1], tile_shape=(1,) * lc.shape[1])
+        R = STR(coords=rc, values=np.zeros((rc.shape[0], 1)), shape=(1,) * rc.shape[1], tile_shape=(1,) * rc.shape[1])
+        li, ri = sd.coordinate_join(L, R, keys)
+        hl, hr = pg.coordinate_join_hash(lc, rc, keys)
+        sl, sr = pg.coordinate_join_sorted(lc, rc, keys)
+        st.put(f"join_{name}", {"kind": "join", "join_keys": [list(k) for k in keys]},
+               lhs_coords=lc, rhs_coords=rc, li=np.asarray(li, np.int64), ri=np.asarray(ri, np.int64),
+               hash_li=np.asarray(hl, np.int64), hash_ri=np.asarray(hr, np.int64),
+               sorted_li=np.asarray(sl, np.int64), sorted_ri=np.asarray(sr, np.int64))
+    # integer shorthand of the hash join (tests/test_pallas.py:268-274)
+    lc = np.array([[0, 0], [1, 1]], dtype=np.int32)
+    hl, hr = pg.coordinate_join_hash(lc, lc, [0, 1])
+    st.put("join_int_shorthand", {"kind": "join_hash_only", "join_dims": [0, 1]},
+           lhs_coords=lc, rhs_coords=lc, hash_li=np.asarray(hl, np.int64), hash_ri=np.asarray(hr, np.int64))
+
+    # segment_sum (tests/test_sparse_dispatch.py:204-257, tests/test_rigorous.py:955-971)
+    seg_cases = {
+        "single": (np.array([[[1.0, 2.0], [3.0, 4.0]]]), np.array([[0, 0]])),
+        "sum_two": (np.array([[[1.0, 0.0], [0.0, 1.0]], [[2.0, 0.0], [0.0, 2.0]]]), np.array([[0, 0], [0, 0]])),
+        "mixed": (np.array([[[1.0]], [[2.0]], [[3.0]]]), np.array([[0, 0], [0, 0], [1, 0]])),
+        "empty": (np.zeros((0, 2, 2)), np.zeros((0, 2), dtype=np.int32)),
+        "sorted": (np.array([[[1.0]], [[2.0]], [[3.0]]]), np.array([[2, 0], [0, 0], [1, 0]])),
+        "three_same": (np.ones((3, 2, 2)), np.array([[0, 0], [0, 0], [0, 0]])),
+    }
+    rng = np.random.default_rng(13)
+    for i, (p, nd, hi, tile) in enumerate([(500, 2, 6, (4, 4)), (300, 3, 4, (2, 3, 2)), (1000, 1, 50, (8,))]):
+        seg_cases[f"random{i}"] = (rng.standard_normal((p, *tile)), rng.integers(0, hi, (p, nd)))
+        seg_cases[f"random{i}_f32"] = (rng.standard_normal((p, *tile)).astype(np.float32), rng.integers(0, hi, (p, nd)))
+    for name, (v, c) in seg_cases.items():
+        uc, uv = sd.segment_sum(v, np.asarray(c, dtype=np.int32))
+        st.put(f"segsum_{name}", {"kind": "segment_sum"}, values=v, out_coords=np.asarray(c, np.int32),
+               res_coords=uc, res_values=uv)
+
+    # kernel_einsum (tests/test_sparse_dispatch.py:137-196, tests/test_rigorous.py:935-952)
+    ker_cases = {
+        "matmul": (np.array([[[1.0, 0.0], [0.0, 1.0]], [[2.0, 0.0], [0.0, 2.0]]]),
+                   np.array([[[3.0, 0.0], [0.0, 3.0]], [[4.0, 0.0], [0.0, 4.0]]]), [0, 1], [0, 1], "ij,jk->ik"),
+        "outer": (np.array([[1.0, 2.0]]), np.array([[3.0, 4.0]]), [0], [0], "i,j->ij"),
+        "dot": (np.array([[1.0, 2.0, 3.0]]), np.array([[4.0, 5.0, 6.0]]), [0], [0], "i,i->"),
+        "empty": (np.zeros((2, 3, 3)), np.zeros((2, 3, 3)), [], [], "ij,jk->ik"),
+        "single_pair": (np.eye(2).reshape(1, 2, 2), np.array([[[1.0, 2.0], [3.0, 4.0]]]), [0], [0], "ij,jk->ik"),
+    }
+    rng = np.random.default_rng(17)
+    for i, (ks, ls, rs) in enumerate([("ij,jk->ik", (4, 6), (6, 5)), ("ij,kj->ik", (4, 6), (5, 6)),
+                                      ("ji,jk->ik", (6, 4), (6, 5)), ("ijk,kl->ijl", (3, 4, 5), (5, 2)),
+                                      ("bij,bjk->bik", (1, 4, 3), (1, 3, 5)), ("ij,ij->ij", (3, 3), (3, 3)),
+                                      ("ij,kl->ij", (2, 3), (4, 2)), ("ii,ij->j", (3, 3), (3, 4)),
+                                      ("ij,jk->ki", (3, 4), (4, 5)), ("ijk,jkl->il", (2, 3, 4), (3, 4, 5))]):
+        nl, nr, p = 5, 6, 12
+        ker_cases[f"random{i}"] = (rng.standard_normal((nl, *ls)), rng.standard_normal((nr, *rs)),
+                                   rng.integers(0, nl, p), rng.integers(0, nr, p), ks)
+    for name, (lv, rv, li, ri, ks) in ker_cases.items():
+        li = np.asarray(li, np.int64); ri = np.asarray(ri, np.int64)
+        out = sd.kernel_einsum(lv, rv, li, ri, ks)
+        jax.F32 = True
+        out32 = sd.kernel_einsum(lv, rv, li, ri, ks)
+        jax.F32 = False
+        st.put(f"kernel_{name}", {"kind": "kernel_einsum", "kernel": ks}, lhs_values=lv, rhs_values=rv,
+               li=li, ri=ri, out=out, out_f32=np.asarray(out32))
+
+    # helpers (tests/test_sparse_dispatch.py:434-468)
+    helper = {"add_batch_dim": {s: sd._add_batch_dim(s) for s in ("ij,jk->ik", "i,j->ij", "i,i->", "bij,bjk->bik")},
+              "infer_tile": [[s, list(a), list(b), list(sd._infer_output_tile_shape(s, a, b))] for s, a, b in [
+                  ("ij,jk->ik", (2, 3), (3, 4)), ("i,j->ij", (3,), (4,)), ("i,i->", (5,), (5,)),
+                  ("ii,ij->j", (3, 3), (3, 4)), ("ijk,kl->ijl", (16, 16, 16), (16, 16))]],
+              "reverse": {s: list(cv._reverse_einsum_string(s)) for s in ("ij,jk->ik", "i,j->ij", "i,i->", "ijk,kl->ijl")},
+              "partition": [[n, d, [list(p) for p in sd._partition_matched_pairs(n, d)]]
+                            for n in (0, 1, 3, 7, 8, 10, 15, 64, 100) for d in (1, 2, 4, 8)]}
+    pspec = []
+    for shape, tile in [((8, 8), (2, 8)), ((8, 8), (8, 8)), ((8, 8), (2, 2)), ((4, 6, 8), (2, 6, 4)),
+                        ((8,), (16,)), ((8, 8), (3, 8)), ((8, 8), (0, 8)), ((8, 8, 8, 8, 8), (1, 1, 1, 1, 1)),
+                        ((8, 8), (2,))]:
+        try:
+            res = list(part.tile_shape_to_partition_spec(shape, tile))
+        except ValueError:
+            res = "ValueError"
+        pspec.append([list(shape), list(tile), res])
+    helper["partition_spec"] = pspec
+    st.put("helpers", helper)
+
+    # execute_sparse end to end (tests/test_sparse_dispatch.py:263-426,
+    # tests/test_rigorous.py:1069-1136, tests/test_pallas.py:53-223)
+    A_t = np.array([[1.0, 2, 0, 0], [3, 4, 0, 0], [0, 0, 5, 6], [0, 0, 7, 8]])
+    Ae = np.zeros((4, 4)); Ae[0, 0] = 1.0
+    Be = np.zeros((4, 4)); Be[2, 2] = 1.0
+    Aag = np.zeros((4, 4)); Aag[0, 0] = 1; Aag[0, 2] = 2; Aag[1, 1] = 3; Aag[1, 3] = 4
+    Bag = np.zeros((4, 4)); Bag[0, 0] = 5; Bag[2, 0] = 6; Bag[1, 1] = 7; Bag[3, 1] = 8
+    Bnum = np.array([[1.0, 2, 0, 0], [0, 3, 4, 0], [0, 0, 5, 6], [0, 0, 0, 7]])
+    MM = ([(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    exe = {
+        "identity": (np.array([[1.0, 2.0], [3.0, 4.0]]), np.eye(2), (1, 1), (1, 1), MM, (2, 2), (1, 1)),
+        "diagonal": (np.diag([1.0, 2, 3, 4]), np.diag([5.0, 6, 7, 8]), (1, 1), (1, 1), MM, (4, 4), (1, 1)),
+        "tiled": (A_t, np.eye(4), (2, 2), (2, 2), MM, (4, 4), (2, 2)),
+        "outer": (np.array([1.0, 0.0, 3.0]).reshape(3, 1), np.array([0.0, 2.0, 4.0]).reshape(1, 3), (1, 1), (1, 1),
+                  ([], "ij,kl->ij", [(0, 0), (1, 1)]), (3, 3), (1, 1)),
+        "elementwise": (np.diag([1.0, 2, 3]), np.diag([4.0, 5, 6]), (1, 1), (1, 1),
+                        ([(0, 0), (1, 1)], "ij,ij->ij", [(0, 0), (0, 1)]), (3, 3), (1, 1)),
+        "empty_result": (Ae, Be, (2, 2), (2, 2), MM, (4, 4), (2, 2)),
+        "inferred": (np.diag([1.0, 2.0]), np.diag([3.0, 4.0]), (1, 1), (1, 1), MM, None, None),
+        "num_vs_dense": (np.eye(4), Bnum, (2, 2), (2, 2), MM, None, None),
+        "aggregation": (Aag, Bag, (2, 2), (2, 2), MM, None, None),
+        "ones_agg": (np.ones((4, 4)), np.ones((4, 4)), (2, 2), (2, 2), MM, (4, 4), (2, 2)),
+        "non_square": (np.array([[1.0, 0, 2, 0], [0, 3, 0, 4], [5, 0, 6, 0]]),
+                       np.array([[1.0, 0], [0, 2], [3, 0], [0, 4]]), (1, 1), (1, 1), MM, None, None),
+    }
+    np.random.seed(42)
+    S1 = np.random.randn(8, 8); S2 = np.random.randn(8, 8)
+    S1[S1 < 0] = 0.0; S2[S2 < 0] = 0.0
+    exe["sharded_match"] = (S1, S2, (2, 2), (2, 2), MM, (8, 8), (2, 2))
+    rng = np.random.default_rng(23)
+
+    def rnd(shape, dens):
+        return rng.standard_normal(shape) * (rng.random(shape) < dens)
+    rand_specs = [
+        ("mm", (32, 48), (48, 40), (4, 8), (8, 5), MM, 0.05),
+        ("mm_t16", (64, 64), (64, 32), (16, 16), (16, 16), MM, 0.02),
+        ("mm_rect", (24, 36), (36, 20), (6, 4), (4, 10), MM, 0.1),
+        ("ij_kj", (32, 40), (24, 40), (4, 8), (6, 8), ([(1, 1)], "ij,kj->ik", [(0, 0), (1, 0)]), 0.05),
+        ("ji_jk", (40, 32), (40, 24), (8, 4), (8, 6), ([(0, 0)], "ji,jk->ik", [(0, 1), (1, 1)]), 0.05),
+        ("ij_jk_ki", (32, 48), (48, 40), (4, 8), (8, 5), ([(1, 0)], "ij,jk->ki", [(1, 1), (0, 0)]), 0.05),
+        ("batched", (3, 16, 24), (3, 24, 16), (1, 4, 8), (1, 8, 4),
+         ([(0, 0), (2, 1)], "bij,bjk->bik", [(0, 0), (0, 1), (1, 2)]), 0.05),
+        ("order3", (8, 8, 16), (16, 12), (2, 4, 4), (4, 6), ([(2, 0)], "ijk,kl->ijl", [(0, 0), (0, 1), (1, 1)]), 0.05),
+        ("hadamard", (16, 16), (16, 16), (4, 4), (4, 4), ([(0, 0), (1, 1)], "ij,ij->ij", [(0, 0), (0, 1)]), 0.2),
+        ("cross_sum", (6, 4), (4, 6), (2, 2), (2, 3), ([], "ij,kl->ij", [(0, 0), (1, 1)]), 0.2),
+        ("two_key", (12, 16, 8), (16, 8, 10), (3, 4, 2), (4, 2, 5),
+         ([(1, 0), (2, 1)], "ijk,jkl->il", [(0, 0), (1, 2)]), 0.1),
+    ]
+    for name, sa, sb, ta, tb, spec, dens in rand_specs:
+        exe[f"rand_{name}"] = (rnd(sa, dens), rnd(sb, dens), ta, tb, spec, None, None)
+    for name, (A, B, ta, tb, (jk, ks, ak), osh, ots) in exe.items():
+        lhs = rel_from_dense(A, ta); rhs = rel_from_dense(B, tb)
+        li, ri = sd.coordinate_join(lhs, rhs, jk)
+        res = sd.execute_sparse(lhs, rhs, jk, ks, ak, osh, ots)
+        jax.F32 = True
+        res32 = sd.execute_sparse(lhs, rhs, jk, ks, ak, osh, ots)
+        jax.F32 = False
+        meta = {"kind": "execute", "join_keys": [list(k) for k in jk], "kernel": ks, "agg_keys": [list(k) for k in ak],
+                "output_shape": None if osh is None else list(osh),
+                "output_tile_shape": None if ots is None else list(ots),
+                "res_shape": list(res.shape), "res_tile": list(res.tile_shape)}
+        sharded = {}
+        for nd in (2, 4, 8):
+            jax.NUM_FAKE_DEVICES = nd
+            mesh = jax.sharding.Mesh(np.array(jax.local_devices()).reshape(-1), ("x",))
+            shr = sd.execute_sharded_sparse(lhs, rhs, jk, ks, ak, osh, ots, mesh=mesh)
+            jax.NUM_FAKE_DEVICES = 1
+            sharded[f"sharded{nd}_coords"] = shr.coords
+            sharded[f"sharded{nd}_values"] = shr.values
+        st.put(f"exec_{name}", meta, **rel_arrays("lhs", lhs), **rel_arrays("rhs", rhs), li=np.asarray(li, np.int64),
+               ri=np.asarray(ri, np.int64), res_coords=res.coords, res_values=res.values,
+               res32_coords=res32.coords, res32_values=res32.values, **sharded)
+        if ks == "ij,jk->ik" and jk == [(1, 0)]:
+            bsm = pm.block_sparse_matmul_generic(lhs, rhs)
+            raw = pm.block_sparse_matmul(lhs.coords, lhs.values, rhs.coords, rhs.values,
+                                         (ta[0], ta[1], tb[1]), lhs.shape, rhs.shape)
+            st.put(f"bsm_{name}", {"kind": "bsm", "block_shape": [ta[0], ta[1], tb[1]]},
+                   **rel_arrays("lhs", lhs), **rel_arrays("rhs", rhs), res_coords=bsm.coords,
+                   res_values=bsm.values, raw_coords=raw.coords, raw_values=raw.values)
+
+    # autodiff: sparse_einsum_raw forward and the reference's own backward rule
+    # (tests/test_autodiff.py:160-403)
+    vjp_cases = {
+        "t2": (np.array([[1.0, 2.0], [3.0, 4.0]]), np.array([[5.0, 6.0], [7.0, 8.0]]), (2, 2), (2, 2), MM),
+        "diag": (np.diag([1.0, 2, 3, 4]), np.diag([5.0, 6, 7, 8]), (2, 2), (2, 2), MM),
+        "accum": (Aag, Bag, (2, 2), (2, 2), MM),
+        "t1": (np.array([[1.0, 0.0], [0.0, 2.0]]), np.array([[3.0, 0.0], [0.0, 4.0]]), (1, 1), (1, 1), MM),
+    }
+    for name, sa, sb, ta, tb, spec, dens in rand_specs[:8]:
+        vjp_cases[f"rand_{name}"] = (rnd(sa, max(dens, 0.1)), rnd(sb, max(dens, 0.1)), ta, tb, spec)
+    for name, (A, B, ta, tb, (jk, ks, ak)) in vjp_cases.items():
+        lhs = rel_from_dense(A, ta); rhs = rel_from_dense(B, tb)
+        li, ri = sd.coordinate_join(lhs, rhs, jk)
+        jax.LAST_VJP.clear()
+        fwd = cv.sparse_einsum_raw(lhs.values, rhs.values, lhs.coords, rhs.coords, li, ri, ks)
+        obj = jax.LAST_VJP[-1]
+        g = rng.standard_normal(np.asarray(fwd).shape)
+        _, resid = obj.fwd(lhs.values, rhs.values)
+        gl, gr = obj.bwd(resid, g)
+        st.put(f"vjp_{name}", {"kind": "vjp", "kernel": ks, "join_keys": [list(k) for k in jk]},
+               lhs_values=lhs.values, rhs_values=rhs.values, lhs_coords=lhs.coords, rhs_coords=rhs.coords,
+               li=np.asarray(li, np.int64), ri=np.asarray(ri, np.int64), fwd=np.asarray(fwd), g=g,
+               grad_lhs=np.asarray(gl), grad_rhs=np.asarray(gr))
+    st.save(os.path.join(HERE, "golden_unit.npz"))
+
+    # ------------------------------------------------------------ config-shaped cases
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from einjax_b200 import workloads as wl
+    cs = Store()
+
+    def run_exec(name, lhs, rhs, jk, ks, ak, extra_inputs):
+        li, ri = sd.coordinate_join(lhs, rhs, jk)
+        jax.F32 = True
+        res = sd.execute_sparse(lhs, rhs, jk, ks, ak)
+        jax.F32 = False
+        cs.put(name, {"kind": "execute_cfg", "join_keys": [list(k) for k in jk], "kernel": ks,
+                      "agg_keys": [list(k) for k in ak], "res_shape": list(res.shape),
+                      "res_tile": list(res.tile_shape)},
+               **extra_inputs, li=np.asarray(li, np.int64), ri=np.asarray(ri, np.int64),
+               res_coords=res.coords, res_values=res.values.astype(np.float32))
+
+    w = wl.c1_block_sparse(seed=0, scale=8)
+    lhs = STR(w.lhs.coords, w.lhs.values.astype(np.float64), w.lhs.shape, w.lhs.tile_shape)
+    rhs = STR(w.rhs.coords, w.rhs.values.astype(np.float64), w.rhs.shape, w.rhs.tile_shape)
+    run_exec("C1_small", lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys,
+             {**rel_arrays("lhs", lhs, np.float32), **rel_arrays("rhs", rhs, np.float32)})
+
+    w = wl.c2_spmm(seed=0, scale=128, n_cols=64)
+    coo = ssp.coo_matrix((w.lhs.values.astype(np.float64), (w.lhs.indices[:, 0], w.lhs.indices[:, 1])),
+                         shape=w.lhs.shape)
+    lhs = sp_mod.SparseTensor("A", coo).to_relation(w.lhs_tile)
+    rhs = sp_mod.SparseTensor("B", w.rhs.astype(np.float64)).to_relation(w.rhs_tile)
+    run_exec("C2_small", lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys,
+             {"a_indices": w.lhs.indices, "a_values": w.lhs.values, "a_shape": np.array(w.lhs.shape),
+              "b_dense": w.rhs, "lhs_coords": lhs.coords, "rhs_coords": rhs.coords})
+
+    w = wl.c3_batched_bf16(seed=0, scale=16, batch=2)
+    lhs = STR(w.lhs.coords, w.lhs.values.astype(np.float64), w.lhs.shape, w.lhs.tile_shape)
+    rhs = STR(w.rhs.coords, w.rhs.values.astype(np.float64), w.rhs.shape, w.rhs.tile_shape)
+    run_exec("C3_small", lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys,
+             {**rel_arrays("lhs", lhs, np.float32), **rel_arrays("rhs", rhs, np.float32)})
+
+    ch = wl.c4_chain(seed=0, scale=32)
+    rels = {k: STR(ch[k].coords, ch[k].values.astype(np.float64), ch[k].shape, ch[k].tile_shape) for k in "ABC"}
+    jax.F32 = True
+    ab = sd.execute_sparse(rels["A"], rels["B"], [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    abc = sd.execute_sparse(ab, rels["C"], [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    jax.F32 = False
+    l1, r1 = sd.coordinate_join(rels["A"], rels["B"], [(1, 0)])
+    cs.put("C4_small", {"kind": "chain"}, **rel_arrays("A", rels["A"], np.float32),
+           **rel_arrays("B", rels["B"], np.float32), **rel_arrays("C", rels["C"], np.float32), ab_coords=ab.coords, ab_values=ab.values.astype(np.float32),
+           abc_coords=abc.coords, abc_values=abc.values.astype(np.float32), l1=l1, r1=r1)
+
+    w = wl.c5_order3(seed=0, scale=32, n_out=32)
+    dense = np.zeros(w.lhs.shape)
+    dense[tuple(w.lhs.indices.T)] = w.lhs.values
+    lhs = sp_mod.SparseTensor("X", dense).to_relation(w.lhs_tile)
+    rhs = sp_mod.SparseTensor("W", w.rhs.astype(np.float64)).to_relation(w.rhs_tile)
+    run_exec("C5_small", lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys,
+             {"x_indices": w.lhs.indices, "x_values": w.lhs.values, "x_shape": np.array(w.lhs.shape),
+              "w_dense": w.rhs, "lhs_coords": lhs.coords, "rhs_coords": rhs.coords})
+    cs.save(os.path.join(HERE, "golden_configs.npz"))
+    print("wrote", len(st.arrays), "+", len(cs.arrays), "arrays")
+
+
+if __name__ == "__main__":
+    main()
