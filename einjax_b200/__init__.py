@@ -1,1 +1,20 @@
-"""einjax_b200 package (placeholder)."""
+"""einjax_b200 — einjax's sparse tensor-relational einsum path on B200 (sm_100a).
+
+Drop-in for the reference's sparse execution path (``execute_sparse`` and
+friends, the kernel registry, the sparse autodiff primitive). Every compute
+step runs in ``libeinsparse.so`` (hand-written CUDA, C ABI in
+``include/einsparse.h``); there is no CPU fallback.
+"""
+
+from ._lib import EinsparseError, EinsparseUnavailable  # noqa: F401
+from .autodiff import _reverse_einsum_string, sparse_einsum, sparse_einsum_raw  # noqa: F401
+from .kernels import (block_sparse_matmul, block_sparse_matmul_generic, coordinate_join_hash,  # noqa: F401
+                      coordinate_join_sorted)
+from .partition import tile_shape_to_partition_spec  # noqa: F401
+from .registry import KernelInfo, KernelRegistry, register_b200_kernels  # noqa: F401
+from .sparse import SparseTensor, SparseTensorRelation, tile_coo, tile_dense  # noqa: F401
+from .sparse_dispatch import (_add_batch_dim, _compute_output_coords, _infer_output_tile_shape,  # noqa: F401
+                              _partition_matched_pairs, coordinate_join, execute_sharded_sparse, execute_sparse,
+                              kernel_einsum, plan_pairs, segment_sum, tile_einsum)
+
+__version__ = "0.1.0"

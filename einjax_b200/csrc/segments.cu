@@ -1,0 +1,386 @@
+// Output-tile grouping, standalone segment-sum and deterministic scatter-add.
+//
+// Grouping follows _compute_output_coords + segment_sum
+// (execution/sparse_dispatch.py:174-223, 129-171): each pair's output tile
+// coordinate is packed into one integer (mixed radix over the output grid,
+// so integer order == lexicographic coordinate order, as `sorted` at :161),
+// pairs are stably radix-sorted by it (inside a group they stay in join
+// order, the order the reference adds them in at :167-169) and group heads
+// are prefix-summed into segment ids.
+#include <cmath>
+
+#include "common.cuh"
+#include "radix_sort.cuh"
+#include "scan.cuh"
+
+namespace es {
+
+struct AggKeys {
+  int out_nd, lhs_nd, rhs_nd;
+  int src[ES_MAX_DIMS];
+  int dim[ES_MAX_DIMS];
+  int64_t ext[ES_MAX_DIMS];
+};
+
+struct SegHeader {
+  int32_t sorted_in_alt;
+};
+
+struct SegWs {
+  SegHeader* hdr;
+  uint64_t* keys;
+  uint32_t* perm;
+  RadixBuffers<uint64_t> rb;
+  uint32_t* flags;
+  uint32_t* excl;
+  uint32_t* scan;
+  int64_t* seg_off;  // used by segsum / scatter-add
+  int64_t* nseg;
+};
+
+template <typename C>
+static void seg_layout(C& c, SegWs& w, int64_t n) {
+  w.hdr = c.template take<SegHeader>(1);
+  w.keys = c.template take<uint64_t>(n);
+  w.perm = c.template take<uint32_t>(n);
+  w.rb.keys_alt = c.template take<uint64_t>(n);
+  w.rb.vals_alt = c.template take<uint32_t>(n);
+  w.rb.hist = c.template take<uint32_t>(RadixScratchSize::hist_elems(n));
+  w.rb.scan = c.template take<uint32_t>(RadixScratchSize::scan_elems(n));
+  w.flags = c.template take<uint32_t>(n);
+  w.excl = c.template take<uint32_t>(n);
+  w.scan = c.template take<uint32_t>(scan_scratch_elems(n));
+  w.seg_off = c.template take<int64_t>(n + 1);
+  w.nseg = c.template take<int64_t>(1);
+}
+
+struct SegSizer {
+  Sizer s;
+  template <typename T>
+  T* take(int64_t n) {
+    s.take<T>(n);
+    return nullptr;
+  }
+};
+
+__global__ void seg_flag_kernel(SegHeader* h, int32_t v) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) h->sorted_in_alt = v;
+}
+
+__global__ void pair_out_keys_kernel(const int32_t* __restrict__ lc, const int32_t* __restrict__ rc,
+                                     const int32_t* __restrict__ li, const int32_t* __restrict__ ri, int64_t P,
+                                     AggKeys ak, uint64_t* __restrict__ keys, uint32_t* __restrict__ perm,
+                                     int32_t* err) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < P; p += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t k = 0;
+    bool ok = true;
+    const int64_t a = li[p], b = ri[p];
+    for (int d = 0; d < ak.out_nd; ++d) {
+      int64_t c = ak.src[d] == 0 ? lc[a * ak.lhs_nd + ak.dim[d]] : rc[b * ak.rhs_nd + ak.dim[d]];
+      if (c < 0 || c >= ak.ext[d]) ok = false;
+      k = k * static_cast<uint64_t>(ak.ext[d]) + static_cast<uint64_t>(c);
+    }
+    if (!ok && err) atomicExch(err, ES_ERR_INDEX);
+    keys[p] = k;
+    perm[p] = static_cast<uint32_t>(p);
+  }
+}
+
+__global__ void row_keys_kernel(const int32_t* __restrict__ coords, int64_t n, int nd, AggKeys ak,
+                                uint64_t* __restrict__ keys, uint32_t* __restrict__ perm, int32_t* err) {
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t k = 0;
+    bool ok = true;
+    for (int d = 0; d < nd; ++d) {
+      int64_t c = coords[r * nd + d];
+      if (c < 0 || c >= ak.ext[d]) ok = false;
+      k = k * static_cast<uint64_t>(ak.ext[d]) + static_cast<uint64_t>(c);
+    }
+    if (!ok && err) atomicExch(err, ES_ERR_INDEX);
+    keys[r] = k;
+    perm[r] = static_cast<uint32_t>(r);
+  }
+}
+
+__global__ void heads_kernel(const SegHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
+                             uint32_t* __restrict__ flags) {
+  const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x)
+    flags[s] = (s == 0 || keys[s] != keys[s - 1]) ? 1u : 0u;
+}
+
+// Segment offsets and (optionally) decoded unique coordinates.
+__global__ void seg_offsets_kernel(const SegHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
+                                   const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
+                                   AggKeys ak, int32_t* __restrict__ out_coords, int64_t* __restrict__ seg_off,
+                                   int64_t* nseg) {
+  const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x) {
+    if (flags[s]) {
+      const int64_t sid = excl[s];
+      seg_off[sid] = s;
+      if (out_coords) {
+        uint64_t k = keys[s];
+        for (int d = ak.out_nd - 1; d >= 0; --d) {
+          out_coords[sid * ak.out_nd + d] = static_cast<int32_t>(k % static_cast<uint64_t>(ak.ext[d]));
+          k /= static_cast<uint64_t>(ak.ext[d]);
+        }
+      }
+    }
+    if (s == n - 1) {
+      const int64_t total = static_cast<int64_t>(excl[s]) + flags[s];
+      seg_off[total] = n;
+      if (nseg) *nseg = total;
+    }
+  }
+}
+
+__global__ void gather_pairs_kernel(const SegHeader* hdr, const uint32_t* p0, const uint32_t* p1, int64_t n,
+                                    const int32_t* __restrict__ li, const int32_t* __restrict__ ri,
+                                    int32_t* __restrict__ sli, int32_t* __restrict__ sri, int32_t* __restrict__ spi) {
+  const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t p = perm[s];
+    if (sli) sli[s] = li[p];
+    if (sri) sri[s] = ri[p];
+    if (spi) spi[s] = static_cast<int32_t>(p);
+  }
+}
+
+// Sum rows of each segment in sorted (== original) order. One CTA per segment
+// (grid-stride over segments, bound read on device); threads stride the row.
+template <typename OutT>
+__global__ void segment_reduce_kernel(const SegHeader* hdr, const uint32_t* p0, const uint32_t* p1,
+                                      const int64_t* __restrict__ seg_off, const int64_t* __restrict__ nseg,
+                                      const void* __restrict__ vals, int vdtype, int64_t te,
+                                      const uint64_t* k0, const uint64_t* k1, int add_into_key_row,
+                                      OutT* __restrict__ out) {
+  const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
+  const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
+  const int64_t ns = *nseg;
+  for (int64_t sg = blockIdx.x; sg < ns; sg += gridDim.x) {
+    const int64_t a = seg_off[sg], b = seg_off[sg + 1];
+    const int64_t orow = add_into_key_row ? static_cast<int64_t>(keys[a]) : sg;
+    for (int64_t e = threadIdx.x; e < te; e += blockDim.x) {
+      float acc = 0.f;
+      for (int64_t s = a; s < b; ++s) acc += load_as_f32(vals, vdtype, static_cast<int64_t>(perm[s]) * te + e);
+      if (add_into_key_row) {
+        out[orow * te + e] = static_cast<OutT>(static_cast<float>(out[orow * te + e]) + acc);
+      } else {
+        out[orow * te + e] = static_cast<OutT>(acc);
+      }
+    }
+  }
+}
+
+template <>
+__global__ void segment_reduce_kernel<__nv_bfloat16>(const SegHeader* hdr, const uint32_t* p0, const uint32_t* p1,
+                                                     const int64_t* __restrict__ seg_off,
+                                                     const int64_t* __restrict__ nseg, const void* __restrict__ vals,
+                                                     int vdtype, int64_t te, const uint64_t* k0, const uint64_t* k1,
+                                                     int add_into_key_row, __nv_bfloat16* __restrict__ out) {
+  const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
+  const int64_t ns = *nseg;
+  for (int64_t sg = blockIdx.x; sg < ns; sg += gridDim.x) {
+    const int64_t a = seg_off[sg], b = seg_off[sg + 1];
+    for (int64_t e = threadIdx.x; e < te; e += blockDim.x) {
+      float acc = 0.f;
+      for (int64_t s = a; s < b; ++s) acc += load_as_f32(vals, vdtype, static_cast<int64_t>(perm[s]) * te + e);
+      out[sg * te + e] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+static int make_agg(const int32_t* agg_keys, int out_nd, int lhs_nd, int rhs_nd, const int64_t* ext, AggKeys* ak,
+                    int* bits) {
+  if (out_nd < 1 || out_nd > ES_MAX_DIMS) return ES_ERR_INVALID;
+  ak->out_nd = out_nd;
+  ak->lhs_nd = lhs_nd;
+  ak->rhs_nd = rhs_nd;
+  double bf = 0;
+  uint64_t prod = 1;
+  for (int d = 0; d < out_nd; ++d) {
+    if (agg_keys) {
+      ak->src[d] = agg_keys[2 * d];
+      ak->dim[d] = agg_keys[2 * d + 1];
+      const int nd = ak->src[d] == 0 ? lhs_nd : rhs_nd;
+      if ((ak->src[d] != 0 && ak->src[d] != 1) || ak->dim[d] < 0 || ak->dim[d] >= nd) return ES_ERR_INVALID;
+    } else {
+      ak->src[d] = 0;
+      ak->dim[d] = d;
+    }
+    if (ext[d] <= 0) return ES_ERR_INVALID;
+    ak->ext[d] = ext[d];
+    bf += std::log2(static_cast<double>(ext[d]));
+    if (bf > 62) return ES_ERR_UNSUPPORTED;
+    prod *= static_cast<uint64_t>(ext[d]);
+  }
+  *bits = bit_length(prod - 1);
+  return ES_OK;
+}
+
+// Sort keys already in w.keys/w.perm, mark heads, scan them. *count_dev gets
+// the number of groups (low 32 bits of an int64 zeroed first).
+static int sort_and_group(SegWs& w, int64_t n, int bits, int64_t* count_dev, cudaStream_t st) {
+  uint64_t* k = w.keys;
+  uint32_t* v = w.perm;
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n, 0, bits, st));
+  ES_LAUNCH(seg_flag_kernel, 1, 32, 0, st, w.hdr, k != w.keys ? 1 : 0);
+  ES_LAUNCH(heads_kernel, grid_for(n, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, n, w.flags);
+  if (count_dev && cudaMemsetAsync(count_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
+  ES_TRY(exclusive_scan<uint32_t>(w.flags, w.excl, n, reinterpret_cast<uint32_t*>(count_dev), w.scan, st));
+  return ES_OK;
+}
+
+}  // namespace es
+
+using namespace es;
+
+extern "C" size_t es_segments_workspace_size(int64_t num_pairs) {
+  SegSizer s;
+  SegWs w;
+  seg_layout(s, w, num_pairs);
+  return s.s.used + 256;
+}
+
+extern "C" int es_segments_plan(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs_coords, int rhs_ndim,
+                                const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs,
+                                const int32_t* agg_keys, int out_ndim, const int64_t* out_extents, void* workspace,
+                                size_t workspace_bytes, int64_t* num_segments_dev, int32_t* error_dev, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_pairs < 0 || num_pairs >= (int64_t)UINT32_MAX) return ES_ERR_UNSUPPORTED;
+  AggKeys ak;
+  int bits = 0;
+  ES_TRY(make_agg(agg_keys, out_ndim, lhs_ndim, rhs_ndim, out_extents, &ak, &bits));
+  if (num_pairs == 0) {
+    if (cudaMemsetAsync(num_segments_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
+    return ES_OK;
+  }
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_pairs);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  ES_LAUNCH(pair_out_keys_kernel, grid_for(num_pairs, 256), 256, 0, st, lhs_coords, rhs_coords, lhs_idx, rhs_idx,
+            num_pairs, ak, w.keys, w.perm, error_dev);
+  return sort_and_group(w, num_pairs, bits, num_segments_dev, st);
+}
+
+extern "C" int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs, int out_ndim,
+                                const int64_t* out_extents, void* workspace, size_t workspace_bytes,
+                                int64_t num_segments, int32_t* out_coords, int64_t* seg_offsets,
+                                int32_t* seg_lhs_idx, int32_t* seg_rhs_idx, int32_t* seg_pair_idx, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_pairs <= 0 || num_segments <= 0) return ES_OK;
+  AggKeys ak;
+  int bits = 0;
+  ES_TRY(make_agg(nullptr, out_ndim, out_ndim, out_ndim, out_extents, &ak, &bits));
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_pairs);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  ES_LAUNCH(seg_offsets_kernel, grid_for(num_pairs, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_pairs, w.flags,
+            w.excl, ak, out_coords, seg_offsets, (int64_t*)nullptr);
+  ES_LAUNCH(gather_pairs_kernel, grid_for(num_pairs, 256), 256, 0, st, w.hdr, w.perm, w.rb.vals_alt, num_pairs,
+            lhs_idx, rhs_idx, seg_lhs_idx, seg_rhs_idx, seg_pair_idx);
+  return ES_OK;
+}
+
+__global__ void output_coords_kernel(const int32_t* __restrict__ lc, const int32_t* __restrict__ rc,
+                                     const int32_t* __restrict__ li, const int32_t* __restrict__ ri, int64_t P,
+                                     AggKeys ak, int32_t* __restrict__ out) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < P; p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t a = li[p], b = ri[p];
+    for (int d = 0; d < ak.out_nd; ++d)
+      out[p * ak.out_nd + d] = ak.src[d] == 0 ? lc[a * ak.lhs_nd + ak.dim[d]] : rc[b * ak.rhs_nd + ak.dim[d]];
+  }
+}
+
+extern "C" int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs_coords, int rhs_ndim,
+                                const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs,
+                                const int32_t* agg_keys, int out_ndim, int32_t* out_coords, void* stream) {
+  if (num_pairs <= 0) return ES_OK;
+  AggKeys ak;
+  int bits = 0;
+  int64_t ext[ES_MAX_DIMS];
+  for (int d = 0; d < ES_MAX_DIMS; ++d) ext[d] = 1;
+  ES_TRY(make_agg(agg_keys, out_ndim, lhs_ndim, rhs_ndim, ext, &ak, &bits));
+  cudaStream_t st = as_stream(stream);
+  ES_LAUNCH(output_coords_kernel, grid_for(num_pairs, 256), 256, 0, st, lhs_coords, rhs_coords, lhs_idx, rhs_idx,
+            num_pairs, ak, out_coords);
+  return ES_OK;
+}
+
+extern "C" size_t es_segsum_workspace_size(int64_t num_rows) { return es_segments_workspace_size(num_rows); }
+
+extern "C" int es_segsum_plan(const int32_t* coords, int64_t num_rows, int nd, const int64_t* extents,
+                              void* workspace, size_t workspace_bytes, int64_t* num_segments_dev, int32_t* error_dev,
+                              void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_rows < 0 || num_rows >= (int64_t)UINT32_MAX) return ES_ERR_UNSUPPORTED;
+  AggKeys ak;
+  int bits = 0;
+  ES_TRY(make_agg(nullptr, nd, nd, nd, extents, &ak, &bits));
+  if (num_rows == 0) {
+    if (cudaMemsetAsync(num_segments_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
+    return ES_OK;
+  }
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_rows);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  ES_LAUNCH(row_keys_kernel, grid_for(num_rows, 256), 256, 0, st, coords, num_rows, nd, ak, w.keys, w.perm, error_dev);
+  return sort_and_group(w, num_rows, bits, num_segments_dev, st);
+}
+
+extern "C" int es_segsum_fill(const void* values, int values_dtype, int64_t num_rows, int64_t tile_elems, int nd,
+                              const int64_t* extents, void* workspace, size_t workspace_bytes, int64_t num_segments,
+                              int32_t* out_coords, void* out_values, int out_dtype, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_rows <= 0 || num_segments <= 0) return ES_OK;
+  if (out_dtype != ES_F32 && out_dtype != ES_BF16) return ES_ERR_UNSUPPORTED;
+  AggKeys ak;
+  int bits = 0;
+  ES_TRY(make_agg(nullptr, nd, nd, nd, extents, &ak, &bits));
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_rows);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  ES_LAUNCH(seg_offsets_kernel, grid_for(num_rows, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_rows, w.flags,
+            w.excl, ak, out_coords, w.seg_off, w.nseg);
+  const int grid = static_cast<int>(num_segments < 148 * 8 ? num_segments : 148 * 8);
+  const int threads = tile_elems >= 256 ? 256 : (tile_elems >= 64 ? 64 : 32);
+  if (out_dtype == ES_F32)
+    ES_LAUNCH(segment_reduce_kernel<float>, grid, threads, 0, st, w.hdr, w.perm, w.rb.vals_alt, w.seg_off, w.nseg,
+              values, values_dtype, tile_elems, w.keys, w.rb.keys_alt, 0, static_cast<float*>(out_values));
+  else
+    ES_LAUNCH(segment_reduce_kernel<__nv_bfloat16>, grid, threads, 0, st, w.hdr, w.perm, w.rb.vals_alt, w.seg_off,
+              w.nseg, values, values_dtype, tile_elems, w.keys, w.rb.keys_alt, 0,
+              static_cast<__nv_bfloat16*>(out_values));
+  return ES_OK;
+}
+
+extern "C" size_t es_scatter_add_workspace_size(int64_t num_rows) { return es_segments_workspace_size(num_rows); }
+
+extern "C" int es_scatter_add_rows(const void* values, int values_dtype, const int32_t* idx, int64_t num_rows,
+                                   int64_t tile_elems, int64_t num_out_rows, void* workspace, size_t workspace_bytes,
+                                   float* out, int32_t* error_dev, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_rows <= 0) return ES_OK;
+  if (num_rows >= (int64_t)UINT32_MAX || num_out_rows <= 0) return ES_ERR_UNSUPPORTED;
+  AggKeys ak;
+  int bits = 0;
+  int64_t ext = num_out_rows;
+  ES_TRY(make_agg(nullptr, 1, 1, 1, &ext, &ak, &bits));
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_rows);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  ES_LAUNCH(row_keys_kernel, grid_for(num_rows, 256), 256, 0, st, idx, num_rows, 1, ak, w.keys, w.perm, error_dev);
+  ES_TRY(sort_and_group(w, num_rows, bits, nullptr, st));
+  ES_LAUNCH(seg_offsets_kernel, grid_for(num_rows, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_rows, w.flags,
+            w.excl, ak, (int32_t*)nullptr, w.seg_off, w.nseg);
+  const int threads = tile_elems >= 256 ? 256 : (tile_elems >= 64 ? 64 : 32);
+  ES_LAUNCH(segment_reduce_kernel<float>, 148 * 8, threads, 0, st, w.hdr, w.perm, w.rb.vals_alt, w.seg_off, w.nseg,
+            values, values_dtype, tile_elems, w.keys, w.rb.keys_alt, 1, out);
+  return ES_OK;
+}

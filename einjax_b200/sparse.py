@@ -1,0 +1,278 @@
+"""Tile-COO relations on the GPU; mirrors einjax ``tensor/sparse.py``.
+
+``SparseTensorRelation`` keeps the reference's layout (``tensor/sparse.py:27-90``):
+``coords`` int32 ``(T, ndim)`` in lexicographic order and ``values``
+``(T, *tile_shape)`` row-major, here as CUDA tensors in float32 (the dtype the
+reference's JAX path computes in with x64 off) or bfloat16.
+``SparseTensor(name, data).to_relation(tile_shape)`` runs the tiling on the
+GPU through ``es_tile_coo_*`` / ``es_tile_dense_*``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from math import prod
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+_TORCH_TO_ES = {torch.float32: L.ES_F32, torch.bfloat16: L.ES_BF16, torch.float64: L.ES_F64}
+_ES_TO_TORCH = {L.ES_F32: torch.float32, L.ES_BF16: torch.bfloat16}
+
+
+def es_dtype(t: torch.Tensor) -> int:
+    try:
+        return _TORCH_TO_ES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported value dtype {t.dtype}") from None
+
+
+def default_device() -> torch.device:
+    if not torch.cuda.is_available():
+        raise L.EinsparseUnavailable("einjax_b200 needs a CUDA device (sm_100a); no CPU fallback exists")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def stream_ptr(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def read_counts(t: torch.Tensor):
+    """Read a small device int64 tensor (count, error, ...) with one sync."""
+    return [int(v) for v in t.tolist()]
+
+
+def value_dtype_for(dtype) -> torch.dtype:
+    """Device storage dtype for an input dtype: bf16 stays bf16, else float32."""
+    if dtype in (torch.bfloat16, "bf16", "bfloat16"):
+        return torch.bfloat16
+    return torch.float32
+
+
+@dataclass
+class SparseTensorRelation:
+    """Tile-COO relation held on the GPU (``tensor/sparse.py:27-90``)."""
+
+    coords: torch.Tensor
+    values: torch.Tensor
+    shape: tuple
+    tile_shape: tuple
+
+    def __post_init__(self):
+        self.shape = tuple(int(s) for s in self.shape)
+        self.tile_shape = tuple(int(t) for t in self.tile_shape)
+
+    @property
+    def num_tuples(self) -> int:
+        return int(self.coords.shape[0])
+
+    @property
+    def ndim(self) -> int:
+        return len(self.shape)
+
+    @property
+    def tile_size(self) -> int:
+        return prod(self.tile_shape)
+
+    @property
+    def nnz(self) -> int:
+        return int(torch.count_nonzero(self.values).item())
+
+    @property
+    def density(self) -> float:
+        total = prod(self.shape)
+        return self.nnz / total if total > 0 else 0.0
+
+    @property
+    def device(self) -> torch.device:
+        return self.values.device
+
+    def grid(self) -> tuple:
+        """Tile-grid extent per dimension (ceil(shape / tile), at least 1)."""
+        return tuple(max(1, -(-s // t)) for s, t in zip(self.shape, self.tile_shape))
+
+    def to_dense(self) -> torch.Tensor:
+        """Scatter tiles into a dense device tensor (``tensor/sparse.py:75-90``)."""
+        out = torch.zeros(self.shape, dtype=self.values.dtype, device=self.values.device)
+        if self.num_tuples == 0:
+            return out
+        g = self.grid()
+        view_shape = []
+        for gd, td in zip(g, self.tile_shape):
+            view_shape += [gd, td]
+        perm = list(range(0, 2 * self.ndim, 2)) + list(range(1, 2 * self.ndim, 2))
+        blocked = out.view(*view_shape).permute(*perm)  # (g0, g1, ..., t0, t1, ...)
+        idx = tuple(self.coords[:, d].long() for d in range(self.ndim))
+        blocked[idx] = self.values.reshape(self.num_tuples, *self.tile_shape)
+        return out
+
+    def to_numpy(self):
+        """``(coords int32, values)`` as numpy arrays (values float32)."""
+        return (self.coords.cpu().numpy(), self.values.float().cpu().numpy())
+
+    @staticmethod
+    def from_arrays(coords, values, shape, tile_shape, device=None, dtype=None) -> "SparseTensorRelation":
+        """Move host (numpy) or device tile-COO arrays onto the GPU.
+
+        float64 values become float32 (JAX's x64-off default), bfloat16 stays.
+        """
+        device = device or default_device()
+        vt = value_dtype_for(dtype if dtype is not None else getattr(values, "dtype", None))
+        c = torch.as_tensor(np.asarray(coords, dtype=np.int32) if not torch.is_tensor(coords) else coords)
+        c = c.to(device=device, dtype=torch.int32).reshape(-1, len(shape)).contiguous()
+        if torch.is_tensor(values):
+            v = values.to(device=device, dtype=vt)
+        else:
+            v = torch.from_numpy(np.ascontiguousarray(values)).to(device=device).to(vt)
+        v = v.reshape(c.shape[0], *tile_shape).contiguous()
+        return SparseTensorRelation(c, v, tuple(shape), tuple(tile_shape))
+
+    @staticmethod
+    def from_reference(rel, device=None, dtype=None) -> "SparseTensorRelation":
+        """Convert any object with ``coords, values, shape, tile_shape`` (e.g. the
+        reference's numpy ``SparseTensorRelation``)."""
+        return SparseTensorRelation.from_arrays(rel.coords, rel.values, rel.shape, rel.tile_shape, device, dtype)
+
+
+def as_relation(x, device=None) -> SparseTensorRelation:
+    if isinstance(x, SparseTensorRelation):
+        return x
+    return SparseTensorRelation.from_reference(x, device)
+
+
+def empty_relation(shape, tile_shape, dtype, device) -> SparseTensorRelation:
+    return SparseTensorRelation(torch.zeros((0, len(shape)), dtype=torch.int32, device=device),
+                                torch.zeros((0, *tile_shape), dtype=dtype, device=device), shape, tile_shape)
+
+
+def _check_divisible(shape, tile_shape):
+    if len(tile_shape) != len(shape):
+        raise ValueError(f"tile_shape rank {len(tile_shape)} != tensor rank {len(shape)}")
+    for d, (s, t) in enumerate(zip(shape, tile_shape)):
+        if t <= 0 or s % t != 0:
+            raise ValueError(f"tile_shape[{d}]={t} does not evenly divide shape[{d}]={s}")
+
+
+def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
+             out_dtype=torch.float32) -> SparseTensorRelation:
+    """Element COO (device tensors) -> tile-COO relation (``tensor/sparse.py:160-219``).
+
+    ``indices`` int32 ``(nnz, ndim)``, ``values`` (nnz,) float32/float64/bf16.
+    Zeros are dropped; the last of repeated coordinates wins.
+    """
+    shape = tuple(int(s) for s in shape)
+    tile_shape = tuple(int(t) for t in tile_shape)
+    _check_divisible(shape, tile_shape)
+    dev = values.device
+    lib = L.lib()
+    nnz = int(values.shape[0])
+    idx = indices.to(device=dev, dtype=torch.int32).contiguous()
+    vals = values.contiguous()
+    if nnz == 0:
+        return empty_relation(shape, tile_shape, out_dtype, dev)
+    sh, tl = L.i64arr(shape), L.i64arr(tile_shape)
+    nd = len(shape)
+    wsb = lib.es_tile_coo_workspace_size(nnz, nd, sh, tl)
+    ws = workspace(wsb, dev)
+    cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+    st = stream_ptr(dev)
+    L.check("es_tile_coo_plan", lib.es_tile_coo_plan(
+        idx.data_ptr(), vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(),
+        cnt.data_ptr(), cnt[1:].data_ptr(), st))
+    T, err = read_counts(cnt)
+    if err:
+        raise ValueError("COO index outside the tensor shape")
+    coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
+    out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+    L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
+        vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T,
+        coords.data_ptr(), out.data_ptr(), L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16, st))
+    return SparseTensorRelation(coords, out, shape, tile_shape)
+
+
+def tile_dense(dense: torch.Tensor, tile_shape, out_dtype=torch.float32) -> SparseTensorRelation:
+    """Dense device array -> tile-COO of its non-zero tiles (``to_relation`` of a
+    dense ``SparseTensor``, ``tensor/sparse.py:104-117,160-219``)."""
+    shape = tuple(int(s) for s in dense.shape)
+    tile_shape = tuple(int(t) for t in tile_shape)
+    _check_divisible(shape, tile_shape)
+    dev = dense.device
+    lib = L.lib()
+    d = dense.contiguous()
+    sh, tl = L.i64arr(shape), L.i64arr(tile_shape)
+    nd = len(shape)
+    ws = workspace(lib.es_tile_dense_workspace_size(nd, sh, tl), dev)
+    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    st = stream_ptr(dev)
+    L.check("es_tile_dense_plan", lib.es_tile_dense_plan(
+        d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), cnt.data_ptr(), st))
+    T = read_counts(cnt)[0]
+    coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
+    out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+    L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
+        d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), out.data_ptr(),
+        L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16, st))
+    return SparseTensorRelation(coords, out, shape, tile_shape)
+
+
+def _extract_coo(data: Any):
+    """Input -> (indices int32 (nnz, ndim), values, shape) on the host, as
+    ``_extract_coo`` (``tensor/sparse.py:234-270``); dense input is kept dense
+    (it is tiled on the GPU without a COO detour)."""
+    try:
+        import scipy.sparse as sp
+        if sp.issparse(data):
+            coo = sp.coo_matrix(data) if data.ndim == 2 else data.tocoo()
+            idx = np.stack([coo.row, coo.col], axis=1).astype(np.int32)
+            return "coo", idx, np.asarray(coo.data, dtype=np.float64), tuple(coo.shape)
+    except ImportError:  # pragma: no cover
+        pass
+    if isinstance(data, tuple) and len(data) == 3:
+        idx, val, shape = data
+        return "coo", idx, val, tuple(int(s) for s in shape)
+    if torch.is_tensor(data):
+        return "dense", data, None, tuple(data.shape)
+    arr = np.asarray(data)
+    if arr.dtype not in (np.float32, np.float64):
+        arr = arr.astype(np.float64)
+    return "dense", arr, None, tuple(arr.shape)
+
+
+class SparseTensor:
+    """User-facing sparse tensor (``tensor/sparse.py:93-231``) whose tiling runs on the GPU.
+
+    ``data``: a scipy sparse matrix, a dense numpy array / torch tensor, or a
+    ``(indices, values, shape)`` COO triple (indices int32 ``(nnz, ndim)``; any
+    rank, unlike scipy). The reference's per-scheme sparsity statistics
+    (``_compute_sparsity_metrics``, planner input) are not computed here.
+    """
+
+    def __init__(self, name: str, data: Any, device=None, dtype=None):
+        self.name = name
+        self.device = device or default_device()
+        self._kind, self._a, self._b, self.shape = _extract_coo(data)
+        self.data = data
+        self._out_dtype = value_dtype_for(dtype)
+
+    @property
+    def ndim(self) -> int:
+        return len(self.shape)
+
+    def to_relation(self, tile_shape) -> SparseTensorRelation:
+        tile_shape = tuple(int(t) for t in tile_shape)
+        _check_divisible(self.shape, tile_shape)
+        if self._kind == "coo":
+            idx = torch.as_tensor(np.asarray(self._a, dtype=np.int32)) if not torch.is_tensor(self._a) else self._a
+            val = torch.as_tensor(np.asarray(self._b)) if not torch.is_tensor(self._b) else self._b
+            idx = idx.to(self.device, non_blocking=True).reshape(-1, len(self.shape))
+            val = val.to(self.device, non_blocking=True)
+            return tile_coo(idx, val, self.shape, tile_shape, self._out_dtype)
+        dense = self._a if torch.is_tensor(self._a) else torch.from_numpy(np.ascontiguousarray(self._a))
+        return tile_dense(dense.to(self.device, non_blocking=True), tile_shape, self._out_dtype)

@@ -1,0 +1,195 @@
+/*
+ * einsparse — C ABI of the B200 (sm_100a) sparse tensor-relational einsum path.
+ *
+ * Each entry point replaces one step of einjax's sparse execution path
+ * (paths below are relative to the einjax project root). All pointers are
+ * device pointers unless stated; all sizes are element counts; every call is
+ * asynchronous on `stream` (a cudaStream_t, 0 = legacy default stream) and
+ * returns an es_status. No entry point allocates memory: multi-phase steps
+ * take a caller-owned workspace whose size the matching *_workspace_size
+ * query reports, and data-dependent output sizes are written to a device
+ * int64 that the caller reads before allocating the outputs of the *_fill
+ * phase. Device-side checks (an index outside its grid) set *error_dev to a
+ * non-zero es_status; the caller reads it together with the size.
+ *
+ * Threading: calls on different streams may run concurrently as long as
+ * they do not share a workspace. The library holds no global mutable state
+ * apart from a launch counter (es_launch_count).
+ */
+#ifndef EINSPARSE_H
+#define EINSPARSE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum es_status {
+  ES_OK = 0,
+  ES_ERR_INVALID = 1,     /* bad shape / argument; the reference raises ValueError */
+  ES_ERR_INDEX = 2,       /* a coordinate outside the grid its shape defines */
+  ES_ERR_WORKSPACE = 3,   /* workspace smaller than *_workspace_size reported */
+  ES_ERR_CUDA = 4,        /* CUDA runtime error (launch or async) */
+  ES_ERR_UNSUPPORTED = 5  /* dtype / rank / size this build does not handle */
+} es_status;
+
+typedef enum es_dtype { ES_F32 = 0, ES_BF16 = 1, ES_F64 = 2, ES_I32 = 3, ES_I64 = 4 } es_dtype;
+
+/* Arithmetic of the tile contraction. EXACT: fp32 FFMA (SIMT); TC: tensor
+ * cores (bf16 inputs: kind::f16; fp32 inputs: 3-pass split TF32, fp32-level
+ * error); AUTO: TC where a tensor-core kernel covers the shape, else EXACT. */
+typedef enum es_precision { ES_PREC_AUTO = 0, ES_PREC_EXACT = 1, ES_PREC_TC = 2 } es_precision;
+
+#define ES_MAX_DIMS 8
+
+/* Library version and a count of kernels launched since load (or since the
+ * last es_launch_count_reset). */
+int es_version(void);
+int64_t es_launch_count(void);
+void es_launch_count_reset(void);
+const char* es_status_string(int status);
+
+/* ---------------------------------------------------------------------------
+ * Tiling: element COO -> tile-COO.
+ * Replaces SparseTensor.to_relation (tensor/sparse.py:160-219) together with
+ * the COO extraction it consumes (tensor/sparse.py:234-270).
+ * indices: int32 (nnz, ndim) row-major; values: (nnz) of values_dtype
+ * (F32/F64/BF16). Entries equal to zero are dropped (sparse.py:185-187);
+ * tiles come out in lexicographic coordinate order (np.unique, :204-206);
+ * when a coordinate repeats, the entry that comes last in input order
+ * wins (NumPy fancy assignment, :211-212). shape[d] % tile[d] != 0 gives
+ * ES_ERR_INVALID (:174-179). Plan writes the tile count T to *num_tiles_dev;
+ * fill writes coords int32 (T, ndim) and values (T, prod(tile)) of out_dtype.
+ * ------------------------------------------------------------------------- */
+size_t es_tile_coo_workspace_size(int64_t nnz, int ndim, const int64_t* shape, const int64_t* tile);
+int es_tile_coo_plan(const int32_t* indices, const void* values, int values_dtype, int64_t nnz,
+                     int ndim, const int64_t* shape, const int64_t* tile,
+                     void* workspace, size_t workspace_bytes,
+                     int64_t* num_tiles_dev, int32_t* error_dev, void* stream);
+int es_tile_coo_fill(const void* values, int values_dtype, int64_t nnz, int ndim,
+                     const int64_t* shape, const int64_t* tile,
+                     void* workspace, size_t workspace_bytes, int64_t num_tiles,
+                     int32_t* coords_out, void* values_out, int out_dtype, void* stream);
+
+/* Dense array (row-major `shape`) -> tile-COO of the tiles holding any
+ * non-zero. Same result as SparseTensor(dense).to_relation(tile)
+ * (tensor/sparse.py:104-117,160-219, via np.nonzero at :260-268). */
+size_t es_tile_dense_workspace_size(int ndim, const int64_t* shape, const int64_t* tile);
+int es_tile_dense_plan(const void* dense, int dtype, int ndim, const int64_t* shape,
+                       const int64_t* tile, void* workspace, size_t workspace_bytes,
+                       int64_t* num_tiles_dev, void* stream);
+int es_tile_dense_fill(const void* dense, int dtype, int ndim, const int64_t* shape,
+                       const int64_t* tile, void* workspace, size_t workspace_bytes,
+                       int64_t num_tiles, int32_t* coords_out, void* values_out, int out_dtype,
+                       void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Coordinate join. Replaces coordinate_join (execution/sparse_dispatch.py:29-82)
+ * and coordinate_join_hash (kernels/pallas_gather.py:19-76).
+ * join_keys: nkeys pairs (lhs_dim, rhs_dim); key_extents[k]: the tile-grid
+ * extent of key k (coordinates must lie in [0, extent), else ES_ERR_INDEX in
+ * *error_dev). Pair order is the reference's: RHS tile j ascending, and for
+ * each j every LHS tile with an equal key, LHS index ascending; nkeys == 0
+ * gives the LHS-major cross product (:53-59). Plan writes P to *num_pairs_dev;
+ * fill writes lhs_idx/rhs_idx as index_dtype (ES_I32 or ES_I64).
+ * ------------------------------------------------------------------------- */
+size_t es_join_workspace_size(int64_t n_lhs, int64_t n_rhs);
+int es_join_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim,
+                 const int32_t* rhs_coords, int64_t n_rhs, int rhs_ndim,
+                 const int32_t* join_keys, int nkeys, const int64_t* key_extents,
+                 void* workspace, size_t workspace_bytes,
+                 int64_t* num_pairs_dev, int32_t* error_dev, void* stream);
+int es_join_fill(int64_t n_lhs, int64_t n_rhs, int nkeys, void* workspace, size_t workspace_bytes,
+                 int64_t num_pairs, void* lhs_idx_out, void* rhs_idx_out, int index_dtype,
+                 void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Output-tile grouping. Replaces _compute_output_coords + the grouping half of
+ * segment_sum (execution/sparse_dispatch.py:174-223, 129-171): the output
+ * coordinate of each pair is gathered through agg_keys (pairs (src, dim),
+ * src 0 = lhs, 1 = rhs); pairs are stably sorted by it, so inside each group
+ * they keep join order (the reference sums each group in pair order,
+ * :165-169). Plan writes the group count O to *num_segments_dev; fill writes
+ * out_coords int32 (O, out_ndim) sorted lexicographically (:161),
+ * seg_offsets int64 (O+1) and the pairs regrouped (seg_lhs_idx,
+ * seg_rhs_idx int32, P each; seg_pair_idx int32 = original pair index, may
+ * be NULL). lhs_idx/rhs_idx are int32.
+ * ------------------------------------------------------------------------- */
+size_t es_segments_workspace_size(int64_t num_pairs);
+int es_segments_plan(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs_coords, int rhs_ndim,
+                     const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs,
+                     const int32_t* agg_keys, int out_ndim, const int64_t* out_extents,
+                     void* workspace, size_t workspace_bytes,
+                     int64_t* num_segments_dev, int32_t* error_dev, void* stream);
+int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs, int out_ndim,
+                     const int64_t* out_extents, void* workspace, size_t workspace_bytes,
+                     int64_t num_segments, int32_t* out_coords, int64_t* seg_offsets,
+                     int32_t* seg_lhs_idx, int32_t* seg_rhs_idx, int32_t* seg_pair_idx,
+                     void* stream);
+
+/* Per-pair output tile coordinates, int32 (P, out_ndim): the gather of
+ * _compute_output_coords (execution/sparse_dispatch.py:174-223). */
+int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs_coords, int rhs_ndim,
+                     const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs,
+                     const int32_t* agg_keys, int out_ndim, int32_t* out_coords, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Segmented tile einsum — the per-pair kernel einsum fused with the
+ * segment-sum (execution/sparse_dispatch.py:85-126 + 129-171; the batched
+ * tile einsum of kernels/pallas_matmul.py:33-113).
+ * kernel_string: the per-tile einsum ("ij,jk->ik", "bij,bjk->bik",
+ * "ijk,kl->ijl", ...; any two-operand string with an explicit "->").
+ * For segment s, out[s_out] = sum over p in [seg_offsets[s], seg_offsets[s+1])
+ * of einsum(lhs_values[pair_lhs[p]], rhs_values[pair_rhs[p]]), accumulated
+ * in fp32, where s_out = seg_out_index ? seg_out_index[s] : s.
+ * seg_offsets == NULL means every pair is its own segment (the unfused
+ * per-pair kernel_einsum, output (P, *out_tile)). Output rows that no segment
+ * writes are left untouched. Values dtypes: F32 / BF16 / F64 inputs;
+ * F32 / BF16 outputs.
+ * ------------------------------------------------------------------------- */
+int es_tile_einsum(const char* kernel_string,
+                   const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
+                   const void* lhs_values, int lhs_dtype, const void* rhs_values, int rhs_dtype,
+                   const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
+                   const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
+                   void* out_values, int out_dtype, int precision, void* stream);
+
+/* Out tile shape of a kernel string (_infer_output_tile_shape,
+ * execution/sparse_dispatch.py:506-545). Host-side; returns the out rank or
+ * a negative es_status. */
+int es_out_tile_shape(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
+                      const int64_t* rhs_tile, int rhs_nd, int64_t* out_tile);
+
+/* ---------------------------------------------------------------------------
+ * Standalone segment-sum (execution/sparse_dispatch.py:129-171): values
+ * (P, tile_elems) grouped by coords (P, nd) int32 with per-dim extents.
+ * Plan (es_segsum_plan) writes O; fill writes unique coords (O, nd) sorted
+ * lexicographically and the per-group sums, added in row order in fp32.
+ * Scatter-add by index (the `.at[idx].add` of autodiff/custom_vjp.py:272-273)
+ * is the nd == 1 case with out rows chosen by the caller via es_tile_einsum's
+ * seg_out_index; see es_scatter_add_rows.
+ * ------------------------------------------------------------------------- */
+size_t es_segsum_workspace_size(int64_t num_rows);
+int es_segsum_plan(const int32_t* coords, int64_t num_rows, int nd, const int64_t* extents,
+                   void* workspace, size_t workspace_bytes, int64_t* num_segments_dev,
+                   int32_t* error_dev, void* stream);
+int es_segsum_fill(const void* values, int values_dtype, int64_t num_rows, int64_t tile_elems, int nd,
+                   const int64_t* extents, void* workspace, size_t workspace_bytes, int64_t num_segments,
+                   int32_t* out_coords, void* out_values, int out_dtype, void* stream);
+
+/* out[idx[r]] += values[r] for r in row order, rows of tile_elems
+ * (autodiff/custom_vjp.py:272-273). out must be F32. Deterministic: rows
+ * are grouped by a stable sort, each group is summed in row order, then
+ * added once. */
+size_t es_scatter_add_workspace_size(int64_t num_rows);
+int es_scatter_add_rows(const void* values, int values_dtype, const int32_t* idx, int64_t num_rows,
+                        int64_t tile_elems, int64_t num_out_rows, void* workspace,
+                        size_t workspace_bytes, float* out, int32_t* error_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EINSPARSE_H */

@@ -265,7 +265,27 @@ def kernel_einsum(lhs_values, rhs_values, lhs_idx, rhs_idx, kernel_string,
         return np.zeros((0, *ots), dtype=lhs_values.dtype)
     a = _cast(lhs_values[np.asarray(lhs_idx)], compute_dtype)
     b = _cast(rhs_values[np.asarray(rhs_idx)], compute_dtype)
+    if _is_matmul(kernel_string):
+        # same contraction through BLAS (XLA's CPU backend also lowers it to
+        # a batched GEMM); only the summation order inside a dot differs
+        return np.matmul(a, b)
     return np.einsum(add_batch_dim(kernel_string), a, b)
+
+
+def _is_matmul(ks: str) -> bool:
+    ks = ks.replace(" ", "")
+    if "->" not in ks:
+        return False
+    ins, out = ks.split("->")
+    t = ins.split(",")
+    if len(t) != 2 or len(t[0]) < 2 or len(t[0]) != len(t[1]) or len(out) != len(t[0]):
+        return False
+    batch = t[0][:-2]
+    i, j = t[0][-2:]
+    j2, k = t[1][-2:]
+    labels = set(batch) | {i, j, k}
+    return (t[1][:-2] == batch and j == j2 and out == batch + i + k
+            and len(labels) == len(batch) + 3)
 
 
 def compute_output_coords(lhs_coords, rhs_coords, lhs_idx, rhs_idx, agg_keys):

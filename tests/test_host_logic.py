@@ -1,0 +1,111 @@
+"""Host-side logic that needs no GPU: registry dispatch, partitioning helpers,
+kernel-string helpers — checked against the reference's golden vectors and
+against the reference tests' expectations (tests/test_pallas.py:346-525)."""
+
+import numpy as np
+import pytest
+
+import einjax_b200 as E
+from einjax_b200 import distributed as D
+from einjax_b200.registry import _backend_matches, _pattern_matches, _sparsity_matches
+from golden_io import load_cases
+
+H = load_cases()["helpers"].meta
+
+
+def test_helpers_match_reference():
+    for s, want in H["add_batch_dim"].items():
+        assert E._add_batch_dim(s) == want
+    for s, a, b, want in H["infer_tile"]:
+        assert list(E._infer_output_tile_shape(s, tuple(a), tuple(b))) == want
+    for s, want in H["reverse"].items():
+        assert list(E._reverse_einsum_string(s)) == want
+    for n, d, want in H["partition"]:
+        assert [list(p) for p in E._partition_matched_pairs(n, d)] == want
+    with pytest.raises(ValueError):
+        E._add_batch_dim("ij,jk")
+
+
+def test_partition_spec_matches_reference():
+    for shape, tile, want in H["partition_spec"]:
+        if want == "ValueError":
+            with pytest.raises(ValueError):
+                E.tile_shape_to_partition_spec(tuple(shape), tuple(tile))
+        else:
+            assert list(E.tile_shape_to_partition_spec(tuple(shape), tuple(tile))) == want
+
+
+def test_matchers():
+    assert _pattern_matches("*", "anything") and not _pattern_matches("ij,jk->ik", "ij,kj->ik")
+    assert _backend_matches("generic", "gpu") and _backend_matches("gpu", "gpu:triton")
+    assert not _backend_matches("gpu", "tpu")
+    assert _sparsity_matches("any", "dense") and not _sparsity_matches("sparse", "dense")
+
+
+def test_registry_dispatch():
+    reg = E.KernelRegistry()
+    info = reg.lookup_info("ij,jk->ik", backend="gpu", sparsity="sparse")
+    assert info.name == "b200_block_sparse_matmul" and info.priority > 0
+    assert reg.lookup_info("bij,bjk->bik", backend="gpu:anything", sparsity="sparse").name == "b200_sparse_einsum"
+    with pytest.raises(ValueError):
+        reg.lookup("ij,jk->ik", backend="gpu", sparsity="dense")
+    with pytest.raises(ValueError):
+        reg.lookup("ij,jk->ik", backend="tpu", sparsity="sparse")
+
+    def custom(*a, **k):
+        return "custom"
+    reg.register(E.KernelInfo("custom", "ij,jk->ik", "generic", "sparse", 99, custom))
+    assert reg.lookup("ij,jk->ik", backend="cpu", sparsity="sparse") is custom
+    assert len(reg.list_kernels(sparsity="sparse")) == 3
+
+
+def test_register_into_foreign_registry():
+    """The adapters register into any registry with the reference's interface."""
+
+    class ForeignInfo:
+        def __init__(self, name, pattern, backend, sparsity, priority, kernel_fn):
+            self.name, self.pattern, self.backend = name, pattern, backend
+            self.sparsity, self.priority, self.kernel_fn = sparsity, priority, kernel_fn
+
+    class ForeignRegistry:
+        def __init__(self):
+            self.k = []
+
+        def register(self, ki):
+            self.k.append(ki)
+
+    r = E.register_b200_kernels(ForeignRegistry(), info_cls=ForeignInfo)
+    names = {k.name: k for k in r.k}
+    assert set(names) == {"b200_block_sparse_matmul", "b200_sparse_einsum"}
+    assert names["b200_sparse_einsum"].pattern == "*" and names["b200_sparse_einsum"].backend == "gpu"
+
+
+@pytest.mark.parametrize("n_ranks", [1, 2, 3, 4, 8])
+def test_balanced_segment_ranges(n_ranks):
+    rng = np.random.default_rng(n_ranks)
+    counts = rng.zipf(1.5, size=500).clip(max=2000)
+    so = np.concatenate([[0], np.cumsum(counts)])
+    parts = D.balanced_segment_ranges(so, n_ranks)
+    assert parts[0][0] == 0 and parts[-1][1] == 500
+    for (a, b), (c, d) in zip(parts, parts[1:]):
+        assert b == c and a <= b
+    loads = [so[b] - so[a] for a, b in parts]
+    assert sum(loads) == so[-1]
+    assert max(loads) <= so[-1] / n_ranks + counts.max()
+
+
+def test_balanced_segment_ranges_edge():
+    assert D.balanced_segment_ranges(np.array([0]), 4) == [(0, 0)] * 4
+    parts = D.balanced_segment_ranges(np.array([0, 5]), 4)
+    assert sum(b - a for a, b in parts) == 1
+
+
+@pytest.mark.parametrize("n_ranks", [1, 2, 4, 8])
+def test_balanced_key_ranges(n_ranks):
+    rng = np.random.default_rng(0)
+    counts = (1000 * np.arange(1, 257, dtype=np.float64) ** -1.2).astype(np.int64) + rng.integers(0, 3, 256)
+    parts = D.balanced_key_ranges(counts, n_ranks)
+    assert parts[0][0] == 0 and parts[-1][1] == 256
+    loads = [counts[a:b].sum() for a, b in parts]
+    assert sum(loads) == counts.sum()
+    assert max(loads) <= counts.sum() / n_ranks + counts.max()
