@@ -140,7 +140,7 @@ def run_ours(args):
             ev.setdefault("g", []).append(torch.cuda.Event(enable_timing=True))
             ev["g"][-1].record()
         vals = SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
-                              precision=args.precision)
+                              precision=args.precision, seg_strip=plan.seg_strip)
         if timing:
             ev.setdefault("h", []).append(torch.cuda.Event(enable_timing=True))
             ev["h"][-1].record()
@@ -177,29 +177,52 @@ def run_ours(args):
     del A, B, plan, vals
 
     # ---- end to end through the public API with host buffers
-    out_h = None
-    torch.cuda.synchronize()
-    barrier()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(args.steps):
+    def e2e_step(out_bufs):
         idx = idx_h.to(dev, non_blocking=True)
         val = val_h.to(dev, non_blocking=True)
         b = b_h.to(dev, non_blocking=True)
         A = E.SparseTensor("A", (idx, val, shape)).to_relation((TILE, TILE))
         B = E.SparseTensor("B", b).to_relation((TILE, TILE))
         res = E.execute_sparse(A, B, jk, ks, ak, precision=args.precision)
-        if out_h is None:
-            out_h = torch.empty(res.values.shape, dtype=res.values.dtype, pin_memory=True)
-            oc_h = torch.empty(res.coords.shape, dtype=res.coords.dtype, pin_memory=True)
-        out_h.copy_(res.values, non_blocking=True)
-        oc_h.copy_(res.coords, non_blocking=True)
+        if out_bufs is None:
+            out_bufs = (torch.empty(res.values.shape, dtype=res.values.dtype, pin_memory=True),
+                        torch.empty(res.coords.shape, dtype=res.coords.dtype, pin_memory=True))
+        out_bufs[0].copy_(res.values, non_blocking=True)
+        out_bufs[1].copy_(res.coords, non_blocking=True)
+        return out_bufs
+
+    bufs = e2e_step(None)  # untimed: allocates the pinned result buffers
+    torch.cuda.synchronize()
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        bufs = e2e_step(bufs)
     e2.record()
     torch.cuda.synchronize()
     barrier()
     e2e_ms = s2.elapsed_time(e2)
+    out_h, oc_h = bufs
     h2d = idx_h.numel() * 4 + val_h.numel() * 4 + b_h.numel() * 4
     d2h = out_h.numel() * out_h.element_size() + oc_h.numel() * 4
+
+    # ---- per-phase split of one device-resident step (untimed for the metric)
+    phases = {}
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    evs[0].record()
+    A = E.tile_coo(idx_d, val_d, shape, (TILE, TILE))
+    evs[1].record()
+    B = E.tile_dense(b_d, (TILE, TILE))
+    evs[2].record()
+    plan = SD.plan_pairs(A, B, jk, ak)
+    evs[3].record()
+    SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets, precision=args.precision,
+                   seg_strip=plan.seg_strip)
+    evs[4].record()
+    torch.cuda.synchronize()
+    for name, i in (("tile_coo_A", 0), ("tile_dense_B", 1), ("join_and_group", 2), ("tile_gemm", 3)):
+        phases[name] = round(evs[i].elapsed_time(evs[i + 1]), 3)
+    del A, B, plan
 
     tot = torch.tensor([ms, e2e_ms, float(P), float(P * FLOPS_PER_PAIR)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -243,6 +266,7 @@ def run_ours(args):
                          "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
                          "kernel_ms": round(g_ms, 3)},
             "gpu_launches": int(launches),
+            "phases_ms": phases,
             "clocks": clk.summary(),
             "gen_s": round(gen_s, 1),
         }

@@ -15,7 +15,7 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("EINSPARSE_LIB", os.path.join(HERE, "libeinsparse.so"))
 
-ES_OK, ES_ERR_INVALID, ES_ERR_INDEX, ES_ERR_WORKSPACE, ES_ERR_CUDA, ES_ERR_UNSUPPORTED = range(6)
+ES_OK, ES_ERR_INVALID, ES_ERR_INDEX, ES_ERR_WORKSPACE, ES_ERR_CUDA, ES_ERR_UNSUPPORTED, ES_ERR_TIMEOUT = range(7)
 ES_F32, ES_BF16, ES_F64, ES_I32, ES_I64 = range(5)
 ES_PREC_AUTO, ES_PREC_EXACT, ES_PREC_TC = range(3)
 
@@ -48,10 +48,14 @@ SIGNATURES = {
     "es_segments_plan": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_i64, c_i32p, c_int, c_i64p, c_vp, c_sz,
                                  c_vp, c_vp, c_vp]),
     "es_segments_fill": (c_int, [c_vp, c_vp, c_i64, c_int, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp,
-                                 c_vp]),
+                                 c_int, c_vp, c_vp]),
     "es_output_coords": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_i64, c_i32p, c_int, c_vp, c_vp]),
-    "es_tile_einsum": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_vp, c_int, c_vp, c_int, c_vp, c_vp,
-                               c_i64, c_vp, c_i64, c_vp, c_vp, c_int, c_int, c_vp]),
+    "es_tile_einsum_workspace_size": (c_sz, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_int, c_int, c_i64,
+                                              c_i64, c_int]),
+    "es_tile_einsum": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_vp, c_int, c_i64, c_vp, c_int, c_i64,
+                               c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_sz, c_vp,
+                               c_vp]),
+    "es_tile_einsum_path": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_int, c_int, c_int]),
     "es_out_tile_shape": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_i64p]),
     "es_segsum_workspace_size": (c_sz, [c_i64]),
     "es_segsum_plan": (c_int, [c_vp, c_i64, c_int, c_i64p, c_vp, c_sz, c_vp, c_vp, c_vp]),
@@ -116,3 +120,8 @@ def check(fn: str, status: int):
         if status in (ES_ERR_INVALID, ES_ERR_INDEX):
             raise ValueError(f"{fn}: {msg}")
         raise EinsparseError(fn, status, msg)
+
+
+def _dtype_code(dt) -> int:
+    import torch
+    return {torch.float32: ES_F32, torch.bfloat16: ES_BF16, torch.float64: ES_F64}[dt]

@@ -60,7 +60,7 @@ def _group_by(index: torch.Tensor, n_rows: int):
     sp = torch.empty(P, dtype=torch.int32, device=dev)
     L.check("es_segments_fill", lib.es_segments_fill(
         idx.data_ptr(), zero.data_ptr(), P, 1, ext, ws.data_ptr(), ws.numel(), G, oc.data_ptr(), so.data_ptr(),
-        None, None, sp.data_ptr(), st))
+        None, None, sp.data_ptr(), 0, None, st))
     return sp, so, oc.reshape(-1)
 
 

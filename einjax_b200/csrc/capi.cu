@@ -19,6 +19,7 @@ extern "C" const char* es_status_string(int status) {
     case ES_ERR_WORKSPACE: return "workspace too small";
     case ES_ERR_CUDA: return "CUDA error";
     case ES_ERR_UNSUPPORTED: return "unsupported dtype, rank or size";
+    case ES_ERR_TIMEOUT: return "a bounded device-side wait ran out";
     default: return "unknown status";
   }
 }

@@ -262,11 +262,37 @@ extern "C" int es_out_tile_shape(const char* kernel_string, const int64_t* lhs_t
   return d.out_nd;
 }
 
+static bool want_tc(int precision) { return precision == ES_PREC_AUTO || precision == ES_PREC_TC; }
+
+extern "C" int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
+                                   const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype,
+                                   int precision) {
+  EinsumDesc d;
+  int st = parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d);
+  if (st != ES_OK) return -st;
+  TcConfig c;
+  if (want_tc(precision) && tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, &c)) return 1;
+  if (precision == ES_PREC_TC) return -ES_ERR_UNSUPPORTED;
+  return 0;
+}
+
+extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
+                                                const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype,
+                                                int64_t rhs_rows, int64_t num_segments, int precision) {
+  EinsumDesc d;
+  if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
+  TcConfig c;
+  if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, &c)) return 0;
+  return tc_workspace_size(c, rhs_rows, num_segments);
+}
+
 extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
-                              int rhs_nd, const void* lhs_values, int lhs_dtype, const void* rhs_values,
-                              int rhs_dtype, const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
-                              const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
-                              void* out_values, int out_dtype, int precision, void* stream) {
+                              int rhs_nd, const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                              const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
+                              const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
+                              int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
+                              void* out_values, int out_dtype, int precision, void* workspace,
+                              size_t workspace_bytes, int32_t* error_dev, void* stream) {
   EinsumDesc d;
   ES_TRY(parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d));
   if (out_dtype != ES_F32 && out_dtype != ES_BF16) return ES_ERR_UNSUPPORTED;
@@ -275,10 +301,16 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
   const int64_t nseg = seg_offsets ? num_segments : num_pairs;
   if (nseg <= 0 || num_pairs <= 0) return ES_OK;
   cudaStream_t st = as_stream(stream);
-  if (precision != ES_PREC_EXACT) {
-    int r = tc_try_launch(d, lhs_values, lhs_dtype, rhs_values, rhs_dtype, pair_lhs, pair_rhs, seg_offsets, nseg,
-                          seg_out_index, out_values, out_dtype, precision, st);
-    if (r != ES_ERR_UNSUPPORTED) return r;
+  if (want_tc(precision)) {
+    TcConfig c;
+    // the tensor-core path walks each segment's pairs as one sorted lhs
+    // sequence; per-pair calls (no segments) stay on the SIMT path
+    if (seg_offsets && tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, &c)) {
+      const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, seg_offsets, nseg,
+                              seg_out_index, seg_strip, out_values, out_dtype, workspace, workspace_bytes, error_dev,
+                              st);
+      if (r != ES_ERR_UNSUPPORTED || precision == ES_PREC_TC) return r;
+    }
     if (precision == ES_PREC_TC) return ES_ERR_UNSUPPORTED;
   }
   return launch_simt(d, lhs_values, lhs_dtype, rhs_values, rhs_dtype, pair_lhs, pair_rhs, seg_offsets, nseg,

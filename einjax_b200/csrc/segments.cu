@@ -135,6 +135,17 @@ __global__ void seg_offsets_kernel(const SegHeader* hdr, const uint64_t* k0, con
   }
 }
 
+// Strip key of each segment: its output key with the trailing
+// (out_nd - strip_dims) coordinates divided out, i.e. the packed leading
+// strip_dims output coordinates. Non-decreasing in segment order.
+__global__ void seg_strip_kernel(const SegHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
+                                 const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
+                                 uint64_t divisor, int64_t* __restrict__ strip) {
+  const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x)
+    if (flags[s]) strip[excl[s]] = static_cast<int64_t>(keys[s] / divisor);
+}
+
 __global__ void gather_pairs_kernel(const SegHeader* hdr, const uint32_t* p0, const uint32_t* p1, int64_t n,
                                     const int32_t* __restrict__ li, const int32_t* __restrict__ ri,
                                     int32_t* __restrict__ sli, int32_t* __restrict__ sri, int32_t* __restrict__ spi) {
@@ -268,7 +279,8 @@ extern "C" int es_segments_plan(const int32_t* lhs_coords, int lhs_ndim, const i
 extern "C" int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs, int out_ndim,
                                 const int64_t* out_extents, void* workspace, size_t workspace_bytes,
                                 int64_t num_segments, int32_t* out_coords, int64_t* seg_offsets,
-                                int32_t* seg_lhs_idx, int32_t* seg_rhs_idx, int32_t* seg_pair_idx, void* stream) {
+                                int32_t* seg_lhs_idx, int32_t* seg_rhs_idx, int32_t* seg_pair_idx, int strip_dims,
+                                int64_t* seg_strip, void* stream) {
   cudaStream_t st = as_stream(stream);
   if (num_pairs <= 0 || num_segments <= 0) return ES_OK;
   AggKeys ak;
@@ -282,6 +294,13 @@ extern "C" int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, 
             w.excl, ak, out_coords, seg_offsets, (int64_t*)nullptr);
   ES_LAUNCH(gather_pairs_kernel, grid_for(num_pairs, 256), 256, 0, st, w.hdr, w.perm, w.rb.vals_alt, num_pairs,
             lhs_idx, rhs_idx, seg_lhs_idx, seg_rhs_idx, seg_pair_idx);
+  if (seg_strip) {
+    if (strip_dims < 0 || strip_dims > out_ndim) return ES_ERR_INVALID;
+    uint64_t div = 1;
+    for (int d = strip_dims; d < out_ndim; ++d) div *= static_cast<uint64_t>(out_extents[d]);
+    ES_LAUNCH(seg_strip_kernel, grid_for(num_pairs, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_pairs, w.flags,
+              w.excl, div, seg_strip);
+  }
   return ES_OK;
 }
 

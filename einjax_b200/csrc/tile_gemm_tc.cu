@@ -1,12 +1,903 @@
-// Tensor-core tile GEMMs (tcgen05 + TMEM) for the segmented tile einsum.
+// Tensor-core tile GEMM (tcgen05 + TMEM + bulk async copies) for plain
+// block-sparse tile matmuls, with the segment-sum fused into the TMEM
+// accumulator.
+//
+// A work item is up to G segments of one "strip" (segments whose output
+// tiles share the lhs-derived coordinates, e.g. one output tile row of a
+// block-sparse matmul). Their pair lists all walk lhs tiles in ascending
+// order; a G-way merge turns them into steps (one lhs tile, up to G rhs
+// tiles), and each step contributes
+//     D(Mt x G*Nt) += lhs(Mt x Kt) * [rhs_0 | ... | rhs_{G-1}](Kt x G*Nt)
+// (absent rhs tiles are zero), or the transposed product when Mt is too
+// small for the 128-row MMA. The whole strip accumulates in TMEM; the
+// epilogue writes each segment's output tile once. Summation order over a
+// segment's pairs is the join order, as in the reference
+// (execution/sparse_dispatch.py:165-169).
+//
+// fp32 operands use the 3-pass split-TF32 scheme (x = hi + lo with hi
+// rounded to TF32; D += A_hi B_hi + A_hi B_lo + A_lo B_hi; Ootomo & Yokota,
+// "Recovering single precision accuracy from Tensor Cores while surpassing
+// the FP32 theoretical peak performance", IJHPCA 2022), giving fp32-level
+// error; bf16 operands take one kind::f16 pass with fp32 accumulation.
+//
+// Roles (160 threads): warps 0-3 produce stages (G-way merge, bulk async
+// copies of the rhs "panel" — pre-split once per call into the exact
+// shared-memory image — and the split of the lhs chunk) and run the
+// epilogue; warp 4 allocates TMEM and one lane issues the MMAs. Every wait
+// is bounded; on expiry the CTA raises ES_ERR_TIMEOUT, drains its own
+// copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstring>
+#include <vector>
+
 #include "common.cuh"
+#include "scan.cuh"
 #include "tile_gemm_tc.h"
 
 namespace es {
+namespace {
 
-int tc_try_launch(const EinsumDesc&, const void*, int, const void*, int, const int32_t*, const int32_t*,
-                  const int64_t*, int64_t, const int32_t*, void*, int, int, cudaStream_t) {
-  return ES_ERR_UNSUPPORTED;
+constexpr int kProducers = 128;  // warps 0-3: split + epilogue
+constexpr int kMmaWarp = 4;
+constexpr int kSchedWarp = 5;     // merge + bulk copies
+constexpr int kThreads = 192;
+constexpr int kMaxG = 8;
+constexpr int kMaxStages = 8;
+constexpr int kWin = 16;          // prefetched pair entries per segment
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+struct Step {
+  int lhs;
+  int k0;
+  int done;
+  int pad;
+  int rhs[kMaxG];
+};
+
+struct Ctrl {
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t copy[kMaxStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  Step ring[kMaxStages];
+  int win_l[kMaxG][kWin];  // scheduler's window of upcoming (lhs, rhs) pairs
+  int win_r[kMaxG][kWin];
+};
+
+struct TcParams {
+  TcConfig c;
+  const uint8_t* lhs;
+  int64_t lhs_rows;
+  const uint8_t* pan_hi;
+  const uint8_t* pan_lo;
+  int64_t rhs_rows;
+  const int32_t* pl;
+  const int32_t* pr;
+  const int64_t* seg_off;
+  const int32_t* item_first;
+  const int32_t* item_count;
+  const int64_t* num_items;
+  const int32_t* seg_out;
+  void* out;
+  int odt;
+  int32_t* err;
+};
+
+// ---------------------------------------------------------------- PTX glue
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// 4-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+template <bool F32>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  if constexpr (F32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accum)
+        : "memory");
+  }
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, no swizzle (canonical "interleaved"
+// layout of 8 x 16-byte core matrices), Blackwell descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B TF32 (2) or BF16 (1), majors, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t make_idesc(bool tf32, bool a_mn, bool b_mn, int M, int N) {
+  return (1u << 4) | ((tf32 ? 2u : 1u) << 7) | ((tf32 ? 2u : 1u) << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Bounded wait. Returns false when this CTA has aborted (here or elsewhere).
+__device__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctrl* ctl, int32_t* err) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
+    if (i > 32) __nanosleep(128);
+  }
+  *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
+  if (err) atomicExch(err, ES_ERR_TIMEOUT);
+  return false;
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight work).
+__device__ void drain_bar(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return;
+    if (i > 32) __nanosleep(128);
+  }
+}
+
+// Round-to-nearest (ties away) of fp32 to the TF32 grid by integer
+// arithmetic on the bit pattern, and the exact fp32 remainder.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  const uint32_t b = __float_as_uint(x);
+  hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
+  lo = x - hi;
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
+                                                               const __grid_constant__ CUtensorMap lhs_map) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const TcConfig& c = p.c;
+  Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t W = *p.num_items;
+  if (static_cast<int64_t>(blockIdx.x) >= W) return;
+
+  constexpr int NH = F32 ? 2 : 1;      // operand copies: hi (and lo)
+  constexpr int EPU = F32 ? 4 : 8;     // elements per 16-byte chunk
+  constexpr int ESZ = F32 ? 4 : 2;
+  constexpr int KSTEP = F32 ? 8 : 16;  // k per MMA instruction
+  // both operands are K-major: 8-row x 16-byte core matrices, k-chunks of a
+  // row group adjacent (LBO = 128 B), row groups KC/EPU chunks apart (SBO)
+  const int sbo = (c.KC / EPU) * 128;
+  const int blk_bytes = c.Nt * c.KC * ESZ;   // one rhs tile's k-chunk = one panel slot
+  const int nchunks = c.Kt / c.KC;
+  // stage layout: [lhs hi | lhs lo | panel hi | panel lo] (bf16: [lhs | panel]);
+  // the TMA lands the raw lhs chunk, already in canonical order, in the last
+  // lhs buffer, where the fp32 split rewrites it chunk by chunk in place
+  const int off_lhs = 0;
+  const int off_raw = (NH - 1) * c.lhs_bytes;
+  const int off_pan = NH * c.lhs_bytes;
+
+  if (tid == 0) {
+    for (int s = 0; s < c.stages; ++s) {
+      mbar_init(&ctl->full[s], kProducers);
+      mbar_init(&ctl->empty[s], 1);
+      mbar_init(&ctl->copy[s], 1);
+    }
+    mbar_init(&ctl->acc_full, 1);
+    mbar_init(&ctl->acc_empty, kProducers);
+    mbar_init(&ctl->drain, 1);
+    ctl->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == kMmaWarp) tmem_alloc(&ctl->tmem_base, static_cast<uint32_t>(c.tmem_cols));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const int col_per_half = c.swap ? c.Mt : c.n_mma;
+
+  if (warp == kSchedWarp) {
+    // ------------------------------------- scheduler: merge + bulk copies
+    uint32_t it = 0;
+    int last_copy_it[kMaxStages];
+    for (int s = 0; s < kMaxStages; ++s) last_copy_it[s] = -1;
+    bool aborted = false;
+    for (int64_t item = blockIdx.x; item < W && !aborted; item += gridDim.x) {
+      const int s0 = p.item_first[item];
+      const int gcnt = p.item_count[item];
+      int64_t cur = 0, end = 0;
+      if (lane < gcnt) {
+        cur = p.seg_off[s0 + lane];
+        end = p.seg_off[s0 + lane + 1];
+      }
+      int wpos = kWin;  // window exhausted: refill on first use
+      int step_lhs = -1, my_rhs = -1, done = 0;
+      for (int chunk = nchunks;; ++chunk) {
+        if (chunk == nchunks) {
+          // next merge step: the smallest pending lhs tile over the segments
+          if (lane < gcnt && wpos == kWin && cur < end) {
+            for (int q = 0; q < kWin; ++q) {
+              const int64_t i = cur + q;
+              ctl->win_l[lane][q] = i < end ? p.pl[i] : INT_MAX;
+              ctl->win_r[lane][q] = i < end ? p.pr[i] : -1;
+            }
+            wpos = 0;
+          }
+          const int v = (lane < gcnt && cur < end) ? ctl->win_l[lane][wpos] : INT_MAX;
+          const int kmin = __reduce_min_sync(0xffffffffu, v);
+          if (kmin == INT_MAX) {
+            done = 1;
+            my_rhs = -1;
+          } else {
+            const bool mine = v == kmin;
+            my_rhs = mine ? ctl->win_r[lane][wpos] : -1;
+            if (mine) {
+              ++cur;
+              ++wpos;
+            }
+            step_lhs = kmin;
+          }
+          chunk = 0;
+        }
+        const int stage = static_cast<int>(it % c.stages);
+        const uint32_t ph = (it / c.stages) & 1u;
+        if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
+          aborted = true;
+          break;
+        }
+        Step& sr = ctl->ring[stage];
+        if (lane < kMaxG) sr.rhs[lane] = done ? -1 : my_rhs;
+        if (lane == 0) {
+          sr.lhs = step_lhs;
+          sr.k0 = chunk * c.KC;
+          sr.done = done;
+        }
+        __syncwarp();
+        if (done) {
+          if (lane == 0) mbar_arrive_expect_tx(&ctl->copy[stage], 0);
+          ++it;
+          break;
+        }
+        const int k0 = chunk * c.KC;
+        uint8_t* sbase = smem + stage * c.stage_bytes;
+        const int li = step_lhs;
+        const bool lok = li >= 0 && li < p.lhs_rows;
+        int present = 0;
+        for (int g = 0; g < c.G; ++g) {
+          const int r = sr.rhs[g];
+          present += (r >= 0 && r < p.rhs_rows) ? 1 : 0;
+        }
+        bool consec = present == c.G && sr.rhs[0] + c.G <= p.rhs_rows;
+        for (int g = 1; g < c.G; ++g) consec = consec && sr.rhs[g] == sr.rhs[0] + g;
+        if (lane == 0) {
+          const uint32_t bytes = static_cast<uint32_t>((lok ? c.lhs_bytes : 0) + present * NH * blk_bytes);
+          mbar_arrive_expect_tx(&ctl->copy[stage], bytes);
+          last_copy_it[stage] = static_cast<int>(it);
+          if (!lok && p.err) atomicExch(p.err, ES_ERR_INDEX);
+          // raw lhs chunk straight into the canonical K-major layout
+          if (lok) tma_load_4d(sbase + off_raw, &lhs_map, 0, 0, k0 / EPU, li * (c.Mt / 8), &ctl->copy[stage]);
+        }
+        // panel: per k-chunk the pre-laid rhs tiles sit tile after tile, so
+        // consecutive rhs tiles (a dense rhs row) arrive in one copy
+        const int64_t cbase = static_cast<int64_t>(k0 / c.KC) * p.rhs_rows;
+        if (consec) {
+          if (lane < NH)
+            bulk_g2s(sbase + off_pan + lane * c.pan_bytes,
+                     (lane ? p.pan_lo : p.pan_hi) + (cbase + sr.rhs[0]) * blk_bytes,
+                     static_cast<uint32_t>(c.G * blk_bytes), &ctl->copy[stage]);
+        } else {
+          for (int j = lane; j < c.G * NH; j += 32) {
+            const int hl = j % NH, g = j / NH;
+            const int r = sr.rhs[g];
+            if (r < 0 || r >= p.rhs_rows) continue;
+            bulk_g2s(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes,
+                     (hl ? p.pan_lo : p.pan_hi) + (cbase + r) * blk_bytes, static_cast<uint32_t>(blk_bytes),
+                     &ctl->copy[stage]);
+          }
+        }
+        ++it;
+      }
+    }
+    if (aborted && lane == 0) {
+      for (int s = 0; s < c.stages; ++s)
+        if (last_copy_it[s] >= 0) drain_bar(&ctl->copy[s], (static_cast<uint32_t>(last_copy_it[s]) / c.stages) & 1u);
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------ split + epilogue
+    uint32_t it = 0, item_iter = 0;
+    bool aborted = false;
+    for (int64_t item = blockIdx.x; item < W; item += gridDim.x, ++item_iter) {
+      const int s0 = p.item_first[item];
+      const int gcnt = p.item_count[item];
+      while (true) {
+        const int stage = static_cast<int>(it % c.stages);
+        const uint32_t ph = (it / c.stages) & 1u;
+        if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) {
+          aborted = true;
+          break;
+        }
+        const Step& st = ctl->ring[stage];
+        if (st.done) {
+          mbar_arrive(&ctl->full[stage]);
+          ++it;
+          break;
+        }
+        uint8_t* sbase = smem + stage * c.stage_bytes;
+        const bool lok = st.lhs >= 0 && st.lhs < p.lhs_rows;
+        // fp32: split the canonical raw chunk in place (x -> hi, lo); a
+        // missing lhs tile reads as zeros
+        if constexpr (F32) {
+          const int nf = c.Mt * (c.KC / EPU);
+          for (int f = tid; f < nf; f += kProducers) {
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (lok) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+            float4 hi, lo;
+            split_tf32(x.x, hi.x, lo.x);
+            split_tf32(x.y, hi.y, lo.y);
+            split_tf32(x.z, hi.z, lo.z);
+            split_tf32(x.w, hi.w, lo.w);
+            *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
+            *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
+          }
+        } else {
+          if (!lok) {
+            for (int f = tid; f < c.lhs_bytes / 16; f += kProducers)
+              *reinterpret_cast<uint4*>(sbase + off_lhs + f * 16) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        // zero the panel slots of absent rhs tiles
+        for (int g = 0; g < c.G; ++g) {
+          const int r = st.rhs[g];
+          if (r >= 0 && r < p.rhs_rows) continue;
+          if (r >= p.rhs_rows && tid == 0 && p.err) atomicExch(p.err, ES_ERR_INDEX);
+          const int per = blk_bytes / 16;
+          for (int q = tid; q < NH * per; q += kProducers) {
+            const int hl = q / per, w16 = q % per;
+            *reinterpret_cast<uint4*>(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes + w16 * 16) =
+                make_uint4(0, 0, 0, 0);
+          }
+        }
+        fence_proxy_async();
+        mbar_arrive(&ctl->full[stage]);
+        ++it;
+      }
+      if (aborted) break;
+      // ---- epilogue
+      if (!wait_bar(&ctl->acc_full, item_iter & 1u, ctl, p.err)) {
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+      const int quad = warp;  // TMEM lanes [32*quad, 32*quad+32)
+      for (int h = 0; h < c.halves; ++h) {
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + h * col_per_half;
+        if (!c.swap) {
+          const int m = h * 128 + quad * 32 + lane;
+          for (int c0 = 0; c0 < c.n_mma; c0 += 32) {
+            float v[32];
+            tmem_ld32(tbase + c0, v);
+            if (m < c.Mt) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const int col = c0 + j;
+                const int g = col / c.Nt, n = col % c.Nt;
+                if (col >= c.n_mma || g >= gcnt) continue;
+                const int64_t row = p.seg_out ? p.seg_out[s0 + g] : static_cast<int64_t>(s0 + g);
+                const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m) * c.Nt + n;
+                if (p.odt == ES_F32) {
+                  *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) =
+                      make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                } else {
+                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + o;
+                  ob[0] = __float2bfloat16_rn(v[j]);
+                  ob[1] = __float2bfloat16_rn(v[j + 1]);
+                  ob[2] = __float2bfloat16_rn(v[j + 2]);
+                  ob[3] = __float2bfloat16_rn(v[j + 3]);
+                }
+              }
+            }
+          }
+        } else {
+          const int r = h * 128 + quad * 32 + lane;  // panel row = (g, n)
+          const int g = r / c.Nt, n = r % c.Nt;
+          const bool live = g < gcnt;
+          const int64_t row = live ? (p.seg_out ? p.seg_out[s0 + g] : static_cast<int64_t>(s0 + g)) : 0;
+          for (int m0 = 0; m0 < c.Mt; m0 += 32) {
+            float v[32];
+            tmem_ld32(tbase + m0, v);
+            if (live) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (m0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
+                const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m0 + j) * c.Nt + n;
+                if (p.odt == ES_F32) static_cast<float*>(p.out)[o] = v[j];
+                else static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v[j]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&ctl->acc_empty);
+    }
+  } else {
+    // ------------------------------------------------------------ MMA warp
+    const uint32_t idesc = make_idesc(F32, false, false, 128, c.swap ? c.Mt : c.n_mma);
+    uint32_t it = 0, item_iter = 0;
+    bool aborted = false;
+    for (int64_t item = blockIdx.x; item < W && !aborted; item += gridDim.x, ++item_iter) {
+      if (item_iter > 0 && !wait_bar(&ctl->acc_empty, (item_iter - 1) & 1u, ctl, p.err)) {
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+      bool first = true;
+      while (true) {
+        const int stage = static_cast<int>(it % c.stages);
+        const uint32_t ph = (it / c.stages) & 1u;
+        if (!wait_bar(&ctl->full[stage], ph, ctl, p.err)) {
+          aborted = true;
+          break;
+        }
+        const int sdone = ctl->ring[stage].done;
+        if (sdone) {
+          if (lane == 0) mbar_arrive(&ctl->empty[stage]);
+          __syncwarp();
+          ++it;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sb = smem_u32(smem + stage * c.stage_bytes);
+          const uint32_t lhs0 = sb + off_lhs, lhs1 = lhs0 + c.lhs_bytes;
+          const uint32_t pan0 = sb + off_pan, pan1 = pan0 + c.pan_bytes;
+          const int ksteps = c.KC / KSTEP;
+          for (int ks = 0; ks < ksteps; ++ks) {
+            const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
+            for (int h = 0; h < c.halves; ++h) {
+              const uint32_t d = tmem + h * col_per_half;
+              const uint32_t acc0 = (first && ks == 0) ? 0u : 1u;
+              const uint32_t hoff = koff + h * 16 * sbo;  // rows 128h.. of the M operand
+              // M operand: lhs (plain) or the rhs panel (transposed product)
+              const uint32_t am0 = (c.swap ? pan0 : lhs0) + hoff, am1 = (c.swap ? pan1 : lhs1) + hoff;
+              const uint32_t bn0 = (c.swap ? lhs0 : pan0) + koff, bn1 = (c.swap ? lhs1 : pan1) + koff;
+              const uint64_t a_hi = smem_desc(am0, 128, sbo), b_hi = smem_desc(bn0, 128, sbo);
+              umma<F32>(d, a_hi, b_hi, idesc, acc0);
+              if constexpr (F32) {
+                umma<F32>(d, a_hi, smem_desc(bn1, 128, sbo), idesc, 1u);
+                umma<F32>(d, smem_desc(am1, 128, sbo), b_hi, idesc, 1u);
+              }
+            }
+          }
+          umma_commit(&ctl->empty[stage]);
+        }
+        __syncwarp();
+        first = false;
+        ++it;
+      }
+      if (aborted) break;
+      if (lane == 0) umma_commit(&ctl->acc_full);
+      __syncwarp();
+    }
+    if (aborted && lane == 0) {
+      umma_commit(&ctl->drain);
+      drain_bar(&ctl->drain, 0);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, static_cast<uint32_t>(c.tmem_cols));
+  }
+}
+
+// ------------------------------------------------------- preparation kernels
+
+// rhs tile t (Kt x Nt, n contiguous) -> per k-chunk c of KC rows a K-major
+// canonical block [n/8][k-chunk of EPU][n%8] of 16-byte chunks, i.e. the
+// transposed tile in exactly the layout one panel slot has in shared memory.
+// Blocks are stored chunk-major ([c][t]) so consecutive tiles of one chunk
+// are contiguous.
+template <bool F32>
+__global__ void layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt, int KC,
+                                  void* __restrict__ hi, void* __restrict__ lo) {
+  constexpr int EPU = F32 ? 4 : 8;
+  const int64_t te = static_cast<int64_t>(Kt) * Nt;
+  const int64_t total = rows * te;
+  const int kq = KC / EPU;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = e / te;
+    const int rem = static_cast<int>(e - t * te);
+    const int k = rem / Nt, n = rem % Nt;
+    const int cidx = k / KC, kl = k % KC;
+    const int64_t blk = (static_cast<int64_t>(cidx) * rows + t) * static_cast<int64_t>(Nt) * KC;
+    const int64_t dst = blk + (static_cast<int64_t>((n / 8) * kq + kl / EPU) * 8 + (n % 8)) * EPU + kl % EPU;
+    if constexpr (F32) {
+      float h, l;
+      split_tf32(static_cast<const float*>(rhs)[e], h, l);
+      static_cast<float*>(hi)[dst] = h;
+      static_cast<float*>(lo)[dst] = l;
+    } else {
+      static_cast<__nv_bfloat16*>(hi)[dst] = static_cast<const __nv_bfloat16*>(rhs)[e];
+    }
+  }
+}
+
+__global__ void item_heads_kernel(const int64_t* __restrict__ strip, int64_t nseg, int G, uint32_t* __restrict__ flags,
+                                  int32_t* __restrict__ cnt) {
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg; s += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t key = strip[s];
+    int64_t lo = 0, hi = s;  // first index with strip >= key
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (strip[mid] < key) lo = mid + 1; else hi = mid;
+    }
+    const int64_t first = lo;
+    lo = s + 1;
+    hi = nseg;  // first index with strip > key
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (strip[mid] <= key) lo = mid + 1; else hi = mid;
+    }
+    const int64_t pos = s - first;
+    flags[s] = (pos % G == 0) ? 1u : 0u;
+    const int64_t left = lo - s;
+    cnt[s] = static_cast<int32_t>(left < G ? left : G);
+  }
+}
+
+__global__ void item_place_kernel(const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
+                                  const int32_t* __restrict__ cnt, int64_t nseg, int32_t* __restrict__ first,
+                                  int32_t* __restrict__ count) {
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg; s += (int64_t)gridDim.x * blockDim.x) {
+    if (!flags[s]) continue;
+    first[excl[s]] = static_cast<int32_t>(s);
+    count[excl[s]] = cnt[s];
+  }
+}
+
+__global__ void item_identity_kernel(int64_t nseg, int32_t* __restrict__ first, int32_t* __restrict__ count,
+                                     int64_t* __restrict__ num) {
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg; s += (int64_t)gridDim.x * blockDim.x) {
+    first[s] = static_cast<int32_t>(s);
+    count[s] = 1;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) *num = nseg;
+}
+
+struct TcWs {
+  uint8_t* pan_hi;
+  uint8_t* pan_lo;
+  int32_t* item_first;
+  int32_t* item_count;
+  uint32_t* flags;
+  uint32_t* excl;
+  int32_t* cnt;
+  uint32_t* scan;
+  int64_t* num_items;
+};
+
+template <typename C>
+void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t nseg) {
+  const int64_t pan_elems = rhs_rows * c.Kt * c.Nt;
+  const int esz = c.fp32 ? 4 : 2;
+  w.pan_hi = cv.template take<uint8_t>(pan_elems * esz);
+  w.pan_lo = c.fp32 ? cv.template take<uint8_t>(pan_elems * esz) : nullptr;
+  w.item_first = cv.template take<int32_t>(nseg);
+  w.item_count = cv.template take<int32_t>(nseg);
+  w.flags = cv.template take<uint32_t>(nseg);
+  w.excl = cv.template take<uint32_t>(nseg);
+  w.cnt = cv.template take<int32_t>(nseg);
+  w.scan = cv.template take<uint32_t>(scan_scratch_elems(nseg));
+  w.num_items = cv.template take<int64_t>(1);
+}
+
+struct SizeOnly {
+  Sizer s;
+  template <typename T>
+  T* take(int64_t n) {
+    s.take<T>(n);
+    return nullptr;
+  }
+};
+
+// Flattened offsets of one label group (mixed radix, outermost first).
+std::vector<int64_t> group_offsets(const EinGroup& g, int which) {
+  std::vector<int64_t> out(g.total);
+  for (int idx = 0; idx < g.total; ++idx) {
+    int rem = idx;
+    int64_t o = 0;
+    for (int q = g.n - 1; q >= 0; --q) {
+      const int x = rem % g.size[q];
+      rem /= g.size[q];
+      const int st = which == 0 ? g.lstride[q] : which == 1 ? g.rstride[q] : g.ostride[q];
+      o += static_cast<int64_t>(x) * st;
+    }
+    out[idx] = o;
+  }
+  return out;
+}
+
+}  // namespace
+
+bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, TcConfig* c) {
+  std::memset(c, 0, sizeof(*c));
+  const bool f32 = ldt == ES_F32 && rdt == ES_F32;
+  const bool b16 = ldt == ES_BF16 && rdt == ES_BF16;
+  if (!f32 && !b16) return false;
+  if (odt != ES_F32 && odt != ES_BF16) return false;
+  if (d.B.total != 1) return false;
+  const int Mt = d.M.total, Kt = d.K.total, Nt = d.N.total;
+  // plain matmul layout: lhs m*Kt + k, rhs k*Nt + n, out m*Nt + n
+  auto lm = group_offsets(d.M, 0), om = group_offsets(d.M, 2);
+  auto lk = group_offsets(d.K, 0), rk = group_offsets(d.K, 1);
+  auto rn = group_offsets(d.N, 1), on = group_offsets(d.N, 2);
+  for (int m = 0; m < Mt; ++m)
+    if (lm[m] != static_cast<int64_t>(m) * Kt || om[m] != static_cast<int64_t>(m) * Nt) return false;
+  for (int k = 0; k < Kt; ++k)
+    if (lk[k] != k || rk[k] != static_cast<int64_t>(k) * Nt) return false;
+  for (int n = 0; n < Nt; ++n)
+    if (rn[n] != n || on[n] != n) return false;
+  const int kstep = f32 ? 8 : 16;
+  if (Kt % kstep != 0 || Mt % 8 != 0 || Nt % 8 != 0) return false;
+  c->fp32 = f32 ? 1 : 0;
+  c->Mt = Mt;
+  c->Kt = Kt;
+  c->Nt = Nt;
+  // orientation
+  if (Mt % 128 == 0 && Mt <= 256) {
+    c->swap = 0;
+    c->halves = Mt / 128;
+    int G = have_strips ? 256 / Nt : 1;
+    if (G > kMaxG) G = kMaxG;
+    if (G < 1) return false;
+    while (G > 1 && (G * Nt) % 16 != 0) --G;
+    if ((G * Nt) % 16 != 0 || G * Nt > 256 || G * Nt < 16) return false;
+    c->G = G;
+    c->n_mma = G * Nt;
+  } else if (Mt % 16 == 0 && Mt <= 256 && Mt >= 16) {
+    c->swap = 1;
+    c->n_mma = Mt;
+    int G = 0;
+    if (256 % Nt == 0 && 256 / Nt <= kMaxG && (have_strips || 256 / Nt == 1)) {
+      G = 256 / Nt;
+      c->halves = 2;
+    } else if (128 % Nt == 0 && 128 / Nt <= kMaxG && (have_strips || 128 / Nt == 1)) {
+      G = 128 / Nt;
+      c->halves = 1;
+    } else {
+      return false;
+    }
+    c->G = G;
+  } else {
+    return false;
+  }
+  int cols = c->halves * (c->swap ? Mt : c->n_mma);
+  int pw = 32;
+  while (pw < cols) pw <<= 1;
+  if (pw > 512) return false;
+  c->tmem_cols = pw;
+  const int esz = f32 ? 4 : 2;
+  const int nh = f32 ? 2 : 1;
+  const int ctrl = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
+  const int budget = 227 * 1024 - ctrl;
+  // largest k-chunk that still leaves >= 3 pipeline stages (else >= 2)
+  for (int min_stages : {3, 2}) {
+    for (int kc : {64, 32, 16, 8}) {
+      if (kc % kstep || Kt % kc) continue;
+      const int lb = Mt * kc * esz, pb = c->G * Nt * kc * esz;
+      const int sb = (nh * (lb + pb) + 127) / 128 * 128;
+      int stages = budget / sb;
+      if (stages > kMaxStages) stages = kMaxStages;
+      if (stages < min_stages) continue;
+      c->KC = kc;
+      c->lhs_bytes = lb;
+      c->pan_bytes = pb;
+      c->stage_bytes = sb;
+      c->stages = stages;
+      // at least half the SM's shared memory, so one CTA runs per SM and its
+      // TMEM allocation never waits on another CTA's
+      c->smem_bytes = stages * sb + ctrl;
+      if (c->smem_bytes < 116 * 1024) c->smem_bytes = 116 * 1024;
+      return true;
+    }
+  }
+  return false;
+}
+
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t nseg) {
+  SizeOnly s;
+  TcWs w;
+  tc_layout(s, w, c, rhs_rows, nseg);
+  return s.s.used + 256;
+}
+
+int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
+              const int32_t* pl, const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out,
+              const int64_t* seg_strip, void* out, int odt, void* ws, size_t ws_bytes, int32_t* err,
+              cudaStream_t st) {
+  if (nseg <= 0) return ES_OK;
+  if (nseg >= INT32_MAX || rhs_rows >= INT32_MAX || lhs_rows >= INT32_MAX) return ES_ERR_UNSUPPORTED;
+  Carver cv(ws, ws_bytes);
+  TcWs w;
+  tc_layout(cv, w, c, rhs_rows, nseg);
+  if (cv.overflow) return ES_ERR_WORKSPACE;
+  // 1. rhs tiles into the shared-memory image (split for fp32)
+  const int64_t pe = rhs_rows * c.Kt * c.Nt;
+  if (pe > 0) {
+    if (c.fp32)
+      ES_LAUNCH(layout_rhs_kernel<true>, grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi,
+                w.pan_lo);
+    else
+      ES_LAUNCH(layout_rhs_kernel<false>, grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi,
+                (void*)nullptr);
+  }
+  // 2. work items
+  if (seg_strip && c.G > 1) {
+    ES_LAUNCH(item_heads_kernel, grid_for(nseg, 256), 256, 0, st, seg_strip, nseg, c.G, w.flags, w.cnt);
+    if (cudaMemsetAsync(w.num_items, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
+    ES_TRY(exclusive_scan<uint32_t>(w.flags, w.excl, nseg, reinterpret_cast<uint32_t*>(w.num_items), w.scan, st));
+    ES_LAUNCH(item_place_kernel, grid_for(nseg, 256), 256, 0, st, w.flags, w.excl, w.cnt, nseg, w.item_first,
+              w.item_count);
+  } else {
+    if (c.G != 1) return ES_ERR_INVALID;
+    ES_LAUNCH(item_identity_kernel, grid_for(nseg, 256), 256, 0, st, nseg, w.item_first, w.item_count, w.num_items);
+  }
+  // 3. persistent tensor-core kernel, one CTA per SM
+  TcParams prm;
+  prm.c = c;
+  prm.lhs = static_cast<const uint8_t*>(lhs);
+  prm.lhs_rows = lhs_rows;
+  prm.pan_hi = w.pan_hi;
+  prm.pan_lo = w.pan_lo;
+  prm.rhs_rows = rhs_rows;
+  prm.pl = pl;
+  prm.pr = pr;
+  prm.seg_off = seg_off;
+  prm.item_first = w.item_first;
+  prm.item_count = w.item_count;
+  prm.num_items = w.num_items;
+  prm.seg_out = seg_out;
+  prm.out = out;
+  prm.odt = odt;
+  prm.err = err;
+  // 4-D view of the lhs values for the TMA: (element in 16-byte chunk,
+  // row in 8-row group, k-chunk, row group over all tiles); a box of
+  // (EPU, 8, KC/EPU, Mt/8) lands in shared memory as the canonical K-major
+  // layout [row group][k-chunk][row][element].
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+      return ES_ERR_CUDA;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const int esz = c.fp32 ? 4 : 2, epu = c.fp32 ? 4 : 8;
+  CUtensorMap lhs_map;
+  std::memset(&lhs_map, 0, sizeof(lhs_map));
+  cuuint64_t gdim[4] = {static_cast<cuuint64_t>(epu), 8, static_cast<cuuint64_t>(c.Kt / epu),
+                        static_cast<cuuint64_t>(lhs_rows) * (c.Mt / 8)};
+  cuuint64_t gstride[3] = {static_cast<cuuint64_t>(c.Kt) * esz, static_cast<cuuint64_t>(epu) * esz,
+                           static_cast<cuuint64_t>(8) * c.Kt * esz};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(epu), 8, static_cast<cuuint32_t>(c.KC / epu),
+                       static_cast<cuuint32_t>(c.Mt / 8)};
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  if (lhs_rows <= 0) return ES_OK;
+  CUresult cr = encode(&lhs_map, c.fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                       const_cast<void*>(lhs), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return ES_ERR_UNSUPPORTED;
+  int dev = 0, sms = kSMs;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = nseg < sms ? nseg : sms;
+  if (c.fp32) {
+    if (cudaFuncSetAttribute(tc_strip_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
+        cudaSuccess)
+      return ES_ERR_CUDA;
+    ES_LAUNCH(tc_strip_kernel<true>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+  } else {
+    if (cudaFuncSetAttribute(tc_strip_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
+        cudaSuccess)
+      return ES_ERR_CUDA;
+    ES_LAUNCH(tc_strip_kernel<false>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+  }
+  return ES_OK;
 }
 
 }  // namespace es

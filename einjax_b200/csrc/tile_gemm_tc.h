@@ -1,4 +1,4 @@
-// Tensor-core (tcgen05 / TMEM) paths of the segmented tile einsum.
+// Tensor-core (tcgen05 / TMEM) path of the segmented tile einsum.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -7,11 +7,33 @@
 
 namespace es {
 
-// Launches a tensor-core kernel when one covers this contraction (layout,
-// dtypes, tile sizes); returns ES_ERR_UNSUPPORTED otherwise so the caller
-// can take the SIMT path.
-int tc_try_launch(const EinsumDesc& d, const void* lhs, int ldt, const void* rhs, int rdt, const int32_t* pl,
-                  const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out, void* out,
-                  int odt, int precision, cudaStream_t st);
+// Geometry of one tensor-core launch, fixed on the host.
+struct TcConfig {
+  int fp32;        // 1: fp32 operands, 3-pass split TF32; 0: bf16 operands
+  int swap;        // 1: compute D^T = panel^T * lhs^T (lhs rows become MMA N)
+  int Mt, Kt, Nt;  // tile dims of the plain matmul view
+  int G;           // rhs tiles (segments of one strip) per work item
+  int KC;          // k elements per pipeline stage
+  int stages;
+  int halves;      // 128-row MMA halves (M = 128 * halves)
+  int n_mma;       // MMA N
+  int tmem_cols;   // allocated TMEM columns (power of two)
+  int lhs_bytes;   // one operand copy of a stage's lhs chunk
+  int pan_bytes;   // one operand copy of a stage's panel chunk
+  int stage_bytes;
+  int smem_bytes;  // dynamic shared memory per CTA
+};
+
+// True when the contraction is a plain tile matmul this path covers:
+// lhs (Mt x Kt) k-contiguous, rhs (Kt x Nt) n-contiguous, out (Mt x Nt),
+// size-1 batch labels only, both operands f32 or both bf16.
+bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, TcConfig* c);
+
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t nseg);
+
+int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
+              const int32_t* pl, const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out,
+              const int64_t* seg_strip, void* out, int odt, void* ws, size_t ws_bytes, int32_t* err,
+              cudaStream_t st);
 
 }  // namespace es

@@ -176,7 +176,8 @@ def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_
     s0, s1 = balanced_segment_ranges(plan.seg_offsets.cpu().numpy(), n)[rank]
     if s1 > s0:
         vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs,
-                           plan.seg_offsets[s0:s1 + 1], precision=precision)
+                           plan.seg_offsets[s0:s1 + 1], precision=precision,
+                           seg_strip=plan.seg_strip[s0:s1] if plan.seg_strip is not None else None)
     else:
         vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs[:0], plan.seg_rhs[:0],
                            None, num_out_rows=0, precision=precision)

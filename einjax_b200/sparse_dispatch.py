@@ -122,12 +122,15 @@ def _es_out(dt):
 
 
 def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_offsets=None, seg_out_index=None,
-                out=None, num_out_rows=None, out_dtype=None, precision="auto"):
+                out=None, num_out_rows=None, out_dtype=None, precision="auto", seg_strip=None, check=True):
     """Segmented tile einsum through ``es_tile_einsum``.
 
     Without ``seg_offsets`` every pair is its own segment (per-pair output,
     ``kernel_einsum``); with it, each segment's pairs are summed in fp32 into
     one output tile (row ``seg_out_index[s]`` of ``out`` if given, else row s).
+    ``seg_strip`` (strip key per segment, from the output grouping) lets the
+    tensor-core path batch the segments of one output strip. With ``check``
+    the device error flag is read back (one 4-byte copy).
     """
     lib = L.lib()
     dev = lhs_values.device
@@ -152,12 +155,36 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     pr = pair_rhs.to(torch.int32).contiguous()
     so = seg_offsets.contiguous() if seg_offsets is not None else None
     sx = seg_out_index.to(torch.int32).contiguous() if seg_out_index is not None else None
+    sg = seg_strip.contiguous() if (seg_strip is not None and so is not None) else None
+    lti, rti = L.i64arr(lt), L.i64arr(rt)
+    prec = _PREC[precision]
+    wsb = lib.es_tile_einsum_workspace_size(ks, lti, len(lt), rti, len(rt), es_dtype(lv), es_dtype(rv),
+                                            int(rv.shape[0]), nseg, prec)
+    ws = workspace(wsb, dev) if wsb else None
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
     L.check("es_tile_einsum", lib.es_tile_einsum(
-        ks, L.i64arr(lt), len(lt), L.i64arr(rt), len(rt), lv.data_ptr(), es_dtype(lv), rv.data_ptr(), es_dtype(rv),
-        pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
-        sx.data_ptr() if sx is not None else None, out.data_ptr(), _es_out(out.dtype), _PREC[precision],
-        stream_ptr(dev)))
+        ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
+        int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
+        sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None, out.data_ptr(),
+        _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        err.data_ptr(), stream_ptr(dev)))
+    if check:
+        e = int(err.item())
+        if e:
+            L.check("es_tile_einsum (device)", e)
     return out
+
+
+def tile_einsum_path(kernel_string, lhs_tile, rhs_tile, lhs_dtype=torch.float32, rhs_dtype=torch.float32,
+                     precision="auto") -> str:
+    """"tc" or "simt": the path ``tile_einsum`` takes for these tiles."""
+    lib = L.lib()
+    ks = kernel_string.replace(" ", "").encode()
+    r = lib.es_tile_einsum_path(ks, L.i64arr(lhs_tile), len(lhs_tile), L.i64arr(rhs_tile), len(rhs_tile),
+                                L._dtype_code(lhs_dtype), L._dtype_code(rhs_dtype), _PREC[precision])
+    if r < 0:
+        raise ValueError(f"tile_einsum_path: {lib.es_status_string(-r).decode()}")
+    return "tc" if r == 1 else "simt"
 
 
 def kernel_einsum(lhs_values, rhs_values, lhs_indices, rhs_indices, kernel_string, precision="auto"):
@@ -237,6 +264,7 @@ class PairPlan:
     seg_lhs: torch.Tensor       # int32 (P,), pairs grouped by output tile
     seg_rhs: torch.Tensor
     seg_pair: torch.Tensor      # int32 (P,), original pair index
+    seg_strip: torch.Tensor | None = None  # int64 (O,), strip key (lhs-derived output coords)
 
     @property
     def num_pairs(self) -> int:
@@ -283,10 +311,16 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     sl = torch.empty(P, dtype=torch.int32, device=dev)
     sr = torch.empty(P, dtype=torch.int32, device=dev)
     sp = torch.empty(P, dtype=torch.int32, device=dev)
+    # segments sharing the leading lhs-derived output coordinates form a strip
+    nlead = 0
+    while nlead < out_nd and agg_keys[nlead][0] == 0:
+        nlead += 1
+    strips = nlead > 0 and all(s == 1 for s, _ in agg_keys[nlead:])
+    sg = torch.empty(O, dtype=torch.int64, device=dev) if strips else None
     L.check("es_segments_fill", lib.es_segments_fill(
         li.data_ptr(), ri.data_ptr(), P, out_nd, ext, ws.data_ptr(), ws.numel(), O, oc.data_ptr(), so.data_ptr(),
-        sl.data_ptr(), sr.data_ptr(), sp.data_ptr(), st))
-    return PairPlan(li, ri, oc, so, sl, sr, sp)
+        sl.data_ptr(), sr.data_ptr(), sp.data_ptr(), nlead, sg.data_ptr() if sg is not None else None, st))
+    return PairPlan(li, ri, oc, so, sl, sr, sp, sg)
 
 
 def _resolve_shapes(lhs, rhs, kernel_string, agg_keys, output_shape, output_tile_shape):
@@ -315,7 +349,7 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
     if plan.num_pairs == 0:
         return empty_relation(output_shape, output_tile_shape, lhs.values.dtype, lhs.device)
     vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
-                       precision=precision)
+                       precision=precision, seg_strip=plan.seg_strip)
     return SparseTensorRelation(plan.out_coords, vals, output_shape, output_tile_shape)
 
 

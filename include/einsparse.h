@@ -32,7 +32,8 @@ typedef enum es_status {
   ES_ERR_INDEX = 2,       /* a coordinate outside the grid its shape defines */
   ES_ERR_WORKSPACE = 3,   /* workspace smaller than *_workspace_size reported */
   ES_ERR_CUDA = 4,        /* CUDA runtime error (launch or async) */
-  ES_ERR_UNSUPPORTED = 5  /* dtype / rank / size this build does not handle */
+  ES_ERR_UNSUPPORTED = 5, /* dtype / rank / size this build does not handle */
+  ES_ERR_TIMEOUT = 6      /* a bounded device-side wait ran out; outputs are invalid */
 } es_status;
 
 typedef enum es_dtype { ES_F32 = 0, ES_BF16 = 1, ES_F64 = 2, ES_I32 = 3, ES_I64 = 4 } es_dtype;
@@ -115,7 +116,11 @@ int es_join_fill(int64_t n_lhs, int64_t n_rhs, int nkeys, void* workspace, size_
  * out_coords int32 (O, out_ndim) sorted lexicographically (:161),
  * seg_offsets int64 (O+1) and the pairs regrouped (seg_lhs_idx,
  * seg_rhs_idx int32, P each; seg_pair_idx int32 = original pair index, may
- * be NULL). lhs_idx/rhs_idx are int32.
+ * be NULL). lhs_idx/rhs_idx are int32. With seg_strip non-NULL, fill also
+ * writes per segment the packed value of its first strip_dims output
+ * coordinates (int64, non-decreasing): segments with equal values form a
+ * "strip" that shares its lhs-derived coordinates, which es_tile_einsum
+ * batches into one tensor-core tile.
  * ------------------------------------------------------------------------- */
 size_t es_segments_workspace_size(int64_t num_pairs);
 int es_segments_plan(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs_coords, int rhs_ndim,
@@ -127,7 +132,7 @@ int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num
                      const int64_t* out_extents, void* workspace, size_t workspace_bytes,
                      int64_t num_segments, int32_t* out_coords, int64_t* seg_offsets,
                      int32_t* seg_lhs_idx, int32_t* seg_rhs_idx, int32_t* seg_pair_idx,
-                     void* stream);
+                     int strip_dims, int64_t* seg_strip, void* stream);
 
 /* Per-pair output tile coordinates, int32 (P, out_ndim): the gather of
  * _compute_output_coords (execution/sparse_dispatch.py:174-223). */
@@ -146,15 +151,31 @@ int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs
  * in fp32, where s_out = seg_out_index ? seg_out_index[s] : s.
  * seg_offsets == NULL means every pair is its own segment (the unfused
  * per-pair kernel_einsum, output (P, *out_tile)). Output rows that no segment
- * writes are left untouched. Values dtypes: F32 / BF16 / F64 inputs;
- * F32 / BF16 outputs.
+ * writes are left untouched. lhs_rows / rhs_rows: tiles in each values array
+ * (pair indices outside them raise ES_ERR_INDEX in *error_dev and read as
+ * zero tiles). Values dtypes: F32 / BF16 / F64 inputs; F32 / BF16 outputs.
+ * seg_strip (optional, from es_segments_fill): strip key per segment; the
+ * tensor-core path computes up to 8 segments of one strip in one tile.
+ * workspace: es_tile_einsum_workspace_size bytes (0 for the SIMT path). A
+ * device-side wait that runs out sets *error_dev to ES_ERR_TIMEOUT.
  * ------------------------------------------------------------------------- */
+size_t es_tile_einsum_workspace_size(const char* kernel_string,
+                                     const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
+                                     int lhs_dtype, int rhs_dtype, int64_t rhs_rows, int64_t num_segments,
+                                     int precision);
 int es_tile_einsum(const char* kernel_string,
                    const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
-                   const void* lhs_values, int lhs_dtype, const void* rhs_values, int rhs_dtype,
+                   const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                   const void* rhs_values, int rhs_dtype, int64_t rhs_rows,
                    const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
                    const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
-                   void* out_values, int out_dtype, int precision, void* stream);
+                   const int64_t* seg_strip, void* out_values, int out_dtype, int precision,
+                   void* workspace, size_t workspace_bytes, int32_t* error_dev, void* stream);
+
+/* Which path es_tile_einsum takes for these arguments: 1 tensor cores,
+ * 0 SIMT, negative es_status if the call would be rejected. Host-side. */
+int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
+                        const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype, int precision);
 
 /* Out tile shape of a kernel string (_infer_output_tile_shape,
  * execution/sparse_dispatch.py:506-545). Host-side; returns the out rank or

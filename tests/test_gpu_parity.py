@@ -323,3 +323,58 @@ def test_bf16_batched_vs_oracle():
     rhs = O.Relation(w.rhs.coords, w.rhs.values.astype(np.float64), w.rhs.shape, w.rhs.tile_shape)
     ref = O.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys)
     _assert_rel(res, ref, _mag(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys), RTOL_BF16)
+
+
+# ------------------------------------------------- tensor-core path geometry
+
+def _random_block_sparse(rng, shape, tile, dens, dtype=np.float64):
+    grid = tuple(s // t for s, t in zip(shape, tile))
+    n = int(np.prod(grid))
+    pos = np.sort(rng.choice(n, max(1, int(round(dens * n))), replace=False))
+    coords = np.stack(np.unravel_index(pos, grid), 1).astype(np.int32)
+    return O.Relation(coords, rng.standard_normal((len(pos), *tile)).astype(dtype), shape, tile)
+
+
+TC_CASES = [
+    # (kernel, join, agg, lhs shape, lhs tile, rhs shape, rhs tile, density A, density B, note)
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (1024, 1024), (128, 128), (1024, 1024), (128, 128), 0.2, 0.3, "C1-like"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (2048, 1024), (32, 32), (1024, 256), (32, 32), 0.02, 1.0, "C2-like"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (1024, 1024), (32, 32), (1024, 256), (32, 32), 0.05, 0.5, "C2 sparse B"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (256, 512), (16, 16), (512, 192), (16, 16), 0.1, 0.3, "16 tiles"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (512, 256), (256, 64), (256, 640), (64, 128), 0.5, 0.6, "M=256"),
+    ("ijk,kl->ijl", [(2, 0)], [(0, 0), (0, 1), (1, 1)], (128, 128, 256), (16, 16, 16), (256, 128), (16, 16), 0.01,
+     1.0, "C5-like"),
+    ("bij,bjk->bik", [(0, 0), (2, 1)], [(0, 0), (0, 1), (1, 2)], (3, 512, 512), (1, 64, 64), (3, 512, 512),
+     (1, 64, 64), 0.1, 0.1, "C3-like f32"),
+]
+
+
+@pytest.mark.parametrize("case", TC_CASES, ids=[c[-1] for c in TC_CASES])
+def test_tensor_core_path(case):
+    ks, jk, ak, sa, ta, sb, tb, da, db, _ = case
+    rng = np.random.default_rng(abs(hash(case[-1])) % 1000)
+    lhs, rhs = _random_block_sparse(rng, sa, ta, da), _random_block_sparse(rng, sb, tb, db)
+    from einjax_b200.sparse_dispatch import tile_einsum_path
+    assert tile_einsum_path(ks, ta, tb) == "tc"
+    res = E.execute_sparse(_dev(lhs), _dev(rhs), jk, ks, ak, precision="tc")
+    lhs32 = O.Relation(lhs.coords, lhs.values.astype(np.float32).astype(np.float64), lhs.shape, lhs.tile_shape)
+    rhs32 = O.Relation(rhs.coords, rhs.values.astype(np.float32).astype(np.float64), rhs.shape, rhs.tile_shape)
+    ref = O.execute_sparse(lhs32, rhs32, jk, ks, ak)
+    _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak))
+    exact = E.execute_sparse(_dev(lhs), _dev(rhs), jk, ks, ak, precision="exact")
+    _assert_rel(exact, ref, _mag(lhs, rhs, jk, ks, ak))
+
+
+@pytest.mark.parametrize("tile,bands", [((64, 64), 2), ((32, 32), 4), ((128, 128), 1)])
+def test_tensor_core_bf16(tile, bands):
+    from einjax_b200 import workloads as W
+    rng = np.random.default_rng(tile[0])
+    n = tile[0] * 8
+    lhs = _random_block_sparse(rng, (2, n, n), (1, *tile), 0.2)
+    rhs = _random_block_sparse(rng, (2, n, n), (1, *tile), 0.2)
+    lhs.values = W.round_to_bf16(lhs.values.astype(np.float32)).astype(np.float64)
+    rhs.values = W.round_to_bf16(rhs.values.astype(np.float32)).astype(np.float64)
+    jk, ks, ak = [(0, 0), (2, 1)], "bij,bjk->bik", [(0, 0), (0, 1), (1, 2)]
+    res = E.execute_sparse(_dev(lhs, torch.bfloat16), _dev(rhs, torch.bfloat16), jk, ks, ak, precision="auto")
+    ref = O.execute_sparse(lhs, rhs, jk, ks, ak)
+    _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak), RTOL_BF16)
