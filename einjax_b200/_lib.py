@@ -44,6 +44,8 @@ SIGNATURES = {
     "es_join_plan": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_i32p, c_int, c_i64p, c_vp, c_sz, c_vp, c_vp,
                              c_vp]),
     "es_join_fill": (c_int, [c_i64, c_i64, c_int, c_vp, c_sz, c_i64, c_vp, c_vp, c_int, c_vp]),
+    "es_join_static": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_i32p, c_int, c_i64p, c_vp, c_vp, c_int, c_i64,
+                               c_vp, c_vp, c_vp]),
     "es_segments_workspace_size": (c_sz, [c_i64]),
     "es_segments_plan": (c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp, c_i64, c_i32p, c_int, c_i64p, c_vp, c_sz,
                                  c_vp, c_vp, c_vp]),

@@ -9,6 +9,9 @@
 // the group sizes are prefix-summed into pair offsets. Fill: one thread per
 // output pair finds its RHS tile by binary search over the offsets
 // (load-balanced however skewed the groups are) and writes (i, j).
+#include <cmath>
+#include <mutex>
+
 #include "common.cuh"
 #include "radix_sort.cuh"
 #include "scan.cuh"
@@ -227,5 +230,156 @@ extern "C" int es_join_fill(int64_t n_lhs, int64_t n_rhs, int nkeys, void* works
   else
     ES_LAUNCH(join_fill_kernel<int64_t>, grid, 256, 0, st, w.hdr, w.idx, w.rb.vals_alt, w.counts, w.lo, n_rhs,
               num_pairs, (int64_t*)lhs_idx_out, (int64_t*)rhs_idx_out);
+  return ES_OK;
+}
+
+// ---------------------------------------------------------------------------
+// es_join_static: the coordinate join without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they join: code
+// running inside a host callback or a custom allocator hook, an engine that
+// hands out all device memory up front and forbids cudaMalloc afterwards, or
+// a plugin whose host framework owns every buffer. For them this entry point
+// takes the join's scratch (sort keys, sort buffers, per-RHS counts) from a
+// fixed array in the library's own device memory instead of a workspace. The
+// caller still provides the outputs (pair index arrays with a capacity) and
+// the device int64 that receives the pair count; nothing is synchronised,
+// so the count can be read whenever the caller next waits on the stream.
+//
+// Limits and sharing: at most kStaticMaxTiles tiles on each side (larger
+// inputs are refused with ES_ERR_UNSUPPORTED). The array lives once per GPU
+// that loads the library, for the life of the process, and every call on
+// that GPU uses the same bytes: two calls whose kernels overlap on the GPU
+// (different streams, no ordering between them) race and corrupt each
+// other; serialise them. Each call rewrites everything it reads from the
+// array, so leftovers from an earlier call cannot leak into a result.
+// The first call on a device looks up the array's device address with
+// cudaGetSymbolAddress (once per device, with that device current); make
+// that first call before any stream capture.
+
+namespace es {
+namespace {
+
+constexpr int64_t kStaticMaxTiles = 65536;
+constexpr size_t kStaticScratchBytes = 3u << 20;
+static __device__ __align__(256) unsigned char g_join_scratch[kStaticScratchBytes];
+
+void* static_scratch_ptr(int* status) {
+  constexpr int kMaxDevices = 64;
+  static void* ptrs[kMaxDevices] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *status = ES_ERR_CUDA;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_join_scratch) != cudaSuccess || !p) {
+      *status = ES_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *status = ES_OK;
+  return ptrs[dev];
+}
+
+// Fill from the device-side pair count, writing at most `capacity` pairs.
+template <typename IdxT>
+__global__ void join_fill_capped_kernel(const JoinHeader* hdr, const uint32_t* i0, const uint32_t* i1,
+                                        const int64_t* __restrict__ offsets, const uint32_t* __restrict__ lo,
+                                        int64_t n_r, const int64_t* __restrict__ num_pairs, int64_t capacity,
+                                        IdxT* __restrict__ li, IdxT* __restrict__ ri, int32_t* err) {
+  const int64_t P = *num_pairs;
+  if (P > capacity && err && blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ES_ERR_WORKSPACE);
+  const int64_t n = P < capacity ? P : capacity;
+  const uint32_t* sidx = hdr->sorted_in_alt ? i1 : i0;
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n; p += (int64_t)gridDim.x * blockDim.x) {
+    int64_t a = 0, b = n_r;
+    while (b - a > 1) {
+      const int64_t m = (a + b) >> 1;
+      if (offsets[m] <= p) a = m; else b = m;
+    }
+    li[p] = static_cast<IdxT>(sidx[lo[a] + (p - offsets[a])]);
+    ri[p] = static_cast<IdxT>(a);
+  }
+}
+
+template <typename IdxT>
+__global__ void cross_fill_capped_kernel(int64_t n_r, int64_t P, int64_t capacity, IdxT* __restrict__ li,
+                                         IdxT* __restrict__ ri, int32_t* err) {
+  if (P > capacity && err && blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, ES_ERR_WORKSPACE);
+  const int64_t n = P < capacity ? P : capacity;
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n; p += (int64_t)gridDim.x * blockDim.x) {
+    li[p] = static_cast<IdxT>(p / n_r);
+    ri[p] = static_cast<IdxT>(p % n_r);
+  }
+}
+
+}  // namespace
+}  // namespace es
+
+extern "C" int es_join_static(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, const int32_t* rhs_coords,
+                              int64_t n_rhs, int rhs_ndim, const int32_t* join_keys, int nkeys,
+                              const int64_t* key_extents, void* lhs_idx_out, void* rhs_idx_out, int index_dtype,
+                              int64_t capacity, int64_t* num_pairs_dev, int32_t* error_dev, void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (n_lhs < 0 || n_rhs < 0 || nkeys < 0 || nkeys > ES_MAX_DIMS || capacity < 0) return ES_ERR_INVALID;
+  if (index_dtype != ES_I32 && index_dtype != ES_I64) return ES_ERR_UNSUPPORTED;
+  if (n_lhs > kStaticMaxTiles || n_rhs > kStaticMaxTiles) return ES_ERR_UNSUPPORTED;
+  int status = ES_OK;
+  void* scratch = static_scratch_ptr(&status);
+  if (status != ES_OK) return status;
+  if (nkeys == 0 || n_lhs == 0 || n_rhs == 0) {
+    const int64_t P = nkeys == 0 ? n_lhs * n_rhs : 0;
+    ES_LAUNCH(write_i64_kernel, 1, 32, 0, st, num_pairs_dev, P);
+    if (P > 0) {
+      const int grid = grid_for(P < capacity ? P : capacity, 256);
+      if (index_dtype == ES_I32)
+        ES_LAUNCH(cross_fill_capped_kernel<int32_t>, grid, 256, 0, st, n_rhs, P, capacity, (int32_t*)lhs_idx_out,
+                  (int32_t*)rhs_idx_out, error_dev);
+      else
+        ES_LAUNCH(cross_fill_capped_kernel<int64_t>, grid, 256, 0, st, n_rhs, P, capacity, (int64_t*)lhs_idx_out,
+                  (int64_t*)rhs_idx_out, error_dev);
+    }
+    return ES_OK;
+  }
+  JoinKeys jk;
+  jk.nkeys = nkeys;
+  jk.lhs_nd = lhs_ndim;
+  jk.rhs_nd = rhs_ndim;
+  double bits_f = 0;
+  uint64_t prod = 1;
+  for (int q = 0; q < nkeys; ++q) {
+    jk.ld[q] = join_keys[2 * q];
+    jk.rd[q] = join_keys[2 * q + 1];
+    jk.ext[q] = key_extents[q];
+    if (jk.ld[q] < 0 || jk.ld[q] >= lhs_ndim || jk.rd[q] < 0 || jk.rd[q] >= rhs_ndim) return ES_ERR_INVALID;
+    if (key_extents[q] <= 0) return ES_ERR_INVALID;
+    bits_f += std::log2(static_cast<double>(key_extents[q]));
+    if (bits_f > 62) return ES_ERR_UNSUPPORTED;
+    prod *= static_cast<uint64_t>(key_extents[q]);
+  }
+  JoinWs w;
+  Carver c(scratch, kStaticScratchBytes);
+  join_layout(c, w, n_lhs, n_rhs);
+  if (c.overflow) return ES_ERR_UNSUPPORTED;
+  ES_LAUNCH(join_lhs_keys_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, jk, w.keys, w.idx, error_dev);
+  uint64_t* k = w.keys;
+  uint32_t* v = w.idx;
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n_lhs, 0, bit_length(prod - 1), st));
+  ES_LAUNCH(join_flag_kernel, 1, 32, 0, st, w.hdr, k != w.keys ? 1 : 0);
+  ES_LAUNCH(join_count_kernel, grid_for(n_rhs, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, n_lhs, rhs_coords,
+            n_rhs, jk, w.counts, w.lo, error_dev);
+  ES_TRY(exclusive_scan<int64_t>(w.counts, w.counts, n_rhs, num_pairs_dev, w.scan, st));
+  const int grid = 148 * 8;
+  if (index_dtype == ES_I32)
+    ES_LAUNCH(join_fill_capped_kernel<int32_t>, grid, 256, 0, st, w.hdr, w.idx, w.rb.vals_alt, w.counts, w.lo, n_rhs,
+              num_pairs_dev, capacity, (int32_t*)lhs_idx_out, (int32_t*)rhs_idx_out, error_dev);
+  else
+    ES_LAUNCH(join_fill_capped_kernel<int64_t>, grid, 256, 0, st, w.hdr, w.idx, w.rb.vals_alt, w.counts, w.lo, n_rhs,
+              num_pairs_dev, capacity, (int64_t*)lhs_idx_out, (int64_t*)rhs_idx_out, error_dev);
   return ES_OK;
 }

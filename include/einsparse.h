@@ -106,6 +106,26 @@ int es_join_fill(int64_t n_lhs, int64_t n_rhs, int nkeys, void* workspace, size_
                  int64_t num_pairs, void* lhs_idx_out, void* rhs_idx_out, int index_dtype,
                  void* stream);
 
+/* Allocation-free coordinate join (no counterpart in the reference; an
+ * addition for callers that may not allocate device memory when they join,
+ * e.g. code in a host callback or an engine that reserves all memory up
+ * front). Same pairs and order as es_join_plan + es_join_fill, but the sort
+ * and count scratch comes from a fixed array inside the library (one per
+ * GPU, kept until the process exits) instead of a workspace. At most 65536
+ * tiles per side, else ES_ERR_UNSUPPORTED. The caller passes the outputs:
+ * lhs_idx_out / rhs_idx_out with room for `capacity` pairs and the device
+ * int64 *num_pairs_dev that receives P; if P > capacity only `capacity`
+ * pairs are written and *error_dev becomes ES_ERR_WORKSPACE. Nothing is
+ * allocated or synchronised. Calls whose kernels overlap on one GPU share the
+ * array and race: order them on one stream. The first call on a device looks
+ * up the array's address (cudaGetSymbolAddress); make it before any stream
+ * capture. */
+int es_join_static(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim,
+                   const int32_t* rhs_coords, int64_t n_rhs, int rhs_ndim,
+                   const int32_t* join_keys, int nkeys, const int64_t* key_extents,
+                   void* lhs_idx_out, void* rhs_idx_out, int index_dtype, int64_t capacity,
+                   int64_t* num_pairs_dev, int32_t* error_dev, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Output-tile grouping. Replaces _compute_output_coords + the grouping half of
  * segment_sum (execution/sparse_dispatch.py:174-223, 129-171): the output
