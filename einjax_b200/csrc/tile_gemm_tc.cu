@@ -34,21 +34,26 @@
 #include <vector>
 
 #include "common.cuh"
+#include "radix_sort.cuh"
 #include "scan.cuh"
 #include "tile_gemm_tc.h"
 
 namespace es {
 namespace {
 
-constexpr int kProducers = 128;  // warps 0-3: split + epilogue
+constexpr int kProducers = 128;  // warps 0-3: fp32 split / zero-fill of absent tiles
 constexpr int kMmaWarp = 4;
-constexpr int kSchedWarp = 5;     // merge + bulk copies
-constexpr int kThreads = 192;
+constexpr int kSchedWarp = 5;     // work queue, merge, TMA + bulk copies
+constexpr int kEpiWarp0 = 6;      // warps 6-9: epilogue (TMEM lane quadrant = warp % 4)
+constexpr int kEpilogue = 128;
+constexpr int kThreads = 320;
+constexpr int kItemLog = 16;
 constexpr int kMaxG = 8;
 constexpr int kMaxStages = 8;
 constexpr int kWin = 16;          // prefetched pair entries per segment
 constexpr uint32_t kWaitLimit = 1u << 22;
 
+// done: 0 data stage, 1 end of a work item, 2 no more items
 struct Step {
   int lhs;
   int k0;
@@ -57,16 +62,23 @@ struct Step {
   int rhs[kMaxG];
 };
 
+struct ItemInfo {
+  int s0;
+  int gcnt;
+};
+
 struct Ctrl {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t copy[kMaxStages];
-  uint64_t acc_full;
-  uint64_t acc_empty;
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   Step ring[kMaxStages];
+  ItemInfo item_log[kItemLog];  // items in the order this CTA takes them
+  int exit_at;                  // item count at which the epilogue stops
   int win_l[kMaxG][kWin];  // scheduler's window of upcoming (lhs, rhs) pairs
   int win_r[kMaxG][kWin];
 };
@@ -84,6 +96,8 @@ struct TcParams {
   const int32_t* item_first;
   const int32_t* item_count;
   const int64_t* num_items;
+  const int32_t* order;   // item indices, largest work first
+  int* queue;             // next position in `order`, zero at launch
   const int32_t* seg_out;
   void* out;
   int odt;
@@ -249,16 +263,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t W = *p.num_items;
-  if (static_cast<int64_t>(blockIdx.x) >= W) return;
 
   constexpr int NH = F32 ? 2 : 1;      // operand copies: hi (and lo)
   constexpr int EPU = F32 ? 4 : 8;     // elements per 16-byte chunk
-  constexpr int ESZ = F32 ? 4 : 2;
   constexpr int KSTEP = F32 ? 8 : 16;  // k per MMA instruction
+  constexpr int ESZ = F32 ? 4 : 2;
   // both operands are K-major: 8-row x 16-byte core matrices, k-chunks of a
   // row group adjacent (LBO = 128 B), row groups KC/EPU chunks apart (SBO)
   const int sbo = (c.KC / EPU) * 128;
-  const int blk_bytes = c.Nt * c.KC * ESZ;   // one rhs tile's k-chunk = one panel slot
+  const int blk_bytes = c.Nt * c.KC * ESZ;  // one rhs tile's k-chunk = one panel slot
   const int nchunks = c.Kt / c.KC;
   // stage layout: [lhs hi | lhs lo | panel hi | panel lo] (bf16: [lhs | panel]);
   // the TMA lands the raw lhs chunk, already in canonical order, in the last
@@ -266,6 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   const int off_lhs = 0;
   const int off_raw = (NH - 1) * c.lhs_bytes;
   const int off_pan = NH * c.lhs_bytes;
+  const int col_per_half = c.swap ? c.Mt : c.n_mma;
+  const int acc_stride = c.halves * col_per_half;  // TMEM columns of one accumulator
 
   if (tid == 0) {
     for (int s = 0; s < c.stages; ++s) {
@@ -273,10 +288,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       mbar_init(&ctl->empty[s], 1);
       mbar_init(&ctl->copy[s], 1);
     }
-    mbar_init(&ctl->acc_full, 1);
-    mbar_init(&ctl->acc_empty, kProducers);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->acc_full[b], 1);
+      mbar_init(&ctl->acc_empty[b], kEpilogue);
+    }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
+    ctl->exit_at = -1;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) tmem_alloc(&ctl->tmem_base, static_cast<uint32_t>(c.tmem_cols));
@@ -284,32 +302,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
-  const int col_per_half = c.swap ? c.Mt : c.n_mma;
 
   if (warp == kSchedWarp) {
-    // ------------------------------------- scheduler: merge + bulk copies
+    // --------------------------- scheduler: work queue, merge, async copies
     uint32_t it = 0;
     int last_copy_it[kMaxStages];
     for (int s = 0; s < kMaxStages; ++s) last_copy_it[s] = -1;
     bool aborted = false;
-    for (int64_t item = blockIdx.x; item < W && !aborted; item += gridDim.x) {
-      const int s0 = p.item_first[item];
-      const int gcnt = p.item_count[item];
+    for (uint32_t item_iter = 0; !aborted; ++item_iter) {
+      int q = 0;
+      if (lane == 0) q = atomicAdd(p.queue, 1);
+      q = __shfl_sync(0xffffffffu, q, 0);
+      const bool exit_now = q >= W;
+      int s0 = 0, gcnt = 0;
+      if (!exit_now) {
+        const int item = p.order[q];
+        s0 = p.item_first[item];
+        gcnt = p.item_count[item];
+        if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt};
+      }
       int64_t cur = 0, end = 0;
       if (lane < gcnt) {
         cur = p.seg_off[s0 + lane];
         end = p.seg_off[s0 + lane + 1];
       }
       int wpos = kWin;  // window exhausted: refill on first use
-      int step_lhs = -1, my_rhs = -1, done = 0;
+      int step_lhs = -1, my_rhs = -1, done = exit_now ? 2 : 0;
       for (int chunk = nchunks;; ++chunk) {
-        if (chunk == nchunks) {
+        if (chunk == nchunks && !done) {
           // next merge step: the smallest pending lhs tile over the segments
           if (lane < gcnt && wpos == kWin && cur < end) {
-            for (int q = 0; q < kWin; ++q) {
-              const int64_t i = cur + q;
-              ctl->win_l[lane][q] = i < end ? p.pl[i] : INT_MAX;
-              ctl->win_r[lane][q] = i < end ? p.pr[i] : -1;
+            for (int qq = 0; qq < kWin; ++qq) {
+              const int64_t i = cur + qq;
+              ctl->win_l[lane][qq] = i < end ? p.pl[i] : INT_MAX;
+              ctl->win_r[lane][qq] = i < end ? p.pr[i] : -1;
             }
             wpos = 0;
           }
@@ -387,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         }
         ++it;
       }
+      if (exit_now) break;
     }
     if (aborted && lane == 0) {
       for (int s = 0; s < c.stages; ++s)
@@ -394,74 +421,151 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     }
     __syncwarp();
   } else if (warp < 4) {
-    // ------------------------------------------------ split + epilogue
-    uint32_t it = 0, item_iter = 0;
-    bool aborted = false;
-    for (int64_t item = blockIdx.x; item < W; item += gridDim.x, ++item_iter) {
-      const int s0 = p.item_first[item];
-      const int gcnt = p.item_count[item];
-      while (true) {
-        const int stage = static_cast<int>(it % c.stages);
-        const uint32_t ph = (it / c.stages) & 1u;
-        if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) {
-          aborted = true;
-          break;
-        }
-        const Step& st = ctl->ring[stage];
-        if (st.done) {
-          mbar_arrive(&ctl->full[stage]);
-          ++it;
-          break;
-        }
-        uint8_t* sbase = smem + stage * c.stage_bytes;
-        const bool lok = st.lhs >= 0 && st.lhs < p.lhs_rows;
-        // fp32: split the canonical raw chunk in place (x -> hi, lo); a
-        // missing lhs tile reads as zeros
-        if constexpr (F32) {
-          const int nf = c.Mt * (c.KC / EPU);
-          for (int f = tid; f < nf; f += kProducers) {
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (lok) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
-            float4 hi, lo;
-            split_tf32(x.x, hi.x, lo.x);
-            split_tf32(x.y, hi.y, lo.y);
-            split_tf32(x.z, hi.z, lo.z);
-            split_tf32(x.w, hi.w, lo.w);
-            *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
-            *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
-          }
-        } else {
-          if (!lok) {
-            for (int f = tid; f < c.lhs_bytes / 16; f += kProducers)
-              *reinterpret_cast<uint4*>(sbase + off_lhs + f * 16) = make_uint4(0, 0, 0, 0);
-          }
-        }
-        // zero the panel slots of absent rhs tiles
-        for (int g = 0; g < c.G; ++g) {
-          const int r = st.rhs[g];
-          if (r >= 0 && r < p.rhs_rows) continue;
-          if (r >= p.rhs_rows && tid == 0 && p.err) atomicExch(p.err, ES_ERR_INDEX);
-          const int per = blk_bytes / 16;
-          for (int q = tid; q < NH * per; q += kProducers) {
-            const int hl = q / per, w16 = q % per;
-            *reinterpret_cast<uint4*>(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes + w16 * 16) =
-                make_uint4(0, 0, 0, 0);
-          }
-        }
-        fence_proxy_async();
+    // ------------------------------ split (fp32) / zero-fill absent tiles
+    uint32_t it = 0;
+    while (true) {
+      const int stage = static_cast<int>(it % c.stages);
+      const uint32_t ph = (it / c.stages) & 1u;
+      if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
+      const Step& st = ctl->ring[stage];
+      const int d = st.done;
+      if (d) {
         mbar_arrive(&ctl->full[stage]);
         ++it;
+        if (d == 2) break;
+        continue;
       }
-      if (aborted) break;
-      // ---- epilogue
-      if (!wait_bar(&ctl->acc_full, item_iter & 1u, ctl, p.err)) {
+      uint8_t* sbase = smem + stage * c.stage_bytes;
+      const bool lok = st.lhs >= 0 && st.lhs < p.lhs_rows;
+      // fp32: split the canonical raw chunk in place (x -> hi, lo); a
+      // missing lhs tile reads as zeros
+      if constexpr (F32) {
+        const int nf = c.Mt * (c.KC / EPU);
+        for (int f = tid; f < nf; f += kProducers) {
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (lok) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+          float4 hi, lo;
+          split_tf32(x.x, hi.x, lo.x);
+          split_tf32(x.y, hi.y, lo.y);
+          split_tf32(x.z, hi.z, lo.z);
+          split_tf32(x.w, hi.w, lo.w);
+          *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
+          *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
+        }
+      } else {
+        if (!lok) {
+          for (int f = tid; f < c.lhs_bytes / 16; f += kProducers)
+            *reinterpret_cast<uint4*>(sbase + off_lhs + f * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      // zero the panel slots of absent rhs tiles
+      for (int g = 0; g < c.G; ++g) {
+        const int r = st.rhs[g];
+        if (r >= 0 && r < p.rhs_rows) continue;
+        if (r >= p.rhs_rows && tid == 0 && p.err) atomicExch(p.err, ES_ERR_INDEX);
+        const int per = blk_bytes / 16;
+        for (int q = tid; q < NH * per; q += kProducers) {
+          const int hl = q / per, w16 = q % per;
+          *reinterpret_cast<uint4*>(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes + w16 * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async();
+      mbar_arrive(&ctl->full[stage]);
+      ++it;
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA warp
+    const uint32_t idesc = make_idesc(F32, false, false, 128, c.swap ? c.Mt : c.n_mma);
+    uint32_t it = 0, item_iter = 0;
+    bool first = true, aborted = false;
+    uint32_t acc = tmem;
+    while (true) {
+      const int stage = static_cast<int>(it % c.stages);
+      const uint32_t ph = (it / c.stages) & 1u;
+      if (!wait_bar(&ctl->full[stage], ph, ctl, p.err)) {
         aborted = true;
         break;
       }
+      const int d = ctl->ring[stage].done;
+      if (d) {
+        if (lane == 0) {
+          mbar_arrive(&ctl->empty[stage]);
+          const int b = static_cast<int>(item_iter % c.acc_bufs);
+          if (d == 1) {
+            umma_commit(&ctl->acc_full[b]);
+          } else {
+            // no more items: wake the epilogue with the exit mark
+            *reinterpret_cast<volatile int*>(&ctl->exit_at) = static_cast<int>(item_iter);
+            __threadfence_block();
+            mbar_arrive(&ctl->acc_full[b]);
+          }
+        }
+        __syncwarp();
+        ++it;
+        if (d == 2) break;
+        ++item_iter;
+        first = true;
+        continue;
+      }
+      if (first) {
+        // the accumulator buffer must have been read out by the epilogue
+        const uint32_t b = item_iter % c.acc_bufs;
+        if (item_iter >= static_cast<uint32_t>(c.acc_bufs) &&
+            !wait_bar(&ctl->acc_empty[b], ((item_iter / c.acc_bufs) - 1) & 1u, ctl, p.err)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        acc = tmem + b * acc_stride;
+      }
       tc_fence_after();
-      const int quad = warp;  // TMEM lanes [32*quad, 32*quad+32)
+      if (lane == 0) {
+        const uint32_t sb = smem_u32(smem + stage * c.stage_bytes);
+        const uint32_t lhs0 = sb + off_lhs, lhs1 = lhs0 + c.lhs_bytes;
+        const uint32_t pan0 = sb + off_pan, pan1 = pan0 + c.pan_bytes;
+        const int ksteps = c.KC / KSTEP;
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
+          for (int h = 0; h < c.halves; ++h) {
+            const uint32_t dt = acc + h * col_per_half;
+            const uint32_t acc0 = (first && ks == 0) ? 0u : 1u;
+            const uint32_t hoff = koff + h * 16 * sbo;  // rows 128h.. of the M operand
+            // M operand: lhs (plain) or the rhs panel (transposed product)
+            const uint32_t am0 = (c.swap ? pan0 : lhs0) + hoff, am1 = (c.swap ? pan1 : lhs1) + hoff;
+            const uint32_t bn0 = (c.swap ? lhs0 : pan0) + koff, bn1 = (c.swap ? lhs1 : pan1) + koff;
+            const uint64_t a_hi = smem_desc(am0, 128, sbo), b_hi = smem_desc(bn0, 128, sbo);
+            umma<F32>(dt, a_hi, b_hi, idesc, acc0);
+            if constexpr (F32) {
+              umma<F32>(dt, a_hi, smem_desc(bn1, 128, sbo), idesc, 1u);
+              umma<F32>(dt, smem_desc(am1, 128, sbo), b_hi, idesc, 1u);
+            }
+          }
+        }
+        umma_commit(&ctl->empty[stage]);
+      }
+      __syncwarp();
+      first = false;
+      ++it;
+    }
+    if (aborted && lane == 0) {
+      umma_commit(&ctl->drain);
+      drain_bar(&ctl->drain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+    // ---------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
+    for (uint32_t item_iter = 0;; ++item_iter) {
+      const uint32_t b = item_iter % c.acc_bufs;
+      if (!wait_bar(&ctl->acc_full[b], (item_iter / c.acc_bufs) & 1u, ctl, p.err)) break;
+      if (*reinterpret_cast<volatile int*>(&ctl->exit_at) == static_cast<int>(item_iter)) break;
+      const ItemInfo info = ctl->item_log[item_iter % kItemLog];
+      const int s0 = info.s0, gcnt = info.gcnt;
+      tc_fence_after();
       for (int h = 0; h < c.halves; ++h) {
-        const uint32_t tbase = tmem + (static_cast<uint32_t>(quad * 32) << 16) + h * col_per_half;
+        const uint32_t tbase =
+            tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride + h * col_per_half;
         if (!c.swap) {
           const int m = h * 128 + quad * 32 + lane;
           for (int c0 = 0; c0 < c.n_mma; c0 += 32) {
@@ -509,72 +613,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         }
       }
       tc_fence_before();
-      mbar_arrive(&ctl->acc_empty);
+      mbar_arrive(&ctl->acc_empty[b]);
     }
-  } else {
-    // ------------------------------------------------------------ MMA warp
-    const uint32_t idesc = make_idesc(F32, false, false, 128, c.swap ? c.Mt : c.n_mma);
-    uint32_t it = 0, item_iter = 0;
-    bool aborted = false;
-    for (int64_t item = blockIdx.x; item < W && !aborted; item += gridDim.x, ++item_iter) {
-      if (item_iter > 0 && !wait_bar(&ctl->acc_empty, (item_iter - 1) & 1u, ctl, p.err)) {
-        aborted = true;
-        break;
-      }
-      tc_fence_after();
-      bool first = true;
-      while (true) {
-        const int stage = static_cast<int>(it % c.stages);
-        const uint32_t ph = (it / c.stages) & 1u;
-        if (!wait_bar(&ctl->full[stage], ph, ctl, p.err)) {
-          aborted = true;
-          break;
-        }
-        const int sdone = ctl->ring[stage].done;
-        if (sdone) {
-          if (lane == 0) mbar_arrive(&ctl->empty[stage]);
-          __syncwarp();
-          ++it;
-          break;
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sb = smem_u32(smem + stage * c.stage_bytes);
-          const uint32_t lhs0 = sb + off_lhs, lhs1 = lhs0 + c.lhs_bytes;
-          const uint32_t pan0 = sb + off_pan, pan1 = pan0 + c.pan_bytes;
-          const int ksteps = c.KC / KSTEP;
-          for (int ks = 0; ks < ksteps; ++ks) {
-            const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
-            for (int h = 0; h < c.halves; ++h) {
-              const uint32_t d = tmem + h * col_per_half;
-              const uint32_t acc0 = (first && ks == 0) ? 0u : 1u;
-              const uint32_t hoff = koff + h * 16 * sbo;  // rows 128h.. of the M operand
-              // M operand: lhs (plain) or the rhs panel (transposed product)
-              const uint32_t am0 = (c.swap ? pan0 : lhs0) + hoff, am1 = (c.swap ? pan1 : lhs1) + hoff;
-              const uint32_t bn0 = (c.swap ? lhs0 : pan0) + koff, bn1 = (c.swap ? lhs1 : pan1) + koff;
-              const uint64_t a_hi = smem_desc(am0, 128, sbo), b_hi = smem_desc(bn0, 128, sbo);
-              umma<F32>(d, a_hi, b_hi, idesc, acc0);
-              if constexpr (F32) {
-                umma<F32>(d, a_hi, smem_desc(bn1, 128, sbo), idesc, 1u);
-                umma<F32>(d, smem_desc(am1, 128, sbo), b_hi, idesc, 1u);
-              }
-            }
-          }
-          umma_commit(&ctl->empty[stage]);
-        }
-        __syncwarp();
-        first = false;
-        ++it;
-      }
-      if (aborted) break;
-      if (lane == 0) umma_commit(&ctl->acc_full);
-      __syncwarp();
-    }
-    if (aborted && lane == 0) {
-      umma_commit(&ctl->drain);
-      drain_bar(&ctl->drain, 0);
-    }
-    __syncwarp();
   }
 
   tc_fence_before();
@@ -659,6 +699,24 @@ __global__ void item_identity_kernel(int64_t nseg, int32_t* __restrict__ first, 
   if (blockIdx.x == 0 && threadIdx.x == 0) *num = nseg;
 }
 
+// Sort key per item slot: items (slot < W) by descending pair count, empty
+// slots last.
+__global__ void item_work_keys_kernel(const int32_t* __restrict__ first, const int32_t* __restrict__ count,
+                                      const int64_t* __restrict__ seg_off, const int64_t* __restrict__ num_items,
+                                      int64_t nslots, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
+  const int64_t W = *num_items;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nslots; i += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t key = 0xFFFFFFFFu;
+    if (i < W) {
+      const int s0 = first[i], g = count[i];
+      const int64_t work = seg_off[s0 + g] - seg_off[s0];
+      key = 0xFFFFFFFEu - static_cast<uint32_t>(work < 0xFFFFFFFEll ? work : 0xFFFFFFFEll);
+    }
+    keys[i] = key;
+    vals[i] = static_cast<uint32_t>(i);
+  }
+}
+
 struct TcWs {
   uint8_t* pan_hi;
   uint8_t* pan_lo;
@@ -669,6 +727,10 @@ struct TcWs {
   int32_t* cnt;
   uint32_t* scan;
   int64_t* num_items;
+  uint32_t* sort_keys;
+  uint32_t* order;
+  RadixBuffers<uint32_t> rb;
+  int* queue;
 };
 
 template <typename C>
@@ -684,6 +746,13 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t nseg
   w.cnt = cv.template take<int32_t>(nseg);
   w.scan = cv.template take<uint32_t>(scan_scratch_elems(nseg));
   w.num_items = cv.template take<int64_t>(1);
+  w.sort_keys = cv.template take<uint32_t>(nseg);
+  w.order = cv.template take<uint32_t>(nseg);
+  w.rb.keys_alt = cv.template take<uint32_t>(nseg);
+  w.rb.vals_alt = cv.template take<uint32_t>(nseg);
+  w.rb.hist = cv.template take<uint32_t>(RadixScratchSize::hist_elems(nseg));
+  w.rb.scan = cv.template take<uint32_t>(RadixScratchSize::scan_elems(nseg));
+  w.queue = cv.template take<int>(1);
 }
 
 struct SizeOnly {
@@ -766,10 +835,11 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   } else {
     return false;
   }
-  int cols = c->halves * (c->swap ? Mt : c->n_mma);
+  const int acc_cols = c->halves * (c->swap ? Mt : c->n_mma);
+  if (acc_cols > 512) return false;
+  c->acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
   int pw = 32;
-  while (pw < cols) pw <<= 1;
-  if (pw > 512) return false;
+  while (pw < c->acc_bufs * acc_cols) pw <<= 1;
   c->tmem_cols = pw;
   const int esz = f32 ? 4 : 2;
   const int nh = f32 ? 2 : 1;
@@ -837,7 +907,19 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     if (c.G != 1) return ES_ERR_INVALID;
     ES_LAUNCH(item_identity_kernel, grid_for(nseg, 256), 256, 0, st, nseg, w.item_first, w.item_count, w.num_items);
   }
-  // 3. persistent tensor-core kernel, one CTA per SM
+  // 3. largest items first, handed out by a device-wide queue
+  ES_LAUNCH(item_work_keys_kernel, grid_for(nseg, 256), 256, 0, st, w.item_first, w.item_count, seg_off, w.num_items,
+            nseg, w.sort_keys, w.order);
+  {
+    uint32_t* k = w.sort_keys;
+    uint32_t* v = w.order;
+    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 32, st));
+    if (v != w.order &&
+        cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return ES_ERR_CUDA;
+  }
+  if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
+  // 4. persistent tensor-core kernel, one CTA per SM
   TcParams prm;
   prm.c = c;
   prm.lhs = static_cast<const uint8_t*>(lhs);
@@ -851,6 +933,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.item_first = w.item_first;
   prm.item_count = w.item_count;
   prm.num_items = w.num_items;
+  prm.order = reinterpret_cast<const int32_t*>(w.order);
+  prm.queue = w.queue;
   prm.seg_out = seg_out;
   prm.out = out;
   prm.odt = odt;

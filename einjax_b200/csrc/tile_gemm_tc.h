@@ -17,6 +17,7 @@ struct TcConfig {
   int stages;
   int halves;      // 128-row MMA halves (M = 128 * halves)
   int n_mma;       // MMA N
+  int acc_bufs;    // TMEM accumulators (2 when they fit: epilogue overlaps the next item)
   int tmem_cols;   // allocated TMEM columns (power of two)
   int lhs_bytes;   // one operand copy of a stage's lhs chunk
   int pan_bytes;   // one operand copy of a stage's panel chunk
