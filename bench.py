@@ -140,7 +140,8 @@ def run_ours(args):
             ev.setdefault("g", []).append(torch.cuda.Event(enable_timing=True))
             ev["g"][-1].record()
         vals = SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
-                              precision=args.precision, seg_strip=plan.seg_strip)
+                              precision=args.precision, seg_strip=plan.seg_strip, pair_key=plan.seg_key,
+                              key_extent=plan.key_extent)
         if timing:
             ev.setdefault("h", []).append(torch.cuda.Event(enable_timing=True))
             ev["h"][-1].record()
@@ -217,7 +218,7 @@ def run_ours(args):
     plan = SD.plan_pairs(A, B, jk, ak)
     evs[3].record()
     SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets, precision=args.precision,
-                   seg_strip=plan.seg_strip)
+                   seg_strip=plan.seg_strip, pair_key=plan.seg_key, key_extent=plan.key_extent)
     evs[4].record()
     torch.cuda.synchronize()
     for name, i in (("tile_coo_A", 0), ("tile_dense_B", 1), ("join_and_group", 2), ("tile_gemm", 3)):

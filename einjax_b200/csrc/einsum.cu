@@ -291,7 +291,8 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
                               const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
                               const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
                               int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
-                              void* out_values, int out_dtype, int precision, void* workspace,
+                              const int32_t* pair_key, int64_t key_extent, void* out_values, int out_dtype,
+                              int precision, void* workspace,
                               size_t workspace_bytes, int32_t* error_dev, void* stream) {
   EinsumDesc d;
   ES_TRY(parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d));
@@ -307,8 +308,8 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
     // sequence; per-pair calls (no segments) stay on the SIMT path
     if (seg_offsets && tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, &c)) {
       const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, seg_offsets, nseg,
-                              seg_out_index, seg_strip, out_values, out_dtype, workspace, workspace_bytes, error_dev,
-                              st);
+                              seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, workspace,
+                              workspace_bytes, error_dev, st);
       if (r != ES_ERR_UNSUPPORTED || precision == ES_PREC_TC) return r;
     }
     if (precision == ES_PREC_TC) return ES_ERR_UNSUPPORTED;

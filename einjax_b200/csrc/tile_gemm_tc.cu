@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -52,6 +53,7 @@ constexpr int kMaxG = 8;
 constexpr int kMaxStages = 8;
 constexpr int kWin = 16;          // prefetched pair entries per segment
 constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 
 // done: 0 data stage, 1 end of a work item, 2 no more items
 struct Step {
@@ -65,6 +67,7 @@ struct Step {
 struct ItemInfo {
   int s0;
   int gcnt;
+  int nsteps;  // data stages this item produced (0: nothing in this key block)
 };
 
 struct Ctrl {
@@ -98,6 +101,9 @@ struct TcParams {
   const int64_t* num_items;
   const int32_t* order;   // item indices, largest work first
   int* queue;             // next position in `order`, zero at launch
+  const int32_t* pair_key;  // contracted coordinate per pair (null: one key block)
+  int k_lo, k_hi;           // this launch's key block
+  int accumulate;           // 1: add into the output (key blocks after the first)
   const int32_t* seg_out;
   void* out;
   int odt;
@@ -319,13 +325,30 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         const int item = p.order[q];
         s0 = p.item_first[item];
         gcnt = p.item_count[item];
-        if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt};
+        if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt, 0};
       }
       int64_t cur = 0, end = 0;
       if (lane < gcnt) {
         cur = p.seg_off[s0 + lane];
         end = p.seg_off[s0 + lane + 1];
+        if (p.pair_key) {
+          // pairs of this key block: keys are non-decreasing inside a segment
+          int64_t lo = cur, hi = end;
+          while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (p.pair_key[mid] < p.k_lo) lo = mid + 1; else hi = mid;
+          }
+          const int64_t a = lo;
+          hi = end;
+          while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (p.pair_key[mid] < p.k_hi) lo = mid + 1; else hi = mid;
+          }
+          cur = a;
+          end = lo;
+        }
       }
+      int nsteps = 0;
       int wpos = kWin;  // window exhausted: refill on first use
       int step_lhs = -1, my_rhs = -1, done = exit_now ? 2 : 0;
       for (int chunk = nchunks;; ++chunk) {
@@ -368,12 +391,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           sr.k0 = chunk * c.KC;
           sr.done = done;
         }
+        if (done == 1 && lane == 0) ctl->item_log[item_iter % kItemLog].nsteps = nsteps;
         __syncwarp();
         if (done) {
           if (lane == 0) mbar_arrive_expect_tx(&ctl->copy[stage], 0);
           ++it;
           break;
         }
+        ++nsteps;
         const int k0 = chunk * c.KC;
         uint8_t* sbase = smem + stage * c.stage_bytes;
         const int li = step_lhs;
@@ -493,7 +518,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           mbar_arrive(&ctl->empty[stage]);
           const int b = static_cast<int>(item_iter % c.acc_bufs);
           if (d == 1) {
-            umma_commit(&ctl->acc_full[b]);
+            if (first) mbar_arrive(&ctl->acc_full[b]);  // nothing accumulated for this item
+            else umma_commit(&ctl->acc_full[b]);
           } else {
             // no more items: wake the epilogue with the exit mark
             *reinterpret_cast<volatile int*>(&ctl->exit_at) = static_cast<int>(item_iter);
@@ -562,8 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       if (*reinterpret_cast<volatile int*>(&ctl->exit_at) == static_cast<int>(item_iter)) break;
       const ItemInfo info = ctl->item_log[item_iter % kItemLog];
       const int s0 = info.s0, gcnt = info.gcnt;
+      const bool empty = info.nsteps == 0;  // zeros: written by the first key block only
       tc_fence_after();
-      for (int h = 0; h < c.halves; ++h) {
+      for (int h = 0; h < c.halves && !(empty && p.accumulate); ++h) {
         const uint32_t tbase =
             tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride + h * col_per_half;
         if (!c.swap) {
@@ -571,6 +598,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           for (int c0 = 0; c0 < c.n_mma; c0 += 32) {
             float v[32];
             tmem_ld32(tbase + c0, v);
+            if (empty) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
             if (m < c.Mt) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
@@ -580,14 +611,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                 const int64_t row = p.seg_out ? p.seg_out[s0 + g] : static_cast<int64_t>(s0 + g);
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m) * c.Nt + n;
                 if (p.odt == ES_F32) {
-                  *reinterpret_cast<float4*>(static_cast<float*>(p.out) + o) =
-                      make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                  float4* of = reinterpret_cast<float4*>(static_cast<float*>(p.out) + o);
+                  float4 r4 = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                  if (p.accumulate) {
+                    const float4 old = *of;
+                    r4.x += old.x; r4.y += old.y; r4.z += old.z; r4.w += old.w;
+                  }
+                  *of = r4;
                 } else {
                   __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + o;
-                  ob[0] = __float2bfloat16_rn(v[j]);
-                  ob[1] = __float2bfloat16_rn(v[j + 1]);
-                  ob[2] = __float2bfloat16_rn(v[j + 2]);
-                  ob[3] = __float2bfloat16_rn(v[j + 3]);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    float x = v[j + q];
+                    if (p.accumulate) x += __bfloat162float(ob[q]);
+                    ob[q] = __float2bfloat16_rn(x);
+                  }
                 }
               }
             }
@@ -605,8 +643,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
               for (int j = 0; j < 32; ++j) {
                 if (m0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m0 + j) * c.Nt + n;
-                if (p.odt == ES_F32) static_cast<float*>(p.out)[o] = v[j];
-                else static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v[j]);
+                float x = empty ? 0.f : v[j];
+                if (p.odt == ES_F32) {
+                  float* of = static_cast<float*>(p.out) + o;
+                  if (p.accumulate) x += *of;
+                  *of = x;
+                } else {
+                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + o;
+                  if (p.accumulate) x += __bfloat162float(*ob);
+                  *ob = __float2bfloat16_rn(x);
+                }
               }
             }
           }
@@ -878,8 +924,8 @@ size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t nseg) {
 
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
               const int32_t* pl, const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out,
-              const int64_t* seg_strip, void* out, int odt, void* ws, size_t ws_bytes, int32_t* err,
-              cudaStream_t st) {
+              const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out, int odt, void* ws,
+              size_t ws_bytes, int32_t* err, cudaStream_t st) {
   if (nseg <= 0) return ES_OK;
   if (nseg >= INT32_MAX || rhs_rows >= INT32_MAX || lhs_rows >= INT32_MAX) return ES_ERR_UNSUPPORTED;
   Carver cv(ws, ws_bytes);
@@ -974,12 +1020,37 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     if (cudaFuncSetAttribute(tc_strip_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
         cudaSuccess)
       return ES_ERR_CUDA;
-    ES_LAUNCH(tc_strip_kernel<true>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
   } else {
     if (cudaFuncSetAttribute(tc_strip_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
         cudaSuccess)
       return ES_ERR_CUDA;
-    ES_LAUNCH(tc_strip_kernel<false>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+  }
+  // Key blocks: the rhs operand re-read by every strip is split along the
+  // contracted range into slices that fit in L2; one launch per slice, in
+  // order, later slices adding into the output.
+  int64_t panel_bytes = rhs_rows * c.Kt * c.Nt * (c.fp32 ? 8 : 2);
+  int nblocks = 1;
+  if (pair_key && key_extent > 1) {
+    // EINSPARSE_KBLOCK_BYTES overrides the per-block panel budget (tuning, tests)
+    int64_t budget = kPanelL2Budget;
+    if (const char* e = std::getenv("EINSPARSE_KBLOCK_BYTES")) {
+      const long long v = std::atoll(e);
+      if (v > 0) budget = v;
+    }
+    nblocks = static_cast<int>((panel_bytes + budget - 1) / budget);
+    if (nblocks > key_extent) nblocks = static_cast<int>(key_extent);
+    if (nblocks < 1) nblocks = 1;
+  }
+  prm.pair_key = nblocks > 1 ? pair_key : nullptr;
+  for (int b = 0; b < nblocks; ++b) {
+    prm.k_lo = static_cast<int>(key_extent * b / nblocks);
+    prm.k_hi = static_cast<int>(key_extent * (b + 1) / nblocks);
+    prm.accumulate = b > 0 ? 1 : 0;
+    if (b > 0 && cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
+    if (c.fp32)
+      ES_LAUNCH(tc_strip_kernel<true>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+    else
+      ES_LAUNCH(tc_strip_kernel<false>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
   }
   return ES_OK;
 }

@@ -177,7 +177,8 @@ def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_
     if s1 > s0:
         vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs,
                            plan.seg_offsets[s0:s1 + 1], precision=precision,
-                           seg_strip=plan.seg_strip[s0:s1] if plan.seg_strip is not None else None)
+                           seg_strip=plan.seg_strip[s0:s1] if plan.seg_strip is not None else None,
+                           pair_key=plan.seg_key, key_extent=plan.key_extent)
     else:
         vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs[:0], plan.seg_rhs[:0],
                            None, num_out_rows=0, precision=precision)

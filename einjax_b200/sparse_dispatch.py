@@ -122,15 +122,18 @@ def _es_out(dt):
 
 
 def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_offsets=None, seg_out_index=None,
-                out=None, num_out_rows=None, out_dtype=None, precision="auto", seg_strip=None, check=True):
+                out=None, num_out_rows=None, out_dtype=None, precision="auto", seg_strip=None, pair_key=None,
+                key_extent=0, check=True):
     """Segmented tile einsum through ``es_tile_einsum``.
 
     Without ``seg_offsets`` every pair is its own segment (per-pair output,
     ``kernel_einsum``); with it, each segment's pairs are summed in fp32 into
     one output tile (row ``seg_out_index[s]`` of ``out`` if given, else row s).
     ``seg_strip`` (strip key per segment, from the output grouping) lets the
-    tensor-core path batch the segments of one output strip. With ``check``
-    the device error flag is read back (one 4-byte copy).
+    tensor-core path batch the segments of one output strip; ``pair_key`` (the
+    contracted tile coordinate of each pair, in ``[0, key_extent)``) lets it
+    block the contracted range so the re-read operand stays in L2. With
+    ``check`` the device error flag is read back (one 4-byte copy).
     """
     lib = L.lib()
     dev = lhs_values.device
@@ -156,6 +159,7 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     so = seg_offsets.contiguous() if seg_offsets is not None else None
     sx = seg_out_index.to(torch.int32).contiguous() if seg_out_index is not None else None
     sg = seg_strip.contiguous() if (seg_strip is not None and so is not None) else None
+    pk = pair_key.to(torch.int32).contiguous() if (pair_key is not None and so is not None) else None
     lti, rti = L.i64arr(lt), L.i64arr(rt)
     prec = _PREC[precision]
     wsb = lib.es_tile_einsum_workspace_size(ks, lti, len(lt), rti, len(rt), es_dtype(lv), es_dtype(rv),
@@ -165,7 +169,8 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     L.check("es_tile_einsum", lib.es_tile_einsum(
         ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
         int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
-        sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None, out.data_ptr(),
+        sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None,
+        pk.data_ptr() if pk is not None else None, int(key_extent) if pk is not None else 0, out.data_ptr(),
         _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         err.data_ptr(), stream_ptr(dev)))
     if check:
@@ -265,6 +270,8 @@ class PairPlan:
     seg_rhs: torch.Tensor
     seg_pair: torch.Tensor      # int32 (P,), original pair index
     seg_strip: torch.Tensor | None = None  # int64 (O,), strip key (lhs-derived output coords)
+    seg_key: torch.Tensor | None = None    # int32 (P,), contracted tile coordinate of each grouped pair
+    key_extent: int = 0
 
     @property
     def num_pairs(self) -> int:
@@ -320,7 +327,17 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     L.check("es_segments_fill", lib.es_segments_fill(
         li.data_ptr(), ri.data_ptr(), P, out_nd, ext, ws.data_ptr(), ws.numel(), O, oc.data_ptr(), so.data_ptr(),
         sl.data_ptr(), sr.data_ptr(), sp.data_ptr(), nlead, sg.data_ptr() if sg is not None else None, st))
-    return PairPlan(li, ri, oc, so, sl, sr, sp, sg)
+    # contracted coordinate (first join key) of each grouped pair
+    sk, kext = None, 0
+    if join_keys:
+        jd = int(join_keys[0][0])
+        sk = torch.empty((P, 1), dtype=torch.int32, device=dev)
+        L.check("es_output_coords", lib.es_output_coords(
+            lhs.coords.contiguous().data_ptr(), lhs.ndim, rhs.coords.contiguous().data_ptr(), rhs.ndim,
+            sl.data_ptr(), sr.data_ptr(), P, L.i32arr([0, jd]), 1, sk.data_ptr(), st))
+        sk = sk.reshape(-1)
+        kext = _key_extents(lhs, rhs, [tuple(join_keys[0])])[0]
+    return PairPlan(li, ri, oc, so, sl, sr, sp, sg, sk, kext)
 
 
 def _resolve_shapes(lhs, rhs, kernel_string, agg_keys, output_shape, output_tile_shape):
@@ -349,7 +366,8 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
     if plan.num_pairs == 0:
         return empty_relation(output_shape, output_tile_shape, lhs.values.dtype, lhs.device)
     vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
-                       precision=precision, seg_strip=plan.seg_strip)
+                       precision=precision, seg_strip=plan.seg_strip, pair_key=plan.seg_key,
+                       key_extent=plan.key_extent)
     return SparseTensorRelation(plan.out_coords, vals, output_shape, output_tile_shape)
 
 

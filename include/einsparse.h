@@ -176,6 +176,11 @@ int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs
  * zero tiles). Values dtypes: F32 / BF16 / F64 inputs; F32 / BF16 outputs.
  * seg_strip (optional, from es_segments_fill): strip key per segment; the
  * tensor-core path computes up to 8 segments of one strip in one tile.
+ * pair_key (optional): the contracted tile coordinate of each pair
+ * (non-decreasing inside a segment), with key_extent its range; when given,
+ * the tensor-core path splits the contracted range into blocks whose rhs
+ * operand fits in L2 and adds the blocks' partial sums into the output in
+ * block order.
  * workspace: es_tile_einsum_workspace_size bytes (0 for the SIMT path). A
  * device-side wait that runs out sets *error_dev to ES_ERR_TIMEOUT.
  * ------------------------------------------------------------------------- */
@@ -189,7 +194,8 @@ int es_tile_einsum(const char* kernel_string,
                    const void* rhs_values, int rhs_dtype, int64_t rhs_rows,
                    const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
                    const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
-                   const int64_t* seg_strip, void* out_values, int out_dtype, int precision,
+                   const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
+                   void* out_values, int out_dtype, int precision,
                    void* workspace, size_t workspace_bytes, int32_t* error_dev, void* stream);
 
 /* Which path es_tile_einsum takes for these arguments: 1 tensor cores,

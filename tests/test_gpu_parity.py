@@ -378,3 +378,32 @@ def test_tensor_core_bf16(tile, bands):
     res = E.execute_sparse(_dev(lhs, torch.bfloat16), _dev(rhs, torch.bfloat16), jk, ks, ak, precision="auto")
     ref = O.execute_sparse(lhs, rhs, jk, ks, ak)
     _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak), RTOL_BF16)
+
+
+@pytest.mark.parametrize("case", [TC_CASES[1], TC_CASES[2], TC_CASES[0], TC_CASES[5]],
+                         ids=["C2-like", "C2 sparse B", "C1-like", "C5-like"])
+def test_tensor_core_key_blocks(case, monkeypatch):
+    """Force many contracted-range blocks (later blocks add into the output)."""
+    monkeypatch.setenv("EINSPARSE_KBLOCK_BYTES", "65536")
+    ks, jk, ak, sa, ta, sb, tb, da, db, _ = case
+    rng = np.random.default_rng(99)
+    lhs, rhs = _random_block_sparse(rng, sa, ta, da), _random_block_sparse(rng, sb, tb, db)
+    res = E.execute_sparse(_dev(lhs), _dev(rhs), jk, ks, ak, precision="tc")
+    lhs32 = O.Relation(lhs.coords, lhs.values.astype(np.float32).astype(np.float64), lhs.shape, lhs.tile_shape)
+    rhs32 = O.Relation(rhs.coords, rhs.values.astype(np.float32).astype(np.float64), rhs.shape, rhs.tile_shape)
+    ref = O.execute_sparse(lhs32, rhs32, jk, ks, ak)
+    _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak))
+
+
+def test_tensor_core_key_blocks_bf16(monkeypatch):
+    monkeypatch.setenv("EINSPARSE_KBLOCK_BYTES", "32768")
+    from einjax_b200 import workloads as W
+    rng = np.random.default_rng(7)
+    lhs = _random_block_sparse(rng, (2, 1024, 1024), (1, 64, 64), 0.2)
+    rhs = _random_block_sparse(rng, (2, 1024, 1024), (1, 64, 64), 0.2)
+    lhs.values = W.round_to_bf16(lhs.values.astype(np.float32)).astype(np.float64)
+    rhs.values = W.round_to_bf16(rhs.values.astype(np.float32)).astype(np.float64)
+    jk, ks, ak = [(0, 0), (2, 1)], "bij,bjk->bik", [(0, 0), (0, 1), (1, 2)]
+    res = E.execute_sparse(_dev(lhs, torch.bfloat16), _dev(rhs, torch.bfloat16), jk, ks, ak, precision="tc")
+    ref = O.execute_sparse(lhs, rhs, jk, ks, ak)
+    _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak), RTOL_BF16)
