@@ -278,12 +278,13 @@ extern "C" int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs
 
 extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
                                                 const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype,
-                                                int64_t rhs_rows, int64_t num_segments, int precision) {
+                                                int64_t rhs_rows, int64_t num_pairs, int64_t num_segments,
+                                                int64_t key_extent, int precision) {
   EinsumDesc d;
   if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
   TcConfig c;
   if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, &c)) return 0;
-  return tc_workspace_size(c, rhs_rows, num_segments);
+  return tc_workspace_size(c, rhs_rows, num_pairs, num_segments, tc_key_blocks(c, rhs_rows, true, key_extent));
 }
 
 extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
@@ -307,9 +308,9 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
     // the tensor-core path walks each segment's pairs as one sorted lhs
     // sequence; per-pair calls (no segments) stay on the SIMT path
     if (seg_offsets && tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, &c)) {
-      const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, seg_offsets, nseg,
-                              seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, workspace,
-                              workspace_bytes, error_dev, st);
+      const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, num_pairs,
+                              seg_offsets, nseg, seg_out_index, seg_strip, pair_key, key_extent, out_values,
+                              out_dtype, workspace, workspace_bytes, error_dev, st);
       if (r != ES_ERR_UNSUPPORTED || precision == ES_PREC_TC) return r;
     }
     if (precision == ES_PREC_TC) return ES_ERR_UNSUPPORTED;

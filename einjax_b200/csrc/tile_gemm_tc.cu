@@ -52,17 +52,29 @@ constexpr int kItemLog = 16;
 constexpr int kMaxG = 8;
 constexpr int kMaxStages = 8;
 constexpr int kWin = 16;          // prefetched pair entries per segment
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s without progress: give up
+constexpr uint64_t kDrainNs = 100000000ull;   // 100 ms to drain own copies / MMAs
+#ifndef EXP_EPI_SLEEP
+#define EXP_EPI_SLEEP 0
+#endif
+constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
+constexpr int kMaxKeyBlocks = 16;
 
 // done: 0 data stage, 1 end of a work item, 2 no more items
 struct Step {
-  int lhs;
-  int k0;
   int done;
-  int pad;
-  int rhs[kMaxG];
 };
+
+// One merge step of a work item (one lhs tile against up to G rhs tiles), as
+// written by tc_merge_kernel: 16 ints, lane j of the scheduler warp loads
+// field j.
+constexpr int kRecInts = 16;
+constexpr int kRecLhs = 0;    // lhs tile
+constexpr int kRecFlags = 1;  // bit 0: rhs tiles 0..G-1 present and consecutive (one copy)
+constexpr int kRecRhs0 = 2;   // first rhs tile
+constexpr int kRecRhs = 4;    // rhs tile per segment slot, -1 absent (slots 0..kMaxG-1)
+constexpr int kRecAhead = 4;  // records the scheduler has in flight ahead of use
 
 struct ItemInfo {
   int s0;
@@ -79,11 +91,10 @@ struct Ctrl {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  uint32_t progress;  // stages the MMA warp has issued (liveness for long waits)
   Step ring[kMaxStages];
   ItemInfo item_log[kItemLog];  // items in the order this CTA takes them
   int exit_at;                  // item count at which the epilogue stops
-  int win_l[kMaxG][kWin];  // scheduler's window of upcoming (lhs, rhs) pairs
-  int win_r[kMaxG][kWin];
 };
 
 struct TcParams {
@@ -93,16 +104,16 @@ struct TcParams {
   const uint8_t* pan_hi;
   const uint8_t* pan_lo;
   int64_t rhs_rows;
-  const int32_t* pl;
-  const int32_t* pr;
+  const int32_t* recs;      // merge steps, kRecInts ints each
+  const int64_t* item_rec;  // per item: nblocks + 1 record boundaries (key blocks)
+  int nblocks, blk;         // key blocks, this launch's block
+  const uint8_t* zeros;     // zero bytes standing in for absent tiles
   const int64_t* seg_off;
   const int32_t* item_first;
   const int32_t* item_count;
   const int64_t* num_items;
   const int32_t* order;   // item indices, largest work first
   int* queue;             // next position in `order`, zero at launch
-  const int32_t* pair_key;  // contracted coordinate per pair (null: one key block)
-  int k_lo, k_hi;           // this launch's key block
   int accumulate;           // 1: add into the output (key blocks after the first)
   const int32_t* seg_out;
   void* out;
@@ -161,10 +172,6 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -183,21 +190,31 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// One MMA, issued by one elected lane of a converged warp (all lanes pass
+// the same operands).
 template <bool F32>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
   if constexpr (F32) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
   } else {
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accum)
         : "memory");
   }
+}
+
+// tcgen05.commit by one elected lane of a converged warp.
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -233,23 +250,61 @@ __host__ __device__ constexpr uint32_t make_idesc(bool tf32, bool a_mn, bool b_m
          ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-// Bounded wait. Returns false when this CTA has aborted (here or elsewhere).
-__device__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctrl* ctl, int32_t* err) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait. Spins on try_wait (which suspends in hardware) with no
+// software sleep while the wait is short, so a pipeline hand-off costs no
+// more than the barrier's own latency; backs off after 100 us; gives up
+// after kWaitNs without progress. `progress`, when given, is a counter the
+// producing side advances; while it moves the wait is not stuck (the
+// epilogue waits a whole work item). Returns false when this CTA has
+// aborted (here or elsewhere).
+__device__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctrl* ctl, int32_t* err,
+                         const uint32_t* progress = nullptr, uint32_t sleep_ns = 0) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = global_ns();
+  uint32_t seen = progress ? *reinterpret_cast<const volatile uint32_t*>(progress) : 0u;
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
-    if (i > 32) __nanosleep(128);
+    if (sleep_ns) __nanosleep(sleep_ns);
+    if ((i & 31) == 0) {
+      if (*reinterpret_cast<volatile int*>(&ctl->abort)) return false;
+      const uint64_t now = global_ns();
+      if (progress) {
+        const uint32_t cur = *reinterpret_cast<const volatile uint32_t*>(progress);
+        if (cur != seen) {
+          seen = cur;
+          t0 = now;
+        }
+      }
+      if (now - t0 > kWaitNs) break;
+      if (now - t0 > 100000) __nanosleep(256);
+    }
   }
   *reinterpret_cast<volatile int*>(&ctl->abort) = 1;
   if (err) atomicExch(err, ES_ERR_TIMEOUT);
   return false;
 }
 
+// wait_bar taken by lane 0 for the whole warp: one poller per warp, and the
+// warp stays converged.
+__device__ __forceinline__ bool wait_bar_warp(uint64_t* bar, uint32_t parity, Ctrl* ctl, int32_t* err,
+                                              const uint32_t* progress = nullptr) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, ctl, err, progress) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // Bounded wait that ignores the abort flag (used to drain in-flight work).
 __device__ void drain_bar(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return;
-    if (i > 32) __nanosleep(128);
+    if ((i & 31) == 0 && global_ns() - t0 > kDrainNs) return;
   }
 }
 
@@ -259,6 +314,146 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   const uint32_t b = __float_as_uint(x);
   hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
   lo = x - hi;
+}
+
+// Operand layout of one stage as the MMA warp sees it.
+struct MmaArgs {
+  uint32_t smem0, tmem;
+  int lane;
+  uint32_t sbo, col_per_half, acc_stride;
+  uint32_t off_m, off_n;  // hi copies of the M and N operands in a stage
+  uint32_t lo_m, lo_n;    // distance to their lo copies (fp32)
+  uint32_t idesc, idesc2;
+};
+
+// MMA warp. The whole warp runs this loop on identical values; one elected
+// lane issues each MMA. The issue order of a stage is fixed at compile time
+// (FOLD, KS k-steps, H halves): with runtime branches between the MMAs each
+// one costs several times its tensor-pipe time.
+template <bool F32, bool FOLD, int KS, int H>
+__device__ void mma_role(const TcParams& p, Ctrl* ctl, const MmaArgs& m) {
+  const TcConfig& c = p.c;
+  const int lane = m.lane;
+  uint32_t it = 0, item_iter = 0;
+  int stage = 0;
+  uint32_t ph = 0;
+  bool first = true, aborted = false;
+  uint32_t acc = m.tmem;
+  while (true) {
+    // fp32 stages pass through the split warps; bf16 stages go straight
+    // from the copies to the MMAs
+    if (!wait_bar_warp(F32 ? &ctl->full[stage] : &ctl->copy[stage], ph, ctl, p.err)) {
+      aborted = true;
+      break;
+    }
+    const int d = __shfl_sync(0xffffffffu, ctl->ring[stage].done, 0);
+    if (d) {
+      if (lane == 0) {
+        mbar_arrive(&ctl->empty[stage]);
+        const int b = static_cast<int>(item_iter % c.acc_bufs);
+        if (d == 1) {
+          if (first) mbar_arrive(&ctl->acc_full[b]);  // nothing accumulated for this item
+          else umma_commit(&ctl->acc_full[b]);
+        } else {
+          // no more items: wake the epilogue with the exit mark
+          *reinterpret_cast<volatile int*>(&ctl->exit_at) = static_cast<int>(item_iter);
+          __threadfence_block();
+          mbar_arrive(&ctl->acc_full[b]);
+        }
+      }
+      __syncwarp();
+      ++it;
+      if (++stage == c.stages) {
+        stage = 0;
+        ph ^= 1u;
+      }
+      if (d == 2) break;
+      ++item_iter;
+      first = true;
+      continue;
+    }
+    if (first) {
+      // the accumulator buffer must have been read out by the epilogue
+      const uint32_t b = item_iter % c.acc_bufs;
+      if (item_iter >= static_cast<uint32_t>(c.acc_bufs) &&
+          !wait_bar_warp(&ctl->acc_empty[b], ((item_iter / c.acc_bufs) - 1) & 1u, ctl, p.err)) {
+        aborted = true;
+        break;
+      }
+      acc = m.tmem + b * m.acc_stride;
+    }
+    tc_fence_after();
+    const uint32_t sb = m.smem0 + static_cast<uint32_t>(stage * c.stage_bytes);
+    const uint32_t m0 = sb + m.off_m, n0 = sb + m.off_n;
+    const uint32_t acc_first = first ? 0u : 1u;
+    if constexpr (FOLD) {
+      // per k-step: panel_hi x [lhs_hi | lhs_lo] (N = 2 Mt) for each half,
+      // then panel_lo x lhs_hi for each half
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
+        const uint32_t acc0 = ks == 0 ? acc_first : 1u;
+        const uint64_t b_hi = smem_desc(n0 + koff, 128, m.sbo);
+#pragma unroll
+        for (int h = 0; h < H; ++h)
+          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + koff + h * 16 * m.sbo, 128, m.sbo), b_hi, m.idesc2, acc0);
+#pragma unroll
+        for (int h = 0; h < H; ++h)
+          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + m.lo_m + koff + h * 16 * m.sbo, 128, m.sbo), b_hi,
+                     m.idesc, 1u);
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const uint32_t koff = ks * 256;
+        const uint32_t acc0 = ks == 0 ? acc_first : 1u;
+        const uint64_t b_hi = smem_desc(n0 + koff, 128, m.sbo);
+#pragma unroll
+        for (int h = 0; h < H; ++h) {
+          const uint32_t dt = acc + h * m.col_per_half;
+          const uint32_t hoff = koff + h * 16 * m.sbo;  // rows 128h.. of the M operand
+          const uint64_t a_hi = smem_desc(m0 + hoff, 128, m.sbo);
+          umma<F32>(dt, a_hi, b_hi, m.idesc, acc0);
+          if constexpr (F32) {
+            umma<true>(dt, a_hi, smem_desc(n0 + m.lo_n + koff, 128, m.sbo), m.idesc, 1u);
+            umma<true>(dt, smem_desc(m0 + m.lo_m + hoff, 128, m.sbo), b_hi, m.idesc, 1u);
+          }
+        }
+      }
+    }
+    umma_commit_warp(&ctl->empty[stage]);
+    if (lane == 0) *reinterpret_cast<volatile uint32_t*>(&ctl->progress) = it;
+    __syncwarp();
+    first = false;
+    ++it;
+    if (++stage == c.stages) {
+      stage = 0;
+      ph ^= 1u;
+    }
+  }
+  if (aborted && lane == 0) {
+    umma_commit(&ctl->drain);
+    drain_bar(&ctl->drain, 0);
+  }
+  __syncwarp();
+}
+
+template <bool F32, bool FOLD>
+__device__ void mma_dispatch(const TcParams& p, Ctrl* ctl, const MmaArgs& m, int ksteps, int halves) {
+  if (halves == 2) {
+    switch (ksteps) {
+      case 1: mma_role<F32, FOLD, 1, 2>(p, ctl, m); return;
+      case 2: mma_role<F32, FOLD, 2, 2>(p, ctl, m); return;
+      case 4: mma_role<F32, FOLD, 4, 2>(p, ctl, m); return;
+      default: mma_role<F32, FOLD, 8, 2>(p, ctl, m); return;
+    }
+  }
+  switch (ksteps) {
+    case 1: mma_role<F32, FOLD, 1, 1>(p, ctl, m); return;
+    case 2: mma_role<F32, FOLD, 2, 1>(p, ctl, m); return;
+    case 4: mma_role<F32, FOLD, 4, 1>(p, ctl, m); return;
+    default: mma_role<F32, FOLD, 8, 1>(p, ctl, m); return;
+  }
 }
 
 template <bool F32>
@@ -285,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   const int off_lhs = 0;
   const int off_raw = (NH - 1) * c.lhs_bytes;
   const int off_pan = NH * c.lhs_bytes;
-  const int col_per_half = c.swap ? c.Mt : c.n_mma;
+  const int col_per_half = c.col_per_half;
   const int acc_stride = c.halves * col_per_half;  // TMEM columns of one accumulator
 
   if (tid == 0) {
@@ -300,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
+    ctl->progress = 0;
     ctl->exit_at = -1;
     fence_mbar_init();
   }
@@ -310,281 +506,180 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   const uint32_t tmem = ctl->tmem_base;
 
   if (warp == kSchedWarp) {
-    // --------------------------- scheduler: work queue, merge, async copies
+    // ------------------- scheduler: work queue, merge-step records, copies
+    // Records of an item are streamed kRecAhead ahead: lane j < kRecInts
+    // holds field j of a record, so one coalesced 64-byte load brings a
+    // whole step. Every data stage is filled completely: absent tiles are
+    // copied from the zero buffer, so the byte count per stage is fixed.
+    const uint32_t stage_tx = static_cast<uint32_t>(c.lhs_bytes + c.G * NH * blk_bytes);
     uint32_t it = 0;
-    int last_copy_it[kMaxStages];
-    for (int s = 0; s < kMaxStages; ++s) last_copy_it[s] = -1;
+    int stage = 0;
+    uint32_t ph = 0;
     bool aborted = false;
+    const int jslot = lane / NH;  // panel slot this lane copies when tiles are not consecutive
+    const int jhl = lane % NH;
     for (uint32_t item_iter = 0; !aborted; ++item_iter) {
       int q = 0;
       if (lane == 0) q = atomicAdd(p.queue, 1);
       q = __shfl_sync(0xffffffffu, q, 0);
-      const bool exit_now = q >= W;
-      int s0 = 0, gcnt = 0;
-      if (!exit_now) {
-        const int item = p.order[q];
-        s0 = p.item_first[item];
-        gcnt = p.item_count[item];
-        if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt, 0};
-      }
-      int64_t cur = 0, end = 0;
-      if (lane < gcnt) {
-        cur = p.seg_off[s0 + lane];
-        end = p.seg_off[s0 + lane + 1];
-        if (p.pair_key) {
-          // pairs of this key block: keys are non-decreasing inside a segment
-          int64_t lo = cur, hi = end;
-          while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (p.pair_key[mid] < p.k_lo) lo = mid + 1; else hi = mid;
-          }
-          const int64_t a = lo;
-          hi = end;
-          while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (p.pair_key[mid] < p.k_hi) lo = mid + 1; else hi = mid;
-          }
-          cur = a;
-          end = lo;
-        }
-      }
-      int nsteps = 0;
-      int wpos = kWin;  // window exhausted: refill on first use
-      int step_lhs = -1, my_rhs = -1, done = exit_now ? 2 : 0;
-      for (int chunk = nchunks;; ++chunk) {
-        if (chunk == nchunks && !done) {
-          // next merge step: the smallest pending lhs tile over the segments
-          if (lane < gcnt && wpos == kWin && cur < end) {
-            for (int qq = 0; qq < kWin; ++qq) {
-              const int64_t i = cur + qq;
-              ctl->win_l[lane][qq] = i < end ? p.pl[i] : INT_MAX;
-              ctl->win_r[lane][qq] = i < end ? p.pr[i] : -1;
-            }
-            wpos = 0;
-          }
-          const int v = (lane < gcnt && cur < end) ? ctl->win_l[lane][wpos] : INT_MAX;
-          const int kmin = __reduce_min_sync(0xffffffffu, v);
-          if (kmin == INT_MAX) {
-            done = 1;
-            my_rhs = -1;
-          } else {
-            const bool mine = v == kmin;
-            my_rhs = mine ? ctl->win_r[lane][wpos] : -1;
-            if (mine) {
-              ++cur;
-              ++wpos;
-            }
-            step_lhs = kmin;
-          }
-          chunk = 0;
-        }
-        const int stage = static_cast<int>(it % c.stages);
-        const uint32_t ph = (it / c.stages) & 1u;
+      if (q >= W) {
+        // no more items: exit marker
         if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
           aborted = true;
           break;
         }
-        Step& sr = ctl->ring[stage];
-        if (lane < kMaxG) sr.rhs[lane] = done ? -1 : my_rhs;
         if (lane == 0) {
-          sr.lhs = step_lhs;
-          sr.k0 = chunk * c.KC;
-          sr.done = done;
+          ctl->ring[stage].done = 2;
+          mbar_arrive_expect_tx(&ctl->copy[stage], 0);
         }
-        if (done == 1 && lane == 0) ctl->item_log[item_iter % kItemLog].nsteps = nsteps;
         __syncwarp();
-        if (done) {
-          if (lane == 0) mbar_arrive_expect_tx(&ctl->copy[stage], 0);
-          ++it;
-          break;
-        }
-        ++nsteps;
-        const int k0 = chunk * c.KC;
-        uint8_t* sbase = smem + stage * c.stage_bytes;
-        const int li = step_lhs;
+        break;
+      }
+      const int item = p.order[q];
+      const int s0 = p.item_first[item];
+      const int gcnt = p.item_count[item];
+      const int64_t* ib = p.item_rec + static_cast<int64_t>(item) * (p.nblocks + 1) + p.blk;
+      const int64_t rb = ib[0], re = ib[1];
+      if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt, static_cast<int>(re - rb)};
+      int ahead[kRecAhead];
+#pragma unroll
+      for (int a = 0; a < kRecAhead; ++a)
+        ahead[a] = (lane < kRecInts && rb + a < re) ? __ldg(p.recs + (rb + a) * kRecInts + lane) : 0;
+      for (int64_t r = rb; r < re && !aborted; ++r) {
+        const int cur = ahead[0];
+#pragma unroll
+        for (int a = 0; a + 1 < kRecAhead; ++a) ahead[a] = ahead[a + 1];
+        ahead[kRecAhead - 1] =
+            (lane < kRecInts && r + kRecAhead < re) ? __ldg(p.recs + (r + kRecAhead) * kRecInts + lane) : 0;
+        const int li = __shfl_sync(0xffffffffu, cur, kRecLhs);
+        const int flags = __shfl_sync(0xffffffffu, cur, kRecFlags);
+        const int rhs0 = __shfl_sync(0xffffffffu, cur, kRecRhs0);
+        const int my_rhs = __shfl_sync(0xffffffffu, cur, kRecRhs + (jslot & (kMaxG - 1)));
         const bool lok = li >= 0 && li < p.lhs_rows;
-        int present = 0;
-        for (int g = 0; g < c.G; ++g) {
-          const int r = sr.rhs[g];
-          present += (r >= 0 && r < p.rhs_rows) ? 1 : 0;
-        }
-        bool consec = present == c.G && sr.rhs[0] + c.G <= p.rhs_rows;
-        for (int g = 1; g < c.G; ++g) consec = consec && sr.rhs[g] == sr.rhs[0] + g;
-        if (lane == 0) {
-          const uint32_t bytes = static_cast<uint32_t>((lok ? c.lhs_bytes : 0) + present * NH * blk_bytes);
-          mbar_arrive_expect_tx(&ctl->copy[stage], bytes);
-          last_copy_it[stage] = static_cast<int>(it);
-          if (!lok && p.err) atomicExch(p.err, ES_ERR_INDEX);
-          // raw lhs chunk straight into the canonical K-major layout
-          if (lok) tma_load_4d(sbase + off_raw, &lhs_map, 0, 0, k0 / EPU, li * (c.Mt / 8), &ctl->copy[stage]);
-        }
-        // panel: per k-chunk the pre-laid rhs tiles sit tile after tile, so
-        // consecutive rhs tiles (a dense rhs row) arrive in one copy
-        const int64_t cbase = static_cast<int64_t>(k0 / c.KC) * p.rhs_rows;
-        if (consec) {
-          if (lane < NH)
-            bulk_g2s(sbase + off_pan + lane * c.pan_bytes,
-                     (lane ? p.pan_lo : p.pan_hi) + (cbase + sr.rhs[0]) * blk_bytes,
-                     static_cast<uint32_t>(c.G * blk_bytes), &ctl->copy[stage]);
-        } else {
-          for (int j = lane; j < c.G * NH; j += 32) {
-            const int hl = j % NH, g = j / NH;
-            const int r = sr.rhs[g];
-            if (r < 0 || r >= p.rhs_rows) continue;
-            bulk_g2s(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes,
-                     (hl ? p.pan_lo : p.pan_hi) + (cbase + r) * blk_bytes, static_cast<uint32_t>(blk_bytes),
-                     &ctl->copy[stage]);
+        const bool consec = (flags & 1) != 0;
+        for (int chunk = 0; chunk < nchunks; ++chunk) {
+          if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
+            aborted = true;
+            break;
+          }
+          const int k0 = chunk * c.KC;
+          uint8_t* sbase = smem + stage * c.stage_bytes;
+          if (lane == 0) {
+            ctl->ring[stage].done = 0;
+            mbar_arrive_expect_tx(&ctl->copy[stage], stage_tx);
+            // raw lhs chunk straight into the canonical K-major layout
+            if (lok)
+              tma_load_4d(sbase + off_raw, &lhs_map, 0, 0, k0 / EPU, li * (c.Mt / 8), &ctl->copy[stage]);
+            else
+              bulk_g2s(sbase + off_raw, p.zeros, static_cast<uint32_t>(c.lhs_bytes), &ctl->copy[stage]);
+          }
+          // panel: per k-chunk the pre-laid rhs tiles sit tile after tile, so
+          // consecutive rhs tiles (a dense rhs row) arrive in one copy
+          const int64_t cbase = static_cast<int64_t>(k0 / c.KC) * p.rhs_rows;
+          if (consec) {
+            if (lane < NH)
+              bulk_g2s(sbase + off_pan + lane * c.pan_bytes, (lane ? p.pan_lo : p.pan_hi) + (cbase + rhs0) * blk_bytes,
+                       static_cast<uint32_t>(c.G * blk_bytes), &ctl->copy[stage]);
+          } else if (lane < c.G * NH) {
+            const bool ok = my_rhs >= 0 && my_rhs < p.rhs_rows;
+            bulk_g2s(sbase + off_pan + jhl * c.pan_bytes + jslot * blk_bytes,
+                     ok ? (jhl ? p.pan_lo : p.pan_hi) + (cbase + my_rhs) * blk_bytes : p.zeros,
+                     static_cast<uint32_t>(blk_bytes), &ctl->copy[stage]);
+          }
+          __syncwarp();
+          ++it;
+          if (++stage == c.stages) {
+            stage = 0;
+            ph ^= 1u;
           }
         }
-        ++it;
       }
-      if (exit_now) break;
-    }
-    if (aborted && lane == 0) {
-      for (int s = 0; s < c.stages; ++s)
-        if (last_copy_it[s] >= 0) drain_bar(&ctl->copy[s], (static_cast<uint32_t>(last_copy_it[s]) / c.stages) & 1u);
-    }
-    __syncwarp();
-  } else if (warp < 4) {
-    // ------------------------------ split (fp32) / zero-fill absent tiles
-    uint32_t it = 0;
-    while (true) {
-      const int stage = static_cast<int>(it % c.stages);
-      const uint32_t ph = (it / c.stages) & 1u;
-      if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
-      const Step& st = ctl->ring[stage];
-      const int d = st.done;
-      if (d) {
-        mbar_arrive(&ctl->full[stage]);
-        ++it;
-        if (d == 2) break;
-        continue;
-      }
-      uint8_t* sbase = smem + stage * c.stage_bytes;
-      const bool lok = st.lhs >= 0 && st.lhs < p.lhs_rows;
-      // fp32: split the canonical raw chunk in place (x -> hi, lo); a
-      // missing lhs tile reads as zeros
-      if constexpr (F32) {
-        const int nf = c.Mt * (c.KC / EPU);
-        for (int f = tid; f < nf; f += kProducers) {
-          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (lok) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
-          float4 hi, lo;
-          split_tf32(x.x, hi.x, lo.x);
-          split_tf32(x.y, hi.y, lo.y);
-          split_tf32(x.z, hi.z, lo.z);
-          split_tf32(x.w, hi.w, lo.w);
-          *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
-          *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
-        }
-      } else {
-        if (!lok) {
-          for (int f = tid; f < c.lhs_bytes / 16; f += kProducers)
-            *reinterpret_cast<uint4*>(sbase + off_lhs + f * 16) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      // zero the panel slots of absent rhs tiles
-      for (int g = 0; g < c.G; ++g) {
-        const int r = st.rhs[g];
-        if (r >= 0 && r < p.rhs_rows) continue;
-        if (r >= p.rhs_rows && tid == 0 && p.err) atomicExch(p.err, ES_ERR_INDEX);
-        const int per = blk_bytes / 16;
-        for (int q = tid; q < NH * per; q += kProducers) {
-          const int hl = q / per, w16 = q % per;
-          *reinterpret_cast<uint4*>(sbase + off_pan + hl * c.pan_bytes + g * blk_bytes + w16 * 16) =
-              make_uint4(0, 0, 0, 0);
-        }
-      }
-      fence_proxy_async();
-      mbar_arrive(&ctl->full[stage]);
-      ++it;
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA warp
-    const uint32_t idesc = make_idesc(F32, false, false, 128, c.swap ? c.Mt : c.n_mma);
-    uint32_t it = 0, item_iter = 0;
-    bool first = true, aborted = false;
-    uint32_t acc = tmem;
-    while (true) {
-      const int stage = static_cast<int>(it % c.stages);
-      const uint32_t ph = (it / c.stages) & 1u;
-      if (!wait_bar(&ctl->full[stage], ph, ctl, p.err)) {
+      if (aborted) break;
+      // end of the item
+      if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
         aborted = true;
         break;
       }
-      const int d = ctl->ring[stage].done;
-      if (d) {
-        if (lane == 0) {
-          mbar_arrive(&ctl->empty[stage]);
-          const int b = static_cast<int>(item_iter % c.acc_bufs);
-          if (d == 1) {
-            if (first) mbar_arrive(&ctl->acc_full[b]);  // nothing accumulated for this item
-            else umma_commit(&ctl->acc_full[b]);
-          } else {
-            // no more items: wake the epilogue with the exit mark
-            *reinterpret_cast<volatile int*>(&ctl->exit_at) = static_cast<int>(item_iter);
-            __threadfence_block();
-            mbar_arrive(&ctl->acc_full[b]);
-          }
-        }
-        __syncwarp();
-        ++it;
-        if (d == 2) break;
-        ++item_iter;
-        first = true;
-        continue;
-      }
-      if (first) {
-        // the accumulator buffer must have been read out by the epilogue
-        const uint32_t b = item_iter % c.acc_bufs;
-        if (item_iter >= static_cast<uint32_t>(c.acc_bufs) &&
-            !wait_bar(&ctl->acc_empty[b], ((item_iter / c.acc_bufs) - 1) & 1u, ctl, p.err)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        acc = tmem + b * acc_stride;
-      }
-      tc_fence_after();
       if (lane == 0) {
-        const uint32_t sb = smem_u32(smem + stage * c.stage_bytes);
-        const uint32_t lhs0 = sb + off_lhs, lhs1 = lhs0 + c.lhs_bytes;
-        const uint32_t pan0 = sb + off_pan, pan1 = pan0 + c.pan_bytes;
-        const int ksteps = c.KC / KSTEP;
-        for (int ks = 0; ks < ksteps; ++ks) {
-          const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
-          for (int h = 0; h < c.halves; ++h) {
-            const uint32_t dt = acc + h * col_per_half;
-            const uint32_t acc0 = (first && ks == 0) ? 0u : 1u;
-            const uint32_t hoff = koff + h * 16 * sbo;  // rows 128h.. of the M operand
-            // M operand: lhs (plain) or the rhs panel (transposed product)
-            const uint32_t am0 = (c.swap ? pan0 : lhs0) + hoff, am1 = (c.swap ? pan1 : lhs1) + hoff;
-            const uint32_t bn0 = (c.swap ? lhs0 : pan0) + koff, bn1 = (c.swap ? lhs1 : pan1) + koff;
-            const uint64_t a_hi = smem_desc(am0, 128, sbo), b_hi = smem_desc(bn0, 128, sbo);
-            umma<F32>(dt, a_hi, b_hi, idesc, acc0);
-            if constexpr (F32) {
-              umma<F32>(dt, a_hi, smem_desc(bn1, 128, sbo), idesc, 1u);
-              umma<F32>(dt, smem_desc(am1, 128, sbo), b_hi, idesc, 1u);
-            }
-          }
-        }
-        umma_commit(&ctl->empty[stage]);
+        ctl->ring[stage].done = 1;
+        mbar_arrive_expect_tx(&ctl->copy[stage], 0);
       }
       __syncwarp();
-      first = false;
       ++it;
+      if (++stage == c.stages) {
+        stage = 0;
+        ph ^= 1u;
+      }
     }
     if (aborted && lane == 0) {
-      umma_commit(&ctl->drain);
-      drain_bar(&ctl->drain, 0);
+      // the last `stages` stages may still have copies landing
+      const uint32_t n = static_cast<uint32_t>(c.stages);
+      for (uint32_t i = it > n ? it - n : 0u; i < it; ++i) drain_bar(&ctl->copy[i % n], (i / n) & 1u);
     }
     __syncwarp();
+  } else if (warp < 4) {
+    // ----------------------------------------- fp32 split of the lhs chunk
+    if constexpr (F32) {
+      uint32_t it = 0;
+      int stage = 0;
+      uint32_t ph = 0;
+      const int nf = c.Mt * (c.KC / EPU);
+      while (true) {
+        if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
+        const int d = ctl->ring[stage].done;
+        if (!d) {
+          // split the canonical raw chunk in place (x -> hi, lo)
+          uint8_t* sbase = smem + stage * c.stage_bytes;
+          for (int f = tid; f < nf; f += kProducers) {
+            const float4 x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+            float4 hi, lo;
+            split_tf32(x.x, hi.x, lo.x);
+            split_tf32(x.y, hi.y, lo.y);
+            split_tf32(x.z, hi.z, lo.z);
+            split_tf32(x.w, hi.w, lo.w);
+            *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
+            *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
+          }
+          fence_proxy_async();
+        }
+        mbar_arrive(&ctl->full[stage]);
+        ++it;
+        if (++stage == c.stages) {
+          stage = 0;
+          ph ^= 1u;
+        }
+        if (d == 2) break;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA warp
+    MmaArgs m;
+    m.smem0 = smem_u32(smem);
+    m.tmem = tmem;
+    m.lane = lane;
+    m.sbo = static_cast<uint32_t>(sbo);
+    m.col_per_half = static_cast<uint32_t>(col_per_half);
+    m.acc_stride = static_cast<uint32_t>(acc_stride);
+    const bool swap = c.swap != 0;
+    m.lo_m = swap ? static_cast<uint32_t>(c.pan_bytes) : static_cast<uint32_t>(c.lhs_bytes);
+    m.lo_n = swap ? static_cast<uint32_t>(c.lhs_bytes) : static_cast<uint32_t>(c.pan_bytes);
+    m.off_m = static_cast<uint32_t>(swap ? off_pan : off_lhs);
+    m.off_n = static_cast<uint32_t>(swap ? off_lhs : off_pan);
+    m.idesc = make_idesc(F32, false, false, 128, swap ? c.Mt : c.n_mma);
+    m.idesc2 = make_idesc(F32, false, false, 128, 2 * c.Mt);
+    const int ksteps = c.KC / KSTEP;
+    if constexpr (F32) {
+      if (c.fold) mma_dispatch<true, true>(p, ctl, m, ksteps, c.halves);
+      else mma_dispatch<true, false>(p, ctl, m, ksteps, c.halves);
+    } else {
+      mma_dispatch<false, false>(p, ctl, m, ksteps, c.halves);
+    }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
     // ---------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
     for (uint32_t item_iter = 0;; ++item_iter) {
       const uint32_t b = item_iter % c.acc_bufs;
-      if (!wait_bar(&ctl->acc_full[b], (item_iter / c.acc_bufs) & 1u, ctl, p.err)) break;
+      if (!wait_bar(&ctl->acc_full[b], (item_iter / c.acc_bufs) & 1u, ctl, p.err, &ctl->progress, kEpiSleepNs)) break;
       if (*reinterpret_cast<volatile int*>(&ctl->exit_at) == static_cast<int>(item_iter)) break;
       const ItemInfo info = ctl->item_log[item_iter % kItemLog];
       const int s0 = info.s0, gcnt = info.gcnt;
@@ -638,6 +733,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           for (int m0 = 0; m0 < c.Mt; m0 += 32) {
             float v[32];
             tmem_ld32(tbase + m0, v);
+            if (c.fold) {
+              // the panel_hi x lhs_lo block sits Mt columns to the right
+              float w[32];
+              tmem_ld32(tbase + c.Mt + m0, w);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += w[j];
+            }
             if (live) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
@@ -763,9 +865,110 @@ __global__ void item_work_keys_kernel(const int32_t* __restrict__ first, const i
   }
 }
 
+// G-way merge of a work item's segment pair lists into step records, one
+// warp per item. Lane g walks segment g; each step takes the smallest
+// pending lhs tile, and every segment whose next pair has that lhs tile
+// contributes its rhs tile (others: -1). Each list keeps its own order, so
+// a segment's pairs are summed in join order. Records of an item start at
+// its first pair index (an item has at least as many pairs as steps) and are
+// in ascending contracted key; item_rec gets, per key block b, the first
+// record with key >= key_extent * b / nblocks (and the end).
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
+    const int32_t* __restrict__ pl, const int32_t* __restrict__ pr, const int32_t* __restrict__ pair_key,
+    const int64_t* __restrict__ seg_off, const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
+    const int64_t* __restrict__ num_items, int G, int64_t lhs_rows, int64_t rhs_rows, int nblocks, int64_t key_extent,
+    int32_t* __restrict__ recs, int64_t* __restrict__ item_rec, int32_t* __restrict__ err) {
+  __shared__ int win_l[kMergeWarps][kMaxG][kWin];
+  __shared__ int win_r[kMergeWarps][kMaxG][kWin];
+  __shared__ int win_k[kMergeWarps][kMaxG][kWin];
+  const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t W = *num_items;
+  const bool keyed = nblocks > 1 && pair_key != nullptr;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; item < W;
+       item += static_cast<int64_t>(gridDim.x) * kMergeWarps) {
+    const int s0 = item_first[item];
+    const int gcnt = item_count[item];
+    int64_t cur = 0, end = 0;
+    if (lane < gcnt) {
+      cur = seg_off[s0 + lane];
+      end = seg_off[s0 + lane + 1];
+    }
+    const int64_t base = seg_off[s0];
+    int64_t* ib = item_rec + item * (nblocks + 1);
+    if (lane == 0) ib[0] = base;
+    int64_t n = 0;
+    int b = 0;
+    int wpos = kWin;
+    bool bad = false;
+    while (true) {
+      if (lane < gcnt && wpos == kWin && cur < end) {
+        int tl[kWin], tr[kWin], tk[kWin];
+#pragma unroll
+        for (int qq = 0; qq < kWin; ++qq) {
+          const int64_t i = cur + qq;
+          tl[qq] = i < end ? __ldg(pl + i) : INT_MAX;
+          tr[qq] = i < end ? __ldg(pr + i) : -1;
+          tk[qq] = (keyed && i < end) ? __ldg(pair_key + i) : 0;
+        }
+#pragma unroll
+        for (int qq = 0; qq < kWin; ++qq) {
+          win_l[wib][lane][qq] = tl[qq];
+          win_r[wib][lane][qq] = tr[qq];
+          win_k[wib][lane][qq] = tk[qq];
+        }
+        wpos = 0;
+      }
+      __syncwarp();
+      const bool live = lane < gcnt && cur < end;
+      const int v = live ? win_l[wib][lane][wpos] : INT_MAX;
+      const int kmin = __reduce_min_sync(0xffffffffu, v);
+      if (kmin == INT_MAX) break;
+      const bool mine = live && v == kmin;
+      int my_rhs = -1, my_key = INT_MAX;
+      if (mine) {
+        my_rhs = win_r[wib][lane][wpos];
+        my_key = win_k[wib][lane][wpos];
+        ++cur;
+        ++wpos;
+      }
+      if (my_rhs < -1 || my_rhs >= rhs_rows) {
+        bad = true;
+        my_rhs = -1;
+      }
+      if (keyed) {
+        const int key = __reduce_min_sync(0xffffffffu, my_key);
+        while (b + 1 <= nblocks - 1 && static_cast<int64_t>(key) >= key_extent * (b + 1) / nblocks) {
+          ++b;
+          if (lane == 0) ib[b] = base + n;
+        }
+      }
+      const int first = __shfl_sync(0xffffffffu, my_rhs, 0);
+      const bool cons = __all_sync(0xffffffffu, lane >= G || (my_rhs >= 0 && my_rhs == first + lane)) &&
+                        first >= 0 && first + G <= rhs_rows;
+      int32_t* rec = recs + (base + n) * kRecInts;
+      if (lane == 0) {
+        rec[kRecLhs] = kmin;
+        rec[kRecFlags] = cons ? 1 : 0;
+        rec[kRecRhs0] = first;
+        if (kmin < 0 || kmin >= lhs_rows) bad = true;
+      }
+      if (lane < kMaxG) rec[kRecRhs + lane] = lane < G ? my_rhs : -1;
+      ++n;
+    }
+    if (lane == 0)
+      for (int bb = b + 1; bb <= nblocks; ++bb) ib[bb] = base + n;
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && err) atomicExch(err, ES_ERR_INDEX);
+  }
+}
+
 struct TcWs {
   uint8_t* pan_hi;
   uint8_t* pan_lo;
+  uint8_t* zeros;
+  int32_t* recs;
+  int64_t* item_rec;
   int32_t* item_first;
   int32_t* item_count;
   uint32_t* flags;
@@ -779,12 +982,20 @@ struct TcWs {
   int* queue;
 };
 
+int64_t zero_bytes(const TcConfig& c) {
+  const int blk = c.Nt * c.KC * (c.fp32 ? 4 : 2);
+  return c.lhs_bytes > blk ? c.lhs_bytes : blk;
+}
+
 template <typename C>
-void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t nseg) {
+void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks) {
   const int64_t pan_elems = rhs_rows * c.Kt * c.Nt;
   const int esz = c.fp32 ? 4 : 2;
   w.pan_hi = cv.template take<uint8_t>(pan_elems * esz);
   w.pan_lo = c.fp32 ? cv.template take<uint8_t>(pan_elems * esz) : nullptr;
+  w.zeros = cv.template take<uint8_t>(zero_bytes(c));
+  w.recs = cv.template take<int32_t>(npairs * kRecInts);
+  w.item_rec = cv.template take<int64_t>(nseg * (nblocks + 1));
   w.item_first = cv.template take<int32_t>(nseg);
   w.item_count = cv.template take<int32_t>(nseg);
   w.flags = cv.template take<uint32_t>(nseg);
@@ -881,12 +1092,15 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   } else {
     return false;
   }
-  const int acc_cols = c->halves * (c->swap ? Mt : c->n_mma);
+  c->fold = (f32 && c->swap && Mt % 32 == 0 && 2 * Mt <= 256) ? 1 : 0;
+  c->col_per_half = c->swap ? (c->fold ? 2 * Mt : Mt) : c->n_mma;
+  const int acc_cols = c->halves * c->col_per_half;
   if (acc_cols > 512) return false;
   c->acc_bufs = 2 * acc_cols <= 512 ? 2 : 1;
-  int pw = 32;
-  while (pw < c->acc_bufs * acc_cols) pw <<= 1;
-  c->tmem_cols = pw;
+  // one CTA per SM (shared memory is sized for it), so all 512 columns are
+  // free; the epilogue reads in 32-column groups that may run past a small
+  // accumulator
+  c->tmem_cols = 512;
   const int esz = f32 ? 4 : 2;
   const int nh = f32 ? 2 : 1;
   const int ctrl = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
@@ -915,23 +1129,43 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   return false;
 }
 
-size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t nseg) {
+// Key blocks: the rhs operand re-read by every strip is split along the
+// contracted range into slices that fit in L2; one launch per slice, in
+// order, later slices adding into the output.
+int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent) {
+  if (!have_key || key_extent <= 1) return 1;
+  const int64_t panel_bytes = rhs_rows * c.Kt * c.Nt * (c.fp32 ? 8 : 2);
+  // EINSPARSE_KBLOCK_BYTES overrides the per-block panel budget (tuning, tests)
+  int64_t budget = kPanelL2Budget;
+  if (const char* e = std::getenv("EINSPARSE_KBLOCK_BYTES")) {
+    const long long v = std::atoll(e);
+    if (v > 0) budget = v;
+  }
+  int64_t nb = (panel_bytes + budget - 1) / budget;
+  if (nb > key_extent) nb = key_extent;
+  if (nb > kMaxKeyBlocks) nb = kMaxKeyBlocks;
+  return nb < 1 ? 1 : static_cast<int>(nb);
+}
+
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks) {
   SizeOnly s;
   TcWs w;
-  tc_layout(s, w, c, rhs_rows, nseg);
+  tc_layout(s, w, c, rhs_rows, npairs, nseg, nblocks);
   return s.s.used + 256;
 }
 
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
-              const int32_t* pl, const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out,
-              const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out, int odt, void* ws,
-              size_t ws_bytes, int32_t* err, cudaStream_t st) {
+              const int32_t* pl, const int32_t* pr, int64_t npairs, const int64_t* seg_off, int64_t nseg,
+              const int32_t* seg_out, const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out,
+              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st) {
   if (nseg <= 0) return ES_OK;
   if (nseg >= INT32_MAX || rhs_rows >= INT32_MAX || lhs_rows >= INT32_MAX) return ES_ERR_UNSUPPORTED;
+  const int nblocks = tc_key_blocks(c, rhs_rows, pair_key != nullptr, key_extent);
   Carver cv(ws, ws_bytes);
   TcWs w;
-  tc_layout(cv, w, c, rhs_rows, nseg);
+  tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks);
   if (cv.overflow) return ES_ERR_WORKSPACE;
+  if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
   // 1. rhs tiles into the shared-memory image (split for fp32)
   const int64_t pe = rhs_rows * c.Kt * c.Nt;
   if (pe > 0) {
@@ -964,8 +1198,14 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;
   }
+  // 4. merge steps of every item (all items in parallel)
+  {
+    const int blocks = static_cast<int>((nseg + kMergeWarps - 1) / kMergeWarps);
+    ES_LAUNCH(tc_merge_kernel, blocks, kMergeWarps * 32, 0, st, pl, pr, pair_key, seg_off, w.item_first,
+              w.item_count, w.num_items, c.G, lhs_rows, rhs_rows, nblocks, key_extent, w.recs, w.item_rec, err);
+  }
   if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
-  // 4. persistent tensor-core kernel, one CTA per SM
+  // 5. persistent tensor-core kernel, one CTA per SM
   TcParams prm;
   prm.c = c;
   prm.lhs = static_cast<const uint8_t*>(lhs);
@@ -973,8 +1213,10 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.pan_hi = w.pan_hi;
   prm.pan_lo = w.pan_lo;
   prm.rhs_rows = rhs_rows;
-  prm.pl = pl;
-  prm.pr = pr;
+  prm.recs = w.recs;
+  prm.item_rec = w.item_rec;
+  prm.nblocks = nblocks;
+  prm.zeros = w.zeros;
   prm.seg_off = seg_off;
   prm.item_first = w.item_first;
   prm.item_count = w.item_count;
@@ -1025,26 +1267,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
         cudaSuccess)
       return ES_ERR_CUDA;
   }
-  // Key blocks: the rhs operand re-read by every strip is split along the
-  // contracted range into slices that fit in L2; one launch per slice, in
-  // order, later slices adding into the output.
-  int64_t panel_bytes = rhs_rows * c.Kt * c.Nt * (c.fp32 ? 8 : 2);
-  int nblocks = 1;
-  if (pair_key && key_extent > 1) {
-    // EINSPARSE_KBLOCK_BYTES overrides the per-block panel budget (tuning, tests)
-    int64_t budget = kPanelL2Budget;
-    if (const char* e = std::getenv("EINSPARSE_KBLOCK_BYTES")) {
-      const long long v = std::atoll(e);
-      if (v > 0) budget = v;
-    }
-    nblocks = static_cast<int>((panel_bytes + budget - 1) / budget);
-    if (nblocks > key_extent) nblocks = static_cast<int>(key_extent);
-    if (nblocks < 1) nblocks = 1;
-  }
-  prm.pair_key = nblocks > 1 ? pair_key : nullptr;
   for (int b = 0; b < nblocks; ++b) {
-    prm.k_lo = static_cast<int>(key_extent * b / nblocks);
-    prm.k_hi = static_cast<int>(key_extent * (b + 1) / nblocks);
+    prm.blk = b;
     prm.accumulate = b > 0 ? 1 : 0;
     if (b > 0 && cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
     if (c.fp32)

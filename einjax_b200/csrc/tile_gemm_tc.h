@@ -17,6 +17,11 @@ struct TcConfig {
   int stages;
   int halves;      // 128-row MMA halves (M = 128 * halves)
   int n_mma;       // MMA N
+  int fold;        // 1 (fp32, swapped, Mt % 32 == 0, 2*Mt <= 256): the lhs hi and lo
+                   // copies sit side by side as one N = 2*Mt operand, so
+                   // panel_hi x [lhs_hi | lhs_lo] is one MMA; the epilogue adds
+                   // the two column blocks
+  int col_per_half;  // TMEM columns of one 128-row half of an accumulator
   int acc_bufs;    // TMEM accumulators (2 when they fit: epilogue overlaps the next item)
   int tmem_cols;   // allocated TMEM columns (power of two)
   int lhs_bytes;   // one operand copy of a stage's lhs chunk
@@ -30,11 +35,14 @@ struct TcConfig {
 // size-1 batch labels only, both operands f32 or both bf16.
 bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, TcConfig* c);
 
-size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t nseg);
+// Launches over the contracted range (one per key block) for these operands.
+int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent);
+
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks);
 
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
-              const int32_t* pl, const int32_t* pr, const int64_t* seg_off, int64_t nseg, const int32_t* seg_out,
-              const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out, int odt, void* ws,
-              size_t ws_bytes, int32_t* err, cudaStream_t st);
+              const int32_t* pl, const int32_t* pr, int64_t npairs, const int64_t* seg_off, int64_t nseg,
+              const int32_t* seg_out, const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out,
+              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st);
 
 }  // namespace es

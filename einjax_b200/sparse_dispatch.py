@@ -162,15 +162,16 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     pk = pair_key.to(torch.int32).contiguous() if (pair_key is not None and so is not None) else None
     lti, rti = L.i64arr(lt), L.i64arr(rt)
     prec = _PREC[precision]
+    kext = int(key_extent) if pk is not None else 0
     wsb = lib.es_tile_einsum_workspace_size(ks, lti, len(lt), rti, len(rt), es_dtype(lv), es_dtype(rv),
-                                            int(rv.shape[0]), nseg, prec)
+                                            int(rv.shape[0]), P, nseg, kext, prec)
     ws = workspace(wsb, dev) if wsb else None
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     L.check("es_tile_einsum", lib.es_tile_einsum(
         ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
         int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
         sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None,
-        pk.data_ptr() if pk is not None else None, int(key_extent) if pk is not None else 0, out.data_ptr(),
+        pk.data_ptr() if pk is not None else None, kext, out.data_ptr(),
         _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         err.data_ptr(), stream_ptr(dev)))
     if check:
