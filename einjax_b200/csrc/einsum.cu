@@ -271,7 +271,7 @@ extern "C" int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs
   int st = parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d);
   if (st != ES_OK) return -st;
   TcConfig c;
-  if (want_tc(precision) && tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, &c)) return 1;
+  if (want_tc(precision) && tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, false, &c)) return 1;
   if (precision == ES_PREC_TC) return -ES_ERR_UNSUPPORTED;
   return 0;
 }
@@ -283,7 +283,7 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
   EinsumDesc d;
   if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
   TcConfig c;
-  if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, &c)) return 0;
+  if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, key_extent > 0, &c)) return 0;
   return tc_workspace_size(c, rhs_rows, num_pairs, num_segments, tc_key_blocks(c, rhs_rows, true, key_extent));
 }
 
@@ -307,7 +307,8 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
     TcConfig c;
     // the tensor-core path walks each segment's pairs as one sorted lhs
     // sequence; per-pair calls (no segments) stay on the SIMT path
-    if (seg_offsets && tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, &c)) {
+    if (seg_offsets &&
+        tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, pair_key != nullptr && key_extent > 0, &c)) {
       const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, num_pairs,
                               seg_offsets, nseg, seg_out_index, seg_strip, pair_key, key_extent, out_values,
                               out_dtype, workspace, workspace_bytes, error_dev, st);

@@ -50,6 +50,7 @@ constexpr int kEpilogue = 128;
 constexpr int kThreads = 320;
 constexpr int kItemLog = 16;
 constexpr int kMaxG = 8;
+constexpr int kMaxSlots = 8;      // lhs strips stacked into one 128-row MMA operand
 constexpr int kMaxStages = 8;
 constexpr int kWin = 16;          // prefetched pair entries per segment
 constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s without progress: give up
@@ -61,25 +62,26 @@ constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 constexpr int kMaxKeyBlocks = 16;
 
-// done: 0 data stage, 1 end of a work item, 2 no more items
+// done: 0 data stage, 1 end of a work item, 2 no more items; mask: lhs
+// slots present in a data stage (stacked mode)
 struct Step {
   int done;
+  int mask;
 };
 
-// One merge step of a work item (one lhs tile against up to G rhs tiles), as
-// written by tc_merge_kernel: 16 ints, lane j of the scheduler warp loads
-// field j.
+// One merge step of a work item, as written by tc_merge_kernel: 16 ints,
+// lane j of the scheduler warp loads field j. With S lhs slots and G rhs
+// slots: [0, S) lhs tile per slot (-1 absent), [S, S+G) rhs tile per
+// segment slot (-1 absent), S+G flags (bit 0: rhs tiles 0..G-1 present and
+// consecutive, one copy), S+G+1 first rhs tile. S + G + 2 <= 16.
 constexpr int kRecInts = 16;
-constexpr int kRecLhs = 0;    // lhs tile
-constexpr int kRecFlags = 1;  // bit 0: rhs tiles 0..G-1 present and consecutive (one copy)
-constexpr int kRecRhs0 = 2;   // first rhs tile
-constexpr int kRecRhs = 4;    // rhs tile per segment slot, -1 absent (slots 0..kMaxG-1)
 constexpr int kRecAhead = 4;  // records the scheduler has in flight ahead of use
 
+// A work item: up to S sub-strips (<= G segments of one strip each).
 struct ItemInfo {
-  int s0;
-  int gcnt;
-  int nsteps;  // data stages this item produced (0: nothing in this key block)
+  int s0[kMaxSlots];    // first segment per slot
+  int gcnt[kMaxSlots];  // segments per slot (0: empty slot)
+  int nsteps;           // data stages this item produced (0: nothing in this key block)
 };
 
 struct Ctrl {
@@ -160,17 +162,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
-// 4-D tiled TMA load (no multicast) completing on an mbarrier.
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar) {
+// 2-D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -234,13 +236,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Shared-memory matrix descriptor, no swizzle (canonical "interleaved"
-// layout of 8 x 16-byte core matrices), Blackwell descriptor version 1.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor of a K-major operand in a swizzled layout
+// (rows of W = 32/64/128 bytes of k, 16-byte chunks XOR-permuted within
+// 8-row atoms, SBO = 8 W between atoms), Blackwell descriptor version 1.
+// `layout` is the descriptor's layout code (6: 32 B, 4: 64 B, 2: 128 B).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t sbo, uint32_t layout) {
   uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1) << 16;  // LBO (unused for swizzled K-major)
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(layout) << 61;
   return d;
 }
 
@@ -320,7 +325,7 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 struct MmaArgs {
   uint32_t smem0, tmem;
   int lane;
-  uint32_t sbo, col_per_half, acc_stride;
+  uint32_t sbo, layout, col_per_half, acc_stride;
   uint32_t off_m, off_n;  // hi copies of the M and N operands in a stage
   uint32_t lo_m, lo_n;    // distance to their lo copies (fp32)
   uint32_t idesc, idesc2;
@@ -391,32 +396,33 @@ __device__ void mma_role(const TcParams& p, Ctrl* ctl, const MmaArgs& m) {
       // then panel_lo x lhs_hi for each half
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        const uint32_t koff = ks * 256;  // KSTEP k = two 16-byte chunks
+        const uint32_t koff = ks * 32;  // one MMA k-step = 32 bytes of a swizzled row
         const uint32_t acc0 = ks == 0 ? acc_first : 1u;
-        const uint64_t b_hi = smem_desc(n0 + koff, 128, m.sbo);
+        const uint64_t b_hi = smem_desc(n0 + koff, m.sbo, m.layout);
 #pragma unroll
         for (int h = 0; h < H; ++h)
-          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + koff + h * 16 * m.sbo, 128, m.sbo), b_hi, m.idesc2, acc0);
+          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + koff + h * 16 * m.sbo, m.sbo, m.layout), b_hi,
+                     m.idesc2, acc0);
 #pragma unroll
         for (int h = 0; h < H; ++h)
-          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + m.lo_m + koff + h * 16 * m.sbo, 128, m.sbo), b_hi,
+          umma<true>(acc + h * m.col_per_half, smem_desc(m0 + m.lo_m + koff + h * 16 * m.sbo, m.sbo, m.layout), b_hi,
                      m.idesc, 1u);
       }
     } else {
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
-        const uint32_t koff = ks * 256;
+        const uint32_t koff = ks * 32;
         const uint32_t acc0 = ks == 0 ? acc_first : 1u;
-        const uint64_t b_hi = smem_desc(n0 + koff, 128, m.sbo);
+        const uint64_t b_hi = smem_desc(n0 + koff, m.sbo, m.layout);
 #pragma unroll
         for (int h = 0; h < H; ++h) {
           const uint32_t dt = acc + h * m.col_per_half;
           const uint32_t hoff = koff + h * 16 * m.sbo;  // rows 128h.. of the M operand
-          const uint64_t a_hi = smem_desc(m0 + hoff, 128, m.sbo);
+          const uint64_t a_hi = smem_desc(m0 + hoff, m.sbo, m.layout);
           umma<F32>(dt, a_hi, b_hi, m.idesc, acc0);
           if constexpr (F32) {
-            umma<true>(dt, a_hi, smem_desc(n0 + m.lo_n + koff, 128, m.sbo), m.idesc, 1u);
-            umma<true>(dt, smem_desc(m0 + m.lo_m + hoff, 128, m.sbo), b_hi, m.idesc, 1u);
+            umma<true>(dt, a_hi, smem_desc(n0 + m.lo_n + koff, m.sbo, m.layout), m.idesc, 1u);
+            umma<true>(dt, smem_desc(m0 + m.lo_m + hoff, m.sbo, m.layout), b_hi, m.idesc, 1u);
           }
         }
       }
@@ -459,9 +465,11 @@ __device__ void mma_dispatch(const TcParams& p, Ctrl* ctl, const MmaArgs& m, int
 template <bool F32>
 __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                                                                const __grid_constant__ CUtensorMap lhs_map) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // swizzled operands need 1024-byte aligned atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const TcConfig& c = p.c;
-  Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);
+  Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);  // after the aligned ring
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t W = *p.num_items;
 
@@ -469,17 +477,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   constexpr int EPU = F32 ? 4 : 8;     // elements per 16-byte chunk
   constexpr int KSTEP = F32 ? 8 : 16;  // k per MMA instruction
   constexpr int ESZ = F32 ? 4 : 2;
-  // both operands are K-major: 8-row x 16-byte core matrices, k-chunks of a
-  // row group adjacent (LBO = 128 B), row groups KC/EPU chunks apart (SBO)
-  const int sbo = (c.KC / EPU) * 128;
+  // both operands are K-major and swizzled: rows of W = KC * ESZ bytes,
+  // atoms of 8 rows (SBO = 8 W)
+  const int sbo = 8 * c.KC * ESZ;
   const int blk_bytes = c.Nt * c.KC * ESZ;  // one rhs tile's k-chunk = one panel slot
   const int nchunks = c.Kt / c.KC;
   // stage layout: [lhs hi | lhs lo | panel hi | panel lo] (bf16: [lhs | panel]);
   // the TMA lands the raw lhs chunk, already in canonical order, in the last
-  // lhs buffer, where the fp32 split rewrites it chunk by chunk in place
+  // lhs buffer, where the fp32 split rewrites it chunk by chunk in place.
+  // Stacked mode: slot s owns rows [s*Mt, s*Mt + Mt) of the lhs operand.
   const int off_lhs = 0;
   const int off_raw = (NH - 1) * c.lhs_bytes;
   const int off_pan = NH * c.lhs_bytes;
+  const int slot_bytes = c.lhs_bytes / c.slots;  // one slot's rows of the lhs operand
   const int col_per_half = c.col_per_half;
   const int acc_stride = c.halves * col_per_half;  // TMEM columns of one accumulator
 
@@ -509,9 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     // ------------------- scheduler: work queue, merge-step records, copies
     // Records of an item are streamed kRecAhead ahead: lane j < kRecInts
     // holds field j of a record, so one coalesced 64-byte load brings a
-    // whole step. Every data stage is filled completely: absent tiles are
-    // copied from the zero buffer, so the byte count per stage is fixed.
-    const uint32_t stage_tx = static_cast<uint32_t>(c.lhs_bytes + c.G * NH * blk_bytes);
+    // whole step. Absent rhs tiles are copied from the zero buffer; absent
+    // lhs slots (stacked mode) are zeroed by the split warps.
+    const int S = c.slots, G = c.G;
+    const int64_t W1 = W;                      // sub-strips
+    const int64_t nitems = (W1 + S - 1) / S;  // work items of S sub-strips
     uint32_t it = 0;
     int stage = 0;
     uint32_t ph = 0;
@@ -522,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       int q = 0;
       if (lane == 0) q = atomicAdd(p.queue, 1);
       q = __shfl_sync(0xffffffffu, q, 0);
-      if (q >= W) {
+      if (q >= nitems) {
         // no more items: exit marker
         if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
           aborted = true;
@@ -535,12 +547,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         __syncwarp();
         break;
       }
-      const int item = p.order[q];
-      const int s0 = p.item_first[item];
-      const int gcnt = p.item_count[item];
-      const int64_t* ib = p.item_rec + static_cast<int64_t>(item) * (p.nblocks + 1) + p.blk;
+      const int64_t* ib = p.item_rec + static_cast<int64_t>(q) * (p.nblocks + 1) + p.blk;
       const int64_t rb = ib[0], re = ib[1];
-      if (lane == 0) ctl->item_log[item_iter % kItemLog] = ItemInfo{s0, gcnt, static_cast<int>(re - rb)};
+      if (lane < kMaxSlots) {
+        ItemInfo& info = ctl->item_log[item_iter % kItemLog];
+        const int64_t sub = static_cast<int64_t>(q) * S + lane;
+        const bool live = lane < S && sub < W1;
+        const int ss = live ? p.order[sub] : 0;
+        info.s0[lane] = live ? p.item_first[ss] : 0;
+        info.gcnt[lane] = live ? p.item_count[ss] : 0;
+        if (lane == 0) info.nsteps = static_cast<int>(re - rb);
+      }
       int ahead[kRecAhead];
 #pragma unroll
       for (int a = 0; a < kRecAhead; ++a)
@@ -551,11 +568,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         for (int a = 0; a + 1 < kRecAhead; ++a) ahead[a] = ahead[a + 1];
         ahead[kRecAhead - 1] =
             (lane < kRecInts && r + kRecAhead < re) ? __ldg(p.recs + (r + kRecAhead) * kRecInts + lane) : 0;
-        const int li = __shfl_sync(0xffffffffu, cur, kRecLhs);
-        const int flags = __shfl_sync(0xffffffffu, cur, kRecFlags);
-        const int rhs0 = __shfl_sync(0xffffffffu, cur, kRecRhs0);
-        const int my_rhs = __shfl_sync(0xffffffffu, cur, kRecRhs + (jslot & (kMaxG - 1)));
-        const bool lok = li >= 0 && li < p.lhs_rows;
+        const int my_lhs = __shfl_sync(0xffffffffu, cur, lane & (kMaxSlots - 1));  // lanes < S: slot lane
+        const int flags = __shfl_sync(0xffffffffu, cur, S + G);
+        const int rhs0 = __shfl_sync(0xffffffffu, cur, S + G + 1);
+        const int my_rhs = __shfl_sync(0xffffffffu, cur, S + (jslot & (kMaxG - 1)));
+        const bool my_lok = lane < S && my_lhs >= 0 && my_lhs < p.lhs_rows;
+        const uint32_t mask = __ballot_sync(0xffffffffu, my_lok);
+        // fp32: absent slots are zeroed by the split warps; bf16 (one slot):
+        // an absent lhs tile is copied from the zero buffer
+        const uint32_t lhs_tx = F32 ? static_cast<uint32_t>(__popc(mask)) * static_cast<uint32_t>(slot_bytes)
+                                    : static_cast<uint32_t>(c.lhs_bytes);
         const bool consec = (flags & 1) != 0;
         for (int chunk = 0; chunk < nchunks; ++chunk) {
           if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
@@ -566,21 +588,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           uint8_t* sbase = smem + stage * c.stage_bytes;
           if (lane == 0) {
             ctl->ring[stage].done = 0;
-            mbar_arrive_expect_tx(&ctl->copy[stage], stage_tx);
-            // raw lhs chunk straight into the canonical K-major layout
-            if (lok)
-              tma_load_4d(sbase + off_raw, &lhs_map, 0, 0, k0 / EPU, li * (c.Mt / 8), &ctl->copy[stage]);
-            else
-              bulk_g2s(sbase + off_raw, p.zeros, static_cast<uint32_t>(c.lhs_bytes), &ctl->copy[stage]);
+            ctl->ring[stage].mask = static_cast<int>(mask);
+            mbar_arrive_expect_tx(&ctl->copy[stage], lhs_tx + static_cast<uint32_t>(G * NH * blk_bytes));
           }
+          __syncwarp();
+          // raw lhs chunk of slot s straight into the canonical K-major
+          // layout, at the slot's rows of the operand
+          if (my_lok)
+            tma_load_2d(sbase + off_raw + lane * slot_bytes, &lhs_map, k0, my_lhs * c.Mt, &ctl->copy[stage]);
+          else if (!F32 && lane == 0)
+            bulk_g2s(sbase + off_raw, p.zeros, static_cast<uint32_t>(c.lhs_bytes), &ctl->copy[stage]);
           // panel: per k-chunk the pre-laid rhs tiles sit tile after tile, so
           // consecutive rhs tiles (a dense rhs row) arrive in one copy
           const int64_t cbase = static_cast<int64_t>(k0 / c.KC) * p.rhs_rows;
           if (consec) {
             if (lane < NH)
               bulk_g2s(sbase + off_pan + lane * c.pan_bytes, (lane ? p.pan_lo : p.pan_hi) + (cbase + rhs0) * blk_bytes,
-                       static_cast<uint32_t>(c.G * blk_bytes), &ctl->copy[stage]);
-          } else if (lane < c.G * NH) {
+                       static_cast<uint32_t>(G * blk_bytes), &ctl->copy[stage]);
+          } else if (lane < G * NH) {
             const bool ok = my_rhs >= 0 && my_rhs < p.rhs_rows;
             bulk_g2s(sbase + off_pan + jhl * c.pan_bytes + jslot * blk_bytes,
                      ok ? (jhl ? p.pan_lo : p.pan_hi) + (cbase + my_rhs) * blk_bytes : p.zeros,
@@ -623,15 +648,19 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       uint32_t it = 0;
       int stage = 0;
       uint32_t ph = 0;
-      const int nf = c.Mt * (c.KC / EPU);
+      const int nf = c.lhs_bytes / 16;    // 16-byte chunks of the lhs operand (all slots)
+      const int slot_f4 = slot_bytes / 16;  // ... of one slot
       while (true) {
         if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
         const int d = ctl->ring[stage].done;
         if (!d) {
-          // split the canonical raw chunk in place (x -> hi, lo)
           uint8_t* sbase = smem + stage * c.stage_bytes;
+          // split the canonical raw chunk in place (x -> hi, lo); slots
+          // absent from this step (stacked mode) become zeros
+          const int mask = ctl->ring[stage].mask;
           for (int f = tid; f < nf; f += kProducers) {
-            const float4 x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if ((mask >> (f / slot_f4)) & 1) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
             float4 hi, lo;
             split_tf32(x.x, hi.x, lo.x);
             split_tf32(x.y, hi.y, lo.y);
@@ -658,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     m.tmem = tmem;
     m.lane = lane;
     m.sbo = static_cast<uint32_t>(sbo);
+    m.layout = static_cast<uint32_t>(c.swz);
     m.col_per_half = static_cast<uint32_t>(col_per_half);
     m.acc_stride = static_cast<uint32_t>(acc_stride);
     const bool swap = c.swap != 0;
@@ -681,15 +711,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       const uint32_t b = item_iter % c.acc_bufs;
       if (!wait_bar(&ctl->acc_full[b], (item_iter / c.acc_bufs) & 1u, ctl, p.err, &ctl->progress, kEpiSleepNs)) break;
       if (*reinterpret_cast<volatile int*>(&ctl->exit_at) == static_cast<int>(item_iter)) break;
-      const ItemInfo info = ctl->item_log[item_iter % kItemLog];
-      const int s0 = info.s0, gcnt = info.gcnt;
+      const ItemInfo& info = ctl->item_log[item_iter % kItemLog];
       const bool empty = info.nsteps == 0;  // zeros: written by the first key block only
       tc_fence_after();
       for (int h = 0; h < c.halves && !(empty && p.accumulate); ++h) {
         const uint32_t tbase =
             tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride + h * col_per_half;
         if (!c.swap) {
-          const int m = h * 128 + quad * 32 + lane;
+          // accumulator row = (lhs slot, row of that slot's tile)
+          const int mm = h * 128 + quad * 32 + lane;
+          const int slot = mm / c.Mt, m = mm - slot * c.Mt;
+          const bool live_slot = slot < c.slots;
+          const int s0 = live_slot ? info.s0[slot] : 0, gcnt = live_slot ? info.gcnt[slot] : 0;
           for (int c0 = 0; c0 < c.n_mma; c0 += 32) {
             float v[32];
             tmem_ld32(tbase + c0, v);
@@ -697,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            if (m < c.Mt) {
+            if (gcnt > 0) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 const int col = c0 + j;
@@ -726,6 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             }
           }
         } else {
+          const int s0 = info.s0[0], gcnt = info.gcnt[0];
           const int r = h * 128 + quad * 32 + lane;  // panel row = (g, n)
           const int g = r / c.Nt, n = r % c.Nt;
           const bool live = g < gcnt;
@@ -776,24 +810,29 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 // ------------------------------------------------------- preparation kernels
 
 // rhs tile t (Kt x Nt, n contiguous) -> per k-chunk c of KC rows a K-major
-// canonical block [n/8][k-chunk of EPU][n%8] of 16-byte chunks, i.e. the
-// transposed tile in exactly the layout one panel slot has in shared memory.
-// Blocks are stored chunk-major ([c][t]) so consecutive tiles of one chunk
-// are contiguous.
+// swizzled block: row n holds the tile's column n over the chunk's k (W =
+// KC * element bytes), its 16-byte pieces XOR-permuted by the row's address
+// bits 7.. (the layout the TMA's swizzle modes produce for a block starting
+// on a 1024-byte boundary), i.e. exactly the image one panel slot has in
+// shared memory. Blocks are stored chunk-major ([c][t]) so consecutive tiles
+// of one chunk are contiguous.
 template <bool F32>
 __global__ void layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt, int KC,
                                   void* __restrict__ hi, void* __restrict__ lo) {
-  constexpr int EPU = F32 ? 4 : 8;
+  constexpr int ESZ = F32 ? 4 : 2;
+  constexpr int EPU = 16 / ESZ;  // elements per 16-byte piece
+  const int W = KC * ESZ;
+  const int pieces = W / 16;
   const int64_t te = static_cast<int64_t>(Kt) * Nt;
   const int64_t total = rows * te;
-  const int kq = KC / EPU;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = e / te;
     const int rem = static_cast<int>(e - t * te);
     const int k = rem / Nt, n = rem % Nt;
     const int cidx = k / KC, kl = k % KC;
     const int64_t blk = (static_cast<int64_t>(cidx) * rows + t) * static_cast<int64_t>(Nt) * KC;
-    const int64_t dst = blk + (static_cast<int64_t>((n / 8) * kq + kl / EPU) * 8 + (n % 8)) * EPU + kl % EPU;
+    const int sw = ((n * W) >> 7) & (pieces - 1);
+    const int64_t dst = blk + static_cast<int64_t>(n) * KC + (((kl / EPU) ^ sw) * EPU) + kl % EPU;
     if constexpr (F32) {
       float h, l;
       split_tf32(static_cast<const float*>(rhs)[e], h, l);
@@ -865,45 +904,54 @@ __global__ void item_work_keys_kernel(const int32_t* __restrict__ first, const i
   }
 }
 
-// G-way merge of a work item's segment pair lists into step records, one
-// warp per item. Lane g walks segment g; each step takes the smallest
-// pending lhs tile, and every segment whose next pair has that lhs tile
-// contributes its rhs tile (others: -1). Each list keeps its own order, so
-// a segment's pairs are summed in join order. Records of an item start at
-// its first pair index (an item has at least as many pairs as steps) and are
-// in ascending contracted key; item_rec gets, per key block b, the first
-// record with key >= key_extent * b / nblocks (and the end).
-constexpr int kMergeWarps = 8;
+// Merge of a work item's segment pair lists into step records, one warp per
+// item. An item is S sub-strips (queue position q takes order[q*S + s]) of
+// up to G segments; lane s*G + g walks segment g of sub-strip s. With one
+// slot the lists merge on the lhs tile; with several on the contracted key.
+// Each step takes the smallest pending value; the sub-strips holding it
+// whose rhs tiles (per segment slot, -1 absent) equal those of the first
+// such sub-strip share the step, the others follow in later steps. Each
+// list keeps its own order, so a segment's pairs are summed in join order.
+// Records of item q start at rec_base[q] (an item has at least as many
+// pairs as steps); item_rec gets, per key block b, the first record with
+// key >= key_extent * b / nblocks (and the end).
+constexpr int kMergeWarps = 4;
 
 __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
     const int32_t* __restrict__ pl, const int32_t* __restrict__ pr, const int32_t* __restrict__ pair_key,
     const int64_t* __restrict__ seg_off, const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
-    const int64_t* __restrict__ num_items, int G, int64_t lhs_rows, int64_t rhs_rows, int nblocks, int64_t key_extent,
-    int32_t* __restrict__ recs, int64_t* __restrict__ item_rec, int32_t* __restrict__ err) {
-  __shared__ int win_l[kMergeWarps][kMaxG][kWin];
-  __shared__ int win_r[kMergeWarps][kMaxG][kWin];
-  __shared__ int win_k[kMergeWarps][kMaxG][kWin];
+    const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub, const uint32_t* __restrict__ rec_base,
+    int S, int G, int64_t lhs_rows, int64_t rhs_rows, int nblocks, int64_t key_extent, int32_t* __restrict__ recs,
+    int64_t* __restrict__ item_rec, int32_t* __restrict__ err) {
+  __shared__ int win_l[kMergeWarps][32][kWin];
+  __shared__ int win_r[kMergeWarps][32][kWin];
+  __shared__ int win_k[kMergeWarps][32][kWin];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t W = *num_items;
-  const bool keyed = nblocks > 1 && pair_key != nullptr;
-  for (int64_t item = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; item < W;
-       item += static_cast<int64_t>(gridDim.x) * kMergeWarps) {
-    const int s0 = item_first[item];
-    const int gcnt = item_count[item];
+  const int64_t W1 = *num_sub;
+  const int64_t nitems = (W1 + S - 1) / S;
+  const bool keyed = pair_key != nullptr && (nblocks > 1 || S > 1);
+  const int ls = lane / G, lg = lane - ls * G;  // this lane's sub-strip and segment slot
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; q < nitems;
+       q += static_cast<int64_t>(gridDim.x) * kMergeWarps) {
+    const int64_t sub = q * S + ls;
     int64_t cur = 0, end = 0;
-    if (lane < gcnt) {
-      cur = seg_off[s0 + lane];
-      end = seg_off[s0 + lane + 1];
+    if (ls < S && sub < W1) {
+      const int ss = static_cast<int>(order[sub]);
+      if (lg < item_count[ss]) {
+        const int s0 = item_first[ss];
+        cur = seg_off[s0 + lg];
+        end = seg_off[s0 + lg + 1];
+      }
     }
-    const int64_t base = seg_off[s0];
-    int64_t* ib = item_rec + item * (nblocks + 1);
+    const int64_t base = rec_base[q];
+    int64_t* ib = item_rec + q * (nblocks + 1);
     if (lane == 0) ib[0] = base;
     int64_t n = 0;
     int b = 0;
     int wpos = kWin;
-    bool bad = false;
+    bool bad = false, contract = false;
     while (true) {
-      if (lane < gcnt && wpos == kWin && cur < end) {
+      if (wpos == kWin && cur < end) {
         int tl[kWin], tr[kWin], tk[kWin];
 #pragma unroll
         for (int qq = 0; qq < kWin; ++qq) {
@@ -921,45 +969,90 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
         wpos = 0;
       }
       __syncwarp();
-      const bool live = lane < gcnt && cur < end;
-      const int v = live ? win_l[wib][lane][wpos] : INT_MAX;
-      const int kmin = __reduce_min_sync(0xffffffffu, v);
-      if (kmin == INT_MAX) break;
-      const bool mine = live && v == kmin;
-      int my_rhs = -1, my_key = INT_MAX;
-      if (mine) {
-        my_rhs = win_r[wib][lane][wpos];
-        my_key = win_k[wib][lane][wpos];
+      const bool live = cur < end;
+      const int hl = live ? win_l[wib][lane][wpos] : INT_MAX;
+      const int hk = live ? win_k[wib][lane][wpos] : INT_MAX;
+      const int v = S > 1 ? hk : hl;
+      const int vmin = __reduce_min_sync(0xffffffffu, v);
+      if (vmin == INT_MAX) break;
+      const bool matched = live && v == vmin;
+      const int hr = matched ? win_r[wib][lane][wpos] : -1;
+      // the first sub-strip holding vmin sets the rhs tiles of the step
+      const uint32_t mm = __ballot_sync(0xffffffffu, matched);
+      const int ref = (__ffs(mm) - 1) / G;
+      const int ref_r = __shfl_sync(0xffffffffu, hr, (ref * G + lg) & 31);
+      const uint32_t eqm = __ballot_sync(0xffffffffu, ls >= S || hr == ref_r);
+      const uint32_t gmask = (G == 32) ? 0xffffffffu : ((1u << G) - 1u);
+      const uint32_t my_grp = gmask << (ls * G);
+      const bool strip_has = (mm & my_grp) != 0u;
+      const bool joins = ls < S && strip_has && (eqm & my_grp) == my_grp;
+      // lhs tile of each joining sub-strip: from its lowest matched lane
+      const int src = joins ? (__ffs(mm & my_grp) - 1) : lane;
+      const int slot_lhs = __shfl_sync(0xffffffffu, hl, src & 31);
+      // the key must name one lhs tile per sub-strip (caller's contract)
+      if (joins && matched && hl != slot_lhs) contract = true;
+      if (joins && matched) {
         ++cur;
         ++wpos;
       }
-      if (my_rhs < -1 || my_rhs >= rhs_rows) {
-        bad = true;
-        my_rhs = -1;
-      }
-      if (keyed) {
-        const int key = __reduce_min_sync(0xffffffffu, my_key);
+      int key = 0;
+      if (keyed) key = __reduce_min_sync(0xffffffffu, matched ? hk : INT_MAX);
+      if (keyed && nblocks > 1) {
         while (b + 1 <= nblocks - 1 && static_cast<int64_t>(key) >= key_extent * (b + 1) / nblocks) {
           ++b;
           if (lane == 0) ib[b] = base + n;
         }
       }
-      const int first = __shfl_sync(0xffffffffu, my_rhs, 0);
-      const bool cons = __all_sync(0xffffffffu, lane >= G || (my_rhs >= 0 && my_rhs == first + lane)) &&
-                        first >= 0 && first + G <= rhs_rows;
-      int32_t* rec = recs + (base + n) * kRecInts;
-      if (lane == 0) {
-        rec[kRecLhs] = kmin;
-        rec[kRecFlags] = cons ? 1 : 0;
-        rec[kRecRhs0] = first;
-        if (kmin < 0 || kmin >= lhs_rows) bad = true;
+      // rhs slot g of the step: lane g holds it after this shuffle
+      int rg = __shfl_sync(0xffffffffu, hr, (ref * G + (lane % G)) & 31);
+      if (lane < G && (rg < -1 || rg >= rhs_rows)) {
+        bad = true;
+        rg = -1;
       }
-      if (lane < kMaxG) rec[kRecRhs + lane] = lane < G ? my_rhs : -1;
+      const int first = __shfl_sync(0xffffffffu, rg, 0);
+      const bool cons = __all_sync(0xffffffffu, lane >= G || (rg >= 0 && rg == first + lane)) && first >= 0 &&
+                        first + G <= rhs_rows;
+      // lhs tile per slot: lane s (< S) takes sub-strip s's value
+      const int lhs_s = __shfl_sync(0xffffffffu, slot_lhs, (lane * G) & 31);
+      const bool joins_s = __shfl_sync(0xffffffffu, joins ? 1 : 0, (lane * G) & 31) != 0;
+      int32_t* rec = recs + (base + n) * kRecInts;
+      if (lane < S) {
+        const int lv = joins_s ? lhs_s : -1;
+        if (joins_s && (lv < 0 || lv >= lhs_rows)) bad = true;
+        rec[lane] = lv;
+      }
+      if (lane < G) rec[S + lane] = rg;
+      if (lane == 0) {
+        rec[S + G] = cons ? 1 : 0;
+        rec[S + G + 1] = first;
+      }
       ++n;
     }
     if (lane == 0)
       for (int bb = b + 1; bb <= nblocks; ++bb) ib[bb] = base + n;
     if (__any_sync(0xffffffffu, bad) && lane == 0 && err) atomicExch(err, ES_ERR_INDEX);
+    if (__any_sync(0xffffffffu, contract) && lane == 0 && err) atomicExch(err, ES_ERR_INVALID);
+  }
+}
+
+// Pairs per work item (S sub-strips), the bound on its step records.
+__global__ void item_pairs_kernel(const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
+                                  const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub,
+                                  const int64_t* __restrict__ seg_off, int S, int64_t nslots,
+                                  uint32_t* __restrict__ pairs) {
+  const int64_t W1 = *num_sub;
+  const int64_t nitems = (W1 + S - 1) / S;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nslots; q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t tot = 0;
+    if (q < nitems)
+      for (int s = 0; s < S; ++s) {
+        const int64_t sub = q * S + s;
+        if (sub >= W1) break;
+        const int ss = static_cast<int>(order[sub]);
+        const int s0 = item_first[ss];
+        tot += seg_off[s0 + item_count[ss]] - seg_off[s0];
+      }
+    pairs[q] = static_cast<uint32_t>(tot);
   }
 }
 
@@ -969,6 +1062,9 @@ struct TcWs {
   uint8_t* zeros;
   int32_t* recs;
   int64_t* item_rec;
+  uint32_t* ipairs;
+  uint32_t* rec_base;
+  uint32_t* rec_total;
   int32_t* item_first;
   int32_t* item_count;
   uint32_t* flags;
@@ -996,6 +1092,9 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npai
   w.zeros = cv.template take<uint8_t>(zero_bytes(c));
   w.recs = cv.template take<int32_t>(npairs * kRecInts);
   w.item_rec = cv.template take<int64_t>(nseg * (nblocks + 1));
+  w.ipairs = cv.template take<uint32_t>(nseg);
+  w.rec_base = cv.template take<uint32_t>(nseg);
+  w.rec_total = cv.template take<uint32_t>(1);
   w.item_first = cv.template take<int32_t>(nseg);
   w.item_count = cv.template take<int32_t>(nseg);
   w.flags = cv.template take<uint32_t>(nseg);
@@ -1040,7 +1139,65 @@ std::vector<int64_t> group_offsets(const EinGroup& g, int which) {
 
 }  // namespace
 
-bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, TcConfig* c) {
+// Largest k-chunk that leaves >= 3 pipeline stages (else >= 2) for an lhs
+// operand of lhs_rows rows (slots of mt rows) and a panel of pan_rows rows
+// (tiles of nt rows); fills KC, the swizzle and the stage geometry. Rows are
+// W = KC * element bytes (32, 64 or 128: the swizzle span); every slot and
+// panel tile must start on a 1024-byte boundary. False when no chunk fits.
+bool pick_stages(int lhs_rows, int mt, int pan_rows, int nt, int Kt, bool f32, TcConfig* c) {
+  const int esz = f32 ? 4 : 2, nh = f32 ? 2 : 1, kstep = f32 ? 8 : 16;
+  const int ctrl = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
+  const int budget = 227 * 1024 - ctrl - 1024;  // 1024: alignment of the stage ring
+  for (int min_stages : {3, 2}) {
+    for (int kc : {64, 32, 16, 8}) {
+      const int W = kc * esz;
+      if (kc % kstep || Kt % kc || W < 32 || W > 128) continue;
+      if ((mt * W) % 1024 || (nt * W) % 1024) continue;
+      const int lb = lhs_rows * W, pb = pan_rows * W;
+      const int sb = (nh * (lb + pb) + 1023) / 1024 * 1024;
+      int stages = budget / sb;
+      if (stages > kMaxStages) stages = kMaxStages;
+      if (stages < min_stages) continue;
+      c->KC = kc;
+      c->swz = W == 128 ? 2 : W == 64 ? 4 : 6;
+      c->lhs_bytes = lb;
+      c->pan_bytes = pb;
+      c->stage_bytes = sb;
+      c->stages = stages;
+      // at least half the SM's shared memory, so one CTA runs per SM and its
+      // TMEM allocation never waits on another CTA's
+      c->smem_bytes = stages * sb + ctrl + 1024;
+      if (c->smem_bytes < 116 * 1024) c->smem_bytes = 116 * 1024;
+      return true;
+    }
+  }
+  return false;
+}
+
+// Stacked mode: 128 / Mt strips share each step's rhs panel as the rows of
+// one M = 128 operand, against N = G * Nt panel columns.
+bool stacked_config(int Mt, int Kt, int Nt, TcConfig* c) {
+  if (Mt != 16 && Mt != 32 && Mt != 64) return false;
+  const int S = 128 / Mt;
+  int G = 256 / Nt;
+  if (G > kMaxG) G = kMaxG;
+  if (G > 32 / S) G = 32 / S;
+  while (G > 1 && (G * Nt) % 16 != 0) --G;
+  if (G < 1 || (G * Nt) % 16 != 0 || S + G + 2 > kRecInts) return false;
+  if (!pick_stages(128, Mt, G * Nt, Nt, Kt, true, c) || c->stages < 3) return false;
+  c->swap = 0;
+  c->halves = 1;
+  c->slots = S;
+  c->G = G;
+  c->n_mma = G * Nt;
+  c->fold = 0;
+  c->col_per_half = c->n_mma;
+  c->acc_bufs = 2 * c->n_mma <= 512 ? 2 : 1;
+  c->tmem_cols = 512;
+  return true;
+}
+
+bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, bool have_keys, TcConfig* c) {
   std::memset(c, 0, sizeof(*c));
   const bool f32 = ldt == ES_F32 && rdt == ES_F32;
   const bool b16 = ldt == ES_BF16 && rdt == ES_BF16;
@@ -1064,6 +1221,9 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   c->Mt = Mt;
   c->Kt = Kt;
   c->Nt = Nt;
+  c->slots = 1;
+  if (f32 && have_strips && have_keys && !std::getenv("EINSPARSE_NO_STACK") && stacked_config(Mt, Kt, Nt, c))
+    return true;
   // orientation
   if (Mt % 128 == 0 && Mt <= 256) {
     c->swap = 0;
@@ -1101,32 +1261,7 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   // free; the epilogue reads in 32-column groups that may run past a small
   // accumulator
   c->tmem_cols = 512;
-  const int esz = f32 ? 4 : 2;
-  const int nh = f32 ? 2 : 1;
-  const int ctrl = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
-  const int budget = 227 * 1024 - ctrl;
-  // largest k-chunk that still leaves >= 3 pipeline stages (else >= 2)
-  for (int min_stages : {3, 2}) {
-    for (int kc : {64, 32, 16, 8}) {
-      if (kc % kstep || Kt % kc) continue;
-      const int lb = Mt * kc * esz, pb = c->G * Nt * kc * esz;
-      const int sb = (nh * (lb + pb) + 127) / 128 * 128;
-      int stages = budget / sb;
-      if (stages > kMaxStages) stages = kMaxStages;
-      if (stages < min_stages) continue;
-      c->KC = kc;
-      c->lhs_bytes = lb;
-      c->pan_bytes = pb;
-      c->stage_bytes = sb;
-      c->stages = stages;
-      // at least half the SM's shared memory, so one CTA runs per SM and its
-      // TMEM allocation never waits on another CTA's
-      c->smem_bytes = stages * sb + ctrl;
-      if (c->smem_bytes < 116 * 1024) c->smem_bytes = 116 * 1024;
-      return true;
-    }
-  }
-  return false;
+  return pick_stages(Mt, Mt, c->G * Nt, Nt, Kt, f32, c);
 }
 
 // Key blocks: the rhs operand re-read by every strip is split along the
@@ -1198,11 +1333,18 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;
   }
-  // 4. merge steps of every item (all items in parallel)
+  // 4. merge steps of every item (all items in parallel); item q takes the
+  //    sub-strips order[q*S .. q*S+S-1], so items come largest first
   {
-    const int blocks = static_cast<int>((nseg + kMergeWarps - 1) / kMergeWarps);
-    ES_LAUNCH(tc_merge_kernel, blocks, kMergeWarps * 32, 0, st, pl, pr, pair_key, seg_off, w.item_first,
-              w.item_count, w.num_items, c.G, lhs_rows, rhs_rows, nblocks, key_extent, w.recs, w.item_rec, err);
+    const int S = c.slots;
+    const int64_t nslots = (nseg + S - 1) / S;
+    ES_LAUNCH(item_pairs_kernel, grid_for(nslots, 256), 256, 0, st, w.item_first, w.item_count, w.order, w.num_items,
+              seg_off, S, nslots, w.ipairs);
+    ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nslots, w.rec_total, w.scan, st));
+    const int blocks = static_cast<int>((nslots + kMergeWarps - 1) / kMergeWarps);
+    ES_LAUNCH(tc_merge_kernel, blocks, kMergeWarps * 32, 0, st, pl, pr, c.slots > 1 || nblocks > 1 ? pair_key : nullptr,
+              seg_off, w.item_first, w.item_count, w.order, w.num_items, w.rec_base, S, c.G, lhs_rows, rhs_rows,
+              nblocks, key_extent, w.recs, w.item_rec, err);
   }
   if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
   // 5. persistent tensor-core kernel, one CTA per SM
@@ -1227,10 +1369,9 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.out = out;
   prm.odt = odt;
   prm.err = err;
-  // 4-D view of the lhs values for the TMA: (element in 16-byte chunk,
-  // row in 8-row group, k-chunk, row group over all tiles); a box of
-  // (EPU, 8, KC/EPU, Mt/8) lands in shared memory as the canonical K-major
-  // layout [row group][k-chunk][row][element].
+  // 2-D view of the lhs values for the TMA: (k, row over all tiles); a box
+  // of (KC, Mt) lands one tile's k-chunk in shared memory as Mt swizzled
+  // rows of W bytes, the operand layout of the MMA.
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -1239,21 +1380,20 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
       return ES_ERR_CUDA;
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
-  const int esz = c.fp32 ? 4 : 2, epu = c.fp32 ? 4 : 8;
+  const int esz = c.fp32 ? 4 : 2;
   CUtensorMap lhs_map;
   std::memset(&lhs_map, 0, sizeof(lhs_map));
-  cuuint64_t gdim[4] = {static_cast<cuuint64_t>(epu), 8, static_cast<cuuint64_t>(c.Kt / epu),
-                        static_cast<cuuint64_t>(lhs_rows) * (c.Mt / 8)};
-  cuuint64_t gstride[3] = {static_cast<cuuint64_t>(c.Kt) * esz, static_cast<cuuint64_t>(epu) * esz,
-                           static_cast<cuuint64_t>(8) * c.Kt * esz};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(epu), 8, static_cast<cuuint32_t>(c.KC / epu),
-                       static_cast<cuuint32_t>(c.Mt / 8)};
-  cuuint32_t estride[4] = {1, 1, 1, 1};
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(c.Kt), static_cast<cuuint64_t>(lhs_rows) * c.Mt};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(c.Kt) * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(c.KC), static_cast<cuuint32_t>(c.Mt)};
+  cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapSwizzle swz = c.swz == 2 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : c.swz == 4 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
   if (lhs_rows <= 0) return ES_OK;
-  CUresult cr = encode(&lhs_map, c.fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
-                       const_cast<void*>(lhs), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult cr = encode(&lhs_map, c.fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                       const_cast<void*>(lhs), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return ES_ERR_UNSUPPORTED;
   int dev = 0, sms = kSMs;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

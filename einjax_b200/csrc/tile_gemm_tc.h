@@ -13,7 +13,10 @@ struct TcConfig {
   int swap;        // 1: compute D^T = panel^T * lhs^T (lhs rows become MMA N)
   int Mt, Kt, Nt;  // tile dims of the plain matmul view
   int G;           // rhs tiles (segments of one strip) per work item
-  int KC;          // k elements per pipeline stage
+  int slots;       // lhs slots per work item: 1, or 128 / Mt strips stacked
+                   // into the 128-row MMA operand (stacked mode)
+  int KC;          // k elements per pipeline stage (operand rows of KC elements)
+  int swz;         // descriptor layout code of the swizzle: 2 (128 B rows), 4 (64 B), 6 (32 B)
   int stages;
   int halves;      // 128-row MMA halves (M = 128 * halves)
   int n_mma;       // MMA N
@@ -24,7 +27,7 @@ struct TcConfig {
   int col_per_half;  // TMEM columns of one 128-row half of an accumulator
   int acc_bufs;    // TMEM accumulators (2 when they fit: epilogue overlaps the next item)
   int tmem_cols;   // allocated TMEM columns (power of two)
-  int lhs_bytes;   // one operand copy of a stage's lhs chunk
+  int lhs_bytes;   // one operand copy of a stage's lhs chunk (all slots)
   int pan_bytes;   // one operand copy of a stage's panel chunk
   int stage_bytes;
   int smem_bytes;  // dynamic shared memory per CTA
@@ -33,7 +36,8 @@ struct TcConfig {
 // True when the contraction is a plain tile matmul this path covers:
 // lhs (Mt x Kt) k-contiguous, rhs (Kt x Nt) n-contiguous, out (Mt x Nt),
 // size-1 batch labels only, both operands f32 or both bf16.
-bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, TcConfig* c);
+// have_keys: pair_key is available (required for stacked mode).
+bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, bool have_keys, TcConfig* c);
 
 // Launches over the contracted range (one per key block) for these operands.
 int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent);

@@ -328,9 +328,13 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     L.check("es_segments_fill", lib.es_segments_fill(
         li.data_ptr(), ri.data_ptr(), P, out_nd, ext, ws.data_ptr(), ws.numel(), O, oc.data_ptr(), so.data_ptr(),
         sl.data_ptr(), sr.data_ptr(), sp.data_ptr(), nlead, sg.data_ptr() if sg is not None else None, st))
-    # contracted coordinate (first join key) of each grouped pair
+    # contracted coordinate of each grouped pair, when it names the lhs tile
+    # of a strip (one join key; lhs coordinates = leading output dims + that
+    # key): the tensor-core path may then merge strips on it
     sk, kext = None, 0
-    if join_keys:
+    lhs_dims = {int(d) for s, d in agg_keys[:nlead]}
+    if strips and len(join_keys) == 1 and lhs_dims | {int(join_keys[0][0])} == set(range(lhs.ndim)) \
+            and len(lhs_dims) == nlead and int(join_keys[0][0]) not in lhs_dims:
         jd = int(join_keys[0][0])
         sk = torch.empty((P, 1), dtype=torch.int32, device=dev)
         L.check("es_output_coords", lib.es_output_coords(

@@ -176,11 +176,14 @@ int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs
  * zero tiles). Values dtypes: F32 / BF16 / F64 inputs; F32 / BF16 outputs.
  * seg_strip (optional, from es_segments_fill): strip key per segment; the
  * tensor-core path computes up to 8 segments of one strip in one tile.
- * pair_key (optional): the contracted tile coordinate of each pair
- * (non-decreasing inside a segment), with key_extent its range; when given,
- * the tensor-core path splits the contracted range into blocks whose rhs
- * operand fits in L2 and adds the blocks' partial sums into the output in
- * block order.
+ * pair_key (optional): the contracted tile coordinate of each pair, with
+ * key_extent its range. Contract: inside a segment keys increase strictly,
+ * and segments of one strip (seg_strip) pair the same lhs tile with a given
+ * key. When given, the tensor-core path may stack up to 128 / Mt strips
+ * into one 128-row operand that shares each step's rhs tiles (fp32, Mt 16,
+ * 32 or 64, Kt 32 or 64), and splits the contracted range into blocks whose
+ * rhs operand fits in L2, adding the blocks' partial sums into the output
+ * in block order. A broken contract sets *error_dev to ES_ERR_INVALID.
  * workspace: es_tile_einsum_workspace_size bytes (0 for the SIMT path),
  * sized for the same rhs_rows, num_pairs, num_segments and key_extent (0
  * when no pair_key is passed). A device-side wait that runs out sets

@@ -346,6 +346,12 @@ TC_CASES = [
      1.0, "C5-like"),
     ("bij,bjk->bik", [(0, 0), (2, 1)], [(0, 0), (0, 1), (1, 2)], (3, 512, 512), (1, 64, 64), (3, 512, 512),
      (1, 64, 64), 0.1, 0.1, "C3-like f32"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (1024, 1024), (64, 32), (1024, 512), (32, 64), 0.1, 0.6,
+     "stacked Mt=64"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (512, 1024), (16, 32), (1024, 256), (32, 16), 0.1, 0.5,
+     "stacked Mt=16"),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (2048, 2048), (32, 64), (2048, 512), (64, 32), 0.03, 0.8,
+     "stacked Kt=64"),
 ]
 
 
@@ -380,8 +386,8 @@ def test_tensor_core_bf16(tile, bands):
     _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak), RTOL_BF16)
 
 
-@pytest.mark.parametrize("case", [TC_CASES[1], TC_CASES[2], TC_CASES[0], TC_CASES[5]],
-                         ids=["C2-like", "C2 sparse B", "C1-like", "C5-like"])
+@pytest.mark.parametrize("case", [TC_CASES[1], TC_CASES[2], TC_CASES[0], TC_CASES[5], TC_CASES[7]],
+                         ids=["C2-like", "C2 sparse B", "C1-like", "C5-like", "stacked Mt=64"])
 def test_tensor_core_key_blocks(case, monkeypatch):
     """Force many contracted-range blocks (later blocks add into the output)."""
     monkeypatch.setenv("EINSPARSE_KBLOCK_BYTES", "65536")
