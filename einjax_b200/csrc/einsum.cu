@@ -284,7 +284,8 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
   if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
   TcConfig c;
   if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, key_extent > 0, &c)) return 0;
-  return tc_workspace_size(c, rhs_rows, num_pairs, num_segments, tc_key_blocks(c, rhs_rows, true, key_extent));
+  return tc_workspace_size(c, rhs_rows, num_pairs, num_segments, tc_key_blocks(c, rhs_rows, true, key_extent),
+                           key_extent);
 }
 
 extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,

@@ -61,6 +61,7 @@ constexpr uint64_t kDrainNs = 100000000ull;   // 100 ms to drain own copies / MM
 constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 constexpr int kMaxKeyBlocks = 16;
+constexpr int kMaxMergeChunks = 64;
 
 // done: 0 data stage, 1 end of a work item, 2 no more items; mask: lhs
 // slots present in a data stage (stacked mode)
@@ -76,6 +77,7 @@ struct Step {
 // consecutive, one copy), S+G+1 first rhs tile. S + G + 2 <= 16.
 constexpr int kRecInts = 16;
 constexpr int kRecAhead = 4;  // records the scheduler has in flight ahead of use
+constexpr int kMaxSplit = 16;  // 16-byte lhs chunks per split thread and stage (lhs operand <= 32 KB)
 
 // A work item: up to S sub-strips (<= G segments of one strip each).
 struct ItemInfo {
@@ -462,12 +464,66 @@ __device__ void mma_dispatch(const TcParams& p, Ctrl* ctl, const MmaArgs& m, int
   }
 }
 
+// Split warps (fp32): each data stage's raw lhs chunk becomes hi (TF32)
+// and lo copies in place; slots absent from the step (stacked mode) become
+// zeros. PER bounds the 16-byte chunks per thread at compile time, so the
+// loads are all issued before the stores.
+template <int PER>
+__device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_lhs, int off_raw, int slot_bytes,
+                           int tid) {
+  const TcConfig& c = p.c;
+  const int nf = c.lhs_bytes / 16;
+  const int slot_f4 = slot_bytes / 16;
+  int slot_of[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) slot_of[j] = (tid + j * kProducers) / slot_f4;
+  int stage = 0;
+  uint32_t ph = 0;
+  while (true) {
+    if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
+    const int d = ctl->ring[stage].done;
+    if (!d) {
+      uint8_t* sbase = smem + stage * c.stage_bytes;
+      const int mask = ctl->ring[stage].mask;
+      float4 x[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int f = tid + j * kProducers;
+        x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (f < nf && ((mask >> slot_of[j]) & 1))
+          x[j] = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int f = tid + j * kProducers;
+        if (f < nf) {
+          float4 hi, lo;
+          split_tf32(x[j].x, hi.x, lo.x);
+          split_tf32(x[j].y, hi.y, lo.y);
+          split_tf32(x[j].z, hi.z, lo.z);
+          split_tf32(x[j].w, hi.w, lo.w);
+          *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
+          *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
+        }
+      }
+      fence_proxy_async();
+    }
+    mbar_arrive(&ctl->full[stage]);
+    if (++stage == c.stages) {
+      stage = 0;
+      ph ^= 1u;
+    }
+    if (d == 2) break;
+  }
+}
+
 template <bool F32>
 __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                                                                const __grid_constant__ CUtensorMap lhs_map) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // swizzled operands need 1024-byte aligned atoms
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // swizzled operands need 1024-byte aligned atoms; offset the shared array
+  // itself (not through an integer) so accesses stay shared-memory accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const TcConfig& c = p.c;
   Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);  // after the aligned ring
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -600,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             bulk_g2s(sbase + off_raw, p.zeros, static_cast<uint32_t>(c.lhs_bytes), &ctl->copy[stage]);
           // panel: per k-chunk the pre-laid rhs tiles sit tile after tile, so
           // consecutive rhs tiles (a dense rhs row) arrive in one copy
-          const int64_t cbase = static_cast<int64_t>(k0 / c.KC) * p.rhs_rows;
+          const int64_t cbase = static_cast<int64_t>(chunk) * p.rhs_rows;
           if (consec) {
             if (lane < NH)
               bulk_g2s(sbase + off_pan + lane * c.pan_bytes, (lane ? p.pan_lo : p.pan_hi) + (cbase + rhs0) * blk_bytes,
@@ -645,40 +701,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   } else if (warp < 4) {
     // ----------------------------------------- fp32 split of the lhs chunk
     if constexpr (F32) {
-      uint32_t it = 0;
-      int stage = 0;
-      uint32_t ph = 0;
-      const int nf = c.lhs_bytes / 16;    // 16-byte chunks of the lhs operand (all slots)
-      const int slot_f4 = slot_bytes / 16;  // ... of one slot
-      while (true) {
-        if (!wait_bar(&ctl->copy[stage], ph, ctl, p.err)) break;
-        const int d = ctl->ring[stage].done;
-        if (!d) {
-          uint8_t* sbase = smem + stage * c.stage_bytes;
-          // split the canonical raw chunk in place (x -> hi, lo); slots
-          // absent from this step (stacked mode) become zeros
-          const int mask = ctl->ring[stage].mask;
-          for (int f = tid; f < nf; f += kProducers) {
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if ((mask >> (f / slot_f4)) & 1) x = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
-            float4 hi, lo;
-            split_tf32(x.x, hi.x, lo.x);
-            split_tf32(x.y, hi.y, lo.y);
-            split_tf32(x.z, hi.z, lo.z);
-            split_tf32(x.w, hi.w, lo.w);
-            *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
-            *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
-          }
-          fence_proxy_async();
-        }
-        mbar_arrive(&ctl->full[stage]);
-        ++it;
-        if (++stage == c.stages) {
-          stage = 0;
-          ph ^= 1u;
-        }
-        if (d == 2) break;
-      }
+      const int nf = c.lhs_bytes / 16;  // 16-byte chunks of the lhs operand (all slots)
+      const int per = (nf + kProducers - 1) / kProducers;
+      if (per <= 1) split_role<1>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
+      else if (per <= 2) split_role<2>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
+      else if (per <= 4) split_role<4>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
+      else if (per <= 8) split_role<8>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
+      else split_role<16>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA warp
@@ -904,35 +933,48 @@ __global__ void item_work_keys_kernel(const int32_t* __restrict__ first, const i
   }
 }
 
-// Merge of a work item's segment pair lists into step records, one warp per
-// item. An item is S sub-strips (queue position q takes order[q*S + s]) of
-// up to G segments; lane s*G + g walks segment g of sub-strip s. With one
-// slot the lists merge on the lhs tile; with several on the contracted key.
-// Each step takes the smallest pending value; the sub-strips holding it
-// whose rhs tiles (per segment slot, -1 absent) equal those of the first
-// such sub-strip share the step, the others follow in later steps. Each
-// list keeps its own order, so a segment's pairs are summed in join order.
-// Records of item q start at rec_base[q] (an item has at least as many
-// pairs as steps); item_rec gets, per key block b, the first record with
-// key >= key_extent * b / nblocks (and the end).
+// Merge of a work item's segment pair lists into step records. An item is S
+// sub-strips (queue position q takes order[q*S + s]) of up to G segments;
+// lane s*G + g walks segment g of sub-strip s. With one slot the lists merge
+// on the lhs tile; with several on the contracted key. Each step takes the
+// smallest pending value; the sub-strips holding it whose rhs tiles (per
+// segment slot, -1 absent) equal those of the first such sub-strip share the
+// step, the others follow in later steps. Each list keeps its own order, so a
+// segment's pairs are summed in join order.
+//
+// With keys, an item's key range is cut into C chunks merged by separate
+// warps (warp w: item w / C, chunk w % C): COUNT writes the steps of each
+// (item, chunk) to cnt, the fill pass writes the records from off[] (the
+// exclusive scan of cnt). Without keys C = 1. Records of an item are in
+// ascending key, chunks in order, so a key block (a run of chunks) is a run
+// of records.
 constexpr int kMergeWarps = 4;
 
+template <bool COUNT>
 __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
     const int32_t* __restrict__ pl, const int32_t* __restrict__ pr, const int32_t* __restrict__ pair_key,
     const int64_t* __restrict__ seg_off, const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
-    const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub, const uint32_t* __restrict__ rec_base,
-    int S, int G, int64_t lhs_rows, int64_t rhs_rows, int nblocks, int64_t key_extent, int32_t* __restrict__ recs,
-    int64_t* __restrict__ item_rec, int32_t* __restrict__ err) {
+    const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub, int S, int G, int64_t lhs_rows,
+    int64_t rhs_rows, int C, int64_t key_extent, int64_t nw, uint32_t* __restrict__ cnt,
+    const uint32_t* __restrict__ off, int32_t* __restrict__ recs, int32_t* __restrict__ err) {
   __shared__ int win_l[kMergeWarps][32][kWin];
   __shared__ int win_r[kMergeWarps][32][kWin];
   __shared__ int win_k[kMergeWarps][32][kWin];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t W1 = *num_sub;
   const int64_t nitems = (W1 + S - 1) / S;
-  const bool keyed = pair_key != nullptr && (nblocks > 1 || S > 1);
+  const bool keyed = pair_key != nullptr;
   const int ls = lane / G, lg = lane - ls * G;  // this lane's sub-strip and segment slot
-  for (int64_t q = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; q < nitems;
-       q += static_cast<int64_t>(gridDim.x) * kMergeWarps) {
+  // nw covers the slots of every possible item; those past the real items
+  // count zero steps, so the scan over all nw entries stays exact
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * kMergeWarps + wib; w < nw;
+       w += static_cast<int64_t>(gridDim.x) * kMergeWarps) {
+    if (w >= nitems * C) {
+      if (COUNT && lane == 0) cnt[w] = 0;
+      continue;
+    }
+    const int64_t q = w / C;
+    const int ck = static_cast<int>(w - q * C);
     const int64_t sub = q * S + ls;
     int64_t cur = 0, end = 0;
     if (ls < S && sub < W1) {
@@ -941,13 +983,27 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
         const int s0 = item_first[ss];
         cur = seg_off[s0 + lg];
         end = seg_off[s0 + lg + 1];
+        if (C > 1) {
+          // this chunk's pairs: keys increase inside a segment
+          const int64_t klo = key_extent * ck / C, khi = key_extent * (ck + 1) / C;
+          int64_t lo = cur, hi = end;
+          while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (pair_key[mid] < klo) lo = mid + 1; else hi = mid;
+          }
+          const int64_t a = lo;
+          hi = end;
+          while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (pair_key[mid] < khi) lo = mid + 1; else hi = mid;
+          }
+          cur = a;
+          end = lo;
+        }
       }
     }
-    const int64_t base = rec_base[q];
-    int64_t* ib = item_rec + q * (nblocks + 1);
-    if (lane == 0) ib[0] = base;
+    const int64_t base = COUNT ? 0 : off[w];
     int64_t n = 0;
-    int b = 0;
     int wpos = kWin;
     bool bad = false, contract = false;
     while (true) {
@@ -995,65 +1051,68 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
         ++cur;
         ++wpos;
       }
-      int key = 0;
-      if (keyed) key = __reduce_min_sync(0xffffffffu, matched ? hk : INT_MAX);
-      if (keyed && nblocks > 1) {
-        while (b + 1 <= nblocks - 1 && static_cast<int64_t>(key) >= key_extent * (b + 1) / nblocks) {
-          ++b;
-          if (lane == 0) ib[b] = base + n;
+      if (!COUNT) {
+        // rhs slot g of the step: lane g holds it after this shuffle
+        int rg = __shfl_sync(0xffffffffu, hr, (ref * G + (lane % G)) & 31);
+        if (lane < G && (rg < -1 || rg >= rhs_rows)) {
+          bad = true;
+          rg = -1;
         }
-      }
-      // rhs slot g of the step: lane g holds it after this shuffle
-      int rg = __shfl_sync(0xffffffffu, hr, (ref * G + (lane % G)) & 31);
-      if (lane < G && (rg < -1 || rg >= rhs_rows)) {
-        bad = true;
-        rg = -1;
-      }
-      const int first = __shfl_sync(0xffffffffu, rg, 0);
-      const bool cons = __all_sync(0xffffffffu, lane >= G || (rg >= 0 && rg == first + lane)) && first >= 0 &&
-                        first + G <= rhs_rows;
-      // lhs tile per slot: lane s (< S) takes sub-strip s's value
-      const int lhs_s = __shfl_sync(0xffffffffu, slot_lhs, (lane * G) & 31);
-      const bool joins_s = __shfl_sync(0xffffffffu, joins ? 1 : 0, (lane * G) & 31) != 0;
-      int32_t* rec = recs + (base + n) * kRecInts;
-      if (lane < S) {
-        const int lv = joins_s ? lhs_s : -1;
-        if (joins_s && (lv < 0 || lv >= lhs_rows)) bad = true;
-        rec[lane] = lv;
-      }
-      if (lane < G) rec[S + lane] = rg;
-      if (lane == 0) {
-        rec[S + G] = cons ? 1 : 0;
-        rec[S + G + 1] = first;
+        const int first = __shfl_sync(0xffffffffu, rg, 0);
+        const bool cons = __all_sync(0xffffffffu, lane >= G || (rg >= 0 && rg == first + lane)) && first >= 0 &&
+                          first + G <= rhs_rows;
+        // lhs tile per slot: lane s (< S) takes sub-strip s's value
+        const int lhs_s = __shfl_sync(0xffffffffu, slot_lhs, (lane * G) & 31);
+        const bool joins_s = __shfl_sync(0xffffffffu, joins ? 1 : 0, (lane * G) & 31) != 0;
+        int32_t* rec = recs + (base + n) * kRecInts;
+        if (lane < S) {
+          const int lv = joins_s ? lhs_s : -1;
+          if (joins_s && (lv < 0 || lv >= lhs_rows)) bad = true;
+          rec[lane] = lv;
+        }
+        if (lane < G) rec[S + lane] = rg;
+        if (lane == 0) {
+          rec[S + G] = cons ? 1 : 0;
+          rec[S + G + 1] = first;
+        }
       }
       ++n;
     }
-    if (lane == 0)
-      for (int bb = b + 1; bb <= nblocks; ++bb) ib[bb] = base + n;
-    if (__any_sync(0xffffffffu, bad) && lane == 0 && err) atomicExch(err, ES_ERR_INDEX);
-    if (__any_sync(0xffffffffu, contract) && lane == 0 && err) atomicExch(err, ES_ERR_INVALID);
+    if (COUNT) {
+      if (lane == 0) cnt[w] = static_cast<uint32_t>(n);
+    } else {
+      if (__any_sync(0xffffffffu, bad) && lane == 0 && err) atomicExch(err, ES_ERR_INDEX);
+      if (__any_sync(0xffffffffu, contract) && lane == 0 && err) atomicExch(err, ES_ERR_INVALID);
+    }
   }
 }
 
-// Pairs per work item (S sub-strips), the bound on its step records.
-__global__ void item_pairs_kernel(const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
-                                  const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub,
-                                  const int64_t* __restrict__ seg_off, int S, int64_t nslots,
-                                  uint32_t* __restrict__ pairs) {
+// Record boundaries of each item's key blocks: block b of item q starts at
+// the record offset of chunk b * (C / nblocks); the last boundary is the
+// next item's first record (or the total).
+__global__ void item_rec_kernel(const uint32_t* __restrict__ off, const uint32_t* __restrict__ total,
+                                const int64_t* __restrict__ num_sub, int S, int C, int nblocks, int64_t nw,
+                                int64_t* __restrict__ item_rec) {
   const int64_t W1 = *num_sub;
   const int64_t nitems = (W1 + S - 1) / S;
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nslots; q += (int64_t)gridDim.x * blockDim.x) {
-    int64_t tot = 0;
-    if (q < nitems)
-      for (int s = 0; s < S; ++s) {
-        const int64_t sub = q * S + s;
-        if (sub >= W1) break;
-        const int ss = static_cast<int>(order[sub]);
-        const int s0 = item_first[ss];
-        tot += seg_off[s0 + item_count[ss]] - seg_off[s0];
-      }
-    pairs[q] = static_cast<uint32_t>(tot);
+  const int m = C / nblocks;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nitems; q += (int64_t)gridDim.x * blockDim.x) {
+    for (int b = 0; b <= nblocks; ++b) {
+      const int64_t w = q * C + static_cast<int64_t>(b) * m;
+      item_rec[q * (nblocks + 1) + b] = w < nw ? off[w] : *total;
+    }
   }
+}
+
+// Key chunks of the merge pass: a multiple of the key blocks, about 256 keys
+// each (1 without keys).
+int merge_chunks(int nblocks, bool have_key, int64_t key_extent) {
+  if (!have_key || key_extent <= 1) return 1;
+  int64_t m = key_extent / (256ll * nblocks);
+  if (m < 1) m = 1;
+  while (nblocks * m > kMaxMergeChunks) --m;
+  if (m < 1) m = 1;
+  return static_cast<int>(nblocks * m);
 }
 
 struct TcWs {
@@ -1065,6 +1124,7 @@ struct TcWs {
   uint32_t* ipairs;
   uint32_t* rec_base;
   uint32_t* rec_total;
+  uint32_t* scan2;
   int32_t* item_first;
   int32_t* item_count;
   uint32_t* flags;
@@ -1084,7 +1144,8 @@ int64_t zero_bytes(const TcConfig& c) {
 }
 
 template <typename C>
-void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks) {
+void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks,
+               int64_t key_extent) {
   const int64_t pan_elems = rhs_rows * c.Kt * c.Nt;
   const int esz = c.fp32 ? 4 : 2;
   w.pan_hi = cv.template take<uint8_t>(pan_elems * esz);
@@ -1092,9 +1153,11 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npai
   w.zeros = cv.template take<uint8_t>(zero_bytes(c));
   w.recs = cv.template take<int32_t>(npairs * kRecInts);
   w.item_rec = cv.template take<int64_t>(nseg * (nblocks + 1));
-  w.ipairs = cv.template take<uint32_t>(nseg);
-  w.rec_base = cv.template take<uint32_t>(nseg);
+  const int nck = merge_chunks(nblocks, key_extent > 0, key_extent);
+  w.ipairs = cv.template take<uint32_t>(nseg * nck);    // steps per (item, key chunk)
+  w.rec_base = cv.template take<uint32_t>(nseg * nck);  // their record offsets
   w.rec_total = cv.template take<uint32_t>(1);
+  w.scan2 = cv.template take<uint32_t>(scan_scratch_elems(nseg * nck));
   w.item_first = cv.template take<int32_t>(nseg);
   w.item_count = cv.template take<int32_t>(nseg);
   w.flags = cv.template take<uint32_t>(nseg);
@@ -1154,6 +1217,7 @@ bool pick_stages(int lhs_rows, int mt, int pan_rows, int nt, int Kt, bool f32, T
       if (kc % kstep || Kt % kc || W < 32 || W > 128) continue;
       if ((mt * W) % 1024 || (nt * W) % 1024) continue;
       const int lb = lhs_rows * W, pb = pan_rows * W;
+      if (f32 && lb > kMaxSplit * kProducers * 16) continue;  // the split warps hold a stage's chunks in registers
       const int sb = (nh * (lb + pb) + 1023) / 1024 * 1024;
       int stages = budget / sb;
       if (stages > kMaxStages) stages = kMaxStages;
@@ -1282,10 +1346,11 @@ int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t ke
   return nb < 1 ? 1 : static_cast<int>(nb);
 }
 
-size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks) {
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks,
+                         int64_t key_extent) {
   SizeOnly s;
   TcWs w;
-  tc_layout(s, w, c, rhs_rows, npairs, nseg, nblocks);
+  tc_layout(s, w, c, rhs_rows, npairs, nseg, nblocks, key_extent);
   return s.s.used + 256;
 }
 
@@ -1298,7 +1363,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   const int nblocks = tc_key_blocks(c, rhs_rows, pair_key != nullptr, key_extent);
   Carver cv(ws, ws_bytes);
   TcWs w;
-  tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks);
+  tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks, pair_key ? key_extent : 0);
   if (cv.overflow) return ES_ERR_WORKSPACE;
   if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
   // 1. rhs tiles into the shared-memory image (split for fp32)
@@ -1333,18 +1398,26 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;
   }
-  // 4. merge steps of every item (all items in parallel); item q takes the
-  //    sub-strips order[q*S .. q*S+S-1], so items come largest first
+  // 4. merge steps of every item (all items and key chunks in parallel);
+  //    item q takes the sub-strips order[q*S .. q*S+S-1], so items come
+  //    largest first
   {
     const int S = c.slots;
     const int64_t nslots = (nseg + S - 1) / S;
-    ES_LAUNCH(item_pairs_kernel, grid_for(nslots, 256), 256, 0, st, w.item_first, w.item_count, w.order, w.num_items,
-              seg_off, S, nslots, w.ipairs);
-    ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nslots, w.rec_total, w.scan, st));
-    const int blocks = static_cast<int>((nslots + kMergeWarps - 1) / kMergeWarps);
-    ES_LAUNCH(tc_merge_kernel, blocks, kMergeWarps * 32, 0, st, pl, pr, c.slots > 1 || nblocks > 1 ? pair_key : nullptr,
-              seg_off, w.item_first, w.item_count, w.order, w.num_items, w.rec_base, S, c.G, lhs_rows, rhs_rows,
-              nblocks, key_extent, w.recs, w.item_rec, err);
+    const int C = merge_chunks(nblocks, pair_key != nullptr, key_extent);
+    const int32_t* keys = (c.slots > 1 || C > 1) ? pair_key : nullptr;
+    const int64_t nw = nslots * C;
+    int64_t nb = (nw + kMergeWarps - 1) / kMergeWarps;
+    const int blocks = static_cast<int>(nb < 65536 ? nb : 65536);  // grid-stride beyond
+    ES_LAUNCH(tc_merge_kernel<true>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
+              w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
+              (const uint32_t*)nullptr, w.recs, err);
+    ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nw, w.rec_total, w.scan2, st));
+    ES_LAUNCH(tc_merge_kernel<false>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
+              w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
+              (const uint32_t*)w.rec_base, w.recs, err);
+    ES_LAUNCH(item_rec_kernel, grid_for(nslots, 256), 256, 0, st, (const uint32_t*)w.rec_base,
+              (const uint32_t*)w.rec_total, w.num_items, S, C, nblocks, nw, w.item_rec);
   }
   if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
   // 5. persistent tensor-core kernel, one CTA per SM

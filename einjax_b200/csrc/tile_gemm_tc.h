@@ -42,7 +42,8 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
 // Launches over the contracted range (one per key block) for these operands.
 int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent);
 
-size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks);
+size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks,
+                         int64_t key_extent);
 
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
               const int32_t* pl, const int32_t* pr, int64_t npairs, const int64_t* seg_off, int64_t nseg,
