@@ -1,31 +1,36 @@
-// Tensor-core tile GEMM (tcgen05 + TMEM + bulk async copies) for plain
-// block-sparse tile matmuls, with the segment-sum fused into the TMEM
-// accumulator.
+// Tensor-core tile GEMM (tcgen05 + TMEM + TMA) for plain block-sparse tile
+// matmuls, with the segment-sum fused into the TMEM accumulator.
 //
 // A work item is up to G segments of one "strip" (segments whose output
 // tiles share the lhs-derived coordinates, e.g. one output tile row of a
-// block-sparse matmul). Their pair lists all walk lhs tiles in ascending
-// order; a G-way merge turns them into steps (one lhs tile, up to G rhs
-// tiles), and each step contributes
+// block-sparse matmul) -- or, in stacked mode, S = 128 / Mt such sub-strips
+// whose lhs tiles are stacked into one 128-row MMA operand. A pre-pass
+// (tc_merge_kernel) merges each item's segment pair lists into step records:
+// one contracted key, the lhs tile per slot and the rhs tile per segment.
+// Each step contributes
 //     D(Mt x G*Nt) += lhs(Mt x Kt) * [rhs_0 | ... | rhs_{G-1}](Kt x G*Nt)
-// (absent rhs tiles are zero), or the transposed product when Mt is too
-// small for the 128-row MMA. The whole strip accumulates in TMEM; the
+// per slot (absent rhs tiles and absent slots are zero), or the transposed
+// product when a lone strip has Mt < 128. The item accumulates in TMEM; the
 // epilogue writes each segment's output tile once. Summation order over a
 // segment's pairs is the join order, as in the reference
 // (execution/sparse_dispatch.py:165-169).
 //
-// fp32 operands use the 3-pass split-TF32 scheme (x = hi + lo with hi
-// rounded to TF32; D += A_hi B_hi + A_hi B_lo + A_lo B_hi; Ootomo & Yokota,
-// "Recovering single precision accuracy from Tensor Cores while surpassing
-// the FP32 theoretical peak performance", IJHPCA 2022), giving fp32-level
-// error; bf16 operands take one kind::f16 pass with fp32 accumulation.
+// fp32 operands use the 3-pass split-TF32 scheme (x = hi + lo; D += A_hi B_hi
+// + A_hi B_lo + A_lo B_hi; Ootomo & Yokota, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance", IJHPCA 2022), giving fp32-level error. hi is x itself, which
+// the tensor core reads truncated to TF32, and lo = x - trunc(x); bf16
+// operands take one kind::f16 pass with fp32 accumulation. Operands are
+// K-major with 32/64/128-byte swizzled rows (the TMA's swizzle modes).
 //
-// Roles (160 threads): warps 0-3 produce stages (G-way merge, bulk async
-// copies of the rhs "panel" — pre-split once per call into the exact
-// shared-memory image — and the split of the lhs chunk) and run the
-// epilogue; warp 4 allocates TMEM and one lane issues the MMAs. Every wait
-// is bounded; on expiry the CTA raises ES_ERR_TIMEOUT, drains its own
-// copies and MMAs, frees TMEM and returns.
+// Roles (320 threads): warps 0-3 compute the lo copy of each stage's lhs
+// chunk; warp 4 allocates TMEM and issues the MMAs (one elected lane); warp 5
+// takes work items from a device-wide queue (largest first), streams their
+// step records and issues the TMA loads of the lhs tiles and the bulk copies
+// of the rhs "panel" (laid out once per call in the exact shared-memory
+// image, hi and lo); warps 6-9 run the epilogue (TMEM lane quadrant = warp %
+// 4). Every wait is bounded; on expiry the CTA raises ES_ERR_TIMEOUT, drains
+// its own copies and MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -315,12 +320,12 @@ __device__ void drain_bar(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// Round-to-nearest (ties away) of fp32 to the TF32 grid by integer
-// arithmetic on the bit pattern, and the exact fp32 remainder.
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-  const uint32_t b = __float_as_uint(x);
-  hi = __uint_as_float((b + 0x1000u) & 0xFFFFE000u);
-  lo = x - hi;
+// The tensor core reads a kind::tf32 operand as an fp32 container and uses
+// its value truncated to TF32 (the low 13 mantissa bits dropped). With x
+// itself as the hi operand, the lo operand is the exact fp32 remainder
+// x - trunc(x) (|lo| < 2^-10 |x|).
+__device__ __forceinline__ float tf32_rem(float x) {
+  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
 // Operand layout of one stage as the MMA warp sees it.
@@ -464,13 +469,12 @@ __device__ void mma_dispatch(const TcParams& p, Ctrl* ctl, const MmaArgs& m, int
   }
 }
 
-// Split warps (fp32): each data stage's raw lhs chunk becomes hi (TF32)
-// and lo copies in place; slots absent from the step (stacked mode) become
-// zeros. PER bounds the 16-byte chunks per thread at compile time, so the
-// loads are all issued before the stores.
+// Split warps (fp32): each data stage's raw lhs chunk (the hi operand as it
+// is) gets its lo copy, x - trunc_tf32(x); slots absent from the step
+// (stacked mode) become zeros in both copies. PER bounds the 16-byte chunks
+// per thread at compile time, so the loads are all issued before the stores.
 template <int PER>
-__device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_lhs, int off_raw, int slot_bytes,
-                           int tid) {
+__device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_lhs, int slot_bytes, int tid) {
   const TcConfig& c = p.c;
   const int nf = c.lhs_bytes / 16;
   const int slot_f4 = slot_bytes / 16;
@@ -486,24 +490,21 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
       uint8_t* sbase = smem + stage * c.stage_bytes;
       const int mask = ctl->ring[stage].mask;
       float4 x[PER];
+      bool on[PER];
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
         const int f = tid + j * kProducers;
+        on[j] = f < nf && ((mask >> slot_of[j]) & 1);
         x[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (f < nf && ((mask >> slot_of[j]) & 1))
-          x[j] = *reinterpret_cast<const float4*>(sbase + off_raw + f * 16);
+        if (on[j]) x[j] = *reinterpret_cast<const float4*>(sbase + off_lhs + f * 16);
       }
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
         const int f = tid + j * kProducers;
         if (f < nf) {
-          float4 hi, lo;
-          split_tf32(x[j].x, hi.x, lo.x);
-          split_tf32(x[j].y, hi.y, lo.y);
-          split_tf32(x[j].z, hi.z, lo.z);
-          split_tf32(x[j].w, hi.w, lo.w);
-          *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
-          *reinterpret_cast<float4*>(sbase + off_raw + f * 16) = lo;
+          const float4 lo = make_float4(tf32_rem(x[j].x), tf32_rem(x[j].y), tf32_rem(x[j].z), tf32_rem(x[j].w));
+          *reinterpret_cast<float4*>(sbase + off_lhs + c.lhs_bytes + f * 16) = lo;
+          if (!on[j]) *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = x[j];  // absent slot: zero hi too
         }
       }
       fence_proxy_async();
@@ -543,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   // lhs buffer, where the fp32 split rewrites it chunk by chunk in place.
   // Stacked mode: slot s owns rows [s*Mt, s*Mt + Mt) of the lhs operand.
   const int off_lhs = 0;
-  const int off_raw = (NH - 1) * c.lhs_bytes;
+  const int off_raw = off_lhs;  // the TMA lands the raw lhs chunk in the hi buffer
   const int off_pan = NH * c.lhs_bytes;
   const int slot_bytes = c.lhs_bytes / c.slots;  // one slot's rows of the lhs operand
   const int col_per_half = c.col_per_half;
@@ -703,11 +704,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     if constexpr (F32) {
       const int nf = c.lhs_bytes / 16;  // 16-byte chunks of the lhs operand (all slots)
       const int per = (nf + kProducers - 1) / kProducers;
-      if (per <= 1) split_role<1>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
-      else if (per <= 2) split_role<2>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
-      else if (per <= 4) split_role<4>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
-      else if (per <= 8) split_role<8>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
-      else split_role<16>(p, ctl, smem, off_lhs, off_raw, slot_bytes, tid);
+      if (per <= 1) split_role<1>(p, ctl, smem, off_lhs, slot_bytes, tid);
+      else if (per <= 2) split_role<2>(p, ctl, smem, off_lhs, slot_bytes, tid);
+      else if (per <= 4) split_role<4>(p, ctl, smem, off_lhs, slot_bytes, tid);
+      else if (per <= 8) split_role<8>(p, ctl, smem, off_lhs, slot_bytes, tid);
+      else split_role<16>(p, ctl, smem, off_lhs, slot_bytes, tid);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA warp
@@ -863,10 +864,9 @@ __global__ void layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, in
     const int sw = ((n * W) >> 7) & (pieces - 1);
     const int64_t dst = blk + static_cast<int64_t>(n) * KC + (((kl / EPU) ^ sw) * EPU) + kl % EPU;
     if constexpr (F32) {
-      float h, l;
-      split_tf32(static_cast<const float*>(rhs)[e], h, l);
-      static_cast<float*>(hi)[dst] = h;
-      static_cast<float*>(lo)[dst] = l;
+      const float x = static_cast<const float*>(rhs)[e];
+      static_cast<float*>(hi)[dst] = x;  // read as TF32 (truncated) by the tensor core
+      static_cast<float*>(lo)[dst] = tf32_rem(x);
     } else {
       static_cast<__nv_bfloat16*>(hi)[dst] = static_cast<const __nv_bfloat16*>(rhs)[e];
     }
