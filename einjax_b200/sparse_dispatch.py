@@ -377,18 +377,22 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
 
 
 def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=None, output_tile_shape=None,
-                           mesh=None, num_devices=None, *, group=None, gather=True, precision="auto"):
+                           mesh=None, num_devices=None, *, group=None, gather=True, precision="auto",
+                           shard="output"):
     """Multi-GPU ``execute_sparse`` (``execution/sparse_dispatch.py:330-478``).
 
     One process per GPU (``torch.distributed``). With no process group, or a
     single rank, this is ``execute_sparse`` (the reference's fallback at
-    :377-393). Otherwise every rank plans the (replicated, small) join and
-    output grouping, then computes a contiguous range of output tiles
+    :377-393). ``shard="output"``: every rank plans the (replicated, small)
+    join and output grouping, then computes a contiguous range of output tiles
     balanced by pair count — output tiles are independent, so no collective
-    touches the data path. With ``gather`` the shards are all-gathered so every
-    rank returns the full relation, as the reference does.
+    touches the data path. ``shard="contracted"``: each rank contracts a
+    contiguous range of the (single) join key and the partial tiles are summed
+    by a sparse reduce-scatter. With ``gather`` every rank returns the full
+    relation, as the reference does.
     ``mesh`` is accepted for signature compatibility; ranks come from ``group``.
     """
     from . import distributed as D
     return D.execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape, output_tile_shape,
-                                    num_devices=num_devices, group=group, gather=gather, precision=precision)
+                                    num_devices=num_devices, group=group, gather=gather, precision=precision,
+                                    shard=shard)
