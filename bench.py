@@ -37,6 +37,11 @@ sys.path.insert(0, ROOT)
 
 TILE = 32
 FLOPS_PER_PAIR = 2 * TILE ** 3
+# DRAM bytes (read + write) of the tile GEMM per joined pair, from the ncu
+# capture of the 1/4-scale C2 case (one key block, 923,064 pairs); the lhs
+# tiles dominate and are read once, so the traffic grows with the pairs.
+TRAFFIC_PER_PAIR = 564.8
+TRAFFIC_SOURCE = "ncu dram bytes of tc_strip_kernel at C2 scale 1/4, scaled by pairs (profiles/tc_strip_kernel_c2_scale4.md)"
 
 
 def _env_rank():
@@ -239,8 +244,8 @@ def run_ours(args):
     if rank == 0:
         hbm, bf16, src = _peaks()
         g_ms = statistics.mean(gemm_ms)
-        # dominant kernel: the fused tile GEMM + segment-sum. Algorithmic
-        # FLOPs = P * 2*32^3 per launch (one launch per step).
+        # dominant kernel: the fused tile GEMM + segment-sum (one es_tile_einsum
+        # call per step). Algorithmic FLOPs = P * 2*32^3 per call.
         achieved = P * FLOPS_PER_PAIR / (g_ms * 1e-3) / 1e12
         bound = "tensor"
         peak = bf16
@@ -263,8 +268,13 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": bound,
                          "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4),
+                         "traffic": int(TRAFFIC_PER_PAIR * P),
+                         "traffic_source": TRAFFIC_SOURCE,
                          "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)",
+                         # fp32 runs as 3 TF32 MMAs per product at half the bf16 rate
+                         "fp32_peak": round(peak / 6, 1),
+                         "frac_fp32_peak": round(achieved / (peak / 6), 4),
                          "kernel_ms": round(g_ms, 3)},
             "gpu_launches": int(launches),
             "phases_ms": phases,
