@@ -288,10 +288,68 @@ def _out_extents(lhs, rhs, agg_keys):
     return [lg[d] if s == 0 else rg[d] for s, d in agg_keys]
 
 
+def _direct_shape(lhs, rhs, join_keys, agg_keys) -> bool:
+    """True for lhs (strip..., k) x rhs (k, col...) -> (strip..., col...): one
+    join key, the last lhs and the first rhs coordinate, output = the other
+    lhs then the other rhs coordinates, and a small (k, col) rhs table."""
+    if len(join_keys) != 1 or tuple(int(v) for v in join_keys[0]) != (lhs.ndim - 1, 0):
+        return False
+    want = [(0, d) for d in range(lhs.ndim - 1)] + [(1, d) for d in range(1, rhs.ndim)]
+    if [tuple(int(v) for v in k) for k in agg_keys] != want or not want:
+        return False
+    lg, rg = lhs.grid(), rhs.grid()
+    cext = prod(rg[1:]) if rhs.ndim > 1 else 1
+    kext = max(lg[-1], rg[0])
+    return kext * cext <= (1 << 26) and cext * max(lhs.num_tuples, 1) < (1 << 31)
+
+
+def _plan_direct(lhs, rhs, join_keys, agg_keys):
+    """Join + grouping without sorts (``es_direct_*``); None when the lhs is
+    not in lexicographic order (the general path then runs)."""
+    dev = lhs.device
+    lib = L.lib()
+    lg, rg = L.i64arr(lhs.grid()), L.i64arr(rhs.grid())
+    nl, nr = lhs.num_tuples, rhs.num_tuples
+    ws = workspace(lib.es_direct_workspace_size(nl, lhs.ndim, nr, rhs.ndim, lg, rg), dev)
+    cnt = torch.zeros(4, dtype=torch.int64, device=dev)  # P, O, out of order, error
+    st = stream_ptr(dev)
+    lc, rc = lhs.coords.contiguous(), rhs.coords.contiguous()
+    L.check("es_direct_plan", lib.es_direct_plan(
+        lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, lg, rg, ws.data_ptr(), ws.numel(),
+        cnt.data_ptr(), cnt[3:].data_ptr(), st))
+    P, O, unordered, err = (int(v) for v in cnt.cpu().tolist())
+    if err:
+        raise ValueError("tile coordinate outside the tensor grid")
+    if unordered:
+        return None
+    out_nd = len(agg_keys)
+    oc = torch.empty((O, out_nd), dtype=torch.int32, device=dev)
+    so = torch.empty(O + 1, dtype=torch.int64, device=dev)
+    sl = torch.empty(P, dtype=torch.int32, device=dev)
+    sr = torch.empty(P, dtype=torch.int32, device=dev)
+    sg = torch.empty(O, dtype=torch.int64, device=dev)
+    sk = torch.empty(P, dtype=torch.int32, device=dev)
+    L.check("es_direct_fill", lib.es_direct_fill(
+        lc.data_ptr(), nl, lhs.ndim, rhs.ndim, lg, rg, ws.data_ptr(), ws.numel(), P, O, oc.data_ptr(), so.data_ptr(),
+        sl.data_ptr(), sr.data_ptr(), sg.data_ptr(), sk.data_ptr(), st))
+    kext = _key_extents(lhs, rhs, [tuple(join_keys[0])])[0]
+    # pairs come grouped; "join order" is taken to be this grouped order
+    ar = torch.arange(P, dtype=torch.int32, device=dev)
+    return PairPlan(sl, sr, oc, so, sl, sr, ar, sg, sk, kext)
+
+
 def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, agg_keys) -> PairPlan:
     """Join the relations and group the pairs by output tile (two host syncs:
-    the pair count and the output-tile count)."""
+    the pair count and the output-tile count).
+
+    Matmul-like shapes (``_direct_shape``) group without sorting; the pairs of
+    each output tile are in join order either way, and ``lhs_idx``/``rhs_idx``
+    then hold the grouped order."""
     dev = lhs.device
+    if lhs.num_tuples > 0 and rhs.num_tuples > 0 and _direct_shape(lhs, rhs, join_keys, agg_keys):
+        plan = _plan_direct(lhs, rhs, join_keys, agg_keys)
+        if plan is not None:
+            return plan
     li, ri = _join_int32(lhs, rhs, join_keys)
     P = int(li.shape[0])
     out_nd = len(agg_keys)

@@ -371,6 +371,53 @@ def test_tensor_core_path(case):
     _assert_rel(exact, ref, _mag(lhs, rhs, jk, ks, ak))
 
 
+DIRECT_CASES = [
+    # (kernel, join, agg, lhs shape, lhs tile, rhs shape, rhs tile, density A, density B)
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (1024, 2048), (32, 32), (2048, 256), (32, 32), 0.05, 1.0),
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (512, 768), (16, 16), (768, 640), (16, 32), 0.2, 0.3),
+    ("ijk,kl->ijl", [(2, 0)], [(0, 0), (0, 1), (1, 1)], (64, 64, 128), (16, 16, 16), (128, 96), (16, 16), 0.05, 0.8),
+    ("ij,j->i", [(1, 0)], [(0, 0)], (256, 512), (16, 16), (512,), (16,), 0.3, 0.7),
+]
+
+
+@pytest.mark.parametrize("case", DIRECT_CASES, ids=[f"{c[0]}-{c[4]}" for c in DIRECT_CASES])
+def test_direct_grouping_matches_sorted(case, monkeypatch):
+    """The sort-free join + grouping gives the same segments, pairs (in join
+    order inside each segment), strips and keys as join + radix grouping."""
+    from einjax_b200 import sparse_dispatch as SD
+    ks, jk, ak, sa, ta, sb, tb, da, db = case
+    rng = np.random.default_rng(5)
+    lhs, rhs = _dev(_random_block_sparse(rng, sa, ta, da)), _dev(_random_block_sparse(rng, sb, tb, db))
+    assert SD._direct_shape(lhs, rhs, jk, ak)
+    d = SD.plan_pairs(lhs, rhs, jk, ak)
+    monkeypatch.setattr(SD, "_direct_shape", lambda *a: False)
+    g = SD.plan_pairs(lhs, rhs, jk, ak)
+    for name in ("out_coords", "seg_offsets", "seg_lhs", "seg_rhs", "seg_key"):
+        assert torch.equal(getattr(d, name).cpu(), getattr(g, name).cpu()), name
+    # strips: same grouping of segments (labels may differ)
+    ds, gs = d.seg_strip.cpu().numpy(), g.seg_strip.cpu().numpy()
+    assert np.array_equal(np.diff(ds) != 0, np.diff(gs) != 0)
+    res = E.execute_sparse(lhs, rhs, jk, ks, ak, precision="exact")
+    ref = O.execute_sparse(*(O.Relation(r.coords.cpu().numpy(), r.values.cpu().double().numpy(), r.shape,
+                                        r.tile_shape) for r in (lhs, rhs)), jk, ks, ak)
+    np.testing.assert_array_equal(res.coords.cpu().numpy(), ref.coords)
+
+
+def test_direct_grouping_unsorted_lhs_falls_back():
+    """An lhs relation out of lexicographic order takes the general path."""
+    from einjax_b200 import sparse_dispatch as SD
+    rng = np.random.default_rng(8)
+    lhs = _random_block_sparse(rng, (256, 256), (32, 32), 0.3)
+    rhs = _random_block_sparse(rng, (256, 128), (32, 32), 0.5)
+    perm = rng.permutation(lhs.coords.shape[0])
+    shuffled = O.Relation(lhs.coords[perm], lhs.values[perm], lhs.shape, lhs.tile_shape)
+    jk, ks, ak = [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)]
+    res = E.execute_sparse(_dev(shuffled), _dev(rhs), jk, ks, ak, precision="exact")
+    ref = O.execute_sparse(shuffled, rhs, jk, ks, ak)
+    np.testing.assert_array_equal(res.coords.cpu().numpy(), ref.coords)
+    np.testing.assert_allclose(res.values.cpu().numpy(), ref.values, rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("tile,bands", [((64, 64), 2), ((32, 32), 4), ((128, 128), 1)])
 def test_tensor_core_bf16(tile, bands):
     from einjax_b200 import workloads as W
