@@ -40,7 +40,7 @@ FLOPS_PER_PAIR = 2 * TILE ** 3
 # DRAM bytes (read + write) of the tile GEMM per joined pair, from the ncu
 # capture of the 1/4-scale C2 case (one key block, 923,064 pairs); the lhs
 # tiles dominate and are read once, so the traffic grows with the pairs.
-TRAFFIC_PER_PAIR = 564.8
+TRAFFIC_PER_PAIR = 569.3
 TRAFFIC_SOURCE = "ncu dram bytes of tc_strip_kernel at C2 scale 1/4, scaled by pairs (profiles/tc_strip_kernel_c2_scale4.md)"
 
 

@@ -138,8 +138,11 @@ class _SparseEinsumAgg(torch.autograd.Function):
         dev = lv.device
         counts = plan.seg_offsets[1:] - plan.seg_offsets[:-1]
         seg_of_sorted = torch.repeat_interleave(torch.arange(plan.num_segments, device=dev), counts)
-        gidx = torch.empty(plan.num_pairs, dtype=torch.int32, device=dev)
-        gidx[plan.seg_pair.long()] = seg_of_sorted.to(torch.int32)
+        if plan.seg_pair is None:  # pairs already in grouped order
+            gidx = seg_of_sorted.to(torch.int32)
+        else:
+            gidx = torch.empty(plan.num_pairs, dtype=torch.int32, device=dev)
+            gidx[plan.seg_pair.long()] = seg_of_sorted.to(torch.int32)
         gl, gr = _vjp_tiles(ctx.kernel_string, lv, rv, g.contiguous(), gidx, plan.lhs_idx, plan.rhs_idx,
                             ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.precision)
         return (gl.to(lv.dtype) if gl is not None else None, gr.to(rv.dtype) if gr is not None else None,

@@ -269,7 +269,7 @@ class PairPlan:
     seg_offsets: torch.Tensor   # int64 (O+1,)
     seg_lhs: torch.Tensor       # int32 (P,), pairs grouped by output tile
     seg_rhs: torch.Tensor
-    seg_pair: torch.Tensor      # int32 (P,), original pair index
+    seg_pair: torch.Tensor | None  # int32 (P,), original pair index (None: identity)
     seg_strip: torch.Tensor | None = None  # int64 (O,), strip key (lhs-derived output coords)
     seg_key: torch.Tensor | None = None    # int32 (P,), contracted tile coordinate of each grouped pair
     key_extent: int = 0
@@ -334,8 +334,8 @@ def _plan_direct(lhs, rhs, join_keys, agg_keys):
         sl.data_ptr(), sr.data_ptr(), sg.data_ptr(), sk.data_ptr(), st))
     kext = _key_extents(lhs, rhs, [tuple(join_keys[0])])[0]
     # pairs come grouped; "join order" is taken to be this grouped order
-    ar = torch.arange(P, dtype=torch.int32, device=dev)
-    return PairPlan(sl, sr, oc, so, sl, sr, ar, sg, sk, kext)
+    # (seg_pair None: the identity)
+    return PairPlan(sl, sr, oc, so, sl, sr, None, sg, sk, kext)
 
 
 def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, agg_keys) -> PairPlan:
