@@ -344,6 +344,111 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_config(args):
+    """The other BASELINE configurations on one GPU, for the results table
+    (the headline line is C2, ``run_ours``). One step = the sparse path on
+    device-resident inputs: C1/C3 ``execute_sparse`` of two tile relations;
+    C4 the chain (A B) C forward and the gradients of all three operands
+    through ``sparse_einsum`` (loss = sum of the output); C5 COO -> tiles of X
+    and W, then ``execute_sparse``."""
+    import torch
+
+    import einjax_b200 as E
+    from einjax_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = args.workload
+    t0 = time.time()
+    if wl == "C4":
+        w = W.c4_chain(seed=args.seed, scale=args.scale)
+        t = w["tile"]
+        ops = [E.SparseTensorRelation.from_arrays(w[k].coords, w[k].values, w[k].shape, w[k].tile_shape,
+                                                  device=dev, dtype=torch.float32) for k in ("A", "B", "C")]
+        desc = (f"C4 ij,jk,kl->il (A B) C: 3 x {ops[0].shape[0]}^2 fp32, {t[0]}^2 tiles at 2%/5%/2% "
+                f"({', '.join(str(o.num_tuples) for o in ops)} tiles), forward + gradients of A, B, C")
+        dtype_s = "f32"
+    elif wl in ("C1", "C3"):
+        w = W.c1_block_sparse(seed=args.seed, scale=args.scale) if wl == "C1" else \
+            W.c3_batched_bf16(seed=args.seed, scale=args.scale)
+        tdt = torch.float32 if wl == "C1" else torch.bfloat16
+        lhs = E.SparseTensorRelation.from_arrays(w.lhs.coords, w.lhs.values, w.lhs.shape, w.lhs.tile_shape,
+                                                 device=dev, dtype=tdt)
+        rhs = E.SparseTensorRelation.from_arrays(w.rhs.coords, w.rhs.values, w.rhs.shape, w.rhs.tile_shape,
+                                                 device=dev, dtype=tdt)
+        desc = (f"{wl} {w.kernel_string}: lhs {w.lhs.shape} {lhs.num_tuples} tiles of {w.lhs_tile}, "
+                f"rhs {w.rhs.shape} {rhs.num_tuples} tiles of {w.rhs_tile}, {'fp32' if wl == 'C1' else 'bf16'}")
+        dtype_s = "f32" if wl == "C1" else "bf16"
+    else:  # C5
+        w = W.c5_order3(seed=args.seed, scale=args.scale)
+        idx = torch.from_numpy(w.lhs.indices).to(dev)
+        val = torch.from_numpy(w.lhs.values).to(dev)
+        wd = torch.from_numpy(w.rhs).to(dev)
+        desc = (f"C5 ijk,kl->ijl: X {w.lhs.shape} COO {len(w.lhs.values)} nnz Zipf(1.2), W {tuple(w.rhs.shape)} "
+                f"dense, tiles 16")
+        dtype_s = "f32"
+    gen_s = time.time() - t0
+
+    def step():
+        if wl == "C4":
+            A, B, C = (E.SparseTensorRelation(o.coords, o.values.detach().requires_grad_(True), o.shape,
+                                              o.tile_shape) for o in ops)
+            AB = E.sparse_einsum(A, B, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+            D = E.sparse_einsum(AB, C, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+            D.values.sum().backward()
+            return AB, D
+        if wl in ("C1", "C3"):
+            return E.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys), None
+        X = E.tile_coo(idx, val, w.lhs.shape, w.lhs_tile)
+        Wt = E.tile_dense(wd, w.rhs_tile)
+        return E.execute_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys), X
+
+    # useful flops of one step: joined pairs x flops per tile pair
+    from einjax_b200 import sparse_dispatch as SD
+    def pairs(lr, rr, jk, ak):
+        return SD.plan_pairs(lr, rr, jk, ak).num_pairs
+    for _ in range(args.warmup):
+        out, aux = step()
+    torch.cuda.synchronize()
+    if wl == "C4":
+        P1 = pairs(ops[0], ops[1], [(1, 0)], [(0, 0), (1, 1)])
+        P2 = pairs(out, ops[2], [(1, 0)], [(0, 0), (1, 1)])
+        flops = 3 * (P1 + P2) * 2 * t[0] ** 3  # forward + two backward products per pair
+        P = P1 + P2
+    elif wl in ("C1", "C3"):
+        P = pairs(lhs, rhs, w.join_keys, w.agg_keys)
+        te = int(np.prod(w.lhs_tile)) * w.rhs_tile[-1]
+        flops = P * 2 * te
+    else:
+        P = pairs(aux, E.tile_dense(wd, w.rhs_tile), w.join_keys, w.agg_keys)
+        flops = P * 2 * 16 ** 4
+    del out, aux
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(args.steps):
+        out, aux = step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    hbm, bf16, src = _peaks()
+    achieved = flops / (ms * 1e-3) / 1e12
+    peak = bf16 if dtype_s == "bf16" else bf16 / 6
+    line = {"metric": f"useful TFLOP/s (sparse einsum, {wl})", "value": round(achieved, 3), "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_s,
+            "data": f"synthetic (seeded {wl} generator)",
+            "config": {"workload": desc + (f" (scale 1/{args.scale})" if args.scale != 1 else ""), "pairs": P,
+                       "l2": "device-resident inputs; no flush"},
+            "pairs_per_s": round(P / (ms * 1e-3), 1),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 3),
+                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{src} bf16 dense" + (" / 6 (fp32 as 3 TF32 passes)" if dtype_s == "f32"
+                                                                 else "")},
+            "gen_s": round(gen_s, 1)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -354,9 +459,13 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", default="auto", choices=["auto", "exact", "tc"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="C2", choices=["C1", "C2", "C3", "C4", "C5"],
+                    help="C2 is the headline line; the others measure one GPU for the results table")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "C2":
+        run_config(args)
     else:
         run_ours(args)
 

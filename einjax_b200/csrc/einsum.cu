@@ -282,10 +282,21 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
                                                 int64_t key_extent, int precision) {
   EinsumDesc d;
   if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
-  TcConfig c;
-  if (!want_tc(precision) || !tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, key_extent > 0, &c)) return 0;
-  return tc_workspace_size(c, rhs_rows, num_pairs, num_segments, tc_key_blocks(c, rhs_rows, true, key_extent),
-                           key_extent);
+  if (!want_tc(precision)) return 0;
+  // the launch's geometry depends on whether strips (seg_strip) and keys
+  // (pair_key) are passed; size for the largest of the candidates
+  size_t best = 0;
+  for (int strips = 0; strips < 2; ++strips) {
+    for (int keys = 0; keys < (key_extent > 0 ? 2 : 1); ++keys) {
+      TcConfig c;
+      if (!tc_config(d, lhs_dtype, rhs_dtype, ES_F32, strips != 0, keys != 0, &c)) continue;
+      const int64_t ke = keys ? key_extent : 0;
+      const size_t sz = tc_workspace_size(c, rhs_rows, num_pairs, num_segments,
+                                          tc_key_blocks(c, rhs_rows, keys != 0, ke), ke);
+      if (sz > best) best = sz;
+    }
+  }
+  return best;
 }
 
 extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,

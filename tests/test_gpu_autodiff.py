@@ -111,3 +111,40 @@ def test_chain_backward():
     assert _bound(dev["C"].values.grad.cpu().numpy(), g_c, m_c)
     assert _bound(dev["A"].values.grad.cpu().numpy(), g_a, m_a)
     assert _bound(dev["B"].values.grad.cpu().numpy(), g_b, m_b)
+
+
+def test_chain_backward_128_tiles():
+    """The C4 tile size (128 x 128, fp32 tensor cores without strips in the
+    autodiff forward): grads of all three operands through two steps."""
+    rng = np.random.default_rng(4)
+
+    def rel(shape, dens):
+        g = (shape[0] // 128, shape[1] // 128)
+        n = g[0] * g[1]
+        pos = np.sort(rng.choice(n, max(1, int(round(dens * n))), replace=False))
+        coords = np.stack([pos // g[1], pos % g[1]], 1).astype(np.int32)
+        vals = rng.standard_normal((len(pos), 128, 128)).astype(np.float32).astype(np.float64)
+        return O.Relation(coords, vals, shape, (128, 128))
+
+    rels = {"A": rel((1024, 1536), 0.3), "B": rel((1536, 1024), 0.4), "C": rel((1024, 768), 0.3)}
+    dev = {k: E.SparseTensorRelation.from_arrays(r.coords, r.values, r.shape, r.tile_shape, dtype=torch.float32)
+           for k, r in rels.items()}
+    for d in dev.values():
+        d.values.requires_grad_(True)
+    mm = ([(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    ab = E.sparse_einsum(dev["A"], dev["B"], *mm)
+    abc = E.sparse_einsum(ab, dev["C"], *mm)
+    abc.values.sum().backward()
+    ab_ref = O.execute_sparse(rels["A"], rels["B"], *mm)
+    abc_ref = O.execute_sparse(ab_ref, rels["C"], *mm)
+    np.testing.assert_array_equal(abc.coords.cpu().numpy(), abc_ref.coords)
+    g_abc = np.ones_like(abc_ref.values)
+    g_ab, g_c = _agg_grads_oracle(ab_ref, rels["C"], *mm, g_abc)
+    g_a, g_b = _agg_grads_oracle(rels["A"], rels["B"], *mm, g_ab)
+    absr = {k: O.Relation(r.coords, np.abs(r.values), r.shape, r.tile_shape) for k, r in rels.items()}
+    ab_abs = O.execute_sparse(absr["A"], absr["B"], *mm)
+    m_ab, m_c = _agg_grads_oracle(ab_abs, absr["C"], *mm, g_abc)
+    m_a, m_b = _agg_grads_oracle(absr["A"], absr["B"], *mm, m_ab)
+    assert _bound(dev["C"].values.grad.cpu().numpy(), g_c, m_c)
+    assert _bound(dev["A"].values.grad.cpu().numpy(), g_a, m_a)
+    assert _bound(dev["B"].values.grad.cpu().numpy(), g_b, m_b)
