@@ -35,6 +35,7 @@
 #include <cudaTypedefs.h>
 
 #include <climits>
+#include <type_traits>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -849,26 +850,37 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 template <bool F32>
 __global__ void layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt, int KC,
                                   void* __restrict__ hi, void* __restrict__ lo) {
+  // one thread per 16-byte piece of the image: (tile t, k-chunk c, piece j
+  // of row n); n varies fastest, so the column reads of a warp are coalesced
+  using E = typename std::conditional<F32, float, __nv_bfloat16>::type;
   constexpr int ESZ = F32 ? 4 : 2;
   constexpr int EPU = 16 / ESZ;  // elements per 16-byte piece
-  const int W = KC * ESZ;
+  const int W = KC * ESZ;        // bytes per image row
   const int pieces = W / 16;
-  const int64_t te = static_cast<int64_t>(Kt) * Nt;
-  const int64_t total = rows * te;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = e / te;
-    const int rem = static_cast<int>(e - t * te);
-    const int k = rem / Nt, n = rem % Nt;
-    const int cidx = k / KC, kl = k % KC;
-    const int64_t blk = (static_cast<int64_t>(cidx) * rows + t) * static_cast<int64_t>(Nt) * KC;
+  const int nck = Kt / KC;
+  const int64_t total = rows * nck * pieces * static_cast<int64_t>(Nt);
+  const E* src = static_cast<const E*>(rhs);
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int n = static_cast<int>(q % Nt);
+    int64_t r = q / Nt;
+    const int j = static_cast<int>(r % pieces);
+    r /= pieces;
+    const int c = static_cast<int>(r % nck);
+    const int64_t t = r / nck;
+    const E* col = src + t * static_cast<int64_t>(Kt) * Nt + (static_cast<int64_t>(c) * KC + j * EPU) * Nt + n;
     const int sw = ((n * W) >> 7) & (pieces - 1);
-    const int64_t dst = blk + static_cast<int64_t>(n) * KC + (((kl / EPU) ^ sw) * EPU) + kl % EPU;
+    const int64_t dst = ((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16);
     if constexpr (F32) {
-      const float x = static_cast<const float*>(rhs)[e];
-      static_cast<float*>(hi)[dst] = x;  // read as TF32 (truncated) by the tensor core
-      static_cast<float*>(lo)[dst] = tf32_rem(x);
+      float4 x, y;
+      x.x = col[0]; x.y = col[Nt]; x.z = col[2 * Nt]; x.w = col[3 * Nt];
+      y = make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;  // read as TF32 (truncated) by the tensor core
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) = y;
     } else {
-      static_cast<__nv_bfloat16*>(hi)[dst] = static_cast<const __nv_bfloat16*>(rhs)[e];
+      __align__(16) E v[EPU];
+#pragma unroll
+      for (int e = 0; e < EPU; ++e) v[e] = col[static_cast<int64_t>(e) * Nt];
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
     }
   }
 }
@@ -1367,7 +1379,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   if (cv.overflow) return ES_ERR_WORKSPACE;
   if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
   // 1. rhs tiles into the shared-memory image (split for fp32)
-  const int64_t pe = rhs_rows * c.Kt * c.Nt;
+  const int64_t pe = rhs_rows * c.Kt * c.Nt / (c.fp32 ? 4 : 8);  // 16-byte pieces of the image
   if (pe > 0) {
     if (c.fp32)
       ES_LAUNCH(layout_rhs_kernel<true>, grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi,
