@@ -281,11 +281,92 @@ def run_ours(args):
             "clocks": clk.summary(),
             "gen_s": round(gen_s, 1),
         }
+        if world == 1:
+            line["hbm_kernels"] = hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, w)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def _marks_ms(marks):
+    """Launch time of one call from its plan0/plan1/fill0/fill1 marks (the
+    host read of the counts between plan and fill is left out)."""
+    d = dict(marks)
+    ms = d["plan0"].elapsed_time(d["plan1"])
+    if "fill0" in d:
+        ms += d["fill0"].elapsed_time(d["fill1"])
+    return ms
+
+
+def hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm, reps=3):
+    """HBM rooflines of the bandwidth-bound phases of the path on the C2
+    inputs: COO->tile-COO tiling of A, join + output grouping, and the
+    unfused segment_sum API on a sample of C2's (pair tile, output tile)
+    rows. Each is timed by CUDA events around its own launches (median of
+    ``reps``), against the algorithmic bytes of the phase."""
+    import torch
+
+    import einjax_b200 as E
+    from einjax_b200 import sparse_dispatch as SD
+
+    def entry(ms, alg, what):
+        gbs = alg / (ms * 1e-3) / 1e9
+        return {"kernel_ms": round(ms, 4), "alg_bytes": int(alg), "achieved_gbs": round(gbs, 1),
+                "peak_gbs": hbm, "frac": round(gbs / hbm, 4), "bytes": what}
+
+    out = {}
+    t = []
+    for _ in range(reps):
+        m = []
+        A = E.tile_coo(idx_d, val_d, shape, (TILE, TILE), marks=m)
+        torch.cuda.synchronize()
+        t.append(_marks_ms(m))
+    nnz, T_A = int(val_d.numel()), A.num_tuples
+    out["tile_coo"] = entry(statistics.median(t), nnz * (2 * 4 + 4) + T_A * (TILE * TILE * 4 + 2 * 4),
+                            "nnz x 12 read + T_A x (4096 + 8) written")
+    B = E.tile_dense(b_d, (TILE, TILE))
+    t = []
+    for _ in range(reps):
+        m = []
+        plan = SD.plan_pairs(A, B, jk, ak, marks=m)
+        torch.cuda.synchronize()
+        t.append(_marks_ms(m))
+    P, T_B = plan.num_pairs, B.num_tuples
+    out["join_group"] = entry(statistics.median(t), 8 * (T_A + T_B) + 8 * P,
+                              "8 x (T_A + T_B) coords read + 8 x P pair indices written")
+    del A, B
+    # segment_sum sample: the first output tiles of C2 up to 2^20 pair rows,
+    # rows in a seeded random order, N(0,1) pair tiles
+    so = plan.seg_offsets
+    lim = torch.tensor([1 << 20], dtype=so.dtype, device=so.device)
+    s_end = max(int(torch.searchsorted(so[1:], lim, right=True)[0]), 1)
+    Ps = int(so[s_end])
+    counts = so[1:s_end + 1] - so[:s_end]
+    dev = so.device
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    oc = torch.repeat_interleave(plan.out_coords[:s_end], counts, dim=0)
+    oc = oc[torch.randperm(Ps, device=dev, generator=g)].contiguous()
+    vals = torch.randn((Ps, TILE, TILE), device=dev, generator=g)
+    del plan
+    t_all, t_red = [], []
+    for _ in range(reps):
+        m = []
+        SD.segment_sum(vals, oc, marks=m)
+        torch.cuda.synchronize()
+        d = dict(m)
+        t_all.append(_marks_ms(m))
+        t_red.append(d["fill0"].elapsed_time(d["fill1"]))
+    alg = (Ps + s_end) * TILE * TILE * 4
+    seg = entry(statistics.median(t_red), alg, "P_s x 4096 read + O_s x 4096 written (the reduction launches)")
+    seg["with_grouping"] = entry(statistics.median(t_all), alg + Ps * 8,
+                                 "as above + 8 x P_s coords read; grouping (radix sort of the coordinates) included")
+    seg["sample"] = f"{Ps} pair tiles into {s_end} output tiles (C2 segment sizes), fp32 32x32"
+    out["segment_sum"] = seg
+    del vals, oc
+    return out
 
 
 def cpu_baseline(args, w=None, budget_s=15.0):

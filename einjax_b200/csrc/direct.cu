@@ -1,30 +1,38 @@
 // Join + output grouping in one go for contractions of the form
-//     lhs (strip..., k) x rhs (k, col...) -> out (strip..., col...)
-// i.e. one join key that is the last lhs coordinate and the first rhs
-// coordinate, the output coordinates being the other lhs coordinates then
-// the other rhs coordinates (execute_sparse's join + _compute_output_coords
-// + segment_sum grouping, execution/sparse_dispatch.py:29-82, 174-223,
-// 129-171, for "ij,jk->ik", "ijk,kl->ijl", ...).
+//     lhs (batch..., strip..., k) x rhs (batch..., k, col...)
+//         -> out (batch..., strip..., col...)
+// i.e. join keys that pair the leading batch coordinates of both sides and
+// the last lhs coordinate with the rhs coordinate after the batch ones, the
+// output coordinates being the other lhs coordinates then the other rhs
+// coordinates (execute_sparse's join + _compute_output_coords + segment_sum
+// grouping, execution/sparse_dispatch.py:29-82, 174-223, 129-171, for
+// "ij,jk->ik", "ijk,kl->ijl", "bij,bjk->bik", ...).
 //
-// The lhs relation is in lexicographic coordinate order (its invariant,
-// checked here), so a strip's tiles are contiguous and in ascending k. The
-// rhs tiles go into a dense (k, col) -> tile table. Output tile (strip s,
-// column c) pairs each lhs tile i of strip s whose (k(i), c) table entry
+// Both relations are in lexicographic coordinate order (their invariant,
+// checked here), so a strip -- the lhs coordinates but the last, batch
+// included -- has its tiles contiguous and in ascending k. The rhs tiles go
+// into a dense ((batch, k), col) -> tile table. Output tile (strip s, column
+// c) pairs each lhs tile i of strip s whose ((batch, k)(i), c) table entry
 // exists with that rhs tile, in ascending k -- the join's order inside a
-// segment (for one rhs tile per pair, rhs ascending). With the hit matrix
-// H[c][i] (1 where the entry exists) and its exclusive scan E, segment (s, c)
-// has E[c][end(s)] - E[c][start(s)] pairs and the pair of lhs tile i goes to
-// offset(s, c) + E[c][i] - E[c][start(s)]: no sort at all.
+// segment (rhs-major over an rhs in lexicographic order). One warp walks
+// strip s for column c twice: once to count the hits, and -- after an
+// exclusive scan of the (strip, column) counts gives each segment its first
+// pair -- once to write the pairs, each lane placing its hit by a ballot
+// prefix. No sort, and nothing of size pairs or (columns x lhs tiles) is
+// materialised besides the pair arrays themselves.
 #include "common.cuh"
 #include "scan.cuh"
 
 namespace es {
 
 struct DirectGeom {
-  int lhs_nd, rhs_nd;
-  int64_t kext;                 // contracted tile extent
+  int lhs_nd, rhs_nd, nb;       // nb: leading batch dims joined pairwise
+  int64_t kx;                   // contracted tile extent
+  int64_t kext;                 // table rows: batch extents x kx
   int64_t cext;                 // product of the rhs column extents
-  int64_t col_ext[ES_MAX_DIMS]; // rhs grid extents of dims 1..rhs_nd-1
+  int64_t sext;                 // product of the lhs strip extents (dims 0..lhs_nd-2)
+  int64_t bat_ext[ES_MAX_DIMS]; // grid extents of the batch dims
+  int64_t col_ext[ES_MAX_DIMS]; // rhs grid extents of dims nb+1..rhs_nd-1
 };
 
 struct DirectWs {
@@ -35,23 +43,28 @@ struct DirectWs {
   uint32_t* sflag;     // (T_L) strip head
   uint32_t* sexcl;     // (T_L) exclusive scan: strip of a head
   uint32_t* sstart;    // (T_L + 1) first lhs tile of each strip, then T_L
-  uint32_t* hit;       // (cext * T_L + 1) H, c-major
-  uint32_t* hscan;     // (cext * T_L + 1) E
-  uint32_t* counts;    // (T_L * cext) pairs per (strip, column)
-  uint32_t* nzflag;    // (T_L * cext)
-  uint32_t* segid;     // (T_L * cext) exclusive scan of nzflag
-  uint32_t* off;       // (T_L * cext + 1) exclusive scan of counts
+  uint32_t* counts;    // (SC) pairs per (strip, present column), strip-major
+  uint32_t* nzflag;    // (SC)
+  uint32_t* segid;     // (SC) exclusive scan of nzflag
+  uint32_t* off;       // (SC + 1) exclusive scan of counts
   uint32_t* scan;      // scan scratch (largest length)
   uint32_t* ncols;     // (1) present columns
   uint32_t* nstrips;   // (1)
   uint32_t* total;     // (1) scratch totals
-  int32_t* bad;        // (1) lhs not in lexicographic order / duplicate coordinates
+  int32_t* bad;        // (1) a relation not in lexicographic order / repeated coordinates
 };
 
+// Upper bound of strips x present columns: strips <= min(T_L, strip extent),
+// present columns <= min(T_R, column extent).
+static int64_t direct_sc_bound(const DirectGeom& g, int64_t nl, int64_t nr) {
+  const int64_t s = nl < g.sext ? nl : g.sext;
+  const int64_t c = nr < g.cext ? nr : g.cext;
+  return s * c;
+}
+
 template <typename C>
-static void direct_layout(C& c, DirectWs& w, int64_t nl, const DirectGeom& g) {
-  const int64_t hn = g.cext * nl + 1;
-  const int64_t sc = nl * g.cext;
+static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const DirectGeom& g) {
+  const int64_t sc = direct_sc_bound(g, nl, nr);
   w.table = c.template take<int32_t>(g.kext * g.cext);
   w.colflag = c.template take<uint32_t>(g.cext);
   w.colrank = c.template take<uint32_t>(g.cext);
@@ -59,13 +72,11 @@ static void direct_layout(C& c, DirectWs& w, int64_t nl, const DirectGeom& g) {
   w.sflag = c.template take<uint32_t>(nl);
   w.sexcl = c.template take<uint32_t>(nl);
   w.sstart = c.template take<uint32_t>(nl + 1);
-  w.hit = c.template take<uint32_t>(hn);
-  w.hscan = c.template take<uint32_t>(hn);
   w.counts = c.template take<uint32_t>(sc);
   w.nzflag = c.template take<uint32_t>(sc);
   w.segid = c.template take<uint32_t>(sc);
   w.off = c.template take<uint32_t>(sc + 1);
-  int64_t mx = hn > sc + 1 ? hn : sc + 1;
+  int64_t mx = sc + 1;
   if (g.cext > mx) mx = g.cext;
   if (nl > mx) mx = nl;
   w.scan = c.template take<uint32_t>(scan_scratch_elems(mx));
@@ -84,27 +95,59 @@ struct DirectSizer {
   }
 };
 
+// Table row of a tile: its batch coordinates (row[0..nb)) then its
+// contracted coordinate row[kdim], linearised; -1 when out of range.
+__device__ __forceinline__ int64_t key_of(const int32_t* row, int kdim, const DirectGeom& g) {
+  int64_t key = 0;
+  for (int d = 0; d < g.nb; ++d) {
+    const int64_t x = row[d];
+    if (x < 0 || x >= g.bat_ext[d]) return -1;
+    key = key * g.bat_ext[d] + x;
+  }
+  const int64_t k = row[kdim];
+  if (k < 0 || k >= g.kx) return -1;
+  return key * g.kx + k;
+}
+
 __device__ __forceinline__ int64_t col_linear(const int32_t* row, const DirectGeom& g, bool* ok) {
   int64_t c = 0;
-  for (int d = 1; d < g.rhs_nd; ++d) {
+  for (int d = g.nb + 1; d < g.rhs_nd; ++d) {
     const int64_t x = row[d];
-    if (x < 0 || x >= g.col_ext[d - 1]) *ok = false;
-    c = c * g.col_ext[d - 1] + x;
+    const int64_t e = g.col_ext[d - g.nb - 1];
+    if (x < 0 || x >= e) *ok = false;
+    c = c * e + x;
   }
   return c;
 }
 
+// Lexicographic comparison of two coordinate rows: -1, 0, 1; *first_diff =
+// the first dimension where they differ (nd when equal).
+__device__ __forceinline__ int lex_cmp(const int32_t* a, const int32_t* b, int nd, int* first_diff) {
+  for (int d = 0; d < nd; ++d)
+    if (a[d] != b[d]) {
+      *first_diff = d;
+      return a[d] > b[d] ? 1 : -1;
+    }
+  *first_diff = nd;
+  return 0;
+}
+
+// rhs tiles into the table; flags an rhs out of lexicographic order.
 __global__ void direct_table_kernel(const int32_t* __restrict__ rc, int64_t nr, DirectGeom g,
-                                    int32_t* __restrict__ table, uint32_t* __restrict__ colflag, int32_t* err) {
+                                    int32_t* __restrict__ table, uint32_t* __restrict__ colflag,
+                                    int32_t* __restrict__ bad, int32_t* err) {
   for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < nr; j += (int64_t)gridDim.x * blockDim.x) {
     const int32_t* row = rc + j * g.rhs_nd;
-    bool ok = row[0] >= 0 && row[0] < g.kext;
+    int fd;
+    if (j > 0 && lex_cmp(row, row - g.rhs_nd, g.rhs_nd, &fd) <= 0) *bad = 1;
+    const int64_t key = key_of(row, g.nb, g);
+    bool ok = key >= 0;
     const int64_t c = col_linear(row, g, &ok);
     if (!ok) {
       if (err) atomicExch(err, ES_ERR_INDEX);
       continue;
     }
-    table[static_cast<int64_t>(row[0]) * g.cext + c] = static_cast<int32_t>(j);
+    table[key * g.cext + c] = static_cast<int32_t>(j);
     colflag[c] = 1u;
   }
 }
@@ -116,28 +159,20 @@ __global__ void direct_colids_kernel(const uint32_t* __restrict__ colflag, const
 }
 
 // Strip heads of the lhs; flags lhs tiles out of lexicographic order (or
-// repeated) and keys outside the contracted range.
+// repeated) and keys outside the table.
 __global__ void direct_strips_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
                                      uint32_t* __restrict__ sflag, int32_t* __restrict__ bad, int32_t* err) {
   const int nd = g.lhs_nd;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nl; i += (int64_t)gridDim.x * blockDim.x) {
     const int32_t* row = lc + i * nd;
-    if (row[nd - 1] < 0 || row[nd - 1] >= g.kext) {
+    if (key_of(row, nd - 1, g) < 0) {
       if (err) atomicExch(err, ES_ERR_INDEX);
     }
     uint32_t head = 1u;
     if (i > 0) {
-      const int32_t* prev = row - nd;
-      int cmp = 0;  // lexicographic compare over all dims; strip = dims 0..nd-2
-      bool same_strip = true;
-      for (int d = 0; d < nd && cmp == 0; ++d) {
-        if (row[d] != prev[d]) {
-          cmp = row[d] > prev[d] ? 1 : -1;
-          if (d < nd - 1) same_strip = false;
-        }
-      }
-      if (cmp <= 0) *bad = 1;
-      head = same_strip ? 0u : 1u;
+      int fd;
+      if (lex_cmp(row, row - nd, nd, &fd) <= 0) *bad = 1;
+      head = fd < nd - 1 ? 1u : 0u;  // strip = dims 0..nd-2
     }
     sflag[i] = head;
   }
@@ -151,40 +186,59 @@ __global__ void direct_sstart_kernel(const uint32_t* __restrict__ sflag, const u
   }
 }
 
-// H[c][i] = 1 when rhs tile (k(i), column c) exists; H[C][0] (the slot after
-// the last used row) = 0 so the scan's tail reads a total.
-__global__ void direct_hits_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
-                                   const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
-                                   const uint32_t* __restrict__ ncols, uint32_t* __restrict__ hit) {
-  const int64_t C = *ncols;
-  const int64_t n = C * nl;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e <= n; e += (int64_t)gridDim.x * blockDim.x) {
-    if (e == n) {
-      hit[e] = 0u;
-      continue;
+// Lookups of one warp step: tiles base + j*32 + lane, j < kDirU, of the strip
+// [.., end). k[j] = contracted coordinate, r[j] = rhs tile joined with the
+// lhs tile for column col, or -1.
+constexpr int kDirU = 4;
+
+__device__ __forceinline__ void direct_probe(const int32_t* __restrict__ lc, const DirectGeom& g,
+                                             const int32_t* __restrict__ table, int64_t col, int64_t base,
+                                             int64_t end, int lane, int32_t (&k)[kDirU], int32_t (&r)[kDirU]) {
+  const int nd = g.lhs_nd;
+  int64_t key[kDirU];
+#pragma unroll
+  for (int j = 0; j < kDirU; ++j) {
+    const int64_t i = base + j * 32 + lane;
+    if (i < end) {
+      const int32_t* row = lc + i * nd;
+      k[j] = __ldg(row + nd - 1);
+      key[j] = g.nb == 0 ? ((k[j] >= 0 && k[j] < g.kx) ? k[j] : -1) : key_of(row, nd - 1, g);
+    } else {
+      k[j] = -1;
+      key[j] = -1;
     }
-    const int64_t c = e / nl, i = e - c * nl;
-    const int32_t k = lc[i * g.lhs_nd + g.lhs_nd - 1];
-    uint32_t h = 0u;
-    if (k >= 0 && k < g.kext) h = table[static_cast<int64_t>(k) * g.cext + colids[c]] >= 0 ? 1u : 0u;
-    hit[e] = h;
   }
+#pragma unroll
+  for (int j = 0; j < kDirU; ++j) r[j] = key[j] >= 0 ? __ldg(table + key[j] * g.cext + col) : -1;
 }
 
-// Pairs per (strip, present column), strip-major.
-__global__ void direct_counts_kernel(const uint32_t* __restrict__ hscan, const uint32_t* __restrict__ sstart,
-                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ ncols,
-                                     int64_t nl, uint32_t* __restrict__ counts, uint32_t* __restrict__ nzflag) {
+// Pairs per (strip, present column), strip-major: one warp per entry.
+__global__ void direct_counts_kernel(const int32_t* __restrict__ lc, DirectGeom g, const int32_t* __restrict__ table,
+                                     const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
+                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
+                                     uint32_t* __restrict__ counts, uint32_t* __restrict__ nzflag) {
   const int64_t S = *nstrips, C = *ncols;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < S * C; e += (int64_t)gridDim.x * blockDim.x) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; e < S * C; e += nw) {
     const int64_t s = e / C, c = e - s * C;
-    const uint32_t n = hscan[c * nl + sstart[s + 1]] - hscan[c * nl + sstart[s]];
-    counts[e] = n;
-    nzflag[e] = n ? 1u : 0u;
+    const int64_t col = colids[c];
+    const int64_t a = sstart[s], b = sstart[s + 1];
+    uint32_t n = 0;
+    for (int64_t base = a; base < b; base += 32 * kDirU) {
+      int32_t k[kDirU], r[kDirU];
+      direct_probe(lc, g, table, col, base, b, lane, k, r);
+#pragma unroll
+      for (int j = 0; j < kDirU; ++j) n += __popc(__ballot_sync(0xffffffffu, r[j] >= 0));
+    }
+    if (lane == 0) {
+      counts[e] = n;
+      nzflag[e] = n ? 1u : 0u;
+    }
   }
 }
 
-// Counts of the host's sizes: [0] pairs, [1] output tiles.
+// Counts of the host's sizes: [0] pairs, [1] output tiles, [2] out of order.
 __global__ void direct_totals_kernel(const uint32_t* __restrict__ off, const uint32_t* __restrict__ segid,
                                      const uint32_t* __restrict__ counts, const uint32_t* __restrict__ nzflag,
                                      const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ ncols,
@@ -201,69 +255,84 @@ __global__ void direct_totals_kernel(const uint32_t* __restrict__ off, const uin
   out[2] = *bad;
 }
 
-__global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
-                                    const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
-                                    const uint32_t* __restrict__ ncols, const uint32_t* __restrict__ hit,
-                                    const uint32_t* __restrict__ hscan, const uint32_t* __restrict__ sflag,
-                                    const uint32_t* __restrict__ sexcl, const uint32_t* __restrict__ sstart,
-                                    const uint32_t* __restrict__ off, int32_t* __restrict__ seg_lhs,
-                                    int32_t* __restrict__ seg_rhs, int32_t* __restrict__ seg_key) {
-  const int64_t C = *ncols;
-  const int64_t n = C * nl;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-    if (!hit[e]) continue;
-    const int64_t c = e / nl, i = e - c * nl;
-    const int64_t s = static_cast<int64_t>(sexcl[i]) + sflag[i] - 1;  // strip of lhs tile i
-    const int64_t pos = static_cast<int64_t>(off[s * C + c]) + (hscan[e] - hscan[c * nl + sstart[s]]);
-    const int32_t k = lc[i * g.lhs_nd + g.lhs_nd - 1];
-    seg_lhs[pos] = static_cast<int32_t>(i);
-    seg_rhs[pos] = table[static_cast<int64_t>(k) * g.cext + colids[c]];
-    if (seg_key) seg_key[pos] = k;
-  }
-}
-
-__global__ void direct_segments_kernel(const int32_t* __restrict__ lc, DirectGeom g,
-                                       const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
-                                       const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                       const uint32_t* __restrict__ nzflag, const uint32_t* __restrict__ segid,
-                                       const uint32_t* __restrict__ off, int32_t* __restrict__ out_coords,
-                                       int64_t* __restrict__ seg_off, int64_t* __restrict__ seg_strip) {
+// Pairs of entry (strip s, present column c) in ascending lhs tile, from
+// off[e]; the first lane also writes the segment's record when it has pairs.
+// The warp of the last segment writes seg_off[O] = P.
+__global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, DirectGeom g, const int32_t* __restrict__ table,
+                                    const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
+                                    const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
+                                    const uint32_t* __restrict__ counts, const uint32_t* __restrict__ off,
+                                    const uint32_t* __restrict__ segid, int64_t num_pairs, int64_t num_segments,
+                                    int32_t* __restrict__ seg_lhs, int32_t* __restrict__ seg_rhs,
+                                    int32_t* __restrict__ seg_key, int32_t* __restrict__ out_coords,
+                                    int64_t* __restrict__ seg_off, int64_t* __restrict__ seg_strip) {
   const int64_t S = *nstrips, C = *ncols;
-  const int out_nd = (g.lhs_nd - 1) + (g.rhs_nd - 1);
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < S * C; e += (int64_t)gridDim.x * blockDim.x) {
-    if (!nzflag[e]) continue;
+  const int lane = threadIdx.x & 31;
+  const uint32_t below = (1u << lane) - 1u;
+  const int ncd = g.rhs_nd - 1 - g.nb;  // rhs column dims
+  const int out_nd = (g.lhs_nd - 1) + ncd;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; e < S * C; e += nw) {
+    if (counts[e] == 0) continue;  // warp-uniform
     const int64_t s = e / C, c = e - s * C;
-    const int64_t o = segid[e];
-    const int32_t* row = lc + static_cast<int64_t>(sstart[s]) * g.lhs_nd;
-    int32_t* oc = out_coords + o * out_nd;
-    for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
-    int64_t cl = colids[c];
-    for (int d = g.rhs_nd - 2; d >= 0; --d) {
-      oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
-      cl /= g.col_ext[d];
+    const int64_t col = colids[c];
+    const int64_t a = sstart[s], b = sstart[s + 1];
+    if (lane == 0) {
+      const int64_t o = segid[e];
+      const int32_t* row = lc + a * g.lhs_nd;
+      int32_t* oc = out_coords + o * out_nd;
+      for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
+      int64_t cl = col;
+      for (int d = ncd - 1; d >= 0; --d) {
+        oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
+        cl /= g.col_ext[d];
+      }
+      seg_off[o] = off[e];
+      if (seg_strip) seg_strip[o] = s;
+      if (o + 1 == num_segments) seg_off[num_segments] = num_pairs;
     }
-    seg_off[o] = off[e];
-    if (seg_strip) seg_strip[o] = s;
+    int64_t pos = off[e];
+    for (int64_t base = a; base < b; base += 32 * kDirU) {
+      int32_t k[kDirU], r[kDirU];
+      direct_probe(lc, g, table, col, base, b, lane, k, r);
+#pragma unroll
+      for (int j = 0; j < kDirU; ++j) {
+        const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
+        if (r[j] >= 0) {
+          const int64_t p = pos + __popc(m & below);
+          seg_lhs[p] = static_cast<int32_t>(base + j * 32 + lane);
+          seg_rhs[p] = r[j];
+          if (seg_key) seg_key[p] = k[j];
+        }
+        pos += __popc(m);
+      }
+    }
   }
 }
 
-__global__ void direct_last_offset_kernel(int64_t* seg_off, int64_t O, int64_t P) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) seg_off[O] = P;
-}
-
-static int make_direct_geom(int lhs_nd, int rhs_nd, const int64_t* lhs_grid, const int64_t* rhs_grid,
+static int make_direct_geom(int lhs_nd, int rhs_nd, int nb, const int64_t* lhs_grid, const int64_t* rhs_grid,
                             DirectGeom* g) {
   if (lhs_nd < 1 || rhs_nd < 1 || lhs_nd > ES_MAX_DIMS || rhs_nd > ES_MAX_DIMS) return ES_ERR_INVALID;
-  if (lhs_nd + rhs_nd - 2 < 1) return ES_ERR_UNSUPPORTED;
+  if (nb < 0 || nb >= lhs_nd || nb >= rhs_nd) return ES_ERR_INVALID;
+  if (lhs_nd + rhs_nd - 2 - nb < 1) return ES_ERR_UNSUPPORTED;
   g->lhs_nd = lhs_nd;
   g->rhs_nd = rhs_nd;
-  g->kext = lhs_grid[lhs_nd - 1] > rhs_grid[0] ? lhs_grid[lhs_nd - 1] : rhs_grid[0];
+  g->nb = nb;
+  g->kx = lhs_grid[lhs_nd - 1] > rhs_grid[nb] ? lhs_grid[lhs_nd - 1] : rhs_grid[nb];
+  g->kext = g->kx;
+  for (int d = 0; d < nb; ++d) {
+    g->bat_ext[d] = lhs_grid[d] > rhs_grid[d] ? lhs_grid[d] : rhs_grid[d];
+    if (g->bat_ext[d] <= 0) return ES_ERR_INVALID;
+    g->kext *= g->bat_ext[d];
+  }
   g->cext = 1;
-  for (int d = 1; d < rhs_nd; ++d) {
-    g->col_ext[d - 1] = rhs_grid[d];
+  for (int d = nb + 1; d < rhs_nd; ++d) {
+    g->col_ext[d - nb - 1] = rhs_grid[d];
     g->cext *= rhs_grid[d];
   }
-  if (g->kext <= 0 || g->cext <= 0) return ES_ERR_INVALID;
+  g->sext = 1;
+  for (int d = 0; d + 1 < lhs_nd; ++d) g->sext *= lhs_grid[d];
+  if (g->kx <= 0 || g->cext <= 0 || g->sext <= 0) return ES_ERR_INVALID;
   return ES_OK;
 }
 
@@ -272,48 +341,47 @@ static int make_direct_geom(int lhs_nd, int rhs_nd, const int64_t* lhs_grid, con
 using namespace es;
 
 extern "C" size_t es_direct_workspace_size(int64_t n_lhs, int lhs_ndim, int64_t n_rhs, int rhs_ndim,
-                                           const int64_t* lhs_grid, const int64_t* rhs_grid) {
+                                           int batch_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid) {
   DirectGeom g;
-  if (make_direct_geom(lhs_ndim, rhs_ndim, lhs_grid, rhs_grid, &g) != ES_OK) return 0;
-  (void)n_rhs;
+  if (make_direct_geom(lhs_ndim, rhs_ndim, batch_ndim, lhs_grid, rhs_grid, &g) != ES_OK) return 0;
   DirectSizer s;
   DirectWs w;
-  direct_layout(s, w, n_lhs, g);
+  direct_layout(s, w, n_lhs, n_rhs, g);
   return s.s.used + 256;
 }
 
 extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, const int32_t* rhs_coords,
-                              int64_t n_rhs, int rhs_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid,
-                              void* workspace, size_t workspace_bytes, int64_t* counts_dev, int32_t* error_dev,
-                              void* stream) {
+                              int64_t n_rhs, int rhs_ndim, int batch_ndim, const int64_t* lhs_grid,
+                              const int64_t* rhs_grid, void* workspace, size_t workspace_bytes, int64_t* counts_dev,
+                              int32_t* error_dev, void* stream) {
   cudaStream_t st = as_stream(stream);
   DirectGeom g;
-  ES_TRY(make_direct_geom(lhs_ndim, rhs_ndim, lhs_grid, rhs_grid, &g));
+  ES_TRY(make_direct_geom(lhs_ndim, rhs_ndim, batch_ndim, lhs_grid, rhs_grid, &g));
   if (n_lhs <= 0 || n_rhs <= 0) return ES_ERR_INVALID;
-  if (g.cext * n_lhs + 1 >= static_cast<int64_t>(UINT32_MAX) || g.kext * g.cext >= static_cast<int64_t>(INT32_MAX) ||
+  // pairs <= n_lhs * present columns must fit the int32 pair arrays
+  const int64_t cmax = n_rhs < g.cext ? n_rhs : g.cext;
+  if (n_lhs >= static_cast<int64_t>(INT32_MAX) / cmax || g.kext * g.cext >= static_cast<int64_t>(INT32_MAX) ||
       n_rhs >= static_cast<int64_t>(INT32_MAX))
     return ES_ERR_UNSUPPORTED;
   Carver cv(workspace, workspace_bytes);
   DirectWs w;
-  direct_layout(cv, w, n_lhs, g);
+  direct_layout(cv, w, n_lhs, n_rhs, g);
   if (cv.overflow) return ES_ERR_WORKSPACE;
   if (cudaMemsetAsync(w.table, 0xFF, g.kext * g.cext * sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
   if (cudaMemsetAsync(w.colflag, 0, g.cext * sizeof(uint32_t), st) != cudaSuccess) return ES_ERR_CUDA;
   if (cudaMemsetAsync(w.bad, 0, sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
-  ES_LAUNCH(direct_table_kernel, grid_for(n_rhs, 256), 256, 0, st, rhs_coords, n_rhs, g, w.table, w.colflag,
+  ES_LAUNCH(direct_table_kernel, grid_for(n_rhs, 256), 256, 0, st, rhs_coords, n_rhs, g, w.table, w.colflag, w.bad,
             error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, w.scan, st));
   ES_LAUNCH(direct_colids_kernel, grid_for(g.cext, 256), 256, 0, st, w.colflag, w.colrank, g.cext, w.colids);
   ES_LAUNCH(direct_strips_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, g, w.sflag, w.bad, error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.sflag, w.sexcl, n_lhs, w.nstrips, w.scan, st));
   ES_LAUNCH(direct_sstart_kernel, grid_for(n_lhs, 256), 256, 0, st, w.sflag, w.sexcl, n_lhs, w.nstrips, w.sstart);
-  const int64_t hn = g.cext * n_lhs + 1;  // the used part is ncols * n_lhs + 1 (device count)
-  ES_LAUNCH(direct_hits_kernel, grid_for(hn, 256), 256, 0, st, lhs_coords, n_lhs, g, w.table, w.colids, w.ncols,
-            w.hit);
-  ES_TRY(exclusive_scan<uint32_t>(w.hit, w.hscan, hn, w.total, w.scan, st));
-  const int64_t sc = n_lhs * g.cext;
-  ES_LAUNCH(direct_counts_kernel, grid_for(sc, 256), 256, 0, st, w.hscan, w.sstart, w.nstrips, w.ncols, n_lhs,
-            w.counts, w.nzflag);
+  // one warp per (strip, present column); both counts live on the device,
+  // so the grid covers the upper bound and warps stride over the used part
+  const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
+  ES_LAUNCH(direct_counts_kernel, grid_for(sc * 32, 256), 256, 0, st, lhs_coords, g, w.table, w.colids, w.ncols,
+            w.nstrips, w.sstart, w.counts, w.nzflag);
   // the scans run over the upper bound; entries past nstrips * ncols are not
   // written and only ever enter prefixes past the used length
   ES_TRY(exclusive_scan<uint32_t>(w.counts, w.off, sc, w.total, w.scan, st));
@@ -323,27 +391,27 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   return ES_OK;
 }
 
-extern "C" int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, int rhs_ndim,
-                              const int64_t* lhs_grid, const int64_t* rhs_grid, void* workspace,
+extern "C" int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, int64_t n_rhs, int rhs_ndim,
+                              int batch_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid, void* workspace,
                               size_t workspace_bytes, int64_t num_pairs, int64_t num_segments, int32_t* out_coords,
                               int64_t* seg_offsets, int32_t* seg_lhs, int32_t* seg_rhs, int64_t* seg_strip,
                               int32_t* seg_key, void* stream) {
   cudaStream_t st = as_stream(stream);
   DirectGeom g;
-  ES_TRY(make_direct_geom(lhs_ndim, rhs_ndim, lhs_grid, rhs_grid, &g));
-  if (n_lhs <= 0) return ES_ERR_INVALID;
+  ES_TRY(make_direct_geom(lhs_ndim, rhs_ndim, batch_ndim, lhs_grid, rhs_grid, &g));
+  if (n_lhs <= 0 || n_rhs <= 0) return ES_ERR_INVALID;
   Carver cv(workspace, workspace_bytes);
   DirectWs w;
-  direct_layout(cv, w, n_lhs, g);
+  direct_layout(cv, w, n_lhs, n_rhs, g);
   if (cv.overflow) return ES_ERR_WORKSPACE;
-  const int64_t hn = g.cext * n_lhs;
-  if (num_pairs > 0)
-    ES_LAUNCH(direct_pairs_kernel, grid_for(hn, 256), 256, 0, st, lhs_coords, n_lhs, g, w.table, w.colids, w.ncols,
-              w.hit, w.hscan, w.sflag, w.sexcl, w.sstart, w.off, seg_lhs, seg_rhs, seg_key);
-  const int64_t sc = n_lhs * g.cext;
-  if (num_segments > 0)
-    ES_LAUNCH(direct_segments_kernel, grid_for(sc, 256), 256, 0, st, lhs_coords, g, w.colids, w.ncols, w.nstrips,
-              w.sstart, w.nzflag, w.segid, w.off, out_coords, seg_offsets, seg_strip);
-  ES_LAUNCH(direct_last_offset_kernel, 1, 32, 0, st, seg_offsets, num_segments, num_pairs);
+  if (num_segments == 0) {
+    // no pairs: the single offset 0
+    if (cudaMemsetAsync(seg_offsets, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
+    return ES_OK;
+  }
+  const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
+  ES_LAUNCH(direct_pairs_kernel, grid_for(sc * 32, 256), 256, 0, st, lhs_coords, g, w.table, w.colids, w.ncols,
+            w.nstrips, w.sstart, w.counts, w.off, w.segid, num_pairs, num_segments, seg_lhs, seg_rhs, seg_key,
+            out_coords, seg_offsets, seg_strip);
   return ES_OK;
 }

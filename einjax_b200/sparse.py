@@ -44,6 +44,16 @@ def workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+def mark(marks, label: str) -> None:
+    """Appends (label, CUDA event recorded on the current stream) to ``marks``
+    when it is a list: lets a caller time the launches of one call without
+    the host reads of counts between them."""
+    if marks is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((label, ev))
+
+
 def read_counts(t: torch.Tensor):
     """Read a small device int64 tensor (count, error, ...) with one sync."""
     return [int(v) for v in t.tolist()]
@@ -161,11 +171,12 @@ def _check_divisible(shape, tile_shape):
 
 
 def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
-             out_dtype=torch.float32) -> SparseTensorRelation:
+             out_dtype=torch.float32, marks=None) -> SparseTensorRelation:
     """Element COO (device tensors) -> tile-COO relation (``tensor/sparse.py:160-219``).
 
     ``indices`` int32 ``(nnz, ndim)``, ``values`` (nnz,) float32/float64/bf16.
-    Zeros are dropped; the last of repeated coordinates wins.
+    Zeros are dropped; the last of repeated coordinates wins. ``marks``: see
+    ``mark`` (plan0/plan1 around the plan launches, fill0/fill1 around the fill).
     """
     shape = tuple(int(s) for s in shape)
     tile_shape = tuple(int(t) for t in tile_shape)
@@ -183,17 +194,21 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
     ws = workspace(wsb, dev)
     cnt = torch.zeros(2, dtype=torch.int64, device=dev)
     st = stream_ptr(dev)
+    mark(marks, "plan0")
     L.check("es_tile_coo_plan", lib.es_tile_coo_plan(
         idx.data_ptr(), vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(),
         cnt.data_ptr(), cnt[1:].data_ptr(), st))
+    mark(marks, "plan1")
     T, err = read_counts(cnt)
     if err:
         raise ValueError("COO index outside the tensor shape")
     coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
     out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+    mark(marks, "fill0")
     L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
         vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T,
         coords.data_ptr(), out.data_ptr(), L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16, st))
+    mark(marks, "fill1")
     return SparseTensorRelation(coords, out, shape, tile_shape)
 
 

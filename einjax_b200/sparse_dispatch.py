@@ -21,7 +21,7 @@ from math import prod
 import torch
 
 from . import _lib as L
-from .sparse import (SparseTensorRelation, as_relation, empty_relation, es_dtype, read_counts, stream_ptr,
+from .sparse import (SparseTensorRelation, as_relation, empty_relation, es_dtype, mark, read_counts, stream_ptr,
                      workspace)
 
 _PREC = {"auto": L.ES_PREC_AUTO, "exact": L.ES_PREC_EXACT, "tc": L.ES_PREC_TC}
@@ -221,11 +221,13 @@ def _compute_output_coords(lhs, rhs, lhs_indices, rhs_indices, join_keys, agg_ke
     return out
 
 
-def segment_sum(values: torch.Tensor, output_coords: torch.Tensor):
+def segment_sum(values: torch.Tensor, output_coords: torch.Tensor, marks=None):
     """Group rows by coordinate and sum them (``execution/sparse_dispatch.py:129-171``).
 
     Returns (unique coords int32 sorted lexicographically, summed values in
     the input's dtype); rows of a group are added in row order, in fp32.
+    ``marks``: see ``sparse.mark`` (plan0/1 around the grouping, fill0/1
+    around the reduction).
     """
     dev = values.device
     oc = torch.as_tensor(output_coords, device=dev).to(torch.int32)
@@ -245,8 +247,10 @@ def segment_sum(values: torch.Tensor, output_coords: torch.Tensor):
     cnt = torch.zeros(2, dtype=torch.int64, device=dev)
     st = stream_ptr(dev)
     e = L.i64arr(ext)
+    mark(marks, "plan0")
     L.check("es_segsum_plan", lib.es_segsum_plan(oc.data_ptr(), n, nd, e, ws.data_ptr(), ws.numel(), cnt.data_ptr(),
                                                  cnt[1:].data_ptr(), st))
+    mark(marks, "plan1")
     O, err = read_counts(cnt)
     if err:
         raise ValueError("segment_sum: coordinate outside its extent")
@@ -254,8 +258,10 @@ def segment_sum(values: torch.Tensor, output_coords: torch.Tensor):
     odt = torch.bfloat16 if vals.dtype == torch.bfloat16 else torch.float32
     uc = torch.empty((O, nd), dtype=torch.int32, device=dev)
     uv = torch.empty((O, *values.shape[1:]), dtype=odt, device=dev)
+    mark(marks, "fill0")
     L.check("es_segsum_fill", lib.es_segsum_fill(vals.data_ptr(), es_dtype(vals), n, te, nd, e, ws.data_ptr(),
                                                  ws.numel(), O, uc.data_ptr(), uv.data_ptr(), _es_out(odt), st))
+    mark(marks, "fill1")
     return uc, uv
 
 
@@ -288,35 +294,54 @@ def _out_extents(lhs, rhs, agg_keys):
     return [lg[d] if s == 0 else rg[d] for s, d in agg_keys]
 
 
-def _direct_shape(lhs, rhs, join_keys, agg_keys) -> bool:
-    """True for lhs (strip..., k) x rhs (k, col...) -> (strip..., col...): one
-    join key, the last lhs and the first rhs coordinate, output = the other
-    lhs then the other rhs coordinates, and a small (k, col) rhs table."""
-    if len(join_keys) != 1 or tuple(int(v) for v in join_keys[0]) != (lhs.ndim - 1, 0):
-        return False
-    want = [(0, d) for d in range(lhs.ndim - 1)] + [(1, d) for d in range(1, rhs.ndim)]
+def _direct_batch_dims(lhs, rhs, join_keys, agg_keys):
+    """Number of leading batch dims when the call has the shape
+    lhs (batch..., strip..., k) x rhs (batch..., k, col...) ->
+    (batch..., strip..., col...): join keys = the batch dims paired (d, d)
+    plus (last lhs dim, first rhs dim after the batch ones), output = the
+    other lhs then the other rhs coordinates, and a small ((batch, k), col)
+    rhs table. None for any other shape."""
+    keys = {tuple(int(v) for v in k) for k in join_keys}
+    if len(keys) != len(join_keys) or not keys:
+        return None
+    nb = len(keys) - 1
+    if nb >= lhs.ndim or nb >= rhs.ndim or keys != {(d, d) for d in range(nb)} | {(lhs.ndim - 1, nb)}:
+        return None
+    want = [(0, d) for d in range(lhs.ndim - 1)] + [(1, d) for d in range(nb + 1, rhs.ndim)]
     if [tuple(int(v) for v in k) for k in agg_keys] != want or not want:
-        return False
+        return None
     lg, rg = lhs.grid(), rhs.grid()
-    cext = prod(rg[1:]) if rhs.ndim > 1 else 1
-    kext = max(lg[-1], rg[0])
-    return kext * cext <= (1 << 26) and cext * max(lhs.num_tuples, 1) < (1 << 31)
+    cext = prod(rg[nb + 1:])
+    kext = max(lg[-1], rg[nb]) * prod(max(lg[d], rg[d]) for d in range(nb))
+    # pairs <= lhs tiles x present columns fit the int32 pair arrays
+    if kext * cext <= (1 << 26) and min(cext, max(rhs.num_tuples, 1)) * max(lhs.num_tuples, 1) < (1 << 31) - 1:
+        return nb
+    return None
 
 
-def _plan_direct(lhs, rhs, join_keys, agg_keys):
-    """Join + grouping without sorts (``es_direct_*``); None when the lhs is
-    not in lexicographic order (the general path then runs)."""
+def _direct_shape(lhs, rhs, join_keys, agg_keys) -> bool:
+    """True when ``_plan_direct`` covers the call (``_direct_batch_dims``)."""
+    return _direct_batch_dims(lhs, rhs, join_keys, agg_keys) is not None
+
+
+def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None):
+    """Join + grouping without sorts (``es_direct_*``); None when a relation
+    is not in lexicographic order (the general path then runs). ``marks``:
+    see ``sparse.mark``."""
     dev = lhs.device
     lib = L.lib()
+    nb = _direct_batch_dims(lhs, rhs, join_keys, agg_keys)
     lg, rg = L.i64arr(lhs.grid()), L.i64arr(rhs.grid())
     nl, nr = lhs.num_tuples, rhs.num_tuples
-    ws = workspace(lib.es_direct_workspace_size(nl, lhs.ndim, nr, rhs.ndim, lg, rg), dev)
+    ws = workspace(lib.es_direct_workspace_size(nl, lhs.ndim, nr, rhs.ndim, nb, lg, rg), dev)
     cnt = torch.zeros(4, dtype=torch.int64, device=dev)  # P, O, out of order, error
     st = stream_ptr(dev)
     lc, rc = lhs.coords.contiguous(), rhs.coords.contiguous()
+    mark(marks, "plan0")
     L.check("es_direct_plan", lib.es_direct_plan(
-        lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, lg, rg, ws.data_ptr(), ws.numel(),
+        lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, nb, lg, rg, ws.data_ptr(), ws.numel(),
         cnt.data_ptr(), cnt[3:].data_ptr(), st))
+    mark(marks, "plan1")
     P, O, unordered, err = (int(v) for v in cnt.cpu().tolist())
     if err:
         raise ValueError("tile coordinate outside the tensor grid")
@@ -328,17 +353,23 @@ def _plan_direct(lhs, rhs, join_keys, agg_keys):
     sl = torch.empty(P, dtype=torch.int32, device=dev)
     sr = torch.empty(P, dtype=torch.int32, device=dev)
     sg = torch.empty(O, dtype=torch.int64, device=dev)
-    sk = torch.empty(P, dtype=torch.int32, device=dev)
+    # the contracted coordinate names the lhs tile of a strip only without
+    # batch dims (the general path's rule): the tensor-core path may then
+    # merge strips on it
+    sk = torch.empty(P, dtype=torch.int32, device=dev) if nb == 0 else None
+    mark(marks, "fill0")
     L.check("es_direct_fill", lib.es_direct_fill(
-        lc.data_ptr(), nl, lhs.ndim, rhs.ndim, lg, rg, ws.data_ptr(), ws.numel(), P, O, oc.data_ptr(), so.data_ptr(),
-        sl.data_ptr(), sr.data_ptr(), sg.data_ptr(), sk.data_ptr(), st))
-    kext = _key_extents(lhs, rhs, [tuple(join_keys[0])])[0]
+        lc.data_ptr(), nl, lhs.ndim, nr, rhs.ndim, nb, lg, rg, ws.data_ptr(), ws.numel(), P, O, oc.data_ptr(),
+        so.data_ptr(), sl.data_ptr(), sr.data_ptr(), sg.data_ptr(), sk.data_ptr() if sk is not None else None, st))
+    mark(marks, "fill1")
+    kext = _key_extents(lhs, rhs, [(lhs.ndim - 1, nb)])[0] if nb == 0 else 0
     # pairs come grouped; "join order" is taken to be this grouped order
     # (seg_pair None: the identity)
     return PairPlan(sl, sr, oc, so, sl, sr, None, sg, sk, kext)
 
 
-def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, agg_keys) -> PairPlan:
+def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, agg_keys,
+               marks=None) -> PairPlan:
     """Join the relations and group the pairs by output tile (two host syncs:
     the pair count and the output-tile count).
 
@@ -347,7 +378,7 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     then hold the grouped order."""
     dev = lhs.device
     if lhs.num_tuples > 0 and rhs.num_tuples > 0 and _direct_shape(lhs, rhs, join_keys, agg_keys):
-        plan = _plan_direct(lhs, rhs, join_keys, agg_keys)
+        plan = _plan_direct(lhs, rhs, join_keys, agg_keys, marks)
         if plan is not None:
             return plan
     li, ri = _join_int32(lhs, rhs, join_keys)

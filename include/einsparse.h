@@ -209,31 +209,37 @@ int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs_tile, int 
                         const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype, int precision);
 
 /* ---------------------------------------------------------------------------
- * Join + output grouping in one pass for lhs (strip..., k) x rhs (k, col...)
- * -> out (strip..., col...): one join key, the last lhs and first rhs
- * coordinate, output = the other lhs then the other rhs coordinates (the
- * matmul-like calls of execute_sparse: coordinate_join + _compute_output_coords
- * + segment_sum grouping, execution/sparse_dispatch.py:29-82, 174-223,
+ * Join + output grouping in one pass for
+ *     lhs (batch..., strip..., k) x rhs (batch..., k, col...)
+ *         -> out (batch..., strip..., col...)
+ * with batch_ndim >= 0 leading batch dims joined pairwise (lhs dim d with rhs
+ * dim d), the last lhs coordinate joined with rhs coordinate batch_ndim, and
+ * output = the other lhs then the other rhs coordinates (the matmul-like
+ * calls of execute_sparse: coordinate_join + _compute_output_coords +
+ * segment_sum grouping, execution/sparse_dispatch.py:29-82, 174-223,
  * 129-171). No reference counterpart as one function: it replaces
  * es_join_plan/_fill + es_segments_plan/_fill for these shapes with no sort.
- * lhs_coords must be in lexicographic order without repeats (a relation's
- * invariant); lhs_grid / rhs_grid are the tile-grid extents.
- * plan writes counts_dev[0] = pairs P, [1] = output tiles O, [2] = 1 when the
- * lhs is not in lexicographic order (then use the general path); fill writes
- * out_coords (O, out_nd) lexicographic, seg_offsets (O+1), seg_lhs / seg_rhs
- * (P) grouped by output tile (pairs of a tile in ascending k = join order),
- * and optionally seg_strip (O) strip index and seg_key (P) the contracted k.
+ * Both coordinate arrays must be in lexicographic order without repeats (a
+ * relation's invariant); lhs_grid / rhs_grid are the tile-grid extents.
+ * plan writes counts_dev[0] = pairs P, [1] = output tiles O, [2] = 1 when a
+ * relation is not in lexicographic order (then use the general path); fill
+ * writes out_coords (O, out_nd) lexicographic, seg_offsets (O+1), seg_lhs /
+ * seg_rhs (P) grouped by output tile (pairs of a tile in ascending k = join
+ * order), and optionally seg_strip (O) strip index and seg_key (P) the
+ * contracted k. fill takes the same sizes, grids and workspace as plan (the
+ * workspace carries the plan's per-(strip, column) offsets).
  * ------------------------------------------------------------------------- */
-size_t es_direct_workspace_size(int64_t n_lhs, int lhs_ndim, int64_t n_rhs, int rhs_ndim,
+size_t es_direct_workspace_size(int64_t n_lhs, int lhs_ndim, int64_t n_rhs, int rhs_ndim, int batch_ndim,
                                 const int64_t* lhs_grid, const int64_t* rhs_grid);
 int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, const int32_t* rhs_coords,
-                   int64_t n_rhs, int rhs_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid,
+                   int64_t n_rhs, int rhs_ndim, int batch_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid,
                    void* workspace, size_t workspace_bytes, int64_t* counts_dev, int32_t* error_dev,
                    void* stream);
-int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, int rhs_ndim,
-                   const int64_t* lhs_grid, const int64_t* rhs_grid, void* workspace, size_t workspace_bytes,
-                   int64_t num_pairs, int64_t num_segments, int32_t* out_coords, int64_t* seg_offsets,
-                   int32_t* seg_lhs, int32_t* seg_rhs, int64_t* seg_strip, int32_t* seg_key, void* stream);
+int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_ndim, int64_t n_rhs, int rhs_ndim,
+                   int batch_ndim, const int64_t* lhs_grid, const int64_t* rhs_grid, void* workspace,
+                   size_t workspace_bytes, int64_t num_pairs, int64_t num_segments, int32_t* out_coords,
+                   int64_t* seg_offsets, int32_t* seg_lhs, int32_t* seg_rhs, int64_t* seg_strip, int32_t* seg_key,
+                   void* stream);
 
 /* Out tile shape of a kernel string (_infer_output_tile_shape,
  * execution/sparse_dispatch.py:506-545). Host-side; returns the out rank or

@@ -377,6 +377,16 @@ DIRECT_CASES = [
     ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (512, 768), (16, 16), (768, 640), (16, 32), 0.2, 0.3),
     ("ijk,kl->ijl", [(2, 0)], [(0, 0), (0, 1), (1, 1)], (64, 64, 128), (16, 16, 16), (128, 96), (16, 16), 0.05, 0.8),
     ("ij,j->i", [(1, 0)], [(0, 0)], (256, 512), (16, 16), (512,), (16,), 0.3, 0.7),
+    # strips longer than one 128-tile warp step, two rhs column dims
+    ("ij,jk->ik", [(1, 0)], [(0, 0), (1, 1)], (128, 16384), (16, 32), (16384, 96), (32, 32), 0.5, 0.6),
+    ("ij,jkl->ikl", [(1, 0)], [(0, 0), (1, 1), (1, 2)], (64, 4096), (8, 16), (4096, 24, 40), (16, 8, 8), 0.6, 0.3),
+    # batch dims joined pairwise (C3's shape), keys listed in either order
+    ("bij,bjk->bik", [(0, 0), (2, 1)], [(0, 0), (0, 1), (1, 2)], (4, 512, 512), (1, 32, 32), (4, 512, 384),
+     (1, 32, 32), 0.1, 0.2),
+    ("bij,bjk->bik", [(2, 1), (0, 0)], [(0, 0), (0, 1), (1, 2)], (3, 256, 2048), (1, 16, 16), (3, 2048, 64),
+     (1, 16, 16), 0.3, 0.4),
+    ("abij,abjk->abik", [(0, 0), (1, 1), (3, 2)], [(0, 0), (0, 1), (0, 2), (1, 3)], (2, 3, 128, 256),
+     (1, 1, 16, 16), (2, 3, 256, 128), (1, 1, 16, 16), 0.2, 0.3),
 ]
 
 
@@ -393,7 +403,10 @@ def test_direct_grouping_matches_sorted(case, monkeypatch):
     monkeypatch.setattr(SD, "_direct_shape", lambda *a: False)
     g = SD.plan_pairs(lhs, rhs, jk, ak)
     for name in ("out_coords", "seg_offsets", "seg_lhs", "seg_rhs", "seg_key"):
-        assert torch.equal(getattr(d, name).cpu(), getattr(g, name).cpu()), name
+        a, b = getattr(d, name), getattr(g, name)
+        assert (a is None) == (b is None), name
+        assert a is None or torch.equal(a.cpu(), b.cpu()), name
+    assert d.key_extent == g.key_extent
     # strips: same grouping of segments (labels may differ)
     ds, gs = d.seg_strip.cpu().numpy(), g.seg_strip.cpu().numpy()
     assert np.array_equal(np.diff(ds) != 0, np.diff(gs) != 0)
@@ -403,17 +416,21 @@ def test_direct_grouping_matches_sorted(case, monkeypatch):
     np.testing.assert_array_equal(res.coords.cpu().numpy(), ref.coords)
 
 
-def test_direct_grouping_unsorted_lhs_falls_back():
-    """An lhs relation out of lexicographic order takes the general path."""
+@pytest.mark.parametrize("side", ["lhs", "rhs"])
+def test_direct_grouping_unsorted_falls_back(side):
+    """A relation out of lexicographic order takes the general path."""
     from einjax_b200 import sparse_dispatch as SD
     rng = np.random.default_rng(8)
     lhs = _random_block_sparse(rng, (256, 256), (32, 32), 0.3)
     rhs = _random_block_sparse(rng, (256, 128), (32, 32), 0.5)
-    perm = rng.permutation(lhs.coords.shape[0])
-    shuffled = O.Relation(lhs.coords[perm], lhs.values[perm], lhs.shape, lhs.tile_shape)
+    rel = lhs if side == "lhs" else rhs
+    perm = rng.permutation(rel.coords.shape[0])
+    shuffled = O.Relation(rel.coords[perm], rel.values[perm], rel.shape, rel.tile_shape)
+    lhs, rhs = (shuffled, rhs) if side == "lhs" else (lhs, shuffled)
     jk, ks, ak = [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)]
-    res = E.execute_sparse(_dev(shuffled), _dev(rhs), jk, ks, ak, precision="exact")
-    ref = O.execute_sparse(shuffled, rhs, jk, ks, ak)
+    assert SD._plan_direct(_dev(lhs), _dev(rhs), jk, ak) is None
+    res = E.execute_sparse(_dev(lhs), _dev(rhs), jk, ks, ak, precision="exact")
+    ref = O.execute_sparse(lhs, rhs, jk, ks, ak)
     np.testing.assert_array_equal(res.coords.cpu().numpy(), ref.coords)
     np.testing.assert_allclose(res.values.cpu().numpy(), ref.values, rtol=1e-5, atol=1e-5)
 
@@ -460,3 +477,32 @@ def test_tensor_core_key_blocks_bf16(monkeypatch):
     res = E.execute_sparse(_dev(lhs, torch.bfloat16), _dev(rhs, torch.bfloat16), jk, ks, ak, precision="tc")
     ref = O.execute_sparse(lhs, rhs, jk, ks, ak)
     _assert_rel(res, ref, _mag(lhs, rhs, jk, ks, ak), RTOL_BF16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("tile", [(32, 32), (4, 4, 4), (3, 5)])
+def test_segment_sum_vector_path(dtype, tile):
+    """segment_sum's 4-element vector reduction (aligned rows) gives the same
+    bits as the scalar reduction (rows off a 16-byte boundary), and both
+    match the oracle's grouping and sums."""
+    from math import prod
+    g = torch.Generator().manual_seed(5)
+    n, te = 3000, prod(tile)
+    oc = torch.randint(0, 13, (n, 2), generator=g, dtype=torch.int32)
+    host = torch.randn(n, *tile, generator=g).to(dtype)
+    aligned = host.cuda()
+    buf = torch.empty(n * te + 8, dtype=dtype, device="cuda")
+    shifted = buf[1:1 + n * te].view(n, *tile)
+    shifted.copy_(aligned)
+    assert shifted.data_ptr() % 16 != 0
+    uc1, uv1 = E.segment_sum(aligned, oc.cuda())
+    uc2, uv2 = E.segment_sum(shifted, oc.cuda())
+    assert torch.equal(uc1, uc2) and torch.equal(uv1.view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
+                                                  uv2.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+    v64 = host.double().numpy()
+    rc, rv = O.segment_sum(v64, oc.numpy())
+    mag = O.segment_sum(np.abs(v64), oc.numpy())[1]
+    np.testing.assert_array_equal(uc1.cpu().numpy(), rc)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    got = uv1.float().cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(got - rv) <= tol * (np.abs(rv) + mag))
