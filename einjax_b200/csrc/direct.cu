@@ -14,12 +14,18 @@
 // into a dense ((batch, k), col) -> tile table. Output tile (strip s, column
 // c) pairs each lhs tile i of strip s whose ((batch, k)(i), c) table entry
 // exists with that rhs tile, in ascending k -- the join's order inside a
-// segment (rhs-major over an rhs in lexicographic order). One warp walks
-// strip s for column c twice: once to count the hits, and -- after an
-// exclusive scan of the (strip, column) counts gives each segment its first
-// pair -- once to write the pairs, each lane placing its hit by a ballot
-// prefix. No sort, and nothing of size pairs or (columns x lhs tiles) is
-// materialised besides the pair arrays themselves.
+// segment (rhs-major over an rhs in lexicographic order).
+//
+// Positions without a sort: the lhs tiles are cut into chunks of 32 (one
+// warp). For every present column c a warp ballots which tiles of its chunk
+// hit, giving a 32-bit hit mask per (column, chunk) and its popcount; one
+// exclusive scan of the popcounts (column-major) gives G_c(t) = hits of
+// column c among tiles [0, t) (plus a per-column constant) for any t, as the
+// chunk's scanned count plus the popcount of its mask below t. Segment
+// (s, c) then holds G_c(end s) - G_c(start s) pairs, and the pair of tile i
+// goes to offset(s, c) + G_c(i) - G_c(start s). Nothing of size pairs or
+// (columns x lhs tiles) is materialised besides the pair arrays themselves:
+// the masks are (columns x tiles / 32) words.
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -43,7 +49,11 @@ struct DirectWs {
   uint32_t* sflag;     // (T_L) strip head
   uint32_t* sexcl;     // (T_L) exclusive scan: strip of a head
   uint32_t* sstart;    // (T_L + 1) first lhs tile of each strip, then T_L
+  uint32_t* mask;      // (CB * (NCH + 1)) hit mask per (present column, 32-tile chunk), column-major
+  uint32_t* ccnt;      // (CB * (NCH + 1)) popcount of mask
+  uint32_t* cscan;     // (CB * (NCH + 1)) exclusive scan of ccnt
   uint32_t* counts;    // (SC) pairs per (strip, present column), strip-major
+  uint32_t* gstart;    // (SC) G_c(first tile of the strip)
   uint32_t* nzflag;    // (SC)
   uint32_t* segid;     // (SC) exclusive scan of nzflag
   uint32_t* off;       // (SC + 1) exclusive scan of counts
@@ -54,13 +64,18 @@ struct DirectWs {
   int32_t* bad;        // (1) a relation not in lexicographic order / repeated coordinates
 };
 
-// Upper bound of strips x present columns: strips <= min(T_L, strip extent),
-// present columns <= min(T_R, column extent).
+// Upper bound of present columns: min(T_R, column extent).
+static int64_t direct_col_bound(const DirectGeom& g, int64_t nr) { return nr < g.cext ? nr : g.cext; }
+
+// Upper bound of strips x present columns: strips <= min(T_L, strip extent).
 static int64_t direct_sc_bound(const DirectGeom& g, int64_t nl, int64_t nr) {
   const int64_t s = nl < g.sext ? nl : g.sext;
-  const int64_t c = nr < g.cext ? nr : g.cext;
-  return s * c;
+  return s * direct_col_bound(g, nr);
 }
+
+// 32-tile chunks of the lhs plus one empty chunk per column (so that
+// G_c(T_L) reads a chunk of its own when T_L is a multiple of 32).
+static int64_t direct_chunks(int64_t nl) { return (nl + 31) / 32 + 1; }
 
 template <typename C>
 static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const DirectGeom& g) {
@@ -72,11 +87,17 @@ static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const Direc
   w.sflag = c.template take<uint32_t>(nl);
   w.sexcl = c.template take<uint32_t>(nl);
   w.sstart = c.template take<uint32_t>(nl + 1);
+  const int64_t hm = direct_col_bound(g, nr) * direct_chunks(nl);
+  w.mask = c.template take<uint32_t>(hm);
+  w.ccnt = c.template take<uint32_t>(hm);
+  w.cscan = c.template take<uint32_t>(hm);
   w.counts = c.template take<uint32_t>(sc);
+  w.gstart = c.template take<uint32_t>(sc);
   w.nzflag = c.template take<uint32_t>(sc);
   w.segid = c.template take<uint32_t>(sc);
   w.off = c.template take<uint32_t>(sc + 1);
   int64_t mx = sc + 1;
+  if (hm > mx) mx = hm;
   if (g.cext > mx) mx = g.cext;
   if (nl > mx) mx = nl;
   w.scan = c.template take<uint32_t>(scan_scratch_elems(mx));
@@ -186,55 +207,79 @@ __global__ void direct_sstart_kernel(const uint32_t* __restrict__ sflag, const u
   }
 }
 
-// Lookups of one warp step: tiles base + j*32 + lane, j < kDirU, of the strip
-// [.., end). k[j] = contracted coordinate, r[j] = rhs tile joined with the
-// lhs tile for column col, or -1.
-constexpr int kDirU = 4;
-
-__device__ __forceinline__ void direct_probe(const int32_t* __restrict__ lc, const DirectGeom& g,
-                                             const int32_t* __restrict__ table, int64_t col, int64_t base,
-                                             int64_t end, int lane, int32_t (&k)[kDirU], int32_t (&r)[kDirU]) {
-  const int nd = g.lhs_nd;
-  int64_t key[kDirU];
-#pragma unroll
-  for (int j = 0; j < kDirU; ++j) {
-    const int64_t i = base + j * 32 + lane;
-    if (i < end) {
-      const int32_t* row = lc + i * nd;
-      k[j] = __ldg(row + nd - 1);
-      key[j] = g.nb == 0 ? ((k[j] >= 0 && k[j] < g.kx) ? k[j] : -1) : key_of(row, nd - 1, g);
-    } else {
-      k[j] = -1;
-      key[j] = -1;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < kDirU; ++j) r[j] = key[j] >= 0 ? __ldg(table + key[j] * g.cext + col) : -1;
+// Table lookup of a tile's key for column col: the rhs tile or -1.
+__device__ __forceinline__ int32_t direct_lookup(const DirectGeom& g, const int32_t* __restrict__ table, int64_t key,
+                                                 int64_t col) {
+  return key >= 0 ? __ldg(table + key * g.cext + col) : -1;
 }
 
-// Pairs per (strip, present column), strip-major: one warp per entry.
-__global__ void direct_counts_kernel(const int32_t* __restrict__ lc, DirectGeom g, const int32_t* __restrict__ table,
-                                     const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
-                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                     uint32_t* __restrict__ counts, uint32_t* __restrict__ nzflag) {
-  const int64_t S = *nstrips, C = *ncols;
+// Table row of lhs tile i (-1 out of range); *k = its contracted coordinate.
+__device__ __forceinline__ int64_t direct_key(const int32_t* __restrict__ lc, const DirectGeom& g, int64_t i,
+                                              int32_t* k) {
+  const int nd = g.lhs_nd;
+  const int32_t* row = lc + i * nd;
+  *k = __ldg(row + nd - 1);
+  if (g.nb == 0) return (*k >= 0 && *k < g.kx) ? *k : -1;
+  return key_of(row, nd - 1, g);
+}
+
+// Columns one warp looks up per unit of work (independent loads in flight).
+constexpr int kDirCols = 8;
+
+// Hit masks: one warp per (32-tile chunk, group of kDirCols present
+// columns); chunks run to nch inclusive, the last one past every tile.
+__global__ void direct_masks_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
+                                    const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
+                                    const uint32_t* __restrict__ ncols, int64_t nchp1, uint32_t* __restrict__ mask,
+                                    uint32_t* __restrict__ ccnt) {
+  const int64_t C = *ncols;
+  const int64_t groups = (C + kDirCols - 1) / kDirCols;
   const int lane = threadIdx.x & 31;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; e < S * C; e += nw) {
-    const int64_t s = e / C, c = e - s * C;
-    const int64_t col = colids[c];
-    const int64_t a = sstart[s], b = sstart[s + 1];
-    uint32_t n = 0;
-    for (int64_t base = a; base < b; base += 32 * kDirU) {
-      int32_t k[kDirU], r[kDirU];
-      direct_probe(lc, g, table, col, base, b, lane, k, r);
+  for (int64_t u = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; u < nchp1 * groups;
+       u += nw) {
+    const int64_t ch = u / groups, c0 = (u - ch * groups) * kDirCols;
+    const int64_t i = ch * 32 + lane;
+    int32_t k;
+    const int64_t key = i < nl ? direct_key(lc, g, i, &k) : -1;
+    int32_t r[kDirCols];
 #pragma unroll
-      for (int j = 0; j < kDirU; ++j) n += __popc(__ballot_sync(0xffffffffu, r[j] >= 0));
+    for (int j = 0; j < kDirCols; ++j)
+      r[j] = c0 + j < C ? direct_lookup(g, table, key, colids[c0 + j]) : -1;
+#pragma unroll
+    for (int j = 0; j < kDirCols; ++j) {
+      const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
+      if (lane == j && c0 + j < C) {
+        mask[(c0 + j) * nchp1 + ch] = m;
+        ccnt[(c0 + j) * nchp1 + ch] = __popc(m);
+      }
     }
-    if (lane == 0) {
-      counts[e] = n;
-      nzflag[e] = n ? 1u : 0u;
-    }
+  }
+}
+
+// G_c(t): hits of present column c among lhs tiles [0, t), plus a constant
+// per column.
+__device__ __forceinline__ uint32_t direct_g(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
+                                             int64_t nchp1, int64_t c, int64_t t) {
+  const int64_t idx = c * nchp1 + (t >> 5);
+  return cscan[idx] + __popc(mask[idx] & ((1u << (t & 31)) - 1u));
+}
+
+// Pairs per (strip, present column), strip-major, one thread per entry.
+__global__ void direct_counts_kernel(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
+                                     int64_t nchp1, const uint32_t* __restrict__ ncols,
+                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
+                                     uint32_t* __restrict__ counts, uint32_t* __restrict__ gstart,
+                                     uint32_t* __restrict__ nzflag) {
+  const int64_t S = *nstrips, C = *ncols;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t s = e / C, c = e - s * C;
+    const uint32_t ga = direct_g(mask, cscan, nchp1, c, sstart[s]);
+    const uint32_t n = direct_g(mask, cscan, nchp1, c, sstart[s + 1]) - ga;
+    counts[e] = n;
+    gstart[e] = ga;
+    nzflag[e] = n ? 1u : 0u;
   }
 }
 
@@ -255,56 +300,75 @@ __global__ void direct_totals_kernel(const uint32_t* __restrict__ off, const uin
   out[2] = *bad;
 }
 
-// Pairs of entry (strip s, present column c) in ascending lhs tile, from
-// off[e]; the first lane also writes the segment's record when it has pairs.
-// The warp of the last segment writes seg_off[O] = P.
-__global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, DirectGeom g, const int32_t* __restrict__ table,
-                                    const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
-                                    const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                    const uint32_t* __restrict__ counts, const uint32_t* __restrict__ off,
-                                    const uint32_t* __restrict__ segid, int64_t num_pairs, int64_t num_segments,
-                                    int32_t* __restrict__ seg_lhs, int32_t* __restrict__ seg_rhs,
-                                    int32_t* __restrict__ seg_key, int32_t* __restrict__ out_coords,
-                                    int64_t* __restrict__ seg_off, int64_t* __restrict__ seg_strip) {
+// Segment records: one thread per (strip, present column) with pairs.
+__global__ void direct_segments_kernel(const int32_t* __restrict__ lc, DirectGeom g,
+                                       const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
+                                       const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
+                                       const uint32_t* __restrict__ counts, const uint32_t* __restrict__ off,
+                                       const uint32_t* __restrict__ segid, int64_t num_pairs, int64_t num_segments,
+                                       int32_t* __restrict__ out_coords, int64_t* __restrict__ seg_off,
+                                       int64_t* __restrict__ seg_strip) {
   const int64_t S = *nstrips, C = *ncols;
-  const int lane = threadIdx.x & 31;
-  const uint32_t below = (1u << lane) - 1u;
   const int ncd = g.rhs_nd - 1 - g.nb;  // rhs column dims
   const int out_nd = (g.lhs_nd - 1) + ncd;
-  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t e = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; e < S * C; e += nw) {
-    if (counts[e] == 0) continue;  // warp-uniform
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (counts[e] == 0) continue;
     const int64_t s = e / C, c = e - s * C;
-    const int64_t col = colids[c];
-    const int64_t a = sstart[s], b = sstart[s + 1];
-    if (lane == 0) {
-      const int64_t o = segid[e];
-      const int32_t* row = lc + a * g.lhs_nd;
-      int32_t* oc = out_coords + o * out_nd;
-      for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
-      int64_t cl = col;
-      for (int d = ncd - 1; d >= 0; --d) {
-        oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
-        cl /= g.col_ext[d];
-      }
-      seg_off[o] = off[e];
-      if (seg_strip) seg_strip[o] = s;
-      if (o + 1 == num_segments) seg_off[num_segments] = num_pairs;
+    const int64_t o = segid[e];
+    const int32_t* row = lc + static_cast<int64_t>(sstart[s]) * g.lhs_nd;
+    int32_t* oc = out_coords + o * out_nd;
+    for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
+    int64_t cl = colids[c];
+    for (int d = ncd - 1; d >= 0; --d) {
+      oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
+      cl /= g.col_ext[d];
     }
-    int64_t pos = off[e];
-    for (int64_t base = a; base < b; base += 32 * kDirU) {
-      int32_t k[kDirU], r[kDirU];
-      direct_probe(lc, g, table, col, base, b, lane, k, r);
+    seg_off[o] = off[e];
+    if (seg_strip) seg_strip[o] = s;
+    if (o + 1 == num_segments) seg_off[num_segments] = num_pairs;
+  }
+}
+
+// Pairs: one warp per (32-tile chunk, column group) as in the mask pass; a
+// hit of tile i for column c goes to off(s, c) + G_c(i) - G_c(start s).
+__global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
+                                    const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
+                                    const uint32_t* __restrict__ ncols, int64_t nchp1,
+                                    const uint32_t* __restrict__ cscan, const uint32_t* __restrict__ sflag,
+                                    const uint32_t* __restrict__ sexcl, const uint32_t* __restrict__ off,
+                                    const uint32_t* __restrict__ gstart, int32_t* __restrict__ seg_lhs,
+                                    int32_t* __restrict__ seg_rhs, int32_t* __restrict__ seg_key) {
+  const int64_t C = *ncols;
+  const int64_t groups = (C + kDirCols - 1) / kDirCols;
+  const int lane = threadIdx.x & 31;
+  const uint32_t below = (1u << lane) - 1u;
+  const int64_t nch = nchp1 - 1;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t u = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; u < nch * groups; u += nw) {
+    const int64_t ch = u / groups, c0 = (u - ch * groups) * kDirCols;
+    const int64_t i = ch * 32 + lane;
+    int32_t k = -1;
+    int64_t key = -1, s = 0;
+    if (i < nl) {
+      key = direct_key(lc, g, i, &k);
+      s = static_cast<int64_t>(sexcl[i]) + sflag[i] - 1;
+    }
+    int32_t r[kDirCols];
 #pragma unroll
-      for (int j = 0; j < kDirU; ++j) {
-        const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
-        if (r[j] >= 0) {
-          const int64_t p = pos + __popc(m & below);
-          seg_lhs[p] = static_cast<int32_t>(base + j * 32 + lane);
-          seg_rhs[p] = r[j];
-          if (seg_key) seg_key[p] = k[j];
-        }
-        pos += __popc(m);
+    for (int j = 0; j < kDirCols; ++j)
+      r[j] = c0 + j < C ? direct_lookup(g, table, key, colids[c0 + j]) : -1;
+#pragma unroll
+    for (int j = 0; j < kDirCols; ++j) {
+      const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
+      if (r[j] >= 0) {
+        const int64_t c = c0 + j;
+        const int64_t e = s * C + c;
+        const uint32_t gi = cscan[c * nchp1 + ch] + __popc(m & below);
+        const int64_t p = static_cast<int64_t>(off[e]) + (gi - gstart[e]);
+        seg_lhs[p] = static_cast<int32_t>(i);
+        seg_rhs[p] = r[j];
+        if (seg_key) seg_key[p] = k;
       }
     }
   }
@@ -377,11 +441,19 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   ES_LAUNCH(direct_strips_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, g, w.sflag, w.bad, error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.sflag, w.sexcl, n_lhs, w.nstrips, w.scan, st));
   ES_LAUNCH(direct_sstart_kernel, grid_for(n_lhs, 256), 256, 0, st, w.sflag, w.sexcl, n_lhs, w.nstrips, w.sstart);
-  // one warp per (strip, present column); both counts live on the device,
-  // so the grid covers the upper bound and warps stride over the used part
+  // hit masks per (present column, chunk), their scan, then the per-(strip,
+  // column) counts; the column count lives on the device, so grids cover the
+  // upper bound and stride over the used part
+  const int64_t nchp1 = direct_chunks(n_lhs);
+  const int64_t cb = direct_col_bound(g, n_rhs);
   const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
-  ES_LAUNCH(direct_counts_kernel, grid_for(sc * 32, 256), 256, 0, st, lhs_coords, g, w.table, w.colids, w.ncols,
-            w.nstrips, w.sstart, w.counts, w.nzflag);
+  ES_LAUNCH(direct_masks_kernel, grid_for(nchp1 * ((cb + kDirCols - 1) / kDirCols) * 32, 256), 256, 0, st,
+            lhs_coords, n_lhs, g, w.table, w.colids, w.ncols, nchp1, w.mask, w.ccnt);
+  // column-major: entries of columns past ncols are not written and only
+  // ever enter prefixes past the used part
+  ES_TRY(exclusive_scan<uint32_t>(w.ccnt, w.cscan, cb * nchp1, w.total, w.scan, st));
+  ES_LAUNCH(direct_counts_kernel, grid_for(sc, 256), 256, 0, st, w.mask, w.cscan, nchp1, w.ncols, w.nstrips,
+            w.sstart, w.counts, w.gstart, w.nzflag);
   // the scans run over the upper bound; entries past nstrips * ncols are not
   // written and only ever enter prefixes past the used length
   ES_TRY(exclusive_scan<uint32_t>(w.counts, w.off, sc, w.total, w.scan, st));
@@ -409,9 +481,13 @@ extern "C" int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
     if (cudaMemsetAsync(seg_offsets, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
     return ES_OK;
   }
+  const int64_t nchp1 = direct_chunks(n_lhs);
+  const int64_t cb = direct_col_bound(g, n_rhs);
   const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
-  ES_LAUNCH(direct_pairs_kernel, grid_for(sc * 32, 256), 256, 0, st, lhs_coords, g, w.table, w.colids, w.ncols,
-            w.nstrips, w.sstart, w.counts, w.off, w.segid, num_pairs, num_segments, seg_lhs, seg_rhs, seg_key,
-            out_coords, seg_offsets, seg_strip);
+  ES_LAUNCH(direct_segments_kernel, grid_for(sc, 256), 256, 0, st, lhs_coords, g, w.colids, w.ncols, w.nstrips,
+            w.sstart, w.counts, w.off, w.segid, num_pairs, num_segments, out_coords, seg_offsets, seg_strip);
+  ES_LAUNCH(direct_pairs_kernel, grid_for((nchp1 - 1) * ((cb + kDirCols - 1) / kDirCols) * 32, 256), 256, 0, st,
+            lhs_coords, n_lhs, g, w.table, w.colids, w.ncols, nchp1, w.cscan, w.sflag, w.sexcl, w.off, w.gstart,
+            seg_lhs, seg_rhs, seg_key);
   return ES_OK;
 }

@@ -1,4 +1,4 @@
-// Device-wide exclusive prefix sum (reduce-then-scan, 4096 elements per CTA).
+// Device-wide exclusive prefix sum (single pass, 4096 elements per CTA).
 #pragma once
 
 #include "common.cuh"
@@ -57,27 +57,6 @@ __device__ T block_exclusive_scan_tile(T* s) {
   return grand;
 }
 
-template <typename T>
-__global__ void scan_tile_sums_kernel(const T* __restrict__ in, int64_t n, T* __restrict__ sums) {
-  __shared__ T red[kScanThreads / 32];
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
-  T acc = 0;
-  for (int i = threadIdx.x; i < kScanTile; i += kScanThreads) {
-    int64_t g = base + i;
-    if (g < n) acc += in[g];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    T v = threadIdx.x < kScanThreads / 32 ? red[threadIdx.x] : T(0);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
-    if (threadIdx.x == 0) sums[blockIdx.x] = v;
-  }
-}
-
 // Scans each tile; adds tile_offsets[blockIdx.x] (if given). Writes the
 // grand total to *total when this is a single-tile scan.
 template <typename T>
@@ -100,25 +79,110 @@ __global__ void scan_tiles_kernel(const T* in, T* out, int64_t n,
   if (total && tile_offsets == nullptr && threadIdx.x == 0) *total = grand;
 }
 
-template <typename T>
-__global__ void write_total_kernel(const T* sums_scanned, const T* sums_raw, int64_t nb, T* total) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) *total = sums_scanned[nb - 1] + sums_raw[nb - 1];
+// Single-pass scan over tiles with decoupled look-back (Merrill & Garland,
+// "Single-pass Parallel Prefix Scan with Decoupled Look-back", 2016). Each
+// CTA takes the next tile from an atomic counter -- so every earlier tile
+// belongs to a CTA that is already running, and the look-back always ends
+// -- scans it in shared memory, publishes the tile's aggregate, then walks
+// back over the status words of earlier tiles (a warp at a time, 32 tiles
+// per step) until it meets an inclusive prefix, and publishes its own.
+// Status word: flag in bits 62-63 (0 none, 1 aggregate, 2 inclusive
+// prefix), value in bits 0-61 (the sums scanned here are non-negative
+// counts, below 2^62). The wait on a tile without status is bounded: after
+// kScanSpin polls the CTA records ES_ERR_TIMEOUT and takes 0 for it.
+constexpr uint64_t kScanAgg = 1ull << 62, kScanInc = 2ull << 62, kScanVal = (1ull << 62) - 1;
+constexpr int kScanSpin = 1 << 22;
+
+__device__ int32_t g_scan_timeout;
+
+__device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Scratch elements (of T) that exclusive_scan needs for n inputs.
-inline int64_t scan_scratch_elems(int64_t n) {
-  int64_t total = 0;
-  while (n > kScanTile) {
-    int64_t nb = (n + kScanTile - 1) / kScanTile;
-    total += 2 * nb;  // raw sums + scanned sums
-    n = nb;
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__global__ void scan_lookback_kernel(const T* in, T* out, int64_t n, uint64_t* __restrict__ status,
+                                     uint32_t* __restrict__ next_tile, T* __restrict__ total, int32_t* err) {
+  __shared__ T s[kScanTile];
+  __shared__ uint32_t tile_sh;
+  __shared__ T excl_sh;
+  if (threadIdx.x == 0) tile_sh = atomicAdd(next_tile, 1u);
+  __syncthreads();
+  const int64_t tile = tile_sh;
+  const int64_t base = tile * kScanTile;
+  for (int i = threadIdx.x; i < kScanTile; i += kScanThreads) {
+    const int64_t g = base + i;
+    s[i] = g < n ? in[g] : T(0);
   }
-  return total + 1;
+  __syncthreads();
+  const T agg = block_exclusive_scan_tile<T>(s);
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    T excl = 0;
+    if (tile == 0) {
+      if (lane == 0) st_release_u64(status, kScanInc | (static_cast<uint64_t>(agg) & kScanVal));
+    } else {
+      if (lane == 0) st_release_u64(status + tile, kScanAgg | (static_cast<uint64_t>(agg) & kScanVal));
+      int64_t hi = tile - 1;  // window [hi - 31, hi], lane l reads tile hi - l
+      int spins = 0;
+      bool timed_out = false;
+      while (true) {
+        const int64_t t = hi - lane;
+        uint64_t w = t >= 0 ? ld_acquire_u64(status + t) : kScanInc;
+        const bool missing = (w >> 62) == 0;
+        if (__any_sync(0xffffffffu, missing)) {
+          if (++spins > kScanSpin) {
+            timed_out = true;
+            if (missing) w = kScanInc;  // give up: counts as 0
+          } else {
+            if (spins > 64) __nanosleep(64);
+            continue;
+          }
+        }
+        // closest inclusive prefix in the window, if any
+        const uint32_t inc = __ballot_sync(0xffffffffu, (w >> 62) == 2);
+        const int stop = inc ? __ffs(inc) - 1 : 32;
+        T v = lane <= stop ? static_cast<T>(w & kScanVal) : T(0);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        excl += v;
+        if (inc) break;
+        hi -= 32;
+      }
+      if (lane == 0) {
+        if (timed_out) atomicExch(err ? err : &g_scan_timeout, ES_ERR_TIMEOUT);
+        st_release_u64(status + tile, kScanInc | (static_cast<uint64_t>(excl + agg) & kScanVal));
+      }
+    }
+    if (lane == 0) excl_sh = excl;
+  }
+  __syncthreads();
+  const T off = excl_sh;
+  for (int i = threadIdx.x; i < kScanTile; i += kScanThreads) {
+    const int64_t g = base + i;
+    if (g < n) out[g] = s[i] + off;
+  }
+  if (total && threadIdx.x == 0 && base + kScanTile >= n) *total = off + agg;
 }
 
-// out[i] = sum(in[0..i)); *total (device, optional) = sum(in). In-place allowed.
+// Scratch elements (of T, 4 or 8 bytes) that exclusive_scan needs for n
+// inputs: one status word per tile and the tile counter.
+inline int64_t scan_scratch_elems(int64_t n) {
+  if (n <= kScanTile) return 1;
+  const int64_t nb = (n + kScanTile - 1) / kScanTile;
+  return 2 * nb + 2;
+}
+
+// out[i] = sum(in[0..i)); *total (device, optional) = sum(in). In-place
+// allowed. Inputs are non-negative. One launch (plus a clear of the tile
+// status) at any size; a look-back timeout is recorded in *err when given.
 template <typename T>
-int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStream_t st) {
+int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStream_t st, int32_t* err = nullptr) {
   if (n <= 0) {
     if (total) {
       if (cudaMemsetAsync(total, 0, sizeof(T), st) != cudaSuccess) return ES_ERR_CUDA;
@@ -129,13 +193,12 @@ int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStr
     ES_LAUNCH(scan_tiles_kernel<T>, 1, kScanThreads, 0, st, in, out, n, (const T*)nullptr, total);
     return ES_OK;
   }
-  int64_t nb = (n + kScanTile - 1) / kScanTile;
-  T* sums = scratch;
-  T* sums_scanned = scratch + nb;
-  ES_LAUNCH(scan_tile_sums_kernel<T>, (int)nb, kScanThreads, 0, st, in, n, sums);
-  ES_TRY(exclusive_scan<T>(sums, sums_scanned, nb, (T*)nullptr, scratch + 2 * nb, st));
-  if (total) ES_LAUNCH(write_total_kernel<T>, 1, 32, 0, st, (const T*)sums_scanned, (const T*)sums, nb, total);
-  ES_LAUNCH(scan_tiles_kernel<T>, (int)nb, kScanThreads, 0, st, in, out, n, (const T*)sums_scanned, (T*)nullptr);
+  const int64_t nb = (n + kScanTile - 1) / kScanTile;
+  uint64_t* status = reinterpret_cast<uint64_t*>(scratch);
+  uint32_t* next_tile = reinterpret_cast<uint32_t*>(status + nb);
+  if (cudaMemsetAsync(status, 0, nb * sizeof(uint64_t) + sizeof(uint32_t), st) != cudaSuccess) return ES_ERR_CUDA;
+  ES_LAUNCH(scan_lookback_kernel<T>, static_cast<int>(nb), kScanThreads, 0, st, in, out, n, status, next_tile, total,
+            err);
   return ES_OK;
 }
 

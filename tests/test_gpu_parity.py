@@ -79,7 +79,9 @@ def test_tiling_rejects_bad_input():
 
 @pytest.mark.parametrize("seed,shape,tile,nnz,dup", [
     (0, (256, 384), (32, 16), 3000, 0.0), (1, (64, 64, 64), (8, 4, 16), 20000, 0.2),
-    (2, (4096, 4096), (32, 32), 50000, 0.05), (3, (1000,), (8,), 400, 0.5), (4, (96, 96), (96, 96), 500, 0.1)])
+    (2, (4096, 4096), (32, 32), 50000, 0.05), (3, (1000,), (8,), 400, 0.5), (4, (96, 96), (96, 96), 500, 0.1),
+    # scans over many 4096-element tiles (several look-back windows)
+    (5, (4096, 8192), (16, 16), 1_500_000, 0.1)])
 def test_tile_coo_random(seed, shape, tile, nnz, dup):
     rng = np.random.default_rng(seed)
     idx = np.stack([rng.integers(0, s, nnz) for s in shape], 1).astype(np.int32)
@@ -506,3 +508,34 @@ def test_segment_sum_vector_path(dtype, tile):
     tol = 1e-5 if dtype == torch.float32 else 2e-2
     got = uv1.float().cpu().numpy().astype(np.float64)
     assert np.all(np.abs(got - rv) <= tol * (np.abs(rv) + mag))
+
+
+@pytest.mark.timeout(600)
+def test_c2_like_large_vs_scipy():
+    """C2's shape at 1/4 of its rows and columns: COO -> tiles -> direct join
+    -> stacked tensor-core GEMM, against scipy's float64 sparse x dense."""
+    import scipy.sparse as sp
+    rng = np.random.default_rng(21)
+    n, m, nnz = 16384, 256, 268_000
+    rows = rng.permutation(n)[np.minimum(rng.zipf(1.1, nnz) - 1, n - 1)]
+    cols = rng.integers(0, n, nnz)
+    a = sp.coo_matrix((rng.standard_normal(nnz).astype(np.float32).astype(np.float64), (rows, cols)), shape=(n, n))
+    a.sum_duplicates()
+    a = a.tocoo()
+    b = rng.standard_normal((n, m)).astype(np.float32)
+    idx = np.stack([a.row, a.col], 1).astype(np.int32)
+    A = E.SparseTensor("A", (idx, a.data.astype(np.float32), (n, n))).to_relation((32, 32))
+    B = E.SparseTensor("B", torch.from_numpy(b).cuda()).to_relation((32, 32))
+    res = E.execute_sparse(A, B, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    ref = a.tocsr() @ b.astype(np.float64)
+    mag = abs(a.tocsr()) @ np.abs(b.astype(np.float64))
+    coords, vals = res.to_numpy()
+    got = np.zeros((n, m))
+    for t, (i, j) in enumerate(coords):
+        got[i * 32:(i + 1) * 32, j * 32:(j + 1) * 32] = vals[t]
+    present = np.zeros((n // 32, m // 32), bool)
+    present[coords[:, 0], coords[:, 1]] = True
+    want = np.zeros_like(present)
+    want[np.unique(a.row // 32)[:, None], np.arange(m // 32)[None, :]] = True
+    assert np.array_equal(present, want)
+    assert np.all(np.abs(got - ref) <= 1e-5 * (np.abs(ref) + mag))
