@@ -68,6 +68,7 @@ constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 constexpr int kMaxKeyBlocks = 16;
 constexpr int kMaxMergeChunks = 64;
+constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;  // per epilogue warp a 32 x 32 fp32 block
 
 // done: 0 data stage, 1 end of a work item, 2 no more items; mask: lhs
 // slots present in a data stage (stacked mode)
@@ -106,6 +107,8 @@ struct Ctrl {
   ItemInfo item_log[kItemLog];  // items in the order this CTA takes them
   int exit_at;                  // item count at which the epilogue stops
 };
+
+constexpr int kCtrlBytes = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
 
 struct TcParams {
   TcConfig c;
@@ -361,6 +364,16 @@ __device__ void mma_role(const TcParams& p, Ctrl* ctl, const MmaArgs& m) {
     }
     const int d = __shfl_sync(0xffffffffu, ctl->ring[stage].done, 0);
     if (d) {
+      // an item without steps (or the exit mark) still hands accumulator
+      // buffer b to the epilogue: wait until the epilogue has released it,
+      // so that each of the buffer's barrier phases is consumed once
+      if ((d == 2 || first) && item_iter >= static_cast<uint32_t>(c.acc_bufs)) {
+        const uint32_t b = item_iter % c.acc_bufs;
+        if (!wait_bar_warp(&ctl->acc_empty[b], ((item_iter / c.acc_bufs) - 1) & 1u, ctl, p.err)) {
+          aborted = true;
+          break;
+        }
+      }
       if (lane == 0) {
         mbar_arrive(&ctl->empty[stage]);
         const int b = static_cast<int>(item_iter % c.acc_bufs);
@@ -528,11 +541,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const TcConfig& c = p.c;
   Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);  // after the aligned ring
+  uint8_t* epi_stg = smem + c.stages * c.stage_bytes + kCtrlBytes;      // swapped epilogue staging
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t W = *p.num_items;
 
   constexpr int NH = F32 ? 2 : 1;      // operand copies: hi (and lo)
-  constexpr int EPU = F32 ? 4 : 8;     // elements per 16-byte chunk
   constexpr int KSTEP = F32 ? 8 : 16;  // k per MMA instruction
   constexpr int ESZ = F32 ? 4 : 2;
   // both operands are K-major and swizzled: rows of W = KC * ESZ bytes,
@@ -588,10 +601,64 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     bool aborted = false;
     const int jslot = lane / NH;  // panel slot this lane copies when tiles are not consecutive
     const int jhl = lane % NH;
+    // Work items are fetched three deep so that every dependent load has a
+    // whole item's copies to complete behind: at the start of item i the
+    // queue atomic for item i+3 goes out, item i+2's metadata (record range,
+    // sub-strip) is loaded from its queue position, and item i+1's segment
+    // info and first records from its metadata.
+    int q3 = 0;  // lane 0: raw atomic result
+    int q2 = 0, q1 = 0;
+    int64_t rb2 = 0, re2 = 0, rb1 = 0, re1 = 0;
+    int ss2 = -1, ss1 = -1, s0_1 = 0, gcnt_1 = 0;
+    int ahead1[kRecAhead] = {};
+    auto load_meta = [&](int q, int64_t& rb_, int64_t& re_, int& ss_) {
+      if (q < nitems) {
+        const int64_t* ib = p.item_rec + static_cast<int64_t>(q) * (p.nblocks + 1) + p.blk;
+        rb_ = ib[0];
+        re_ = ib[1];
+        const int64_t sub = static_cast<int64_t>(q) * S + lane;
+        ss_ = (lane < S && sub < W1) ? p.order[sub] : -1;
+      }
+    };
+    auto load_info = [&]() {
+      if (q1 < nitems) {
+        s0_1 = ss1 >= 0 ? p.item_first[ss1] : 0;
+        gcnt_1 = ss1 >= 0 ? p.item_count[ss1] : 0;
+#pragma unroll
+        for (int a = 0; a < kRecAhead; ++a)
+          ahead1[a] = (lane < kRecInts && rb1 + a < re1) ? __ldg(p.recs + (rb1 + a) * kRecInts + lane) : 0;
+      }
+    };
+    // prologue: items 0 and 1 fully, item 2's position requested
+    {
+      int v0 = 0, v1 = 0;
+      if (lane == 0) {
+        v0 = atomicAdd(p.queue, 1);
+        v1 = atomicAdd(p.queue, 1);
+        q3 = atomicAdd(p.queue, 1);
+      }
+      q1 = __shfl_sync(0xffffffffu, v0, 0);
+      q2 = __shfl_sync(0xffffffffu, v1, 0);
+      load_meta(q1, rb1, re1, ss1);
+      load_meta(q2, rb2, re2, ss2);
+      load_info();
+    }
     for (uint32_t item_iter = 0; !aborted; ++item_iter) {
-      int q = 0;
-      if (lane == 0) q = atomicAdd(p.queue, 1);
-      q = __shfl_sync(0xffffffffu, q, 0);
+      // rotate: item i+1 becomes current, i+2 becomes i+1, i+3 becomes i+2
+      const int q = q1;
+      const int64_t rb = rb1, re = re1;
+      const int s0_cur = s0_1, gcnt_cur = gcnt_1;
+      int ahead[kRecAhead];
+#pragma unroll
+      for (int a = 0; a < kRecAhead; ++a) ahead[a] = ahead1[a];
+      q1 = q2;
+      rb1 = rb2;
+      re1 = re2;
+      ss1 = ss2;
+      q2 = __shfl_sync(0xffffffffu, q3, 0);
+      if (lane == 0 && q2 < nitems) q3 = atomicAdd(p.queue, 1);
+      load_meta(q2, rb2, re2, ss2);
+      load_info();
       if (q >= nitems) {
         // no more items: exit marker
         if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
@@ -605,21 +672,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         __syncwarp();
         break;
       }
-      const int64_t* ib = p.item_rec + static_cast<int64_t>(q) * (p.nblocks + 1) + p.blk;
-      const int64_t rb = ib[0], re = ib[1];
       if (lane < kMaxSlots) {
         ItemInfo& info = ctl->item_log[item_iter % kItemLog];
-        const int64_t sub = static_cast<int64_t>(q) * S + lane;
-        const bool live = lane < S && sub < W1;
-        const int ss = live ? p.order[sub] : 0;
-        info.s0[lane] = live ? p.item_first[ss] : 0;
-        info.gcnt[lane] = live ? p.item_count[ss] : 0;
+        info.s0[lane] = s0_cur;
+        info.gcnt[lane] = gcnt_cur;
         if (lane == 0) info.nsteps = static_cast<int>(re - rb);
       }
-      int ahead[kRecAhead];
-#pragma unroll
-      for (int a = 0; a < kRecAhead; ++a)
-        ahead[a] = (lane < kRecInts && rb + a < re) ? __ldg(p.recs + (rb + a) * kRecInts + lane) : 0;
       for (int64_t r = rb; r < re && !aborted; ++r) {
         const int cur = ahead[0];
 #pragma unroll
@@ -787,6 +845,92 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                   }
                 }
               }
+            }
+          }
+        } else if (c.epi_stage) {
+          // the warp's 32 panel rows are columns n0..n0+31 of one output
+          // tile g0; its 32 x 32 blocks go through shared memory so that the
+          // stores are 16-byte pieces of the tile's rows
+          const int s0 = info.s0[0], gcnt = info.gcnt[0];
+          const int r0 = h * 128 + quad * 32;
+          const int g0 = r0 / c.Nt, n0 = r0 % c.Nt;
+          if (g0 < gcnt) {
+            const int64_t row = p.seg_out ? p.seg_out[s0 + g0] : static_cast<int64_t>(s0 + g0);
+            const int64_t tile0 = row * c.Mt * c.Nt + n0;
+            float* stg = reinterpret_cast<float*>(epi_stg + (warp - kEpiWarp0) * (kEpiStageBytes / 4));
+            for (int m0 = 0; m0 < c.Mt; m0 += 32) {
+              float v[32];
+              tmem_ld32(tbase + m0, v);
+              if (c.fold) {
+                float w[32];
+                tmem_ld32(tbase + c.Mt + m0, w);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += w[j];
+              }
+              if (empty) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              }
+              const int rows = c.Mt - m0 < 32 ? c.Mt - m0 : 32;
+              if (p.odt == ES_F32) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = v[j];
+                __syncwarp();
+#pragma unroll
+                for (int it2 = 0; it2 < 8; ++it2) {
+                  const int j = it2 * 4 + (lane >> 3), piece = lane & 7;
+                  if (j < rows) {
+                    float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + tile0 +
+                                                            static_cast<int64_t>(m0 + j) * c.Nt) + piece;
+                    if (p.accumulate) {
+                      const float4 o = *dst;
+                      x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+                    }
+                    *dst = x;
+                  }
+                }
+              } else {
+                __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(stg);
+                if (p.accumulate) {
+                  // add the old values in fp32 before the one rounding
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = v[j];
+                  __syncwarp();
+#pragma unroll
+                  for (int it2 = 0; it2 < 4; ++it2) {
+                    const int j = it2 * 8 + (lane >> 2), piece = lane & 3;
+                    if (j < rows) {
+                      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
+                                                            static_cast<int64_t>(m0 + j) * c.Nt) + piece;
+                      const uint4 o = *dst;
+                      const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+                      uint32_t nw[4];
+#pragma unroll
+                      for (int q = 0; q < 4; ++q) {
+                        const float a0 = stg[j * 32 + piece * 8 + 2 * q] + __uint_as_float(ow[q] << 16);
+                        const float a1 = stg[j * 32 + piece * 8 + 2 * q + 1] + __uint_as_float(ow[q] & 0xFFFF0000u);
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(a0, a1);
+                        nw[q] = *reinterpret_cast<const uint32_t*>(&b2);
+                      }
+                      *dst = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+                    }
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) sb16[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+                  __syncwarp();
+#pragma unroll
+                  for (int it2 = 0; it2 < 4; ++it2) {
+                    const int j = it2 * 8 + (lane >> 2), piece = lane & 3;
+                    if (j < rows)
+                      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
+                                               static_cast<int64_t>(m0 + j) * c.Nt)[piece] =
+                          reinterpret_cast<const uint4*>(sb16 + j * 32)[piece];
+                  }
+                }
+              }
+              __syncwarp();
             }
           }
         } else {
@@ -1221,7 +1365,7 @@ std::vector<int64_t> group_offsets(const EinGroup& g, int which) {
 // panel tile must start on a 1024-byte boundary. False when no chunk fits.
 bool pick_stages(int lhs_rows, int mt, int pan_rows, int nt, int Kt, bool f32, TcConfig* c) {
   const int esz = f32 ? 4 : 2, nh = f32 ? 2 : 1, kstep = f32 ? 8 : 16;
-  const int ctrl = static_cast<int>((sizeof(Ctrl) + 127) / 128 * 128);
+  const int ctrl = kCtrlBytes + (c->epi_stage ? kEpiStageBytes : 0);
   const int budget = 227 * 1024 - ctrl - 1024;  // 1024: alignment of the stage ring
   for (int min_stages : {3, 2}) {
     for (int kc : {64, 32, 16, 8}) {
@@ -1314,8 +1458,12 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   } else if (Mt % 16 == 0 && Mt <= 256 && Mt >= 16) {
     c->swap = 1;
     c->n_mma = Mt;
+    c->epi_stage = Nt % 32 == 0 ? 1 : 0;
     int G = 0;
-    if (256 % Nt == 0 && 256 / Nt <= kMaxG && (have_strips || 256 / Nt == 1)) {
+    // EINSPARSE_TC_MAXG caps the rhs tiles per item (tuning experiments)
+    const char* gcap = std::getenv("EINSPARSE_TC_MAXG");
+    const int maxg = gcap ? std::atoi(gcap) : kMaxG;
+    if (256 % Nt == 0 && 256 / Nt <= kMaxG && 256 / Nt <= maxg && (have_strips || 256 / Nt == 1)) {
       G = 256 / Nt;
       c->halves = 2;
     } else if (128 % Nt == 0 && 128 / Nt <= kMaxG && (have_strips || 128 / Nt == 1)) {
@@ -1435,6 +1583,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   // 5. persistent tensor-core kernel, one CTA per SM
   TcParams prm;
   prm.c = c;
+  // the staged epilogue stores 16-byte pieces (its shared memory stays reserved)
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) prm.c.epi_stage = 0;
   prm.lhs = static_cast<const uint8_t*>(lhs);
   prm.lhs_rows = lhs_rows;
   prm.pan_hi = w.pan_hi;

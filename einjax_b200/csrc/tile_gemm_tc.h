@@ -30,6 +30,9 @@ struct TcConfig {
   int lhs_bytes;   // one operand copy of a stage's lhs chunk (all slots)
   int pan_bytes;   // one operand copy of a stage's panel chunk
   int stage_bytes;
+  int epi_stage;   // swapped epilogue through shared memory (Nt % 32 == 0): each epilogue
+                   // warp transposes its 32 panel rows x 32 lhs rows block and stores
+                   // 16-byte row pieces of the output tile
   int smem_bytes;  // dynamic shared memory per CTA
 };
 
