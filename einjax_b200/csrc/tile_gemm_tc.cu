@@ -68,7 +68,6 @@ constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 constexpr int kMaxKeyBlocks = 16;
 constexpr int kMaxMergeChunks = 64;
-constexpr int kEpiStageBytes = 4 * 32 * 32 * 4;  // per epilogue warp a 32 x 32 fp32 block
 
 // done: 0 data stage, 1 end of a work item, 2 no more items; mask: lhs
 // slots present in a data stage (stacked mode)
@@ -245,6 +244,33 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// tcgen05.ld without the wait: the registers are valid only after
+// tmem_wait32 on the same array (which names them, so the compiler cannot
+// read them earlier).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major operand in a swizzled layout
@@ -532,6 +558,128 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
   }
 }
 
+// Swapped epilogue through shared memory (TcConfig::epi_stage): accumulator
+// row r = h * 128 + 32 * quad + lane is column n of output tile g = r / Nt,
+// and its TMEM columns are the tile's rows m. Per 32 x 32 block the warp
+// writes its columns into shared memory (stg: 4 KB for fp32 output, 2 KB for
+// bf16) and reads back 16-byte pieces of rows, which it stores (or adds)
+// into the output tile.
+__device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_t (&r)[32], int64_t tile0, int m0,
+                                                bool empty, float* stg, int lane) {
+  const TcConfig& c = p.c;
+  const int rows = c.Mt - m0 < 32 ? c.Mt - m0 : 32;
+  if (p.odt == ES_F32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = empty ? 0.f : __uint_as_float(r[j]);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int j = it * 4 + (lane >> 3), piece = lane & 7;
+      if (j < rows) {
+        float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
+        float4* dst =
+            reinterpret_cast<float4*>(static_cast<float*>(p.out) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt) +
+            piece;
+        if (p.accumulate) {
+          const float4 o = *dst;
+          x.x += o.x;
+          x.y += o.y;
+          x.z += o.z;
+          x.w += o.w;
+        }
+        *dst = x;
+      }
+    }
+  } else if (p.accumulate) {
+    // add the old values in fp32 before the one rounding: two passes of 16
+    // rows through the 2 KB staging area
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) stg[j * 32 + lane] = empty ? 0.f : __uint_as_float(r[pass * 16 + j]);
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {
+        const int j = it * 8 + (lane >> 2), piece = lane & 3;
+        if (pass * 16 + j < rows) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
+                                                static_cast<int64_t>(m0 + pass * 16 + j) * c.Nt) +
+                       piece;
+          const uint4 o = *dst;
+          const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+          uint32_t nw[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a0 = stg[j * 32 + piece * 8 + 2 * q] + __uint_as_float(ow[q] << 16);
+            const float a1 = stg[j * 32 + piece * 8 + 2 * q + 1] + __uint_as_float(ow[q] & 0xFFFF0000u);
+            const __nv_bfloat162 b2 = __floats2bfloat162_rn(a0, a1);
+            nw[q] = *reinterpret_cast<const uint32_t*>(&b2);
+          }
+          *dst = make_uint4(nw[0], nw[1], nw[2], nw[3]);
+        }
+      }
+      __syncwarp();
+    }
+    return;
+  } else {
+    __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(stg);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sb16[j * 32 + lane] = __float2bfloat16_rn(empty ? 0.f : __uint_as_float(r[j]));
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int j = it * 8 + (lane >> 2), piece = lane & 3;
+      if (j < rows)
+        reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt)
+            [piece] = reinterpret_cast<const uint4*>(sb16 + j * 32)[piece];
+    }
+  }
+  __syncwarp();
+}
+
+// The blocks t0, t0 + tstep, ... (block t: half t / nmb, lhs rows 32 (t %
+// nmb)..) of one item for one epilogue warp; with two epilogue groups each
+// takes every other block. tacc: the accumulator's first column, in this
+// warp's TMEM lane quadrant. The next block's TMEM load is in flight while
+// a block is stored.
+__device__ void epi_swap_staged(const TcParams& p, const ItemInfo& info, uint32_t tacc, int quad, int lane,
+                                float* stg, bool empty, int t0, int tstep) {
+  const TcConfig& c = p.c;
+  const int s0 = info.s0[0], gcnt = info.gcnt[0];
+  const int nmb = (c.Mt + 31) / 32;
+  const int nblk = c.halves * nmb;
+  uint32_t ra[32], rb[32];
+  // per half: the output tile's column-n0 offset, or -1 when the warp's
+  // rows are past the item's segments
+  int64_t t0a = -1, t0b = -1;
+  for (int h = 0; h < c.halves; ++h) {
+    const int r0 = h * 128 + quad * 32;
+    const int g0 = r0 / c.Nt;
+    if (g0 < gcnt) {
+      const int64_t row = p.seg_out ? p.seg_out[s0 + g0] : static_cast<int64_t>(s0 + g0);
+      (h == 0 ? t0a : t0b) = row * c.Mt * c.Nt + r0 % c.Nt;
+    }
+  }
+  auto tile_of = [&](int t) { return t / nmb == 0 ? t0a : t0b; };
+  auto addr = [&](int t) {
+    return tacc + static_cast<uint32_t>((t / nmb) * c.col_per_half + (t % nmb) * 32);
+  };
+  if (t0 >= nblk) return;
+  tmem_ld32_async(addr(t0), ra);
+  tmem_wait32(ra);
+  for (int t = t0; t < nblk; t += 2 * tstep) {
+    const int u = t + tstep;
+    if (u < nblk) tmem_ld32_async(addr(u), rb);
+    if (tile_of(t) >= 0) epi_store_block(p, ra, tile_of(t), (t % nmb) * 32, empty, stg, lane);
+    if (u < nblk) {
+      tmem_wait32(rb);
+      if (u + tstep < nblk) tmem_ld32_async(addr(u + tstep), ra);
+      if (tile_of(u) >= 0) epi_store_block(p, rb, tile_of(u), (u % nmb) * 32, empty, stg, lane);
+      if (u + tstep < nblk) tmem_wait32(ra);
+    }
+  }
+}
+
 template <bool F32>
 __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                                                                const __grid_constant__ CUtensorMap lhs_map) {
@@ -542,6 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
   const TcConfig& c = p.c;
   Ctrl* ctl = reinterpret_cast<Ctrl*>(smem + c.stages * c.stage_bytes);  // after the aligned ring
   uint8_t* epi_stg = smem + c.stages * c.stage_bytes + kCtrlBytes;      // swapped epilogue staging
+  const bool dual = !F32 && c.epi_stage && c.epi_dual;  // warps 0-3: second epilogue group
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t W = *p.num_items;
 
@@ -572,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&ctl->acc_full[b], 1);
-      mbar_init(&ctl->acc_empty[b], kEpilogue);
+      mbar_init(&ctl->acc_empty[b], dual ? 2 * kEpilogue : kEpilogue);
     }
     mbar_init(&ctl->drain, 1);
     ctl->abort = 0;
@@ -601,6 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     bool aborted = false;
     const int jslot = lane / NH;  // panel slot this lane copies when tiles are not consecutive
     const int jhl = lane % NH;
+    uint64_t zmask = 0;  // bit stage * kMaxG + g: panel slot g of the stage holds zeros (bf16)
     // Work items are fetched three deep so that every dependent load has a
     // whole item's copies to complete behind: at the start of item i the
     // queue atomic for item i+3 goes out, item i+2's metadata (record range,
@@ -678,12 +828,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         info.gcnt[lane] = gcnt_cur;
         if (lane == 0) info.nsteps = static_cast<int>(re - rb);
       }
-      for (int64_t r = rb; r < re && !aborted; ++r) {
-        const int cur = ahead[0];
+      // ahead[] is a ring indexed at compile time (the loop below is
+      // unrolled by kRecAhead): record r sits in ahead[r % kRecAhead] and is
+      // replaced by record r + kRecAhead as soon as it is read, so no step
+      // waits on the load issued by the step before it
+      for (int64_t r = rb; r < re && !aborted;) {
 #pragma unroll
-        for (int a = 0; a + 1 < kRecAhead; ++a) ahead[a] = ahead[a + 1];
-        ahead[kRecAhead - 1] =
-            (lane < kRecInts && r + kRecAhead < re) ? __ldg(p.recs + (r + kRecAhead) * kRecInts + lane) : 0;
+        for (int a = 0; a < kRecAhead; ++a) {
+        if (r >= re || aborted) break;
+        const int cur = ahead[a];
+        ahead[a] = (lane < kRecInts && r + kRecAhead < re) ? __ldg(p.recs + (r + kRecAhead) * kRecInts + lane) : 0;
+        ++r;
         const int my_lhs = __shfl_sync(0xffffffffu, cur, lane & (kMaxSlots - 1));  // lanes < S: slot lane
         const int flags = __shfl_sync(0xffffffffu, cur, S + G);
         const int rhs0 = __shfl_sync(0xffffffffu, cur, S + G + 1);
@@ -695,6 +850,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         const uint32_t lhs_tx = F32 ? static_cast<uint32_t>(__popc(mask)) * static_cast<uint32_t>(slot_bytes)
                                     : static_cast<uint32_t>(c.lhs_bytes);
         const bool consec = (flags & 1) != 0;
+        // bf16, scattered rhs tiles: absent panel slots are zero-filled in
+        // shared memory by this warp (and left alone when the stage's slot
+        // already holds zeros) instead of copied from the zero buffer
+        const bool zfill = !F32 && !consec;
+        const uint32_t present =
+            zfill ? __ballot_sync(0xffffffffu, lane < G && my_rhs >= 0 && my_rhs < p.rhs_rows) : 0u;
+        const uint32_t absent = zfill ? (((1u << G) - 1u) & ~present) : 0u;
+        const uint32_t pan_tx =
+            zfill ? static_cast<uint32_t>(__popc(present) * blk_bytes) : static_cast<uint32_t>(G * NH * blk_bytes);
         for (int chunk = 0; chunk < nchunks; ++chunk) {
           if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
             aborted = true;
@@ -702,10 +866,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           }
           const int k0 = chunk * c.KC;
           uint8_t* sbase = smem + stage * c.stage_bytes;
+          if (zfill) {
+            const int sh = stage * kMaxG;
+            uint32_t need = absent & ~static_cast<uint32_t>((zmask >> sh) & 0xFFull);
+            zmask = (zmask & ~(0xFFull << sh)) | (static_cast<uint64_t>(absent) << sh);
+            if (need) {
+              while (need) {
+                const int g = __ffs(need) - 1;
+                need &= need - 1;
+                uint4* z = reinterpret_cast<uint4*>(sbase + off_pan + g * blk_bytes);
+                for (int i = lane; i < blk_bytes / 16; i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
+              }
+              fence_proxy_async();  // the MMAs read these zeros through the async proxy
+              __syncwarp();
+            }
+          }
           if (lane == 0) {
             ctl->ring[stage].done = 0;
             ctl->ring[stage].mask = static_cast<int>(mask);
-            mbar_arrive_expect_tx(&ctl->copy[stage], lhs_tx + static_cast<uint32_t>(G * NH * blk_bytes));
+            mbar_arrive_expect_tx(&ctl->copy[stage], lhs_tx + pan_tx);
           }
           __syncwarp();
           // raw lhs chunk of slot s straight into the canonical K-major
@@ -723,9 +902,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                        static_cast<uint32_t>(G * blk_bytes), &ctl->copy[stage]);
           } else if (lane < G * NH) {
             const bool ok = my_rhs >= 0 && my_rhs < p.rhs_rows;
-            bulk_g2s(sbase + off_pan + jhl * c.pan_bytes + jslot * blk_bytes,
-                     ok ? (jhl ? p.pan_lo : p.pan_hi) + (cbase + my_rhs) * blk_bytes : p.zeros,
-                     static_cast<uint32_t>(blk_bytes), &ctl->copy[stage]);
+            if (ok || !zfill)
+              bulk_g2s(sbase + off_pan + jhl * c.pan_bytes + jslot * blk_bytes,
+                       ok ? (jhl ? p.pan_lo : p.pan_hi) + (cbase + my_rhs) * blk_bytes : p.zeros,
+                       static_cast<uint32_t>(blk_bytes), &ctl->copy[stage]);
           }
           __syncwarp();
           ++it;
@@ -733,6 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             stage = 0;
             ph ^= 1u;
           }
+        }
         }
       }
       if (aborted) break;
@@ -758,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       for (uint32_t i = it > n ? it - n : 0u; i < it; ++i) drain_bar(&ctl->copy[i % n], (i / n) & 1u);
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else if (warp < 4 && !dual) {
     // ----------------------------------------- fp32 split of the lhs chunk
     if constexpr (F32) {
       const int nf = c.lhs_bytes / 16;  // 16-byte chunks of the lhs operand (all slots)
@@ -793,9 +974,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     } else {
       mma_dispatch<false, false>(p, ctl, m, ksteps, c.halves);
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+  } else if ((warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) || warp < 4) {
     // ---------------------------------------------------------- epilogue
+    // group 0: warps 6-9; group 1 (dual only): warps 0-3
     const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
+    const int grp = warp < 4 ? 1 : 0;
+    float* stg = reinterpret_cast<float*>(epi_stg + (grp * 4 + quad) * c.epi_warp_bytes);
     for (uint32_t item_iter = 0;; ++item_iter) {
       const uint32_t b = item_iter % c.acc_bufs;
       if (!wait_bar(&ctl->acc_full[b], (item_iter / c.acc_bufs) & 1u, ctl, p.err, &ctl->progress, kEpiSleepNs)) break;
@@ -848,91 +1032,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             }
           }
         } else if (c.epi_stage) {
-          // the warp's 32 panel rows are columns n0..n0+31 of one output
-          // tile g0; its 32 x 32 blocks go through shared memory so that the
-          // stores are 16-byte pieces of the tile's rows
-          const int s0 = info.s0[0], gcnt = info.gcnt[0];
-          const int r0 = h * 128 + quad * 32;
-          const int g0 = r0 / c.Nt, n0 = r0 % c.Nt;
-          if (g0 < gcnt) {
-            const int64_t row = p.seg_out ? p.seg_out[s0 + g0] : static_cast<int64_t>(s0 + g0);
-            const int64_t tile0 = row * c.Mt * c.Nt + n0;
-            float* stg = reinterpret_cast<float*>(epi_stg + (warp - kEpiWarp0) * (kEpiStageBytes / 4));
-            for (int m0 = 0; m0 < c.Mt; m0 += 32) {
-              float v[32];
-              tmem_ld32(tbase + m0, v);
-              if (c.fold) {
-                float w[32];
-                tmem_ld32(tbase + c.Mt + m0, w);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += w[j];
-              }
-              if (empty) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = 0.f;
-              }
-              const int rows = c.Mt - m0 < 32 ? c.Mt - m0 : 32;
-              if (p.odt == ES_F32) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = v[j];
-                __syncwarp();
-#pragma unroll
-                for (int it2 = 0; it2 < 8; ++it2) {
-                  const int j = it2 * 4 + (lane >> 3), piece = lane & 7;
-                  if (j < rows) {
-                    float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + tile0 +
-                                                            static_cast<int64_t>(m0 + j) * c.Nt) + piece;
-                    if (p.accumulate) {
-                      const float4 o = *dst;
-                      x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-                    }
-                    *dst = x;
-                  }
-                }
-              } else {
-                __nv_bfloat16* sb16 = reinterpret_cast<__nv_bfloat16*>(stg);
-                if (p.accumulate) {
-                  // add the old values in fp32 before the one rounding
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = v[j];
-                  __syncwarp();
-#pragma unroll
-                  for (int it2 = 0; it2 < 4; ++it2) {
-                    const int j = it2 * 8 + (lane >> 2), piece = lane & 3;
-                    if (j < rows) {
-                      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
-                                                            static_cast<int64_t>(m0 + j) * c.Nt) + piece;
-                      const uint4 o = *dst;
-                      const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-                      uint32_t nw[4];
-#pragma unroll
-                      for (int q = 0; q < 4; ++q) {
-                        const float a0 = stg[j * 32 + piece * 8 + 2 * q] + __uint_as_float(ow[q] << 16);
-                        const float a1 = stg[j * 32 + piece * 8 + 2 * q + 1] + __uint_as_float(ow[q] & 0xFFFF0000u);
-                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(a0, a1);
-                        nw[q] = *reinterpret_cast<const uint32_t*>(&b2);
-                      }
-                      *dst = make_uint4(nw[0], nw[1], nw[2], nw[3]);
-                    }
-                  }
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) sb16[j * 32 + lane] = __float2bfloat16_rn(v[j]);
-                  __syncwarp();
-#pragma unroll
-                  for (int it2 = 0; it2 < 4; ++it2) {
-                    const int j = it2 * 8 + (lane >> 2), piece = lane & 3;
-                    if (j < rows)
-                      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
-                                               static_cast<int64_t>(m0 + j) * c.Nt)[piece] =
-                          reinterpret_cast<const uint4*>(sb16 + j * 32)[piece];
-                  }
-                }
-              }
-              __syncwarp();
-            }
-          }
+          // all halves at once (see epi_swap_staged)
+          if (h == 0)
+            epi_swap_staged(p, info, tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride, quad, lane,
+                            stg, empty, grp, dual ? 2 : 1);
         } else {
           const int s0 = info.s0[0], gcnt = info.gcnt[0];
           const int r = h * 128 + quad * 32 + lane;  // panel row = (g, n)
@@ -1078,11 +1181,21 @@ __global__ void item_work_keys_kernel(const int32_t* __restrict__ first, const i
                                       int64_t nslots, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
   const int64_t W = *num_items;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nslots; i += (int64_t)gridDim.x * blockDim.x) {
-    uint32_t key = 0xFFFFFFFFu;
+    // 8-bit key, largest work first: half-octave buckets of the pair count
+    // (bit length and the next bit), so one stable radix pass orders them;
+    // empty items and padding slots go last
+    uint32_t key = 0xFFu;
     if (i < W) {
       const int s0 = first[i], g = count[i];
       const int64_t work = seg_off[s0 + g] - seg_off[s0];
-      key = 0xFFFFFFFEu - static_cast<uint32_t>(work < 0xFFFFFFFEll ? work : 0xFFFFFFFEll);
+      if (work > 0) {
+        const int b = 64 - __clzll(static_cast<unsigned long long>(work));
+        const int frac = b >= 2 ? static_cast<int>((work >> (b - 2)) & 1) : 0;
+        const int level = 2 * b + frac;  // 2 .. 129
+        key = static_cast<uint32_t>(250 - level);
+      } else {
+        key = 0xFEu;
+      }
     }
     keys[i] = key;
     vals[i] = static_cast<uint32_t>(i);
@@ -1365,7 +1478,7 @@ std::vector<int64_t> group_offsets(const EinGroup& g, int which) {
 // panel tile must start on a 1024-byte boundary. False when no chunk fits.
 bool pick_stages(int lhs_rows, int mt, int pan_rows, int nt, int Kt, bool f32, TcConfig* c) {
   const int esz = f32 ? 4 : 2, nh = f32 ? 2 : 1, kstep = f32 ? 8 : 16;
-  const int ctrl = kCtrlBytes + (c->epi_stage ? kEpiStageBytes : 0);
+  const int ctrl = kCtrlBytes + (c->epi_stage ? (c->epi_dual ? 8 : 4) * c->epi_warp_bytes : 0);
   const int budget = 227 * 1024 - ctrl - 1024;  // 1024: alignment of the stage ring
   for (int min_stages : {3, 2}) {
     for (int kc : {64, 32, 16, 8}) {
@@ -1458,7 +1571,6 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
   } else if (Mt % 16 == 0 && Mt <= 256 && Mt >= 16) {
     c->swap = 1;
     c->n_mma = Mt;
-    c->epi_stage = Nt % 32 == 0 ? 1 : 0;
     int G = 0;
     // EINSPARSE_TC_MAXG caps the rhs tiles per item (tuning experiments)
     const char* gcap = std::getenv("EINSPARSE_TC_MAXG");
@@ -1477,6 +1589,9 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
     return false;
   }
   c->fold = (f32 && c->swap && Mt % 32 == 0 && 2 * Mt <= 256) ? 1 : 0;
+  c->epi_stage = (c->swap && !c->fold && Nt % 32 == 0) ? 1 : 0;
+  c->epi_dual = (c->epi_stage && !f32) ? 1 : 0;
+  c->epi_warp_bytes = odt == ES_BF16 ? 2048 : 4096;
   c->col_per_half = c->swap ? (c->fold ? 2 * Mt : Mt) : c->n_mma;
   const int acc_cols = c->halves * c->col_per_half;
   if (acc_cols > 512) return false;
@@ -1553,7 +1668,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   {
     uint32_t* k = w.sort_keys;
     uint32_t* v = w.order;
-    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 32, st));
+    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st));
     if (v != w.order &&
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;
@@ -1584,7 +1699,10 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   TcParams prm;
   prm.c = c;
   // the staged epilogue stores 16-byte pieces (its shared memory stays reserved)
-  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) prm.c.epi_stage = 0;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) {
+    prm.c.epi_stage = 0;
+    prm.c.epi_dual = 0;
+  }
   prm.lhs = static_cast<const uint8_t*>(lhs);
   prm.lhs_rows = lhs_rows;
   prm.pan_hi = w.pan_hi;

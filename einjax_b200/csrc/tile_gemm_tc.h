@@ -33,6 +33,9 @@ struct TcConfig {
   int epi_stage;   // swapped epilogue through shared memory (Nt % 32 == 0): each epilogue
                    // warp transposes its 32 panel rows x 32 lhs rows block and stores
                    // 16-byte row pieces of the output tile
+  int epi_dual;    // bf16 operands with the staged epilogue: warps 0-3 (idle without the fp32
+                   // split) form a second epilogue group; the groups take alternate blocks
+  int epi_warp_bytes;  // staging bytes per epilogue warp (2 KB for bf16 output, 4 KB for fp32)
   int smem_bytes;  // dynamic shared memory per CTA
 };
 
