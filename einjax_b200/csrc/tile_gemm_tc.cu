@@ -368,6 +368,15 @@ struct MmaArgs {
   uint32_t idesc, idesc2;
 };
 
+// Waits (warp-wide) until the epilogue has released the accumulator buffer
+// that item item_iter will use; false when the CTA aborted. Kept out of line:
+// it only runs for items without steps and at the exit mark.
+__device__ __noinline__ bool acc_released(Ctrl* ctl, int32_t* err, uint32_t item_iter, int acc_bufs) {
+  if (item_iter < static_cast<uint32_t>(acc_bufs)) return true;
+  const uint32_t b = item_iter % acc_bufs;
+  return wait_bar_warp(&ctl->acc_empty[b], ((item_iter / acc_bufs) - 1) & 1u, ctl, err);
+}
+
 // MMA warp. The whole warp runs this loop on identical values; one elected
 // lane issues each MMA. The issue order of a stage is fixed at compile time
 // (FOLD, KS k-steps, H halves): with runtime branches between the MMAs each
@@ -389,16 +398,13 @@ __device__ void mma_role(const TcParams& p, Ctrl* ctl, const MmaArgs& m) {
       break;
     }
     const int d = __shfl_sync(0xffffffffu, ctl->ring[stage].done, 0);
-    if (d) {
+    if (__builtin_expect(d != 0, 0)) {
       // an item without steps (or the exit mark) still hands accumulator
       // buffer b to the epilogue: wait until the epilogue has released it,
       // so that each of the buffer's barrier phases is consumed once
-      if ((d == 2 || first) && item_iter >= static_cast<uint32_t>(c.acc_bufs)) {
-        const uint32_t b = item_iter % c.acc_bufs;
-        if (!wait_bar_warp(&ctl->acc_empty[b], ((item_iter / c.acc_bufs) - 1) & 1u, ctl, p.err)) {
-          aborted = true;
-          break;
-        }
+      if ((d == 2 || first) && !acc_released(ctl, p.err, item_iter, c.acc_bufs)) {
+        aborted = true;
+        break;
       }
       if (lane == 0) {
         mbar_arrive(&ctl->empty[stage]);
@@ -751,64 +757,88 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     const int jslot = lane / NH;  // panel slot this lane copies when tiles are not consecutive
     const int jhl = lane % NH;
     uint64_t zmask = 0;  // bit stage * kMaxG + g: panel slot g of the stage holds zeros (bf16)
-    // Work items are fetched three deep so that every dependent load has a
-    // whole item's copies to complete behind: at the start of item i the
-    // queue atomic for item i+3 goes out, item i+2's metadata (record range,
-    // sub-strip) is loaded from its queue position, and item i+1's segment
-    // info and first records from its metadata.
-    int q3 = 0;  // lane 0: raw atomic result
-    int q2 = 0, q1 = 0;
-    int64_t rb2 = 0, re2 = 0, rb1 = 0, re1 = 0;
-    int ss2 = -1, ss1 = -1, s0_1 = 0, gcnt_1 = 0;
-    int ahead1[kRecAhead] = {};
-    auto load_meta = [&](int q, int64_t& rb_, int64_t& re_, int& ss_) {
-      if (q < nitems) {
-        const int64_t* ib = p.item_rec + static_cast<int64_t>(q) * (p.nblocks + 1) + p.blk;
+    // Work-item prefetch. With many items per CTA (deep) the queue position
+    // of item i+2 is claimed at the start of item i and the metadata and
+    // first records follow one item behind, so every dependent load has a
+    // whole item's copies to complete behind. With few items per CTA a
+    // claim held that long unbalances the largest-first queue, so the next
+    // item is claimed during the current item's last kRecAhead steps and its
+    // metadata and records are loaded at the item's end.
+    const bool deep = nitems >= 16 * static_cast<int64_t>(gridDim.x);
+    int nq_raw = 0;  // lane 0: raw atomic result
+    int nq = 0, n_ss = -1, n_s0 = 0, n_gcnt = 0, pf = 0;  // next item (A)
+    int64_t n_rb = 0, n_re = 0;
+    int n_ahead[kRecAhead] = {};
+    int bq = 0, b_ss = -1;  // deep: the item after next (B)
+    int64_t b_rb = 0, b_re = 0;
+    auto load_meta = [&](int q_, int64_t& rb_, int64_t& re_, int& ss_) {
+      if (q_ < nitems) {
+        const int64_t* ib = p.item_rec + static_cast<int64_t>(q_) * (p.nblocks + 1) + p.blk;
         rb_ = ib[0];
         re_ = ib[1];
-        const int64_t sub = static_cast<int64_t>(q) * S + lane;
+        const int64_t sub = static_cast<int64_t>(q_) * S + lane;
         ss_ = (lane < S && sub < W1) ? p.order[sub] : -1;
       }
     };
     auto load_info = [&]() {
-      if (q1 < nitems) {
-        s0_1 = ss1 >= 0 ? p.item_first[ss1] : 0;
-        gcnt_1 = ss1 >= 0 ? p.item_count[ss1] : 0;
+      if (nq < nitems) {
+        n_s0 = n_ss >= 0 ? p.item_first[n_ss] : 0;
+        n_gcnt = n_ss >= 0 ? p.item_count[n_ss] : 0;
 #pragma unroll
         for (int a = 0; a < kRecAhead; ++a)
-          ahead1[a] = (lane < kRecInts && rb1 + a < re1) ? __ldg(p.recs + (rb1 + a) * kRecInts + lane) : 0;
+          n_ahead[a] = (lane < kRecInts && n_rb + a < n_re) ? __ldg(p.recs + (n_rb + a) * kRecInts + lane) : 0;
       }
     };
-    // prologue: items 0 and 1 fully, item 2's position requested
-    {
+    auto pf_advance = [&]() {  // shallow mode: one stage for the next item
+      if (pf == 0) {
+        if (lane == 0) nq_raw = atomicAdd(p.queue, 1);
+      } else if (pf == 1) {
+        nq = __shfl_sync(0xffffffffu, nq_raw, 0);
+        load_meta(nq, n_rb, n_re, n_ss);
+      } else if (pf == 2) {
+        load_info();
+      }
+      ++pf;
+    };
+    if (deep) {
       int v0 = 0, v1 = 0;
       if (lane == 0) {
         v0 = atomicAdd(p.queue, 1);
         v1 = atomicAdd(p.queue, 1);
-        q3 = atomicAdd(p.queue, 1);
+        nq_raw = atomicAdd(p.queue, 1);
       }
-      q1 = __shfl_sync(0xffffffffu, v0, 0);
-      q2 = __shfl_sync(0xffffffffu, v1, 0);
-      load_meta(q1, rb1, re1, ss1);
-      load_meta(q2, rb2, re2, ss2);
+      nq = __shfl_sync(0xffffffffu, v0, 0);
+      bq = __shfl_sync(0xffffffffu, v1, 0);
+      load_meta(nq, n_rb, n_re, n_ss);
+      load_meta(bq, b_rb, b_re, b_ss);
       load_info();
+    } else {
+      pf_advance();
+      pf_advance();
+      pf_advance();
     }
-    for (uint32_t item_iter = 0; !aborted; ++item_iter) {
-      // rotate: item i+1 becomes current, i+2 becomes i+1, i+3 becomes i+2
-      const int q = q1;
-      const int64_t rb = rb1, re = re1;
-      const int s0_cur = s0_1, gcnt_cur = gcnt_1;
+    // item_iter counts the items handed to the MMA warp and the epilogue
+    for (uint32_t item_iter = 0; !aborted;) {
+      const int q = nq;
+      const int64_t rb = n_rb, re = n_re;
+      const int s0_cur = n_s0, gcnt_cur = n_gcnt;
       int ahead[kRecAhead];
 #pragma unroll
-      for (int a = 0; a < kRecAhead; ++a) ahead[a] = ahead1[a];
-      q1 = q2;
-      rb1 = rb2;
-      re1 = re2;
-      ss1 = ss2;
-      q2 = __shfl_sync(0xffffffffu, q3, 0);
-      if (lane == 0 && q2 < nitems) q3 = atomicAdd(p.queue, 1);
-      load_meta(q2, rb2, re2, ss2);
-      load_info();
+      for (int a = 0; a < kRecAhead; ++a) ahead[a] = n_ahead[a];
+      if (deep) {
+        // B becomes the next item; claim the one after it
+        nq = bq;
+        n_rb = b_rb;
+        n_re = b_re;
+        n_ss = b_ss;
+        bq = __shfl_sync(0xffffffffu, nq_raw, 0);
+        if (lane == 0 && bq < nitems) nq_raw = atomicAdd(p.queue, 1);
+        load_meta(bq, b_rb, b_re, b_ss);
+        load_info();
+        pf = 3;
+      } else {
+        pf = 0;
+      }
       if (q >= nitems) {
         // no more items: exit marker
         if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
@@ -822,6 +852,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         __syncwarp();
         break;
       }
+      if (p.accumulate && re == rb) {
+        // nothing to add from this key block: the item is not handed on
+        while (pf < 3) pf_advance();
+        continue;
+      }
       if (lane < kMaxSlots) {
         ItemInfo& info = ctl->item_log[item_iter % kItemLog];
         info.s0[lane] = s0_cur;
@@ -833,6 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       // replaced by record r + kRecAhead as soon as it is read, so no step
       // waits on the load issued by the step before it
       for (int64_t r = rb; r < re && !aborted;) {
+        if (pf == 0 && re - r <= kRecAhead) pf_advance();  // shallow: claim the next item near the end
 #pragma unroll
         for (int a = 0; a < kRecAhead; ++a) {
         if (r >= re || aborted) break;
@@ -917,6 +953,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         }
       }
       if (aborted) break;
+      while (pf < 3) pf_advance();
       // end of the item
       if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
         aborted = true;
@@ -928,6 +965,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       }
       __syncwarp();
       ++it;
+      ++item_iter;
       if (++stage == c.stages) {
         stage = 0;
         ph ^= 1u;
