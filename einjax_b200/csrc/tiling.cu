@@ -167,6 +167,11 @@ __device__ __forceinline__ float cvt_out<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
+// One CTA per kChunk elements of the tile value array: the chunk is first
+// written as zeros with 16-byte stores, then (after the block barrier, which
+// orders the zero stores before them) the chunk's entries are stored over it
+// -- the last of repeated coordinates only. Every output byte goes to L2 once
+// as a full line; the few entry stores land on lines still in L2.
 template <typename OutT>
 __global__ void __launch_bounds__(256) densify_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1,
                                                       const uint32_t* p0, const uint32_t* p1, int64_t n,
@@ -174,33 +179,31 @@ __global__ void __launch_bounds__(256) densify_kernel(const TileHeader* hdr, con
                                                       const uint32_t* __restrict__ excl,
                                                       const int64_t* __restrict__ chunk_start,
                                                       const void* __restrict__ vals, int vdtype, uint64_t tile_elems,
-                                                      int64_t total_out, OutT* __restrict__ out) {
-  __shared__ __align__(16) OutT buf[kChunk];
+                                                      int64_t total_out, int vec_ok, OutT* __restrict__ out) {
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
   const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
   const int64_t c = blockIdx.x;
   const int64_t base = c * kChunk;
   constexpr int kVec = 16 / sizeof(OutT);
-  for (int i = threadIdx.x * kVec; i < kChunk; i += blockDim.x * kVec) {
-    *reinterpret_cast<uint4*>(&buf[i]) = make_uint4(0, 0, 0, 0);
+  const int64_t len = min(static_cast<int64_t>(kChunk), total_out - base);
+  // with a 16-byte aligned value array (vec_ok) a full chunk is whole
+  // 16-byte pieces (kChunk is a multiple of kVec)
+  if (len == kChunk && vec_ok) {
+#pragma unroll 4
+    for (int i = threadIdx.x * kVec; i < kChunk; i += blockDim.x * kVec)
+      *reinterpret_cast<uint4*>(&out[base + i]) = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    for (int64_t i = threadIdx.x; i < len; i += blockDim.x) out[base + i] = cvt_out<OutT>(0.f);
   }
   __syncthreads();
   const int64_t s0 = chunk_start[c], s1 = chunk_start[c + 1];
   for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
-    uint64_t k = keys[s];
-    bool last = (s + 1 >= n) || keys[s + 1] != k;
+    const uint64_t k = keys[s];
+    const bool last = (s + 1 >= n) || keys[s + 1] != k;
     if (!last) continue;
-    int64_t tid = static_cast<int64_t>(excl[s]) + flags[s] - 1;
-    int64_t f = tid * static_cast<int64_t>(tile_elems) + static_cast<int64_t>(k % tile_elems);
-    buf[f - base] = cvt_out<OutT>(load_as_f32(vals, vdtype, perm[s]));
-  }
-  __syncthreads();
-  const int64_t len = min(static_cast<int64_t>(kChunk), total_out - base);
-  if (len == kChunk) {
-    for (int i = threadIdx.x * kVec; i < kChunk; i += blockDim.x * kVec)
-      *reinterpret_cast<uint4*>(&out[base + i]) = *reinterpret_cast<const uint4*>(&buf[i]);
-  } else {
-    for (int i = threadIdx.x; i < len; i += blockDim.x) out[base + i] = buf[i];
+    const int64_t tid = static_cast<int64_t>(excl[s]) + flags[s] - 1;
+    const int64_t f = tid * static_cast<int64_t>(tile_elems) + static_cast<int64_t>(k % tile_elems);
+    out[f] = cvt_out<OutT>(load_as_f32(vals, vdtype, perm[s]));
   }
 }
 
@@ -349,14 +352,15 @@ extern "C" int es_tile_coo_fill(const void* values, int values_dtype, int64_t nn
             coords_out);
   ES_LAUNCH(chunk_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz, w.flags,
             w.excl, static_cast<uint64_t>(g.tile_elems), sentinel, num_chunks, w.chunk_start);
+  const int vec_ok = (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0 ? 1 : 0;
   if (out_dtype == ES_F32) {
     ES_LAUNCH(densify_kernel<float>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
               w.rb.vals_alt, nnz, w.flags, w.excl, w.chunk_start, values, values_dtype,
-              static_cast<uint64_t>(g.tile_elems), total_out, static_cast<float*>(values_out));
+              static_cast<uint64_t>(g.tile_elems), total_out, vec_ok, static_cast<float*>(values_out));
   } else {
     ES_LAUNCH(densify_kernel<__nv_bfloat16>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
               w.rb.vals_alt, nnz, w.flags, w.excl, w.chunk_start, values, values_dtype,
-              static_cast<uint64_t>(g.tile_elems), total_out, static_cast<__nv_bfloat16*>(values_out));
+              static_cast<uint64_t>(g.tile_elems), total_out, vec_ok, static_cast<__nv_bfloat16*>(values_out));
   }
   return ES_OK;
 }
