@@ -58,7 +58,7 @@ SIGNATURES = {
     "es_direct_fill": (c_int, [c_vp, c_i64, c_int, c_i64, c_int, c_int, c_i64p, c_i64p, c_vp, c_sz, c_i64, c_i64, c_vp,
                                c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "es_tile_einsum_workspace_size": (c_sz, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_int, c_int, c_i64,
-                                              c_i64, c_i64, c_i64, c_int]),
+                                              c_i64, c_i64, c_i64, c_i64, c_int]),
     "es_tile_einsum": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_vp, c_int, c_i64, c_vp, c_int, c_i64,
                                c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_int, c_vp,
                                c_sz, c_vp, c_vp]),

@@ -264,6 +264,96 @@ extern "C" int es_out_tile_shape(const char* kernel_string, const int64_t* lhs_t
 
 static bool want_tc(int precision) { return precision == ES_PREC_AUTO || precision == ES_PREC_TC; }
 
+// A contraction the tensor-core path covers after swapping the last two tile
+// dims of the lhs and/or rhs operand (e.g. the autodiff strings
+// "ik,jk->ij" = g . rhs^T and "ij,ik->jk" = lhs^T . g): the swapped
+// operands are transposed into the workspace, a pure copy.
+struct TcVariant {
+  int tl = 0, tr = 0;  // transpose lhs / rhs
+  std::string ks;
+  int64_t lt[ES_MAX_DIMS], rt[ES_MAX_DIMS];
+  EinsumDesc d;
+};
+
+static bool tc_variant(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
+                       int rhs_nd, int ldt, int rdt, int odt, bool strips, bool keys, TcVariant* v, TcConfig* c) {
+  std::string clean;
+  for (const char* p = kernel_string; *p; ++p)
+    if (*p != ' ') clean.push_back(*p);
+  const size_t comma = clean.find(','), arrow = clean.find("->");
+  if (comma == std::string::npos || arrow == std::string::npos || comma > arrow) return false;
+  if (lhs_nd > ES_MAX_DIMS || rhs_nd > ES_MAX_DIMS) return false;
+  for (int t = 0; t < 4; ++t) {
+    const int tl = t & 1, tr = (t >> 1) & 1;
+    if ((tl && lhs_nd < 2) || (tr && rhs_nd < 2)) continue;
+    std::string ks = clean;
+    for (int i = 0; i < lhs_nd; ++i) v->lt[i] = lhs_tile[i];
+    for (int i = 0; i < rhs_nd; ++i) v->rt[i] = rhs_tile[i];
+    if (tl) {
+      std::swap(ks[comma - 2], ks[comma - 1]);
+      std::swap(v->lt[lhs_nd - 2], v->lt[lhs_nd - 1]);
+    }
+    if (tr) {
+      std::swap(ks[arrow - 2], ks[arrow - 1]);
+      std::swap(v->rt[rhs_nd - 2], v->rt[rhs_nd - 1]);
+    }
+    if (parse_einsum(ks.c_str(), v->lt, lhs_nd, v->rt, rhs_nd, &v->d) != ES_OK) continue;
+    if (!tc_config(v->d, ldt, rdt, odt, strips, keys, c)) continue;
+    v->tl = tl;
+    v->tr = tr;
+    v->ks = ks;
+    return true;
+  }
+  return false;
+}
+
+// out[m][c][r] = in[m][r][c] for nmat matrices of R x C elements of esz
+// bytes (4 or 2): 32 x 32 blocks through shared memory, coalesced both ways.
+template <typename T>
+__global__ void __launch_bounds__(256) tiles_transpose_kernel(const T* __restrict__ in, T* __restrict__ out,
+                                                              int64_t nmat, int R, int C) {
+  __shared__ T blk[32][33];
+  const int br = (R + 31) / 32, bc = (C + 31) / 32;
+  const int64_t nblk = nmat * br * bc;
+  for (int64_t b = blockIdx.x; b < nblk; b += gridDim.x) {
+    const int64_t m = b / (br * bc);
+    const int rem = static_cast<int>(b - m * br * bc);
+    const int r0 = (rem / bc) * 32, c0 = (rem % bc) * 32;
+    const T* src = in + m * R * C;
+    T* dst = out + m * R * C;
+    for (int i = threadIdx.y; i < 32; i += 8) {
+      const int r = r0 + i, cc = c0 + threadIdx.x;
+      if (r < R && cc < C) blk[i][threadIdx.x] = src[static_cast<int64_t>(r) * C + cc];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += 8) {
+      const int cc = c0 + i, r = r0 + threadIdx.x;
+      if (r < R && cc < C) dst[static_cast<int64_t>(cc) * R + r] = blk[threadIdx.x][i];
+    }
+    __syncthreads();
+  }
+}
+
+static int transpose_tiles(const void* in, void* out, int dtype, int64_t rows, const int64_t* tile, int nd,
+                           cudaStream_t st) {
+  int64_t lead = 1;
+  for (int i = 0; i + 2 < nd; ++i) lead *= tile[i];
+  const int64_t nmat = rows * lead;
+  const int R = static_cast<int>(tile[nd - 2]), C = static_cast<int>(tile[nd - 1]);
+  const int64_t nblk = nmat * ((R + 31) / 32) * ((C + 31) / 32);
+  const int grid = static_cast<int>(nblk < 148 * 64 ? nblk : 148 * 64);
+  if (nblk <= 0) return ES_OK;
+  if (dtype == ES_F32)
+    ES_LAUNCH(tiles_transpose_kernel<float>, grid, dim3(32, 8), 0, st, static_cast<const float*>(in),
+              static_cast<float*>(out), nmat, R, C);
+  else
+    ES_LAUNCH(tiles_transpose_kernel<uint16_t>, grid, dim3(32, 8), 0, st, static_cast<const uint16_t*>(in),
+              static_cast<uint16_t*>(out), nmat, R, C);
+  return ES_OK;
+}
+
+static size_t round256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
 extern "C" int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
                                    const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype,
                                    int precision) {
@@ -271,15 +361,18 @@ extern "C" int es_tile_einsum_path(const char* kernel_string, const int64_t* lhs
   int st = parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d);
   if (st != ES_OK) return -st;
   TcConfig c;
-  if (want_tc(precision) && tc_config(d, lhs_dtype, rhs_dtype, ES_F32, true, false, &c)) return 1;
+  TcVariant v;
+  if (want_tc(precision) && tc_variant(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_dtype, rhs_dtype,
+                                       ES_F32, true, false, &v, &c))
+    return 1;
   if (precision == ES_PREC_TC) return -ES_ERR_UNSUPPORTED;
   return 0;
 }
 
 extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
                                                 const int64_t* rhs_tile, int rhs_nd, int lhs_dtype, int rhs_dtype,
-                                                int64_t rhs_rows, int64_t num_pairs, int64_t num_segments,
-                                                int64_t key_extent, int precision) {
+                                                int64_t lhs_rows, int64_t rhs_rows, int64_t num_pairs,
+                                                int64_t num_segments, int64_t key_extent, int precision) {
   EinsumDesc d;
   if (parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d) != ES_OK) return 0;
   if (!want_tc(precision)) return 0;
@@ -289,10 +382,15 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
   for (int strips = 0; strips < 2; ++strips) {
     for (int keys = 0; keys < (key_extent > 0 ? 2 : 1); ++keys) {
       TcConfig c;
-      if (!tc_config(d, lhs_dtype, rhs_dtype, ES_F32, strips != 0, keys != 0, &c)) continue;
+      TcVariant v;
+      if (!tc_variant(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_dtype, rhs_dtype, ES_F32, strips != 0,
+                      keys != 0, &v, &c))
+        continue;
       const int64_t ke = keys ? key_extent : 0;
-      const size_t sz = tc_workspace_size(c, rhs_rows, num_pairs, num_segments,
-                                          tc_key_blocks(c, rhs_rows, keys != 0, ke), ke);
+      size_t sz = tc_workspace_size(c, rhs_rows, num_pairs, num_segments,
+                                    tc_key_blocks(c, rhs_rows, keys != 0, ke), ke);
+      if (v.tl) sz += round256(static_cast<size_t>(lhs_rows) * d.lhs_te * dtype_size(lhs_dtype)) + 256;
+      if (v.tr) sz += round256(static_cast<size_t>(rhs_rows) * d.rhs_te * dtype_size(rhs_dtype)) + 256;
       if (sz > best) best = sz;
     }
   }
@@ -317,13 +415,38 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
   cudaStream_t st = as_stream(stream);
   if (want_tc(precision)) {
     TcConfig c;
+    TcVariant v;
     // the tensor-core path walks each segment's pairs as one sorted lhs
     // sequence; per-pair calls (no segments) stay on the SIMT path
-    if (seg_offsets &&
-        tc_config(d, lhs_dtype, rhs_dtype, out_dtype, seg_strip != nullptr, pair_key != nullptr && key_extent > 0, &c)) {
-      const int r = tc_launch(c, lhs_values, lhs_rows, rhs_values, rhs_rows, pair_lhs, pair_rhs, num_pairs,
-                              seg_offsets, nseg, seg_out_index, seg_strip, pair_key, key_extent, out_values,
-                              out_dtype, workspace, workspace_bytes, error_dev, st);
+    if (seg_offsets && tc_variant(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_dtype, rhs_dtype, out_dtype,
+                                  seg_strip != nullptr, pair_key != nullptr && key_extent > 0, &v, &c)) {
+      char* ws = static_cast<char*>(workspace);
+      size_t left = workspace_bytes;
+      const void* lv = lhs_values;
+      const void* rv = rhs_values;
+      auto take = [&](size_t bytes) -> void* {
+        char* p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~static_cast<uintptr_t>(255));
+        const size_t used = static_cast<size_t>(p - ws) + round256(bytes);
+        if (used > left) return nullptr;
+        ws += used;
+        left -= used;
+        return p;
+      };
+      if (v.tl) {
+        void* t = take(static_cast<size_t>(lhs_rows) * d.lhs_te * dtype_size(lhs_dtype));
+        if (!t) return ES_ERR_WORKSPACE;
+        ES_TRY(transpose_tiles(lhs_values, t, lhs_dtype, lhs_rows, lhs_tile, lhs_nd, st));
+        lv = t;
+      }
+      if (v.tr) {
+        void* t = take(static_cast<size_t>(rhs_rows) * d.rhs_te * dtype_size(rhs_dtype));
+        if (!t) return ES_ERR_WORKSPACE;
+        ES_TRY(transpose_tiles(rhs_values, t, rhs_dtype, rhs_rows, rhs_tile, rhs_nd, st));
+        rv = t;
+      }
+      const int r = tc_launch(c, lv, lhs_rows, rv, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets, nseg,
+                              seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, ws, left,
+                              error_dev, st);
       if (r != ES_ERR_UNSUPPORTED || precision == ES_PREC_TC) return r;
     }
     if (precision == ES_PREC_TC) return ES_ERR_UNSUPPORTED;

@@ -164,7 +164,7 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     prec = _PREC[precision]
     kext = int(key_extent) if pk is not None else 0
     wsb = lib.es_tile_einsum_workspace_size(ks, lti, len(lt), rti, len(rt), es_dtype(lv), es_dtype(rv),
-                                            int(rv.shape[0]), P, nseg, kext, prec)
+                                            int(lv.shape[0]), int(rv.shape[0]), P, nseg, kext, prec)
     ws = workspace(wsb, dev) if wsb else None
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     L.check("es_tile_einsum", lib.es_tile_einsum(

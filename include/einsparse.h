@@ -184,15 +184,19 @@ int es_output_coords(const int32_t* lhs_coords, int lhs_ndim, const int32_t* rhs
  * 32 or 64, Kt 32 or 64), and splits the contracted range into blocks whose
  * rhs operand fits in L2, adding the blocks' partial sums into the output
  * in block order. A broken contract sets *error_dev to ES_ERR_INVALID.
+ * A contraction that is a plain tile matmul after swapping the last two tile
+ * dims of an operand ("ik,jk->ij", "ij,ik->jk": the autodiff strings) also
+ * takes the tensor-core path; the swapped operand is transposed into the
+ * workspace first (a copy, no rounding).
  * workspace: es_tile_einsum_workspace_size bytes (0 for the SIMT path),
- * sized for the same rhs_rows, num_pairs, num_segments and key_extent (0
- * when no pair_key is passed). A device-side wait that runs out sets
- * *error_dev to ES_ERR_TIMEOUT.
+ * sized for the same lhs_rows, rhs_rows, num_pairs, num_segments and
+ * key_extent (0 when no pair_key is passed). A device-side wait that runs
+ * out sets *error_dev to ES_ERR_TIMEOUT.
  * ------------------------------------------------------------------------- */
 size_t es_tile_einsum_workspace_size(const char* kernel_string,
                                      const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
-                                     int lhs_dtype, int rhs_dtype, int64_t rhs_rows, int64_t num_pairs,
-                                     int64_t num_segments, int64_t key_extent, int precision);
+                                     int lhs_dtype, int rhs_dtype, int64_t lhs_rows, int64_t rhs_rows,
+                                     int64_t num_pairs, int64_t num_segments, int64_t key_extent, int precision);
 int es_tile_einsum(const char* kernel_string,
                    const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
                    const void* lhs_values, int lhs_dtype, int64_t lhs_rows,

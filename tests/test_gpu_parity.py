@@ -539,3 +539,29 @@ def test_c2_like_large_vs_scipy():
     want[np.unique(a.row // 32)[:, None], np.arange(m // 32)[None, :]] = True
     assert np.array_equal(present, want)
     assert np.all(np.abs(got - ref) <= 1e-5 * (np.abs(ref) + mag))
+
+
+@pytest.mark.parametrize("ks,lt,rt", [("ik,jk->ij", (64, 32), (128, 32)), ("ij,ik->jk", (32, 64), (32, 128)),
+                                      ("ki,kj->ij", (32, 128), (32, 64)), ("bik,bjk->bij", (1, 64, 32), (1, 128, 32))])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tile_einsum_transposed_operands(ks, lt, rt, dtype):
+    """Contractions that are a plain tile matmul after swapping an operand's
+    last two dims (the autodiff strings) take the tensor-core path through a
+    transposed copy and agree with the exact SIMT path."""
+    from einjax_b200 import sparse_dispatch as SD
+    assert SD.tile_einsum_path(ks, lt, rt, dtype, dtype) == "tc"
+    g = torch.Generator().manual_seed(3)
+    nl, nr, P, nseg = 37, 29, 400, 61
+    lv = torch.randn(nl, *lt, generator=g).to(dtype).cuda()
+    rv = torch.randn(nr, *rt, generator=g).to(dtype).cuda()
+    pl = torch.randint(0, nl, (P,), generator=g, dtype=torch.int32)
+    pr = torch.randint(0, nr, (P,), generator=g, dtype=torch.int32)
+    cuts = torch.sort(torch.randperm(P - 1, generator=g)[:nseg - 1] + 1).values
+    so = torch.cat([torch.zeros(1, dtype=torch.int64), cuts.to(torch.int64), torch.full((1,), P, dtype=torch.int64)])
+    args = (ks, lv, rv, pl.cuda(), pr.cuda(), so.cuda())
+    got = SD.tile_einsum(*args, out_dtype=torch.float32, precision="tc")
+    ref = SD.tile_einsum(*args, out_dtype=torch.float32, precision="exact")
+    mag = SD.tile_einsum(ks, lv.float().abs(), rv.float().abs(), pl.cuda(), pr.cuda(), so.cuda(),
+                         out_dtype=torch.float32, precision="exact")
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert torch.all((got - ref).abs() <= tol * (ref.abs() + mag) + 1e-6)
