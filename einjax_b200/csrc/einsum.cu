@@ -266,8 +266,9 @@ static bool want_tc(int precision) { return precision == ES_PREC_AUTO || precisi
 
 // A contraction the tensor-core path covers after swapping the last two tile
 // dims of the lhs and/or rhs operand (e.g. the autodiff strings
-// "ik,jk->ij" = g . rhs^T and "ij,ik->jk" = lhs^T . g): the swapped
-// operands are transposed into the workspace, a pure copy.
+// "ik,jk->ij" = g . rhs^T and "ij,ik->jk" = lhs^T . g): a swapped lhs is
+// transposed into the workspace (a pure copy); a swapped rhs is read in its
+// own (k-contiguous) layout when the panel image is built.
 struct TcVariant {
   int tl = 0, tr = 0;  // transpose lhs / rhs
   std::string ks;
@@ -390,7 +391,6 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
       size_t sz = tc_workspace_size(c, rhs_rows, num_pairs, num_segments,
                                     tc_key_blocks(c, rhs_rows, keys != 0, ke), ke);
       if (v.tl) sz += round256(static_cast<size_t>(lhs_rows) * d.lhs_te * dtype_size(lhs_dtype)) + 256;
-      if (v.tr) sz += round256(static_cast<size_t>(rhs_rows) * d.rhs_te * dtype_size(rhs_dtype)) + 256;
       if (sz > best) best = sz;
     }
   }
@@ -438,12 +438,9 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
         ES_TRY(transpose_tiles(lhs_values, t, lhs_dtype, lhs_rows, lhs_tile, lhs_nd, st));
         lv = t;
       }
-      if (v.tr) {
-        void* t = take(static_cast<size_t>(rhs_rows) * d.rhs_te * dtype_size(rhs_dtype));
-        if (!t) return ES_ERR_WORKSPACE;
-        ES_TRY(transpose_tiles(rhs_values, t, rhs_dtype, rhs_rows, rhs_tile, rhs_nd, st));
-        rv = t;
-      }
+      // a transposed rhs needs no copy: the panel image is built from its
+      // k-contiguous rows directly
+      if (v.tr) c.rhs_kmajor = 1;
       const int r = tc_launch(c, lv, lhs_rows, rv, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets, nseg,
                               seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, ws, left,
                               error_dev, st);

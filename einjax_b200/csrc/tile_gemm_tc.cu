@@ -1125,48 +1125,126 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 
 // ------------------------------------------------------- preparation kernels
 
-// rhs tile t (Kt x Nt, n contiguous) -> per k-chunk c of KC rows a K-major
-// swizzled block: row n holds the tile's column n over the chunk's k (W =
-// KC * element bytes), its 16-byte pieces XOR-permuted by the row's address
-// bits 7.. (the layout the TMA's swizzle modes produce for a block starting
-// on a 1024-byte boundary), i.e. exactly the image one panel slot has in
-// shared memory. Blocks are stored chunk-major ([c][t]) so consecutive tiles
-// of one chunk are contiguous.
-template <bool F32>
-__global__ void layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt, int KC,
-                                  void* __restrict__ hi, void* __restrict__ lo) {
-  // one thread per 16-byte piece of the image: (tile t, k-chunk c, piece j
-  // of row n); n varies fastest, so the column reads of a warp are coalesced
+// rhs tile t -> per k-chunk c of KC rows a K-major swizzled block: row n
+// holds the tile's column n over the chunk's k (W = KC * element bytes), its
+// 16-byte pieces XOR-permuted by the row's address bits 7.. (the layout the
+// TMA's swizzle modes produce for a block starting on a 1024-byte boundary),
+// i.e. exactly the image one panel slot has in shared memory. Blocks are
+// stored chunk-major ([c][t]) so consecutive tiles of one chunk are
+// contiguous.
+// Source tiles are Kt x Nt with n contiguous, or (KMAJOR) Nt x Kt with k
+// contiguous, which is already the image's row order. fp32 writes the raw
+// value (read as TF32 by the tensor core) to hi and x - trunc_tf32(x) to lo.
+template <bool F32, bool KMAJOR>
+__global__ void __launch_bounds__(256) layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt,
+                                                         int KC, void* __restrict__ hi, void* __restrict__ lo) {
   using E = typename std::conditional<F32, float, __nv_bfloat16>::type;
   constexpr int ESZ = F32 ? 4 : 2;
   constexpr int EPU = 16 / ESZ;  // elements per 16-byte piece
   const int W = KC * ESZ;        // bytes per image row
   const int pieces = W / 16;
   const int nck = Kt / KC;
-  const int64_t total = rows * nck * pieces * static_cast<int64_t>(Nt);
   const E* src = static_cast<const E*>(rhs);
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
-    const int n = static_cast<int>(q % Nt);
-    int64_t r = q / Nt;
-    const int j = static_cast<int>(r % pieces);
-    r /= pieces;
-    const int c = static_cast<int>(r % nck);
-    const int64_t t = r / nck;
-    const E* col = src + t * static_cast<int64_t>(Kt) * Nt + (static_cast<int64_t>(c) * KC + j * EPU) * Nt + n;
-    const int sw = ((n * W) >> 7) & (pieces - 1);
-    const int64_t dst = ((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16);
+  auto put = [&](int64_t dst, const E (&v)[EPU]) {
     if constexpr (F32) {
-      float4 x, y;
-      x.x = col[0]; x.y = col[Nt]; x.z = col[2 * Nt]; x.w = col[3 * Nt];
-      y = make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
-      *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;  // read as TF32 (truncated) by the tensor core
-      *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) = y;
+      const float4 x = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) =
+          make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
     } else {
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
+    }
+  };
+  if constexpr (KMAJOR) {
+    // one thread per 16-byte piece, pieces of one row adjacent: a straight
+    // (swizzled) copy of the source rows
+    const int64_t total = rows * nck * static_cast<int64_t>(Nt) * pieces;
+    for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+      const int j = static_cast<int>(q % pieces);
+      int64_t r = q / pieces;
+      const int n = static_cast<int>(r % Nt);
+      r /= Nt;
+      const int c = static_cast<int>(r % nck);
+      const int64_t t = r / nck;
+      __align__(16) E v[EPU];
+      *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(
+          src + (t * Nt + n) * static_cast<int64_t>(Kt) + static_cast<int64_t>(c) * KC + j * EPU);
+      const int sw = ((n * W) >> 7) & (pieces - 1);
+      put(((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16), v);
+    }
+  } else {
+    // one thread per 16-byte piece of the image: (tile t, k-chunk c, piece j
+    // of row n); n varies fastest, so the column reads of a warp are coalesced
+    const int64_t total = rows * nck * pieces * static_cast<int64_t>(Nt);
+    for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+      const int n = static_cast<int>(q % Nt);
+      int64_t r = q / Nt;
+      const int j = static_cast<int>(r % pieces);
+      r /= pieces;
+      const int c = static_cast<int>(r % nck);
+      const int64_t t = r / nck;
+      const E* col = src + t * static_cast<int64_t>(Kt) * Nt + (static_cast<int64_t>(c) * KC + j * EPU) * Nt + n;
       __align__(16) E v[EPU];
 #pragma unroll
       for (int e = 0; e < EPU; ++e) v[e] = col[static_cast<int64_t>(e) * Nt];
-      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
+      const int sw = ((n * W) >> 7) & (pieces - 1);
+      put(((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16), v);
     }
+  }
+}
+
+// layout_rhs_kernel for wide row-major tiles (Nt >= 128): one CTA per
+// (tile, chunk, 32 columns) reads the KC x 32 block with coalesced row
+// segments into shared memory and writes its 32 image rows -- 32 * W
+// contiguous bytes -- as consecutive 16-byte pieces (the per-piece mapping
+// scatters each warp's stores over 32 rows of W bytes).
+constexpr int kLayoutCols = 32;
+
+template <bool F32>
+__global__ void __launch_bounds__(256) layout_rhs_wide_kernel(const void* __restrict__ rhs, int64_t rows, int Kt,
+                                                              int Nt, int KC, void* __restrict__ hi,
+                                                              void* __restrict__ lo) {
+  using E = typename std::conditional<F32, float, __nv_bfloat16>::type;
+  constexpr int ESZ = F32 ? 4 : 2;
+  constexpr int EPU = 16 / ESZ;
+  const int W = KC * ESZ;
+  const int pieces = W / 16;
+  const int nck = Kt / KC;
+  const E* src = static_cast<const E*>(rhs);
+  __shared__ float blk[64][kLayoutCols + 1];
+  const int nb = (Nt + kLayoutCols - 1) / kLayoutCols;
+  const int64_t nblk = rows * nck * nb;
+  for (int64_t b = blockIdx.x; b < nblk; b += gridDim.x) {
+    const int cb = static_cast<int>(b % nb);
+    const int64_t r = b / nb;
+    const int c = static_cast<int>(r % nck);
+    const int64_t t = r / nck;
+    const int n0 = cb * kLayoutCols;
+    const int ncols = Nt - n0 < kLayoutCols ? Nt - n0 : kLayoutCols;
+    const E* tile = src + t * static_cast<int64_t>(Kt) * Nt + static_cast<int64_t>(c) * KC * Nt + n0;
+    for (int e = threadIdx.x; e < KC * kLayoutCols; e += blockDim.x) {
+      const int k = e / kLayoutCols, nn = e % kLayoutCols;
+      if (nn < ncols) blk[k][nn] = static_cast<float>(tile[static_cast<int64_t>(k) * Nt + nn]);
+    }
+    __syncthreads();
+    for (int pq = threadIdx.x; pq < ncols * pieces; pq += blockDim.x) {
+      const int nn = pq / pieces, j = pq % pieces;
+      const int n = n0 + nn;
+      __align__(16) E v[EPU];
+#pragma unroll
+      for (int e = 0; e < EPU; ++e) v[e] = static_cast<E>(blk[j * EPU + e][nn]);
+      const int sw = ((n * W) >> 7) & (pieces - 1);
+      const int64_t dst = ((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16);
+      if constexpr (F32) {
+        const float4 x = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;
+        *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) =
+            make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
+      } else {
+        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -1682,12 +1760,25 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   // 1. rhs tiles into the shared-memory image (split for fp32)
   const int64_t pe = rhs_rows * c.Kt * c.Nt / (c.fp32 ? 4 : 8);  // 16-byte pieces of the image
   if (pe > 0) {
-    if (c.fp32)
-      ES_LAUNCH(layout_rhs_kernel<true>, grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi,
-                w.pan_lo);
-    else
-      ES_LAUNCH(layout_rhs_kernel<false>, grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi,
-                (void*)nullptr);
+    if (c.rhs_kmajor) {
+      if (c.fp32)
+        ES_LAUNCH((layout_rhs_kernel<true, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, w.pan_lo);
+      else
+        ES_LAUNCH((layout_rhs_kernel<false, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, (void*)nullptr);
+    } else if (c.fp32 && c.Nt >= 128) {
+      const int64_t nblk = rhs_rows * (c.Kt / c.KC) * ((c.Nt + kLayoutCols - 1) / kLayoutCols);
+      const int g = static_cast<int>(nblk < 148 * 16 ? nblk : 148 * 16);
+      ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo);
+    } else {
+      if (c.fp32)
+        ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, w.pan_lo);
+      else
+        ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, (void*)nullptr);
+    }
   }
   // 2. work items
   if (seg_strip && c.G > 1) {

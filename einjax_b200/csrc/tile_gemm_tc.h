@@ -37,6 +37,8 @@ struct TcConfig {
                    // split) form a second epilogue group; the groups take alternate blocks
   int epi_warp_bytes;  // staging bytes per epilogue warp (2 KB for bf16 output, 4 KB for fp32)
   int smem_bytes;  // dynamic shared memory per CTA
+  int rhs_kmajor;  // set by the caller: rhs tiles are stored Nt x Kt (k contiguous), the
+                   // transposed form of the contraction's rhs
 };
 
 // True when the contraction is a plain tile matmul this path covers:
