@@ -52,15 +52,14 @@ struct DirectWs {
   uint32_t* mask;      // (CB * (NCH + 1)) hit mask per (present column, 32-tile chunk), column-major
   uint32_t* ccnt;      // (CB * (NCH + 1)) popcount of mask
   uint32_t* cscan;     // (CB * (NCH + 1)) exclusive scan of ccnt
-  uint32_t* counts;    // (SC) pairs per (strip, present column), strip-major
+  uint64_t* cnz;       // (SC) per (strip, present column), strip-major: pairs | (pairs > 0) << 32
+  uint64_t* pos;       // (SC) exclusive scan of cnz: first pair | output tile index << 32
   uint32_t* gstart;    // (SC) G_c(first tile of the strip)
-  uint32_t* nzflag;    // (SC)
-  uint32_t* segid;     // (SC) exclusive scan of nzflag
-  uint32_t* off;       // (SC + 1) exclusive scan of counts
-  uint32_t* scan;      // scan scratch (largest length)
+  uint32_t* scan;      // scan scratch (largest length, also used as 64-bit words)
   uint32_t* ncols;     // (1) present columns
   uint32_t* nstrips;   // (1)
   uint32_t* total;     // (1) scratch totals
+  uint64_t* total64;   // (1)
   int32_t* bad;        // (1) a relation not in lexicographic order / repeated coordinates
 };
 
@@ -91,11 +90,9 @@ static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const Direc
   w.mask = c.template take<uint32_t>(hm);
   w.ccnt = c.template take<uint32_t>(hm);
   w.cscan = c.template take<uint32_t>(hm);
-  w.counts = c.template take<uint32_t>(sc);
+  w.cnz = c.template take<uint64_t>(sc);
+  w.pos = c.template take<uint64_t>(sc);
   w.gstart = c.template take<uint32_t>(sc);
-  w.nzflag = c.template take<uint32_t>(sc);
-  w.segid = c.template take<uint32_t>(sc);
-  w.off = c.template take<uint32_t>(sc + 1);
   int64_t mx = sc + 1;
   if (hm > mx) mx = hm;
   if (g.cext > mx) mx = g.cext;
@@ -104,6 +101,7 @@ static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const Direc
   w.ncols = c.template take<uint32_t>(1);
   w.nstrips = c.template take<uint32_t>(1);
   w.total = c.template take<uint32_t>(1);
+  w.total64 = c.template take<uint64_t>(1);
   w.bad = c.template take<int32_t>(1);
 }
 
@@ -153,57 +151,71 @@ __device__ __forceinline__ int lex_cmp(const int32_t* a, const int32_t* b, int n
   return 0;
 }
 
-// rhs tiles into the table; flags an rhs out of lexicographic order.
-__global__ void direct_table_kernel(const int32_t* __restrict__ rc, int64_t nr, DirectGeom g,
-                                    int32_t* __restrict__ table, uint32_t* __restrict__ colflag,
-                                    int32_t* __restrict__ bad, int32_t* err) {
-  for (int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < nr; j += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t* row = rc + j * g.rhs_nd;
-    int fd;
-    if (j > 0 && lex_cmp(row, row - g.rhs_nd, g.rhs_nd, &fd) <= 0) *bad = 1;
-    const int64_t key = key_of(row, g.nb, g);
-    bool ok = key >= 0;
-    const int64_t c = col_linear(row, g, &ok);
-    if (!ok) {
-      if (err) atomicExch(err, ES_ERR_INDEX);
-      continue;
-    }
-    table[key * g.cext + c] = static_cast<int32_t>(j);
-    colflag[c] = 1u;
+// Clears the table (-1), the column flags and the order flag.
+__global__ void direct_init_kernel(int32_t* __restrict__ table, int64_t tn, uint32_t* __restrict__ colflag,
+                                   int64_t cext, int32_t* __restrict__ bad) {
+  const int64_t n = tn > cext ? tn : cext;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < tn) table[i] = -1;
+    if (i < cext) colflag[i] = 0u;
+    if (i == 0) *bad = 0;
   }
 }
 
-__global__ void direct_colids_kernel(const uint32_t* __restrict__ colflag, const uint32_t* __restrict__ colrank,
-                                     int64_t cext, uint32_t* __restrict__ colids) {
-  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < cext; c += (int64_t)gridDim.x * blockDim.x)
-    if (colflag[c]) colids[colrank[c]] = static_cast<uint32_t>(c);
-}
-
-// Strip heads of the lhs; flags lhs tiles out of lexicographic order (or
-// repeated) and keys outside the table.
-__global__ void direct_strips_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
-                                     uint32_t* __restrict__ sflag, int32_t* __restrict__ bad, int32_t* err) {
-  const int nd = g.lhs_nd;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nl; i += (int64_t)gridDim.x * blockDim.x) {
-    const int32_t* row = lc + i * nd;
-    if (key_of(row, nd - 1, g) < 0) {
-      if (err) atomicExch(err, ES_ERR_INDEX);
-    }
-    uint32_t head = 1u;
-    if (i > 0) {
+// Threads [0, nr): rhs tile j into the table (flags an rhs out of
+// lexicographic order). Threads [nr, nr + nl): strip head flag of lhs tile
+// i (flags lhs tiles out of lexicographic order or repeated, and keys
+// outside the table).
+__global__ void direct_inputs_kernel(const int32_t* __restrict__ rc, int64_t nr, const int32_t* __restrict__ lc,
+                                     int64_t nl, DirectGeom g, int32_t* __restrict__ table,
+                                     uint32_t* __restrict__ colflag, uint32_t* __restrict__ sflag,
+                                     int32_t* __restrict__ bad, int32_t* err) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nr + nl; q += (int64_t)gridDim.x * blockDim.x) {
+    if (q < nr) {
+      const int64_t j = q;
+      const int32_t* row = rc + j * g.rhs_nd;
       int fd;
-      if (lex_cmp(row, row - nd, nd, &fd) <= 0) *bad = 1;
-      head = fd < nd - 1 ? 1u : 0u;  // strip = dims 0..nd-2
+      if (j > 0 && lex_cmp(row, row - g.rhs_nd, g.rhs_nd, &fd) <= 0) *bad = 1;
+      const int64_t key = key_of(row, g.nb, g);
+      bool ok = key >= 0;
+      const int64_t c = col_linear(row, g, &ok);
+      if (!ok) {
+        if (err) atomicExch(err, ES_ERR_INDEX);
+        continue;
+      }
+      table[key * g.cext + c] = static_cast<int32_t>(j);
+      colflag[c] = 1u;
+    } else {
+      const int64_t i = q - nr;
+      const int nd = g.lhs_nd;
+      const int32_t* row = lc + i * nd;
+      if (key_of(row, nd - 1, g) < 0) {
+        if (err) atomicExch(err, ES_ERR_INDEX);
+      }
+      uint32_t head = 1u;
+      if (i > 0) {
+        int fd;
+        if (lex_cmp(row, row - nd, nd, &fd) <= 0) *bad = 1;
+        head = fd < nd - 1 ? 1u : 0u;  // strip = dims 0..nd-2
+      }
+      sflag[i] = head;
     }
-    sflag[i] = head;
   }
 }
 
-__global__ void direct_sstart_kernel(const uint32_t* __restrict__ sflag, const uint32_t* __restrict__ sexcl,
-                                     int64_t nl, const uint32_t* __restrict__ nstrips, uint32_t* __restrict__ sstart) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nl; i += (int64_t)gridDim.x * blockDim.x) {
-    if (sflag[i]) sstart[sexcl[i]] = static_cast<uint32_t>(i);
-    if (i == 0) sstart[*nstrips] = static_cast<uint32_t>(nl);
+// Threads [0, cext): present column ids in order; threads [0, nl): first lhs
+// tile of each strip, then sstart[nstrips] = nl.
+__global__ void direct_index_kernel(const uint32_t* __restrict__ colflag, const uint32_t* __restrict__ colrank,
+                                    int64_t cext, uint32_t* __restrict__ colids, const uint32_t* __restrict__ sflag,
+                                    const uint32_t* __restrict__ sexcl, int64_t nl,
+                                    const uint32_t* __restrict__ nstrips, uint32_t* __restrict__ sstart) {
+  const int64_t n = nl > cext ? nl : cext;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < cext && colflag[i]) colids[colrank[i]] = static_cast<uint32_t>(i);
+    if (i < nl) {
+      if (sflag[i]) sstart[sexcl[i]] = static_cast<uint32_t>(i);
+      if (i == 0) sstart[*nstrips] = static_cast<uint32_t>(nl);
+    }
   }
 }
 
@@ -269,77 +281,69 @@ __device__ __forceinline__ uint32_t direct_g(const uint32_t* __restrict__ mask, 
 __global__ void direct_counts_kernel(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
                                      int64_t nchp1, const uint32_t* __restrict__ ncols,
                                      const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                     uint32_t* __restrict__ counts, uint32_t* __restrict__ gstart,
-                                     uint32_t* __restrict__ nzflag) {
+                                     uint64_t* __restrict__ cnz, uint32_t* __restrict__ gstart) {
   const int64_t S = *nstrips, C = *ncols;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t s = e / C, c = e - s * C;
     const uint32_t ga = direct_g(mask, cscan, nchp1, c, sstart[s]);
     const uint32_t n = direct_g(mask, cscan, nchp1, c, sstart[s + 1]) - ga;
-    counts[e] = n;
+    cnz[e] = static_cast<uint64_t>(n) | (n ? (1ull << 32) : 0ull);
     gstart[e] = ga;
-    nzflag[e] = n ? 1u : 0u;
   }
 }
 
 // Counts of the host's sizes: [0] pairs, [1] output tiles, [2] out of order.
-__global__ void direct_totals_kernel(const uint32_t* __restrict__ off, const uint32_t* __restrict__ segid,
-                                     const uint32_t* __restrict__ counts, const uint32_t* __restrict__ nzflag,
+__global__ void direct_totals_kernel(const uint64_t* __restrict__ pos, const uint64_t* __restrict__ cnz,
                                      const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ ncols,
                                      const int32_t* __restrict__ bad, int64_t* __restrict__ out) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const int64_t n = static_cast<int64_t>(*nstrips) * (*ncols);
-  if (n == 0) {
-    out[0] = 0;
-    out[1] = 0;
-  } else {
-    out[0] = static_cast<int64_t>(off[n - 1]) + counts[n - 1];
-    out[1] = static_cast<int64_t>(segid[n - 1]) + nzflag[n - 1];
-  }
+  const uint64_t t = n == 0 ? 0ull : pos[n - 1] + cnz[n - 1];
+  out[0] = static_cast<int64_t>(t & 0xFFFFFFFFull);
+  out[1] = static_cast<int64_t>(t >> 32);
   out[2] = *bad;
 }
 
-// Segment records: one thread per (strip, present column) with pairs.
-__global__ void direct_segments_kernel(const int32_t* __restrict__ lc, DirectGeom g,
-                                       const uint32_t* __restrict__ colids, const uint32_t* __restrict__ ncols,
-                                       const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                       const uint32_t* __restrict__ counts, const uint32_t* __restrict__ off,
-                                       const uint32_t* __restrict__ segid, int64_t num_pairs, int64_t num_segments,
-                                       int32_t* __restrict__ out_coords, int64_t* __restrict__ seg_off,
-                                       int64_t* __restrict__ seg_strip) {
-  const int64_t S = *nstrips, C = *ncols;
-  const int ncd = g.rhs_nd - 1 - g.nb;  // rhs column dims
-  const int out_nd = (g.lhs_nd - 1) + ncd;
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    if (counts[e] == 0) continue;
-    const int64_t s = e / C, c = e - s * C;
-    const int64_t o = segid[e];
-    const int32_t* row = lc + static_cast<int64_t>(sstart[s]) * g.lhs_nd;
-    int32_t* oc = out_coords + o * out_nd;
-    for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
-    int64_t cl = colids[c];
-    for (int d = ncd - 1; d >= 0; --d) {
-      oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
-      cl /= g.col_ext[d];
-    }
-    seg_off[o] = off[e];
-    if (seg_strip) seg_strip[o] = s;
-    if (o + 1 == num_segments) seg_off[num_segments] = num_pairs;
-  }
-}
-
-// Pairs: one warp per (32-tile chunk, column group) as in the mask pass; a
-// hit of tile i for column c goes to off(s, c) + G_c(i) - G_c(start s).
+// Fill. Threads first write the output-tile records of the (strip, present
+// column) entries with pairs (coordinates, first pair, strip; the last
+// record also writes seg_off[O] = P). Then, one warp per (32-tile chunk,
+// column group) as in the mask pass, a hit of tile i for column c goes to
+// first(s, c) + G_c(i) - G_c(start s).
 __global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
                                     const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
-                                    const uint32_t* __restrict__ ncols, int64_t nchp1,
+                                    const uint32_t* __restrict__ ncols, const uint32_t* __restrict__ nstrips,
+                                    const uint32_t* __restrict__ sstart, int64_t nchp1,
                                     const uint32_t* __restrict__ cscan, const uint32_t* __restrict__ sflag,
-                                    const uint32_t* __restrict__ sexcl, const uint32_t* __restrict__ off,
-                                    const uint32_t* __restrict__ gstart, int32_t* __restrict__ seg_lhs,
-                                    int32_t* __restrict__ seg_rhs, int32_t* __restrict__ seg_key) {
+                                    const uint32_t* __restrict__ sexcl, const uint64_t* __restrict__ cnz,
+                                    const uint64_t* __restrict__ posw, const uint32_t* __restrict__ gstart,
+                                    int64_t num_pairs, int64_t num_segments, int32_t* __restrict__ seg_lhs,
+                                    int32_t* __restrict__ seg_rhs, int32_t* __restrict__ seg_key,
+                                    int32_t* __restrict__ out_coords, int64_t* __restrict__ seg_off,
+                                    int64_t* __restrict__ seg_strip) {
   const int64_t C = *ncols;
+  {
+    const int64_t S = *nstrips;
+    const int ncd = g.rhs_nd - 1 - g.nb;  // rhs column dims
+    const int out_nd = (g.lhs_nd - 1) + ncd;
+    for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
+         e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      if ((cnz[e] & 0xFFFFFFFFull) == 0) continue;
+      const int64_t s = e / C, c = e - s * C;
+      const int64_t o = static_cast<int64_t>(posw[e] >> 32);
+      const int32_t* row = lc + static_cast<int64_t>(sstart[s]) * g.lhs_nd;
+      int32_t* oc = out_coords + o * out_nd;
+      for (int d = 0; d < g.lhs_nd - 1; ++d) oc[d] = row[d];
+      int64_t cl = colids[c];
+      for (int d = ncd - 1; d >= 0; --d) {
+        oc[g.lhs_nd - 1 + d] = static_cast<int32_t>(cl % g.col_ext[d]);
+        cl /= g.col_ext[d];
+      }
+      seg_off[o] = static_cast<int64_t>(posw[e] & 0xFFFFFFFFull);
+      if (seg_strip) seg_strip[o] = s;
+      if (o + 1 == num_segments) seg_off[num_segments] = num_pairs;
+    }
+  }
   const int64_t groups = (C + kDirCols - 1) / kDirCols;
   const int lane = threadIdx.x & 31;
   const uint32_t below = (1u << lane) - 1u;
@@ -365,7 +369,7 @@ __global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, 
         const int64_t c = c0 + j;
         const int64_t e = s * C + c;
         const uint32_t gi = cscan[c * nchp1 + ch] + __popc(m & below);
-        const int64_t p = static_cast<int64_t>(off[e]) + (gi - gstart[e]);
+        const int64_t p = static_cast<int64_t>(posw[e] & 0xFFFFFFFFull) + (gi - gstart[e]);
         seg_lhs[p] = static_cast<int32_t>(i);
         seg_rhs[p] = r[j];
         if (seg_key) seg_key[p] = k;
@@ -431,16 +435,15 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   DirectWs w;
   direct_layout(cv, w, n_lhs, n_rhs, g);
   if (cv.overflow) return ES_ERR_WORKSPACE;
-  if (cudaMemsetAsync(w.table, 0xFF, g.kext * g.cext * sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
-  if (cudaMemsetAsync(w.colflag, 0, g.cext * sizeof(uint32_t), st) != cudaSuccess) return ES_ERR_CUDA;
-  if (cudaMemsetAsync(w.bad, 0, sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
-  ES_LAUNCH(direct_table_kernel, grid_for(n_rhs, 256), 256, 0, st, rhs_coords, n_rhs, g, w.table, w.colflag, w.bad,
-            error_dev);
+  const int64_t tn = g.kext * g.cext;
+  ES_LAUNCH(direct_init_kernel, grid_for(tn > g.cext ? tn : g.cext, 256), 256, 0, st, w.table, tn, w.colflag, g.cext,
+            w.bad);
+  ES_LAUNCH(direct_inputs_kernel, grid_for(n_rhs + n_lhs, 256), 256, 0, st, rhs_coords, n_rhs, lhs_coords, n_lhs, g,
+            w.table, w.colflag, w.sflag, w.bad, error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, w.scan, st));
-  ES_LAUNCH(direct_colids_kernel, grid_for(g.cext, 256), 256, 0, st, w.colflag, w.colrank, g.cext, w.colids);
-  ES_LAUNCH(direct_strips_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, g, w.sflag, w.bad, error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.sflag, w.sexcl, n_lhs, w.nstrips, w.scan, st));
-  ES_LAUNCH(direct_sstart_kernel, grid_for(n_lhs, 256), 256, 0, st, w.sflag, w.sexcl, n_lhs, w.nstrips, w.sstart);
+  ES_LAUNCH(direct_index_kernel, grid_for(n_lhs > g.cext ? n_lhs : g.cext, 256), 256, 0, st, w.colflag, w.colrank,
+            g.cext, w.colids, w.sflag, w.sexcl, n_lhs, w.nstrips, w.sstart);
   // hit masks per (present column, chunk), their scan, then the per-(strip,
   // column) counts; the column count lives on the device, so grids cover the
   // upper bound and stride over the used part
@@ -453,13 +456,12 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   // ever enter prefixes past the used part
   ES_TRY(exclusive_scan<uint32_t>(w.ccnt, w.cscan, cb * nchp1, w.total, w.scan, st));
   ES_LAUNCH(direct_counts_kernel, grid_for(sc, 256), 256, 0, st, w.mask, w.cscan, nchp1, w.ncols, w.nstrips,
-            w.sstart, w.counts, w.gstart, w.nzflag);
-  // the scans run over the upper bound; entries past nstrips * ncols are not
+            w.sstart, w.cnz, w.gstart);
+  // one scan gives first pairs (low word) and output tile indices (high);
+  // it runs over the upper bound: entries past nstrips * ncols are not
   // written and only ever enter prefixes past the used length
-  ES_TRY(exclusive_scan<uint32_t>(w.counts, w.off, sc, w.total, w.scan, st));
-  ES_TRY(exclusive_scan<uint32_t>(w.nzflag, w.segid, sc, w.total, w.scan, st));
-  ES_LAUNCH(direct_totals_kernel, 1, 32, 0, st, w.off, w.segid, w.counts, w.nzflag, w.nstrips, w.ncols, w.bad,
-            counts_dev);
+  ES_TRY(exclusive_scan<uint64_t>(w.cnz, w.pos, sc, w.total64, reinterpret_cast<uint64_t*>(w.scan), st));
+  ES_LAUNCH(direct_totals_kernel, 1, 32, 0, st, w.pos, w.cnz, w.nstrips, w.ncols, w.bad, counts_dev);
   return ES_OK;
 }
 
@@ -484,10 +486,9 @@ extern "C" int es_direct_fill(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   const int64_t nchp1 = direct_chunks(n_lhs);
   const int64_t cb = direct_col_bound(g, n_rhs);
   const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
-  ES_LAUNCH(direct_segments_kernel, grid_for(sc, 256), 256, 0, st, lhs_coords, g, w.colids, w.ncols, w.nstrips,
-            w.sstart, w.counts, w.off, w.segid, num_pairs, num_segments, out_coords, seg_offsets, seg_strip);
-  ES_LAUNCH(direct_pairs_kernel, grid_for((nchp1 - 1) * ((cb + kDirCols - 1) / kDirCols) * 32, 256), 256, 0, st,
-            lhs_coords, n_lhs, g, w.table, w.colids, w.ncols, nchp1, w.cscan, w.sflag, w.sexcl, w.off, w.gstart,
-            seg_lhs, seg_rhs, seg_key);
+  const int64_t units = (nchp1 - 1) * ((cb + kDirCols - 1) / kDirCols) * 32;
+  ES_LAUNCH(direct_pairs_kernel, grid_for(units > sc ? units : sc, 256), 256, 0, st, lhs_coords, n_lhs, g, w.table,
+            w.colids, w.ncols, w.nstrips, w.sstart, nchp1, w.cscan, w.sflag, w.sexcl, w.cnz, w.pos, w.gstart,
+            num_pairs, num_segments, seg_lhs, seg_rhs, seg_key, out_coords, seg_offsets, seg_strip);
   return ES_OK;
 }
