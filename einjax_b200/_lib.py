@@ -65,6 +65,9 @@ SIGNATURES = {
     "es_tile_einsum_path": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_int, c_int, c_int]),
     "es_out_tile_shape": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_i64p]),
     "es_segsum_workspace_size": (c_sz, [c_i64]),
+    "es_sparsity_stats_workspace_size": (c_sz, [c_i64, c_int, c_i64p, c_i64p, c_int]),
+    "es_sparsity_stats": (c_int, [c_vp, c_vp, c_int, c_i64, c_int, c_i64p, c_i64p, c_int, c_vp, c_sz, c_vp, c_vp, c_vp,
+                                  c_vp]),
     "es_segsum_plan": (c_int, [c_vp, c_i64, c_int, c_i64p, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "es_segsum_fill": (c_int, [c_vp, c_int, c_i64, c_i64, c_int, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_int, c_vp]),
     "es_scatter_add_workspace_size": (c_sz, [c_i64]),

@@ -260,13 +260,87 @@ def _extract_coo(data: Any):
     return "dense", arr, None, tuple(arr.shape)
 
 
+def find_all_factors(n: int) -> list:
+    """Sorted divisors of n (``core/notation.py:27-43``)."""
+    n = int(n)
+    if n <= 0:
+        raise ValueError(f"n must be positive, got {n}")
+    out = set()
+    for i in range(1, int(n ** 0.5) + 1):
+        if n % i == 0:
+            out.update((i, n // i))
+    return sorted(out)
+
+
+def factor_tile_shapes(shape) -> list:
+    """The tiling schemes a tensor of this shape enumerates: every tile shape
+    whose sides divide the shape (``tensor/base.py:43-49``), sorted."""
+    import itertools
+    return sorted(itertools.product(*[find_all_factors(n) for n in shape]))
+
+
+def _sparsity_stats(indices, values, shape, tile_shapes, device):
+    lib = L.lib()
+    shape = tuple(int(s) for s in shape)
+    nd = len(shape)
+    ts = [tuple(int(t) for t in x) for x in tile_shapes]
+    for t in ts:
+        if len(t) != nd or min(t) <= 0:
+            raise ValueError(f"tile shape {t} does not fit a tensor of shape {shape}")
+    dev = torch.device(device) if device is not None else default_device()
+    if indices is not None:
+        idx = torch.as_tensor(np.asarray(indices) if not torch.is_tensor(indices) else indices)
+        idx = idx.to(device=dev, dtype=torch.int32).reshape(-1, nd).contiguous()
+        n = int(idx.shape[0])
+    else:
+        idx = None
+        n = prod(shape)
+    vals = None
+    if values is not None:
+        vals = values if torch.is_tensor(values) else torch.as_tensor(np.asarray(values))
+        if vals.dtype not in (torch.float32, torch.float64, torch.bfloat16):
+            vals = vals.to(torch.float64)
+        vals = vals.to(dev).reshape(-1).contiguous()
+        if int(vals.shape[0]) != n:
+            raise ValueError("values and indices disagree in length")
+    S = len(ts)
+    sh, tl = L.i64arr(shape), L.i64arr([v for t in ts for v in t])
+    ws = workspace(lib.es_sparsity_stats_workspace_size(n, nd, sh, tl, S), dev)
+    nt = torch.zeros(max(S, 1), dtype=torch.int64, device=dev)
+    vc = torch.zeros((max(S, 1), nd), dtype=torch.int64, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    L.check("es_sparsity_stats", lib.es_sparsity_stats(
+        idx.data_ptr() if idx is not None else None, vals.data_ptr() if vals is not None else None,
+        es_dtype(vals) if vals is not None else L.ES_F32, n, nd, sh, tl, S, ws.data_ptr(), ws.numel(),
+        nt.data_ptr(), vc.data_ptr(), err.data_ptr(), stream_ptr(dev)))
+    nt_h, vc_h, e = nt.cpu().tolist(), vc.cpu().tolist(), int(err.item())
+    if e:
+        raise ValueError("COO index outside the tensor shape")
+    return {t: (int(nt_h[i]), tuple(int(v) for v in vc_h[i])) for i, t in enumerate(ts)}
+
+
+def compute_sparsity_stats_coo(indices, values, shape, tile_shapes, device=None) -> dict:
+    """T(U) and V(l, U) for every tile shape U (``tensor/stats.py:25-80``):
+    ``{tile_shape: (num_tuples, value_count)}``, computed on the GPU. Zero
+    values do not count; repeated coordinates count once."""
+    return _sparsity_stats(indices, values, shape, tile_shapes, device)
+
+
+def compute_sparsity_stats_dense(data, tile_shapes, device=None) -> dict:
+    """``compute_sparsity_stats_coo`` of a dense array's non-zeros
+    (``tensor/stats.py:81-117``), reading the dense array directly."""
+    d = data if torch.is_tensor(data) else torch.as_tensor(np.asarray(data))
+    return _sparsity_stats(None, d, tuple(d.shape), tile_shapes, device)
+
+
 class SparseTensor:
     """User-facing sparse tensor (``tensor/sparse.py:93-231``) whose tiling runs on the GPU.
 
     ``data``: a scipy sparse matrix, a dense numpy array / torch tensor, or a
     ``(indices, values, shape)`` COO triple (indices int32 ``(nnz, ndim)``; any
-    rank, unlike scipy). The reference's per-scheme sparsity statistics
-    (``_compute_sparsity_metrics``, planner input) are not computed here.
+    rank, unlike scipy). The reference computes per-scheme sparsity
+    statistics (``_compute_sparsity_metrics``, planner input) in its
+    constructor; here ``sparsity_stats()`` computes them on the GPU on demand.
     """
 
     def __init__(self, name: str, data: Any, device=None, dtype=None):
@@ -279,6 +353,16 @@ class SparseTensor:
     @property
     def ndim(self) -> int:
         return len(self.shape)
+
+    def sparsity_stats(self, tile_shapes=None) -> dict:
+        """``{tile_shape: (num_tuples, value_count)}`` for the given tile shapes,
+        by default every tiling scheme of the shape (the ``num_tuples`` and
+        ``value_count`` of the reference's ``self.schemes``,
+        ``tensor/sparse.py:122-158``)."""
+        ts = factor_tile_shapes(self.shape) if tile_shapes is None else tile_shapes
+        if self._kind == "coo":
+            return _sparsity_stats(self._a, self._b, self.shape, ts, self.device)
+        return _sparsity_stats(None, self._a, self.shape, ts, self.device)
 
     def to_relation(self, tile_shape) -> SparseTensorRelation:
         tile_shape = tuple(int(t) for t in tile_shape)

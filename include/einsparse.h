@@ -277,6 +277,30 @@ int es_scatter_add_rows(const void* values, int values_dtype, const int32_t* idx
                         int64_t tile_elems, int64_t num_out_rows, void* workspace,
                         size_t workspace_bytes, float* out, int32_t* error_dev, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Sparsity statistics per tiling scheme, the contraction planner's input
+ * (tensor/stats.py:25-80 compute_sparsity_stats_coo; the metrics
+ * SparseTensor / DenseTensor compute for every scheme, tensor/sparse.py:122-158,
+ * tensor/dense.py:44-94). For each of num_schemes tile shapes U
+ * (tile_shapes: host int64 (num_schemes, ndim), sides >= 1):
+ *   num_tuples_dev[u]            = T(U), tiles holding a non-zero entry;
+ *   value_count_dev[u*ndim + l]  = V(l, U), distinct tile coordinates along l.
+ * Entries: COO (indices int32 (num_entries, ndim), values of values_dtype or
+ * NULL when every entry counts), or with indices == NULL a dense row-major
+ * array `values` of `shape` (num_entries = its element count). Zeros do not
+ * count; repeated coordinates count once. A coordinate outside the shape sets
+ * *error_dev to ES_ERR_INDEX. Tile grids up to 2^32 tiles use a bitmap (the
+ * workspace holds up to 512 MB of them per pass, several schemes per pass);
+ * larger grids count distinct tile keys after a radix sort of the entries.
+ * workspace: es_sparsity_stats_workspace_size bytes for the same arguments.
+ * ------------------------------------------------------------------------- */
+size_t es_sparsity_stats_workspace_size(int64_t num_entries, int ndim, const int64_t* shape,
+                                        const int64_t* tile_shapes, int num_schemes);
+int es_sparsity_stats(const int32_t* indices, const void* values, int values_dtype, int64_t num_entries, int ndim,
+                      const int64_t* shape, const int64_t* tile_shapes, int num_schemes, void* workspace,
+                      size_t workspace_bytes, int64_t* num_tuples_dev, int64_t* value_count_dev,
+                      int32_t* error_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,7 +34,7 @@ __all__ = [
     "partition_matched_pairs", "execute_sharded_sparse",
     "block_sparse_matmul_generic", "reverse_einsum_string",
     "sparse_einsum_raw_fwd", "sparse_einsum_raw_bwd", "canonical_pairs",
-    "relation_allclose",
+    "relation_allclose", "find_all_factors", "factor_tile_shapes", "compute_sparsity_stats_coo",
 ]
 
 
@@ -475,3 +475,44 @@ def relation_allclose(got_coords, got_values, ref: Relation, rtol, mag=None):
         return False, (f"{int(bad.sum())} elements out of tolerance; worst flat index {i}: "
                        f"got {g.flat[i]!r} ref {r.flat[i]!r}")
     return True, "ok"
+
+
+# ------------------------------------------------------------ sparsity statistics
+
+
+def find_all_factors(n: int) -> list:
+    """Sorted divisors of n (``core/notation.py:27-43``)."""
+    if n <= 0:
+        raise ValueError(f"n must be positive, got {n}")
+    out = set()
+    for i in range(1, int(n ** 0.5) + 1):
+        if n % i == 0:
+            out.add(i)
+            out.add(n // i)
+    return sorted(out)
+
+
+def factor_tile_shapes(shape) -> list:
+    """Every tile shape whose sides divide the shape: the tiling schemes a
+    tensor enumerates (``tensor/base.py:43-49``), in lexicographic order."""
+    import itertools
+    return sorted(itertools.product(*[find_all_factors(int(n)) for n in shape]))
+
+
+def compute_sparsity_stats_coo(indices, values, shape, tile_shapes) -> dict:
+    """T(U) (non-empty tiles) and V(l, U) (distinct tile coordinates along
+    dimension l) per tiling scheme U, over the non-zero entries
+    (``tensor/stats.py:25-80``; ``SparseTensor._compute_sparsity_metrics``,
+    ``tensor/sparse.py:122-158``). Repeated coordinates count once."""
+    idx = np.asarray(indices).reshape(len(values), -1).astype(np.int64)
+    nz = idx[np.asarray(values) != 0]
+    nd = len(shape)
+    out = {}
+    for ts in tile_shapes:
+        ts = tuple(int(t) for t in ts)
+        if len(nz) == 0:
+            out[ts] = (0, tuple(0 for _ in range(nd)))
+            continue
+        tc = nz // np.array(ts, dtype=np.int64)
+        out[ts] = (int(len(np.unique(tc, axis=0))), tuple(int(len(np.unique(tc[:, d]))) for d in range(nd)))
+    return out

@@ -18,6 +18,9 @@ benchmark configurations. Outputs go to ``tests/golden/*.npz`` (keys
 ``<case>__<field>``, with a JSON ``<case>__meta``).
 
 Usage:  python tests/golden/make_golden.py --reference <path-to-einjax>
+        python tests/golden/make_golden.py --reference <path> --stats-only
+            (only ``golden_stats.npz``: per-tiling-scheme sparsity statistics
+            from ``tensor/stats.py`` and ``SparseTensor``'s metrics)
 """
 
 from __future__ import annotations
@@ -45,7 +48,7 @@ def load_reference(root: str):
         m.__path__ = [os.path.join(root, sub)]
         sys.modules[f"einjax.{sub}"] = m
     mods = {}
-    for name in ("tensor.sparse", "execution.sparse_dispatch", "kernels.pallas_matmul",
+    for name in ("tensor.sparse", "tensor.stats", "execution.sparse_dispatch", "kernels.pallas_matmul",
                  "kernels.pallas_gather", "kernels.registry", "autodiff.custom_vjp",
                  "sharding.partition"):
         mods[name] = importlib.import_module(f"einjax.{name}")
@@ -66,11 +69,51 @@ class Store:
         np.savez_compressed(path, **self.arrays)
 
 
+def make_stats(mods):
+    """Sparsity statistics T(U), V(l, U) per tiling scheme: the reference's
+    SparseTensor metrics (tensor/sparse.py:122-158, all factor tile shapes of
+    the shape) and compute_sparsity_stats_coo (tensor/stats.py:25-80), on
+    seeded inputs with explicit zeros and repeated coordinates."""
+    sp_mod, stats = mods["tensor.sparse"], mods["tensor.stats"]
+    st = Store()
+    rng = np.random.default_rng(31)
+    dense_cases = {"dense2d": (12, 18), "dense3d": (8, 12, 6), "dense1d": (30,)}
+    for name, shape in dense_cases.items():
+        d = rng.standard_normal(shape) * (rng.random(shape) < 0.15)
+        t = sp_mod.SparseTensor(name, d)
+        ts = sorted(t.schemes)
+        st.put(f"stats_{name}", {"kind": "stats", "source": "SparseTensor"}, dense=d,
+               shape=np.array(shape, dtype=np.int64), tile_shapes=np.array(ts, dtype=np.int64),
+               num_tuples=np.array([t.schemes[k].num_tuples for k in ts], dtype=np.int64),
+               value_count=np.array([t.schemes[k].value_count for k in ts], dtype=np.int64))
+    coo_cases = {"coo2d": ((64, 48), 300), "coo3d": ((16, 24, 10), 500), "coo2d_large": ((256, 512), 4000)}
+    for name, (shape, nnz) in coo_cases.items():
+        idx = np.stack([rng.integers(0, n, nnz) for n in shape], 1).astype(np.int32)
+        idx[rng.choice(nnz, nnz // 10, replace=False)] = idx[rng.choice(nnz, nnz // 10)]  # repeats
+        val = rng.standard_normal(nnz)
+        val[rng.random(nnz) < 0.1] = 0.0  # explicit zeros do not count
+        factors = [mods["core.notation"].find_all_factors(n) for n in shape]
+        import itertools
+        ts = sorted(itertools.product(*factors))
+        res = stats.compute_sparsity_stats_coo(idx, val, tuple(shape), ts)
+        st.put(f"stats_{name}", {"kind": "stats", "source": "compute_sparsity_stats_coo"}, indices=idx, values=val,
+               shape=np.array(shape, dtype=np.int64), tile_shapes=np.array(ts, dtype=np.int64),
+               num_tuples=np.array([res[k][0] for k in ts], dtype=np.int64),
+               value_count=np.array([res[k][1] for k in ts], dtype=np.int64))
+    st.save(os.path.join(HERE, "golden_stats.npz"))
+    print("wrote", len(st.arrays), "arrays to golden_stats.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--stats-only", action="store_true")
     args = ap.parse_args()
     mods = load_reference(os.path.abspath(args.reference))
+    mods["core.notation"] = importlib.import_module("einjax.core.notation")
+    make_stats(mods)
+    if args.stats_only:
+        return
     import jax
     sp_mod = mods["tensor.sparse"]
     sd = mods["execution.sparse_dispatch"]

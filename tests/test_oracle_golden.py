@@ -178,3 +178,21 @@ def test_config_chain():
     abc = O.execute_sparse(ab, C, mm[0], mm[1], mm[2], compute_dtype="f32")
     np.testing.assert_array_equal(abc.coords, c["abc_coords"])
     _close(abc.values, c["abc_values"], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("name", sorted(cases_of_kind("stats", "golden_stats.npz")))
+def test_sparsity_stats(name):
+    """T(U) and V(l, U) of every tiling scheme, against the reference's own
+    SparseTensor metrics / compute_sparsity_stats_coo."""
+    c = load_cases("golden_stats.npz")[name]
+    shape = tuple(int(v) for v in c["shape"])
+    if "dense" in c:
+        nzi = np.nonzero(c["dense"])
+        idx, val = np.stack(nzi, 1).astype(np.int32), c["dense"][nzi]
+    else:
+        idx, val = c["indices"], c["values"]
+    ts = [tuple(int(v) for v in t) for t in c["tile_shapes"]]
+    assert ts == O.factor_tile_shapes(shape)
+    res = O.compute_sparsity_stats_coo(idx, val, shape, ts)
+    np.testing.assert_array_equal([res[t][0] for t in ts], c["num_tuples"])
+    np.testing.assert_array_equal([res[t][1] for t in ts], c["value_count"])
