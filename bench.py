@@ -462,6 +462,57 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_stats(args):
+    """Sparsity statistics of every tiling scheme (planner input, tensor/stats.py)
+    on C2's COO: A 65536^2 with 4,294,967 entries, all 17 x 17 = 289 factor
+    tile shapes. One step = T(U) and V(l, U) of all schemes, device-resident
+    COO. The reference's own per-scheme np.unique is timed beside it on a
+    sample of schemes (cpu_baseline, extrapolated per scheme)."""
+    import torch
+
+    import einjax_b200 as E
+    import oracle as O
+    from einjax_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = W.c2_spmm(seed=args.seed, scale=args.scale)
+    shape = w.lhs.shape
+    idx = torch.from_numpy(w.lhs.indices).to(dev)
+    val = torch.from_numpy(w.lhs.values).to(dev)
+    ts = E.factor_tile_shapes(shape)
+    for _ in range(args.warmup):
+        got = E.compute_sparsity_stats_coo(idx, val, shape, ts, device=dev)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        got = E.compute_sparsity_stats_coo(idx, val, shape, ts, device=dev)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    nnz = int(val.numel())
+    # check a sample of schemes against the oracle (integers: exact)
+    sample = [ts[0], ts[len(ts) // 3], ts[len(ts) // 2], ts[-1]]
+    t0 = time.time()
+    ref = O.compute_sparsity_stats_coo(w.lhs.indices, w.lhs.values, shape, sample)
+    cpu_s = (time.time() - t0) / len(sample)
+    assert all(got[t] == ref[t] for t in sample), "sparsity statistics differ from the oracle"
+    line = {
+        "metric": "sparsity statistics: tiling schemes per second (C2 COO, all factor tile shapes)",
+        "value": round(len(ts) / (ms * 1e-3), 1), "unit": "schemes/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic (seeded C2 generator)",
+        "config": {"workload": f"STATS: A {shape[0]}x{shape[1]} COO {nnz} entries, {len(ts)} tile shapes",
+                   "l2": "device-resident COO (51 MB) is re-read once per batch of schemes"},
+        "entries_x_schemes_per_s": round(nnz * len(ts) / (ms * 1e-3), 1),
+        "cpu_baseline": {"value": round(1.0 / cpu_s, 3), "unit": "schemes/s", "cores": 1, "kind": "port",
+                         "sample": f"np.unique over {nnz} entries for {len(sample)} of the {len(ts)} schemes, "
+                                   f"{cpu_s:.2f} s per scheme"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_config(args):
     """The other BASELINE configurations on one GPU, for the results table
     (the headline line is C2, ``run_ours``). One step = the sparse path on
@@ -577,11 +628,13 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", default="auto", choices=["auto", "exact", "tc"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="C2", choices=["C1", "C2", "C3", "C4", "C5"],
+    ap.add_argument("--workload", default="C2", choices=["C1", "C2", "C3", "C4", "C5", "STATS"],
                     help="C2 is the headline line; the others measure one GPU for the results table")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "STATS":
+        run_stats(args)
     elif args.workload != "C2":
         run_config(args)
     else:

@@ -95,8 +95,14 @@ __device__ __forceinline__ bool stats_entry(const int32_t* __restrict__ idx, con
   return true;
 }
 
+// Sets a bit, skipping the atomic when a plain read already sees it set:
+// bits only go from 0 to 1 during a pass, so a stale read can only cost a
+// redundant atomic. Coarse tilings (few tiles, every entry on a handful of
+// words) would otherwise serialise millions of atomics on one L2 line.
 __device__ __forceinline__ void set_bit(uint32_t* bm, uint64_t bit) {
-  atomicOr(bm + (bit >> 5), 1u << (bit & 31));
+  uint32_t* w = bm + (bit >> 5);
+  const uint32_t m = 1u << (bit & 31);
+  if (!(*reinterpret_cast<volatile uint32_t*>(w) & m)) atomicOr(w, m);
 }
 
 // Per-dimension coordinate bitmaps.
