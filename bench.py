@@ -517,8 +517,9 @@ def run_config(args):
     """The other BASELINE configurations on one GPU, for the results table
     (the headline line is C2, ``run_ours``). One step = the sparse path on
     device-resident inputs: C1/C3 ``execute_sparse`` of two tile relations;
-    C4 the chain (A B) C forward and the gradients of all three operands
-    through ``sparse_einsum`` (loss = sum of the output); C5 COO -> tiles of X
+    C4 the plan (A B) C through ``execute_sparse_plan`` (intermediate kept
+    on the GPU), forward and the gradients of all three operands (loss = sum
+    of the output); C5 COO -> tiles of X
     and W, then ``execute_sparse``."""
     import torch
 
@@ -531,6 +532,7 @@ def run_config(args):
     t0 = time.time()
     if wl == "C4":
         w = W.c4_chain(seed=args.seed, scale=args.scale)
+        c4_plan = E.plan_from_path("ij,jk,kl->il", [(0, 1), (0, 1)])  # (A B) C
         t = w["tile"]
         ops = [E.SparseTensorRelation.from_arrays(w[k].coords, w[k].values, w[k].shape, w[k].tile_shape,
                                                   device=dev, dtype=torch.float32) for k in ("A", "B", "C")]
@@ -560,12 +562,11 @@ def run_config(args):
 
     def step():
         if wl == "C4":
-            A, B, C = (E.SparseTensorRelation(o.coords, o.values.detach().requires_grad_(True), o.shape,
-                                              o.tile_shape) for o in ops)
-            AB = E.sparse_einsum(A, B, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
-            D = E.sparse_einsum(AB, C, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+            rels = [E.SparseTensorRelation(o.coords, o.values.detach().requires_grad_(True), o.shape,
+                                           o.tile_shape) for o in ops]
+            D = E.execute_sparse_plan(c4_plan, rels, differentiable=True)
             D.values.sum().backward()
-            return AB, D
+            return D, None
         if wl in ("C1", "C3"):
             return E.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys), None
         X = E.tile_coo(idx, val, w.lhs.shape, w.lhs_tile)
@@ -580,8 +581,10 @@ def run_config(args):
         out, aux = step()
     torch.cuda.synchronize()
     if wl == "C4":
+        AB = E.execute_sparse(ops[0], ops[1], [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
         P1 = pairs(ops[0], ops[1], [(1, 0)], [(0, 0), (1, 1)])
-        P2 = pairs(out, ops[2], [(1, 0)], [(0, 0), (1, 1)])
+        P2 = pairs(AB, ops[2], [(1, 0)], [(0, 0), (1, 1)])
+        del AB
         flops = 3 * (P1 + P2) * 2 * t[0] ** 3  # forward + two backward products per pair
         P = P1 + P2
     elif wl in ("C1", "C3"):

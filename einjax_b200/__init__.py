@@ -11,6 +11,7 @@ from .autodiff import _reverse_einsum_string, sparse_einsum, sparse_einsum_raw  
 from .kernels import (block_sparse_matmul, block_sparse_matmul_generic, coordinate_join_hash,  # noqa: F401
                       coordinate_join_sorted)
 from .partition import tile_shape_to_partition_spec  # noqa: F401
+from .plan import PlanStep, execute_sparse_plan, plan_from_path, reduction_keys  # noqa: F401
 from .registry import KernelInfo, KernelRegistry, register_b200_kernels  # noqa: F401
 from .sparse import (SparseTensor, SparseTensorRelation, compute_sparsity_stats_coo,  # noqa: F401
                      compute_sparsity_stats_dense, factor_tile_shapes, find_all_factors, tile_coo, tile_dense)

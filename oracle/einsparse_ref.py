@@ -35,6 +35,7 @@ __all__ = [
     "block_sparse_matmul_generic", "reverse_einsum_string",
     "sparse_einsum_raw_fwd", "sparse_einsum_raw_bwd", "canonical_pairs",
     "relation_allclose", "find_all_factors", "factor_tile_shapes", "compute_sparsity_stats_coo",
+    "infer_reduction_keys", "execute_plan",
 ]
 
 
@@ -340,6 +341,38 @@ def execute_sparse(lhs: Relation, rhs: Relation, join_keys, kernel_string, agg_k
     oc = compute_output_coords(lhs.coords, rhs.coords, li, ri, agg_keys)
     coords, vals = segment_sum(tiles, oc)
     return Relation(coords, vals, output_shape, output_tile_shape)
+
+
+def infer_reduction_keys(formula: str):
+    """Join keys, aggregation keys (as ``(side, dim)``) and output shape labels of a
+    binary formula: ``optimizer/dp.py:50-95``. Scans lhs then rhs labels; a label
+    seen before joins (its first position, this position); each output label
+    aggregates from its first position."""
+    ins, out = formula.replace(" ", "").split("->")
+    terms = ins.split(",")
+    first, join_keys = {}, []
+    for side, labels in enumerate(terms):
+        for i, c in enumerate(labels):
+            if c in first:
+                join_keys.append((first[c][1], i))
+            else:
+                first[c] = (side, i)
+    return join_keys, [first[c] for c in out]
+
+
+def execute_plan(steps, operands, compute_dtype="f64") -> Relation:
+    """``ExecutionEngine.execute_plan`` (``execution/engine.py:264-324``) over
+    tile-COO relations: ``steps`` are ``(formula, (i, j))``; each step contracts
+    working operands i and j with ``execute_sparse``, deletes them (higher index
+    first) and appends the result; the last intermediate is returned."""
+    work = list(operands)
+    for formula, (i, j) in steps:
+        jk, ak = infer_reduction_keys(formula)
+        res = execute_sparse(work[i], work[j], jk, formula.replace(" ", ""), ak, compute_dtype=compute_dtype)
+        for k in sorted((i, j), reverse=True):
+            del work[k]
+        work.append(res)
+    return work[-1]
 
 
 def partition_matched_pairs(num_matches: int, num_devices: int):

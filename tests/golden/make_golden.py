@@ -21,6 +21,10 @@ Usage:  python tests/golden/make_golden.py --reference <path-to-einjax>
         python tests/golden/make_golden.py --reference <path> --stats-only
             (only ``golden_stats.npz``: per-tiling-scheme sparsity statistics
             from ``tensor/stats.py`` and ``SparseTensor``'s metrics)
+        python tests/golden/make_golden.py --reference <path> --plan-only
+            (only ``golden_plan.npz``: join / aggregation keys from
+            ``optimizer/dp.py``'s ``infer_reduction_info`` and multi-step plans
+            run by ``execution/engine.py``'s ``ExecutionEngine.execute_plan``)
 """
 
 from __future__ import annotations
@@ -43,7 +47,11 @@ def load_reference(root: str):
     pkg = types.ModuleType("einjax")
     pkg.__path__ = [root]
     sys.modules["einjax"] = pkg
-    for sub in ("core", "tensor", "execution", "kernels", "autodiff", "sharding"):
+    if "opt_einsum" not in sys.modules:
+        # optimizer/contraction_path.py imports opt_einsum at module level but only
+        # get_contraction_order calls it; the plans below give their steps explicitly.
+        sys.modules["opt_einsum"] = types.ModuleType("opt_einsum")
+    for sub in ("core", "tensor", "execution", "kernels", "autodiff", "sharding", "optimizer"):
         m = types.ModuleType(f"einjax.{sub}")
         m.__path__ = [os.path.join(root, sub)]
         sys.modules[f"einjax.{sub}"] = m
@@ -104,16 +112,113 @@ def make_stats(mods):
     print("wrote", len(st.arrays), "arrays to golden_stats.npz")
 
 
+KEY_FORMULAS = ["ij,jk->ik", "bij,bjk->bik", "ijk,kl->ijl", "ij,kj->ik", "ij,ij->ij", "i,j->ij", "ijk,jk->i",
+                "abc,cab->b", "jk,kl->jl", "bkl,bik->bil", "jm,ijl->ilm", "ji,jk->ki", "ij,jk->ki"]
+
+# (einsum string, operand shapes, operand tile shapes, element density, path, step formulas)
+PLANS = {
+    "plan_chain3": ("ij,jk,kl->il", [(96, 64), (64, 80), (80, 48)], [(16, 16), (16, 16), (16, 16)], 0.05,
+                    [(1, 2), (0, 1)], ["jk,kl->jl", "ij,jl->il"]),
+    "plan_chain4": ("ij,jk,kl,lm->im", [(64, 48), (48, 32), (32, 40), (40, 24)], [(8, 8)] * 4, 0.08,
+                    [(0, 1), (0, 1), (0, 1)], ["ij,jk->ik", "kl,lm->km", "ik,km->im"]),
+    "plan_batched": ("bij,jk,bkl->bil", [(3, 32, 24), (24, 40), (3, 40, 16)], [(1, 8, 8), (8, 8), (1, 8, 8)], 0.1,
+                     [(0, 1), (0, 1)], ["bij,jk->bik", "bkl,bik->bil"]),
+    "plan_order3": ("ijk,kl,jm->ilm", [(16, 24, 32), (32, 20), (24, 12)], [(4, 8, 8), (8, 4), (8, 4)], 0.1,
+                    [(0, 1), (0, 1)], ["ijk,kl->ijl", "jm,ijl->ilm"]),
+}
+
+
+def make_plan(mods):
+    """Join / aggregation keys from the reference's infer_reduction_info
+    (optimizer/dp.py:50-95) for single binary formulas, and multi-operand plans
+    executed two ways by the reference: ExecutionEngine.execute_plan
+    (execution/engine.py:264-324) over the dense operands, and the same steps
+    as a chain of its sparse execute_sparse over tile-COO relations."""
+    import jax
+    dp = importlib.import_module("einjax.optimizer.dp")
+    base = importlib.import_module("einjax.tensor.base")
+    cp = importlib.import_module("einjax.optimizer.contraction_path")
+    eng = importlib.import_module("einjax.execution.engine")
+    sp_mod, sd = mods["tensor.sparse"], mods["execution.sparse_dispatch"]
+    st = Store()
+
+    def keys(formula, lshape, rshape):
+        ins, out = formula.split("->")
+        a, b = ins.split(",")
+        lt, rt = base.BaseTensor("L", lshape), base.BaseTensor("R", rshape)
+        info = dp.infer_reduction_info(out, base.IndexedTerm(lt, a), base.IndexedTerm(rt, b))
+        side = lambda t: 0 if t is lt else 1  # noqa: E731
+        return info, {"join_keys": [[jl[1], jr[1]] for jl, jr in info.join_keys],
+                      "join_sides": [[side(jl[0]), side(jr[0])] for jl, jr in info.join_keys],
+                      "agg_keys": [[side(t), i] for t, i in info.aggregation_keys],
+                      "output_shape": list(info.output_shape)}
+
+    for n, f in enumerate(KEY_FORMULAS):
+        ins = f.split("->")[0].split(",")
+        dims = {}
+        for c in "".join(ins):
+            dims.setdefault(c, 2 + len(dims))
+        _, meta = keys(f, tuple(dims[c] for c in ins[0]), tuple(dims[c] for c in ins[1]))
+        st.put(f"keys_{n}", {"kind": "keys", "formula": f, **meta})
+
+    rng = np.random.default_rng(77)
+    for name, (es, shapes, tiles, dens, path, formulas) in PLANS.items():
+        dense = [rng.standard_normal(s) * (rng.random(s) < dens) for s in shapes]
+        tensors = [base.BaseTensor(f"x{i}", s) for i, s in enumerate(shapes)]
+        ops_t, steps, metas = list(tensors), [], []
+        for k, ((i, j), f) in enumerate(zip(path, formulas)):
+            ins, out = f.split("->")
+            a, b = ins.split(",")
+            info, meta = keys(f, ops_t[i].shape, ops_t[j].shape)
+            res_t = base.BaseTensor(f"_t{k}", info.output_shape)
+            steps.append(cp.ContractionStep(k, f, (i, j), a, b, out, res_t, info))
+            metas.append({"formula": f, "input_indices": [i, j], **meta})
+            for idx in sorted((i, j), reverse=True):
+                del ops_t[idx]
+            ops_t.append(res_t)
+        plan = cp.ContractionPlan(es, steps, 0.0, [])
+        out_dense = np.asarray(eng.ExecutionEngine().execute_plan(plan, [np.asarray(d) for d in dense]))
+        # the same steps over tile-COO relations through the reference's sparse path
+        work = [sp_mod.SparseTensor(f"x{i}", d).to_relation(t) for i, (d, t) in enumerate(zip(dense, tiles))]
+        arrays = {}
+        for i, r in enumerate(work):
+            arrays[f"op{i}_coords"] = r.coords
+            arrays[f"op{i}_values"] = r.values.astype(np.float32)
+            arrays[f"op{i}_shape"] = np.array(r.shape, np.int64)
+            arrays[f"op{i}_tile"] = np.array(r.tile_shape, np.int64)
+            arrays[f"op{i}_dense"] = dense[i]
+        jax.F32 = True
+        for m in metas:
+            i, j = m["input_indices"]
+            res = sd.execute_sparse(work[i], work[j], [tuple(k) for k in m["join_keys"]], m["formula"],
+                                    [tuple(k) for k in m["agg_keys"]])
+            for idx in sorted((i, j), reverse=True):
+                del work[idx]
+            work.append(res)
+        jax.F32 = False
+        fin = work[-1]
+        st.put(name, {"kind": "plan", "einsum": es, "path": [list(p) for p in path], "steps": metas,
+                      "n_ops": len(shapes), "res_shape": list(fin.shape), "res_tile": list(fin.tile_shape)},
+               **arrays, out_dense=out_dense, res_coords=fin.coords, res_values=np.asarray(fin.values, np.float32))
+    st.save(os.path.join(HERE, "golden_plan.npz"))
+    print("wrote", len(st.arrays), "arrays to golden_plan.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--stats-only", action="store_true")
+    ap.add_argument("--plan-only", action="store_true")
     args = ap.parse_args()
     mods = load_reference(os.path.abspath(args.reference))
     mods["core.notation"] = importlib.import_module("einjax.core.notation")
+    if args.plan_only:
+        make_plan(mods)
+        return
     make_stats(mods)
     if args.stats_only:
         return
+    make_plan(mods)
     import jax
     sp_mod = mods["tensor.sparse"]
     sd = mods["execution.sparse_dispatch"]

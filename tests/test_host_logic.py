@@ -109,3 +109,36 @@ def test_balanced_key_ranges(n_ranks):
     loads = [counts[a:b].sum() for a, b in parts]
     assert sum(loads) == counts.sum()
     assert max(loads) <= counts.sum() / n_ranks + counts.max()
+
+
+PLAN = load_cases("golden_plan.npz")
+
+
+@pytest.mark.parametrize("name", sorted(k for k in PLAN if PLAN[k].meta["kind"] == "keys"))
+def test_reduction_keys_match_reference(name):
+    """Keys of the plan executor's steps against the reference's infer_reduction_info."""
+    m = PLAN[name].meta
+    jk, ks, ak = E.reduction_keys(m["formula"])
+    assert [list(k) for k in jk] == m["join_keys"]
+    assert [list(k) for k in ak] == m["agg_keys"]
+    assert ks == m["formula"]
+
+
+@pytest.mark.parametrize("name", sorted(k for k in PLAN if PLAN[k].meta["kind"] == "plan"))
+def test_plan_from_path_matches_reference_steps(name):
+    m = PLAN[name].meta
+    steps = E.plan_from_path(m["einsum"], m["path"])
+    assert [s.formula for s in steps] == [s["formula"] for s in m["steps"]]
+    assert [list(s.input_indices) for s in steps] == [s["input_indices"] for s in m["steps"]]
+
+
+def test_plan_helpers_reject_bad_input():
+    for bad in ("ij,jk", "ij->i", "ii,ij->j", "ij,jk->iq", "ij,jk,kl->il"):
+        with pytest.raises(ValueError):
+            E.reduction_keys(bad)
+    with pytest.raises(ValueError):
+        E.plan_from_path("ij,jk,kl->il", [(0, 1)])
+    with pytest.raises(ValueError):
+        E.plan_from_path("ij,jk->ik", [(0, 0)])
+    steps = E.plan_from_path("ij,jk->ki", [(0, 1)])
+    assert steps[0].formula == "ij,jk->ki"

@@ -196,3 +196,40 @@ def test_sparsity_stats(name):
     res = O.compute_sparsity_stats_coo(idx, val, shape, ts)
     np.testing.assert_array_equal([res[t][0] for t in ts], c["num_tuples"])
     np.testing.assert_array_equal([res[t][1] for t in ts], c["value_count"])
+
+
+PLAN = load_cases("golden_plan.npz")
+
+
+def _plan_ops(c):
+    return [O.Relation(c[f"op{i}_coords"], c[f"op{i}_values"].astype(np.float64),
+                       tuple(int(v) for v in c[f"op{i}_shape"]), tuple(int(v) for v in c[f"op{i}_tile"]))
+            for i in range(c.meta["n_ops"])]
+
+
+@pytest.mark.parametrize("name", sorted(cases_of_kind("keys", "golden_plan.npz")))
+def test_reduction_keys(name):
+    """Join / aggregation keys against the reference's infer_reduction_info."""
+    m = PLAN[name].meta
+    assert all(s == [0, 1] for s in m["join_sides"])
+    jk, ak = O.infer_reduction_keys(m["formula"])
+    assert [list(k) for k in jk] == m["join_keys"]
+    assert [list(k) for k in ak] == m["agg_keys"]
+
+
+@pytest.mark.parametrize("name", sorted(cases_of_kind("plan", "golden_plan.npz")))
+def test_execute_plan(name):
+    """The plan walk over tile-COO relations against the reference's sparse
+    chain (coordinates bit-exact, in order) and against its dense
+    ExecutionEngine.execute_plan result."""
+    c = PLAN[name]
+    steps = [(s["formula"], tuple(s["input_indices"])) for s in c.meta["steps"]]
+    for i in range(c.meta["n_ops"]):
+        ops = _plan_ops(c)
+        np.testing.assert_array_equal(ops[i].to_dense(), c[f"op{i}_dense"].astype(np.float32))
+    res = O.execute_plan(steps, _plan_ops(c), compute_dtype="f32")
+    np.testing.assert_array_equal(res.coords, c["res_coords"])
+    _close(res.values, c["res_values"], rtol=1e-5, atol=1e-5)
+    assert list(res.shape) == c.meta["res_shape"] and list(res.tile_shape) == c.meta["res_tile"]
+    res64 = O.execute_plan(steps, _plan_ops(c))
+    _close(res64.to_dense(), c["out_dense"], rtol=1e-5, atol=1e-6)
