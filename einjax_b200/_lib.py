@@ -18,6 +18,7 @@ LIB_PATH = os.environ.get("EINSPARSE_LIB", os.path.join(HERE, "libeinsparse.so")
 ES_OK, ES_ERR_INVALID, ES_ERR_INDEX, ES_ERR_WORKSPACE, ES_ERR_CUDA, ES_ERR_UNSUPPORTED, ES_ERR_TIMEOUT = range(7)
 ES_F32, ES_BF16, ES_F64, ES_I32, ES_I64 = range(5)
 ES_PREC_AUTO, ES_PREC_EXACT, ES_PREC_TC = range(3)
+ES_DUP_LAST, ES_DUP_SUM = range(2)
 
 c_i64 = ctypes.c_int64
 c_int = ctypes.c_int
@@ -37,6 +38,9 @@ SIGNATURES = {
     "es_tile_coo_plan": (c_int, [c_vp, c_vp, c_int, c_i64, c_int, c_i64p, c_i64p, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "es_tile_coo_fill": (c_int, [c_vp, c_int, c_i64, c_int, c_i64p, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_int,
                                  c_vp]),
+    "es_coo_coalesce_workspace_size": (c_sz, [c_i64, c_int, c_i64p]),
+    "es_coo_coalesce": (c_int, [c_vp, c_vp, c_int, c_i64, c_int, c_i64p, c_int, c_vp, c_sz, c_vp, c_vp, c_int, c_vp,
+                                c_vp, c_vp]),
     "es_tile_dense_workspace_size": (c_sz, [c_int, c_i64p, c_i64p]),
     "es_tile_dense_plan": (c_int, [c_vp, c_int, c_int, c_i64p, c_i64p, c_vp, c_sz, c_vp, c_vp]),
     "es_tile_dense_fill": (c_int, [c_vp, c_int, c_int, c_i64p, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_int, c_vp]),

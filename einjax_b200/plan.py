@@ -89,6 +89,27 @@ def plan_from_path(einsum_string: str, path: Sequence[Sequence[int]]) -> list:
     return steps
 
 
+def _operand_order(formula, lhs, rhs, precision):
+    """The step with its operands swapped (``"b,a->o"`` over (rhs, lhs)) when
+    only that order maps the tile product onto the tensor-core kernel, e.g.
+    ``"kl,ik->il"`` -> ``"ik,kl->il"``. The result relation is the same (a
+    dense einsum's value does not depend on the operand order; coordinates come
+    out sorted either way); the plan's choice of lhs is arbitrary."""
+    from .sparse_dispatch import tile_einsum_path
+    ins, out = formula.split("->")
+    a, b = ins.split(",")
+    swapped = f"{b},{a}->{out}"
+
+    def path(ks, l, r):
+        try:
+            return tile_einsum_path(ks, l.tile_shape, r.tile_shape, l.values.dtype, r.values.dtype, precision)
+        except ValueError:
+            return "none"
+    if path(formula, lhs, rhs) != "tc" and path(swapped, rhs, lhs) == "tc":
+        return swapped, rhs, lhs
+    return formula, lhs, rhs
+
+
 def execute_sparse_plan(steps, operands: Sequence, *, differentiable: bool = False,
                         precision: str = "auto") -> SparseTensorRelation:
     """Runs ``steps`` (``PlanStep``s, objects with ``formula`` and
@@ -96,7 +117,9 @@ def execute_sparse_plan(steps, operands: Sequence, *, differentiable: bool = Fal
     ``(formula, (i, j))`` pairs; a ``ContractionPlan`` is read through its
     ``steps``) over tile-COO operands
     (``execution/engine.py:264-324``): each step contracts operands i and j,
-    removes them and appends the result; returns the last intermediate. With
+    removes them and appends the result; returns the last intermediate. A
+    step whose tile product only the swapped operand order puts on the
+    tensor cores runs swapped (same result relation). With
     ``differentiable`` the steps run through ``sparse_einsum`` so gradients
     flow to every operand's values."""
     from .autodiff import sparse_einsum
@@ -106,8 +129,9 @@ def execute_sparse_plan(steps, operands: Sequence, *, differentiable: bool = Fal
     for step in steps:
         formula, idx = (step.formula, step.input_indices) if hasattr(step, "formula") else step
         i, j = (int(v) for v in idx)
-        jk, ks, ak = reduction_keys(formula)
         lhs, rhs = work[i], work[j]
+        formula, lhs, rhs = _operand_order(formula.replace(" ", ""), lhs, rhs, precision)
+        jk, ks, ak = reduction_keys(formula)
         if differentiable:
             res = sparse_einsum(lhs, rhs, jk, ks, ak, precision=precision)
         else:

@@ -170,14 +170,78 @@ def _check_divisible(shape, tile_shape):
             raise ValueError(f"tile_shape[{d}]={t} does not evenly divide shape[{d}]={s}")
 
 
+DUPLICATE_POLICIES = ("last", "sum", "error")
+
+
+def as_device_tensor(x, device=None) -> torch.Tensor:
+    """A torch tensor for ``x``: torch tensors as they are, objects exporting
+    DLPack (JAX / CuPy arrays; zero-copy when they already live on the GPU)
+    through ``torch.from_dlpack``, anything else through numpy; then moved
+    to ``device`` when given (no copy if it is already there)."""
+    if torch.is_tensor(x):
+        t = x
+    elif hasattr(x, "__dlpack__") and not isinstance(x, np.ndarray):
+        t = torch.from_dlpack(x)
+    else:
+        t = torch.as_tensor(np.asarray(x))
+    return t if device is None else t.to(device)
+
+
+def coalesce_coo(indices, values, shape, duplicates="sum", out_dtype=torch.float64):
+    """One entry per distinct coordinate holding a non-zero value, in row-major
+    coordinate order, on the GPU (``es_coo_coalesce``): ``duplicates="sum"``
+    adds repeated coordinates (float64, input order; scipy / torch sparse
+    semantics), ``"last"`` keeps the last in input order (the reference's
+    tiling, ``tensor/sparse.py:211-212``). Zero entries are dropped first.
+    Returns ``(indices int32 (n, ndim), values (n,), nonzero_inputs)``."""
+    if duplicates not in ("sum", "last"):
+        raise ValueError(f"duplicates must be 'sum' or 'last', got {duplicates!r}")
+    shape = tuple(int(s) for s in shape)
+    nd = len(shape)
+    vals = as_device_tensor(values)
+    dev = vals.device if vals.is_cuda else default_device()
+    vals = vals.to(dev)
+    if vals.dtype not in _TORCH_TO_ES:
+        vals = vals.to(torch.float64)
+    vals = vals.reshape(-1).contiguous()
+    idx = as_device_tensor(indices, dev).to(torch.int32).reshape(-1, nd).contiguous()
+    n = int(vals.shape[0])
+    if int(idx.shape[0]) != n:
+        raise ValueError("values and indices disagree in length")
+    lib = L.lib()
+    sh = L.i64arr(shape)
+    ws = workspace(lib.es_coo_coalesce_workspace_size(n, nd, sh), dev)
+    oi = torch.empty((max(n, 1), nd), dtype=torch.int32, device=dev)
+    ov = torch.empty(max(n, 1), dtype=out_dtype, device=dev)
+    cnt = torch.zeros(3, dtype=torch.int64, device=dev)
+    L.check("es_coo_coalesce", lib.es_coo_coalesce(
+        idx.data_ptr(), vals.data_ptr(), es_dtype(vals), n, nd, sh,
+        L.ES_DUP_SUM if duplicates == "sum" else L.ES_DUP_LAST, ws.data_ptr(), ws.numel(), oi.data_ptr(),
+        ov.data_ptr(), es_dtype(ov), cnt.data_ptr(), cnt[2:].data_ptr(), stream_ptr(dev)))
+    u, nz, err = read_counts(cnt)
+    if err & 0xFFFFFFFF:
+        raise ValueError("COO index outside the tensor shape")
+    return oi[:u], ov[:u], nz
+
+
 def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
-             out_dtype=torch.float32, marks=None) -> SparseTensorRelation:
+             out_dtype=torch.float32, marks=None, duplicates="last") -> SparseTensorRelation:
     """Element COO (device tensors) -> tile-COO relation (``tensor/sparse.py:160-219``).
 
     ``indices`` int32 ``(nnz, ndim)``, ``values`` (nnz,) float32/float64/bf16.
-    Zeros are dropped; the last of repeated coordinates wins. ``marks``: see
-    ``mark`` (plan0/plan1 around the plan launches, fill0/fill1 around the fill).
+    Zeros are dropped. Repeated coordinates: ``duplicates="last"`` (the
+    reference's behaviour) keeps the last in input order, ``"sum"`` adds them
+    (``coalesce_coo`` first), ``"error"`` raises ``ValueError``. ``marks``:
+    see ``mark`` (plan0/plan1 around the plan launches, fill0/fill1 around the
+    fill).
     """
+    if duplicates not in DUPLICATE_POLICIES:
+        raise ValueError(f"duplicates must be one of {DUPLICATE_POLICIES}, got {duplicates!r}")
+    if duplicates != "last":
+        ci, cv, nz = coalesce_coo(indices, values, shape, "sum" if duplicates == "sum" else "last")
+        if duplicates == "error" and int(ci.shape[0]) != nz:
+            raise ValueError(f"{nz - int(ci.shape[0])} repeated COO coordinates (duplicates='error')")
+        indices, values = ci, cv
     shape = tuple(int(s) for s in shape)
     tile_shape = tuple(int(t) for t in tile_shape)
     _check_divisible(shape, tile_shape)
@@ -252,8 +316,17 @@ def _extract_coo(data: Any):
     if isinstance(data, tuple) and len(data) == 3:
         idx, val, shape = data
         return "coo", idx, val, tuple(int(s) for s in shape)
+    if torch.is_tensor(data) and data.layout != torch.strided:
+        coo = data if data.layout == torch.sparse_coo else data.to_sparse_coo()
+        return "coo", coo._indices().t(), coo._values(), tuple(coo.shape)
     if torch.is_tensor(data):
         return "dense", data, None, tuple(data.shape)
+    if hasattr(data, "coords") and hasattr(data, "data") and hasattr(data, "shape"):
+        # COO objects with (ndim, nnz) coordinates, e.g. pydata sparse's COO
+        return "coo", as_device_tensor(data.coords).t(), data.data, tuple(int(s) for s in data.shape)
+    if hasattr(data, "__dlpack__") and not isinstance(data, np.ndarray):
+        t = torch.from_dlpack(data)  # JAX / CuPy arrays: zero-copy on the device
+        return "dense", t, None, tuple(t.shape)
     arr = np.asarray(data)
     if arr.dtype not in (np.float32, np.float64):
         arr = arr.astype(np.float64)
@@ -289,15 +362,14 @@ def _sparsity_stats(indices, values, shape, tile_shapes, device):
             raise ValueError(f"tile shape {t} does not fit a tensor of shape {shape}")
     dev = torch.device(device) if device is not None else default_device()
     if indices is not None:
-        idx = torch.as_tensor(np.asarray(indices) if not torch.is_tensor(indices) else indices)
-        idx = idx.to(device=dev, dtype=torch.int32).reshape(-1, nd).contiguous()
+        idx = as_device_tensor(indices).to(device=dev, dtype=torch.int32).reshape(-1, nd).contiguous()
         n = int(idx.shape[0])
     else:
         idx = None
         n = prod(shape)
     vals = None
     if values is not None:
-        vals = values if torch.is_tensor(values) else torch.as_tensor(np.asarray(values))
+        vals = as_device_tensor(values)
         if vals.dtype not in (torch.float32, torch.float64, torch.bfloat16):
             vals = vals.to(torch.float64)
         vals = vals.to(dev).reshape(-1).contiguous()
@@ -336,19 +408,34 @@ def compute_sparsity_stats_dense(data, tile_shapes, device=None) -> dict:
 class SparseTensor:
     """User-facing sparse tensor (``tensor/sparse.py:93-231``) whose tiling runs on the GPU.
 
-    ``data``: a scipy sparse matrix, a dense numpy array / torch tensor, or a
-    ``(indices, values, shape)`` COO triple (indices int32 ``(nnz, ndim)``; any
-    rank, unlike scipy). The reference computes per-scheme sparsity
-    statistics (``_compute_sparsity_metrics``, planner input) in its
-    constructor; here ``sparsity_stats()`` computes them on the GPU on demand.
+    ``data``: a scipy sparse matrix, a dense numpy array / torch tensor, a
+    torch sparse (COO / CSR) tensor, a COO object with ``coords`` ``(ndim,
+    nnz)``, ``data`` and ``shape`` (pydata sparse), any DLPack exporter (JAX
+    / CuPy arrays, taken without a copy when on the GPU), or an ``(indices,
+    values, shape)`` COO triple (indices ``(nnz, ndim)``; any rank, unlike
+    scipy; its arrays may be torch tensors or DLPack exporters too).
+
+    ``duplicates`` says what repeated coordinates mean: ``"last"`` (the
+    reference's tiling: the last in input order wins), ``"sum"`` (scipy /
+    torch sparse semantics) or ``"error"``; the default is ``"sum"`` for
+    torch sparse tensors and ``"last"`` for everything else.
+
+    The reference computes per-scheme sparsity statistics
+    (``_compute_sparsity_metrics``, planner input) in its constructor; here
+    ``sparsity_stats()`` computes them on the GPU on demand.
     """
 
-    def __init__(self, name: str, data: Any, device=None, dtype=None):
+    def __init__(self, name: str, data: Any, device=None, dtype=None, duplicates=None):
         self.name = name
         self.device = device or default_device()
         self._kind, self._a, self._b, self.shape = _extract_coo(data)
         self.data = data
         self._out_dtype = value_dtype_for(dtype)
+        if duplicates is None:
+            duplicates = "sum" if torch.is_tensor(data) and data.layout != torch.strided else "last"
+        if duplicates not in DUPLICATE_POLICIES:
+            raise ValueError(f"duplicates must be one of {DUPLICATE_POLICIES}, got {duplicates!r}")
+        self.duplicates = duplicates
 
     @property
     def ndim(self) -> int:
@@ -368,10 +455,10 @@ class SparseTensor:
         tile_shape = tuple(int(t) for t in tile_shape)
         _check_divisible(self.shape, tile_shape)
         if self._kind == "coo":
-            idx = torch.as_tensor(np.asarray(self._a, dtype=np.int32)) if not torch.is_tensor(self._a) else self._a
-            val = torch.as_tensor(np.asarray(self._b)) if not torch.is_tensor(self._b) else self._b
-            idx = idx.to(self.device, non_blocking=True).reshape(-1, len(self.shape))
-            val = val.to(self.device, non_blocking=True)
-            return tile_coo(idx, val, self.shape, tile_shape, self._out_dtype)
+            idx = as_device_tensor(self._a).to(self.device, non_blocking=True).reshape(-1, len(self.shape))
+            val = as_device_tensor(self._b).to(self.device, non_blocking=True)
+            if val.dtype not in _TORCH_TO_ES:
+                val = val.to(torch.float64)
+            return tile_coo(idx, val, self.shape, tile_shape, self._out_dtype, duplicates=self.duplicates)
         dense = self._a if torch.is_tensor(self._a) else torch.from_numpy(np.ascontiguousarray(self._a))
         return tile_dense(dense.to(self.device, non_blocking=True), tile_shape, self._out_dtype)

@@ -74,6 +74,33 @@ int es_tile_coo_fill(const void* values, int values_dtype, int64_t nnz, int ndim
                      void* workspace, size_t workspace_bytes, int64_t num_tiles,
                      int32_t* coords_out, void* values_out, int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * COO ingestion: coalescing repeated coordinates.
+ * The reference feeds element COO to its tiling as it comes
+ * (_extract_coo, tensor/sparse.py:234-270) and the last repeated coordinate
+ * wins there (:211-212); scipy CSR and torch's uncoalesced sparse tensors add
+ * repeated coordinates instead. es_coo_coalesce states the policy: it writes
+ * one entry per distinct coordinate holding a non-zero value, in row-major
+ * coordinate order -- ES_DUP_LAST: the value that comes last in input order;
+ * ES_DUP_SUM: the sum of the run, accumulated in float64 in input order (what
+ * scipy's sum_duplicates and numpy.add.at compute). Zero entries are dropped
+ * before coalescing (tensor/sparse.py:185-187); a sum that cancels to zero is
+ * written as 0 (the tiling drops it). indices_out int32 (nnz, ndim) and
+ * values_out (nnz) of out_dtype (F32/F64/BF16) are caller buffers of the input
+ * size; counts_dev[0] = entries written, counts_dev[1] = non-zero input
+ * entries (they differ exactly when a coordinate repeats). A coordinate
+ * outside `shape` sets *error_dev to ES_ERR_INDEX. This entry point has no
+ * counterpart in the reference (it is the explicit form of its implicit
+ * last-wins policy).
+ * ------------------------------------------------------------------------- */
+typedef enum es_dup_policy { ES_DUP_LAST = 0, ES_DUP_SUM = 1 } es_dup_policy;
+size_t es_coo_coalesce_workspace_size(int64_t nnz, int ndim, const int64_t* shape);
+int es_coo_coalesce(const int32_t* indices, const void* values, int values_dtype, int64_t nnz,
+                    int ndim, const int64_t* shape, int policy,
+                    void* workspace, size_t workspace_bytes,
+                    int32_t* indices_out, void* values_out, int out_dtype,
+                    int64_t* counts_dev, int32_t* error_dev, void* stream);
+
 /* Dense array (row-major `shape`) -> tile-COO of the tiles holding any
  * non-zero. Same result as SparseTensor(dense).to_relation(tile)
  * (tensor/sparse.py:104-117,160-219, via np.nonzero at :260-268). */

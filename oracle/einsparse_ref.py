@@ -35,7 +35,7 @@ __all__ = [
     "block_sparse_matmul_generic", "reverse_einsum_string",
     "sparse_einsum_raw_fwd", "sparse_einsum_raw_bwd", "canonical_pairs",
     "relation_allclose", "find_all_factors", "factor_tile_shapes", "compute_sparsity_stats_coo",
-    "infer_reduction_keys", "execute_plan",
+    "infer_reduction_keys", "execute_plan", "coalesce_coo",
 ]
 
 
@@ -120,6 +120,32 @@ def to_relation(indices, values, shape, tile_shape) -> Relation:
     vals = np.zeros((uniq.shape[0], *tile_shape), dtype=np.float64)
     vals[(inv,) + tuple(within[:, d] for d in range(ndim))] = nz_val
     return Relation(uniq.astype(np.int32), vals, shape, tile_shape)
+
+
+def coalesce_coo(indices, values, shape, duplicates="sum"):
+    """One entry per distinct coordinate with a non-zero value, row-major
+    coordinate order. Zeros are dropped first (``tensor/sparse.py:185-187``);
+    ``"last"`` keeps the last value in input order (the reference's NumPy
+    assignment, ``tensor/sparse.py:211-212``), ``"sum"`` adds a coordinate's
+    values in float64 in input order (``numpy.add.at``; what scipy's
+    ``sum_duplicates`` computes). Returns ``(indices int32, values float64,
+    number of non-zero inputs)``."""
+    idx = np.asarray(indices, dtype=np.int64).reshape(-1, len(shape))
+    val = np.asarray(values, dtype=np.float64).reshape(-1)
+    nz = val != 0
+    idx, val = idx[nz], val[nz]
+    if len(val) and ((idx < 0).any() or (idx >= np.asarray(shape)).any()):
+        raise ValueError("COO index outside the tensor shape")
+    lin = np.ravel_multi_index(tuple(idx.T), shape) if len(val) else np.zeros(0, np.int64)
+    uniq, inv = np.unique(lin, return_inverse=True)
+    out = np.zeros(len(uniq))
+    if duplicates == "sum":
+        np.add.at(out, inv.reshape(-1), val)
+    else:
+        out[inv.reshape(-1)] = val  # sequential assignment: the last in input order stays
+    coords = np.stack(np.unravel_index(uniq, shape), 1).astype(np.int32) if len(uniq) else \
+        np.zeros((0, len(shape)), np.int32)
+    return coords, out, int(len(val))
 
 
 def relation_from_dense(dense, tile_shape) -> Relation:

@@ -25,6 +25,10 @@ Usage:  python tests/golden/make_golden.py --reference <path-to-einjax>
             (only ``golden_plan.npz``: join / aggregation keys from
             ``optimizer/dp.py``'s ``infer_reduction_info`` and multi-step plans
             run by ``execution/engine.py``'s ``ExecutionEngine.execute_plan``)
+        python tests/golden/make_golden.py --reference <path> --ingest-only
+            (only ``golden_ingest.npz``: COO input with repeated coordinates
+            tiled by ``SparseTensor.to_relation``, given as a COO matrix --
+            the last repeat wins -- and as scipy's CSR of it -- repeats added)
 """
 
 from __future__ import annotations
@@ -204,21 +208,60 @@ def make_plan(mods):
     print("wrote", len(st.arrays), "arrays to golden_plan.npz")
 
 
+def make_ingest(mods):
+    """COO input with repeated coordinates, explicit zeros and repeats that
+    cancel: SparseTensor(coo_matrix).to_relation (tensor/sparse.py:160-270;
+    the last repeat wins) and SparseTensor(coo_matrix.tocsr()).to_relation
+    (scipy adds repeats first), plus scipy's coalesced COO of the same input."""
+    import scipy.sparse as ssp
+    sp_mod = mods["tensor.sparse"]
+    st = Store()
+    rng = np.random.default_rng(41)
+    for name, (shape, nnz, tile) in {"ingest_small": ((12, 16), 60, (4, 4)),
+                                     "ingest_rect": ((64, 48), 900, (8, 16)),
+                                     "ingest_dense_dups": ((8, 8), 400, (2, 4))}.items():
+        idx = np.stack([rng.integers(0, n, nnz) for n in shape], 1).astype(np.int32)
+        rep = rng.choice(nnz, nnz // 4, replace=False)
+        idx[rep] = idx[rng.choice(nnz, nnz // 4)]
+        val = np.round(rng.standard_normal(nnz), 3)
+        val[rng.random(nnz) < 0.1] = 0.0
+        # a repeated coordinate whose values cancel, alone in its tile
+        in_last = (idx[:, 0] // tile[0] == shape[0] // tile[0] - 1) & (idx[:, 1] // tile[1] == shape[1] // tile[1] - 1)
+        idx[in_last] = 0
+        idx[:2] = [shape[0] - 1, shape[1] - 1]
+        val[:2] = [1.25, -1.25]
+        coo = ssp.coo_matrix((val, (idx[:, 0], idx[:, 1])), shape=shape)
+        last = sp_mod.SparseTensor("t", coo).to_relation(tile)
+        csr = coo.tocsr()
+        summed = sp_mod.SparseTensor("t", csr).to_relation(tile)
+        cc = csr.tocoo()
+        st.put(name, {"kind": "ingest", "shape": list(shape), "tile": list(tile)}, indices=idx, values=val,
+               last_coords=last.coords, last_values=last.values, sum_coords=summed.coords, sum_values=summed.values,
+               coalesced_indices=np.stack([cc.row, cc.col], 1).astype(np.int32), coalesced_values=cc.data)
+    st.save(os.path.join(HERE, "golden_ingest.npz"))
+    print("wrote", len(st.arrays), "arrays to golden_ingest.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
     ap.add_argument("--stats-only", action="store_true")
     ap.add_argument("--plan-only", action="store_true")
+    ap.add_argument("--ingest-only", action="store_true")
     args = ap.parse_args()
     mods = load_reference(os.path.abspath(args.reference))
     mods["core.notation"] = importlib.import_module("einjax.core.notation")
     if args.plan_only:
         make_plan(mods)
         return
+    if args.ingest_only:
+        make_ingest(mods)
+        return
     make_stats(mods)
     if args.stats_only:
         return
     make_plan(mods)
+    make_ingest(mods)
     import jax
     sp_mod = mods["tensor.sparse"]
     sd = mods["execution.sparse_dispatch"]

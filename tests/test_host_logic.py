@@ -142,3 +142,39 @@ def test_plan_helpers_reject_bad_input():
         E.plan_from_path("ij,jk->ik", [(0, 0)])
     steps = E.plan_from_path("ij,jk->ki", [(0, 1)])
     assert steps[0].formula == "ij,jk->ki"
+
+
+def test_extract_coo_input_kinds():
+    """The COO boundary on the host: torch sparse tensors (uncoalesced COO and
+    CSR), pydata-style COO objects, DLPack exporters, COO triples."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from einjax_b200.sparse import _extract_coo, as_device_tensor
+    i = torch.tensor([[0, 2, 0], [1, 3, 1]])
+    ts = torch.sparse_coo_tensor(i, torch.tensor([1.0, 2.0, 3.0]), (4, 5))
+    kind, idx, val, shape = _extract_coo(ts)
+    assert kind == "coo" and shape == (4, 5) and idx.tolist() == [[0, 1], [2, 3], [0, 1]]
+    assert val.tolist() == [1.0, 2.0, 3.0]  # uncoalesced: repeats kept for the policy to resolve
+    kind, idx, val, shape = _extract_coo(ts.coalesce().to_sparse_csr())
+    assert kind == "coo" and idx.tolist() == [[0, 1], [2, 3]] and val.tolist() == [4.0, 2.0]
+    pyd = SimpleNamespace(coords=np.array([[1, 2], [0, 4]]), data=np.array([5.0, 6.0]), shape=(3, 5))
+    kind, idx, val, shape = _extract_coo(pyd)
+    assert kind == "coo" and idx.tolist() == [[1, 0], [2, 4]] and shape == (3, 5)
+
+    class DL:
+        def __init__(self, t):
+            self.t = t
+
+        def __dlpack__(self, **kw):
+            return self.t.__dlpack__(**kw)
+
+        def __dlpack_device__(self):
+            return self.t.__dlpack_device__()
+    d = torch.arange(6.0).reshape(2, 3)
+    kind, arr, _, shape = _extract_coo(DL(d))
+    assert kind == "dense" and shape == (2, 3) and arr.data_ptr() == d.data_ptr()
+    assert as_device_tensor(DL(d)).data_ptr() == d.data_ptr()
+    assert as_device_tensor(np.array([1, 2])).tolist() == [1, 2]
+    assert E.DUPLICATE_POLICIES == ("last", "sum", "error")

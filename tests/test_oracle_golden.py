@@ -233,3 +233,32 @@ def test_execute_plan(name):
     assert list(res.shape) == c.meta["res_shape"] and list(res.tile_shape) == c.meta["res_tile"]
     res64 = O.execute_plan(steps, _plan_ops(c))
     _close(res64.to_dense(), c["out_dense"], rtol=1e-5, atol=1e-6)
+
+
+INGEST = load_cases("golden_ingest.npz")
+
+
+@pytest.mark.parametrize("name", sorted(cases_of_kind("ingest", "golden_ingest.npz")))
+def test_coalesce_and_duplicate_policies(name):
+    """Repeated COO coordinates: "last" against the reference's tiling of the
+    COO matrix (bit-exact), "sum" against its tiling of scipy's CSR of it and
+    against scipy's coalesced COO (float64 sums to 1e-12: scipy may add a
+    row's repeats in another order)."""
+    c = INGEST[name]
+    shape, tile = tuple(c.meta["shape"]), tuple(c.meta["tile"])
+    r = O.to_relation(c["indices"], c["values"], shape, tile)
+    np.testing.assert_array_equal(r.coords, c["last_coords"])
+    np.testing.assert_array_equal(r.values, c["last_values"])
+    li, lv, nz = O.coalesce_coo(c["indices"], c["values"], shape, "last")
+    assert nz == int((c["values"] != 0).sum()) and len(lv) < nz
+    r = O.to_relation(li, lv, shape, tile)
+    np.testing.assert_array_equal(r.coords, c["last_coords"])
+    np.testing.assert_array_equal(r.values, c["last_values"])
+    si, sv, _ = O.coalesce_coo(c["indices"], c["values"], shape, "sum")
+    np.testing.assert_array_equal(si, li)
+    ref = {tuple(i): v for i, v in zip(c["coalesced_indices"].tolist(), c["coalesced_values"])}
+    assert all(ref.pop(tuple(i)) == pytest.approx(v, rel=1e-12, abs=1e-12) for i, v in zip(si.tolist(), sv))
+    assert all(v == 0 for v in ref.values())  # coordinates whose inputs were all zero
+    r = O.to_relation(si, sv, shape, tile)
+    np.testing.assert_array_equal(r.coords, c["sum_coords"])
+    _close(r.values, c["sum_values"])
