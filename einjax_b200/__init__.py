@@ -8,6 +8,7 @@ step runs in ``libeinsparse.so`` (hand-written CUDA, C ABI in
 
 from ._lib import EinsparseError, EinsparseUnavailable  # noqa: F401
 from .autodiff import _reverse_einsum_string, sparse_einsum, sparse_einsum_raw  # noqa: F401
+from .cost_model import B200_PROFILE, calibrate, detect_device_type, install_b200_profile  # noqa: F401
 from .kernels import (block_sparse_matmul, block_sparse_matmul_generic, coordinate_join_hash,  # noqa: F401
                       coordinate_join_sorted)
 from .partition import tile_shape_to_partition_spec  # noqa: F401

@@ -178,3 +178,61 @@ def test_extract_coo_input_kinds():
     assert as_device_tensor(DL(d)).data_ptr() == d.data_ptr()
     assert as_device_tensor(np.array([1, 2])).tolist() == [1, 2]
     assert E.DUPLICATE_POLICIES == ("last", "sum", "error")
+
+
+def _fake_cost_module():
+    """A stand-in with the shape of einjax's optimizer/cost_model.py: a profile
+    table, a CostModelConfig with from_device_type, and a detection rule that
+    sends unknown GPUs to the A100 profile (optimizer/cost_model.py:291-333)."""
+    import types
+    from dataclasses import dataclass
+
+    m = types.ModuleType("fake_cost_model")
+    m._HARDWARE_PROFILES = {"gpu:a100": {"hbm_bandwidth": 2.0e12, "interconnect_bandwidth": 600e9,
+                                         "peak_flops": 19.5e12, "launch_overhead": 5e-6}}
+
+    @dataclass
+    class CostModelConfig:
+        hbm_bandwidth: float
+        interconnect_bandwidth: float
+        peak_flops: float
+        launch_overhead: float
+        num_devices: int
+        device_type: str
+
+        @classmethod
+        def from_device_type(cls, device_type, num_devices=1):
+            p = m._HARDWARE_PROFILES[device_type]
+            return cls(num_devices=num_devices, device_type=device_type, **p)
+
+    m.CostModelConfig = CostModelConfig
+    m.detect_device_config = lambda: CostModelConfig.from_device_type("gpu:a100", 1)
+    return m
+
+
+def test_b200_cost_profile_detection(monkeypatch):
+    from einjax_b200 import cost_model as CM
+    assert CM.device_type_for("NVIDIA B200") == "gpu:b200"
+    assert CM.device_type_for("NVIDIA GB200") == "gpu:b200"
+    assert CM.device_type_for("", (10, 0)) == "gpu:b200"
+    assert CM.device_type_for("NVIDIA H100 80GB HBM3", (9, 0)) is None
+    assert CM.device_type_for("NVIDIA A100-SXM4-80GB") is None
+    m = _fake_cost_module()
+    CM.install_b200_profile(m)
+    CM.install_b200_profile(m)  # idempotent
+    assert m._HARDWARE_PROFILES["gpu:b200"] == CM.B200_PROFILE
+    # a JAX GPU device reporting "NVIDIA B200" (8 of them) gets the B200 profile
+    monkeypatch.setattr(CM, "_jax_device_kind", lambda: ("NVIDIA B200", 8))
+    cfg = m.detect_device_config()
+    assert cfg.device_type == "gpu:b200" and cfg.num_devices == 8
+    assert cfg.hbm_bandwidth == CM.B200_PROFILE["hbm_bandwidth"]
+    assert cfg == m.CostModelConfig(**CM.b200_config_kwargs(8))
+    # other devices keep the module's own rule
+    monkeypatch.setattr(CM, "_jax_device_kind", lambda: ("NVIDIA H100 80GB HBM3", 8))
+    assert m.detect_device_config().device_type == "gpu:a100"
+    # no JAX: the torch device decides
+    monkeypatch.setattr(CM, "_jax_device_kind", lambda: (None, 0))
+    monkeypatch.setattr(CM, "detect_device_type", lambda: "gpu:b200")
+    monkeypatch.setattr(CM, "_torch_device_count", lambda: 2)
+    cfg = m.detect_device_config()
+    assert cfg.device_type == "gpu:b200" and cfg.num_devices == 2
