@@ -329,8 +329,11 @@ def run_ours(args):
 
 def _marks_ms(marks):
     """Launch time of one call from its plan0/plan1/fill0/fill1 marks (the
-    host read of the counts between plan and fill is left out)."""
+    host read of the counts between plan and fill is left out), or from its
+    coalesce0/coalesce1 marks."""
     d = dict(marks)
+    if "coalesce0" in d:
+        return d["coalesce0"].elapsed_time(d["coalesce1"])
     ms = d["plan0"].elapsed_time(d["plan1"])
     if "fill0" in d:
         ms += d["fill0"].elapsed_time(d["fill1"])
@@ -339,7 +342,8 @@ def _marks_ms(marks):
 
 def hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm, reps=3):
     """HBM rooflines of the bandwidth-bound phases of the path on the C2
-    inputs: COO->tile-COO tiling of A, join + output grouping, and the
+    inputs: COO->tile-COO tiling of A, coalescing A's COO (duplicates="sum"),
+    join + output grouping, and the
     unfused segment_sum API on a sample of C2's (pair tile, output tile)
     rows. Each is timed by CUDA events around its own launches (median of
     ``reps``), against the algorithmic bytes of the phase."""
@@ -363,6 +367,16 @@ def hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm, reps=3):
     nnz, T_A = int(val_d.numel()), A.num_tuples
     out["tile_coo"] = entry(statistics.median(t), nnz * (2 * 4 + 4) + T_A * (TILE * TILE * 4 + 2 * 4),
                             "nnz x 12 read + T_A x (4096 + 8) written")
+    t = []
+    for _ in range(reps):
+        m = []
+        ci, cv, _ = E.coalesce_coo(idx_d, val_d, shape, "sum", marks=m)
+        torch.cuda.synchronize()
+        t.append(_marks_ms(m))
+    U = int(ci.shape[0])
+    del ci, cv
+    out["coo_coalesce"] = entry(statistics.median(t), nnz * (2 * 4 + 4) + U * (2 * 4 + 8),
+                                "nnz x 12 read + U x (8 + 8) written (float64 sums); one 64-bit key sort between")
     B = E.tile_dense(b_d, (TILE, TILE))
     t = []
     for _ in range(reps):

@@ -1,12 +1,22 @@
-// Stable LSD radix sort of (key, uint32 payload) pairs, 8 bits per pass.
+// Stable LSD radix sort of (key, uint32 payload) pairs, 8 bits per pass,
+// "onesweep" style (Adinets & Merrill, "Onesweep: A Faster Least Significant
+// Digit Radix Sort for GPUs", 2022): one upsweep reads the keys once and
+// builds the global digit histogram of every pass; then each pass is ONE
+// launch. A CTA takes the next 4096-key tile from an atomic counter, ranks
+// its keys stably -- warp w owns keys [w*512, w*512+512) of the tile and
+// walks them 32 at a time, eight ballots group lanes with equal digits and a
+// per-warp digit counter gives the running rank -- publishes the
+// tile's per-digit counts, finds the counts of all earlier tiles by a
+// decoupled look-back over their per-digit status words (one thread per
+// digit), and writes the tile reordered through shared memory so every
+// digit's run leaves as one coalesced store.
 //
-// Per pass: (1) per-tile digit histograms (4096 keys per CTA, warp-aggregated
-// shared atomics), (2) one exclusive scan over the digit-major histogram
-// matrix gives every (digit, tile) its global offset, (3) each CTA ranks its
-// keys stably — warp w owns keys [w*512, w*512+512) of the tile and walks
-// them 32 at a time, __match_any_sync groups lanes with equal digits and a
-// per-warp digit counter gives the running rank — then reorders the tile in
-// shared memory so every digit's run leaves as one coalesced store.
+// Status word (64 bits): the count in the low 32 bits, a code in the high 32
+// -- 2p+1 "aggregate of this tile" or 2p+2 "inclusive prefix up to this
+// tile" for pass p. The words are cleared once per sort; codes only grow
+// from pass to pass, so a word left from the previous pass reads as "not yet
+// published". Waits are bounded: after kScanSpin polls the CTA records
+// ES_ERR_TIMEOUT and takes 0 (the output is then invalid).
 #pragma once
 
 #include "common.cuh"
@@ -19,35 +29,78 @@ constexpr int kRsWarps = kRsThreads / 32;
 constexpr int kRsChunks = 16;  // chunks of 32 keys per warp
 constexpr int kRsTile = kRsThreads * kRsChunks;
 constexpr int kRsBins = 256;
+constexpr int kRsMaxPasses = 8;
+constexpr int kRsLook = 8;  // status words read per look-back step
 
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Lanes of this warp whose key has the same digit (valid lanes only; the
+// result of an invalid lane is unused): eight ballots, one per digit bit
+// (warp-level multisplit, in place of __match_any_sync).
+__device__ __forceinline__ unsigned warp_peers(uint32_t dig, int nbits, bool valid) {
+  unsigned peers = __ballot_sync(0xffffffffu, valid);
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    if (b < nbits) {  // nbits is the same for the whole warp
+      const bool bit = (dig >> b) & 1u;
+      const unsigned bb = __ballot_sync(0xffffffffu, bit);
+      peers &= bit ? bb : ~bb;
+    }
+  }
+  return peers;
+}
+
+// Global digit histograms of every pass: ghist[p * 256 + d]. A warp whose 32
+// keys share a digit adds 32 once; otherwise each lane adds 1.
 template <typename K>
-__global__ void __launch_bounds__(kRsThreads) rs_hist_kernel(const K* __restrict__ keys, int64_t n, int shift,
-                                                             uint32_t mask, uint32_t* __restrict__ hist,
-                                                             int64_t num_tiles) {
-  __shared__ uint32_t h[kRsBins];
-  for (int i = threadIdx.x; i < kRsBins; i += kRsThreads) h[i] = 0;
+__global__ void __launch_bounds__(kRsThreads) rs_upsweep_kernel(const K* __restrict__ keys, int64_t n, int begin_bit,
+                                                                int end_bit, uint32_t* __restrict__ ghist) {
+  __shared__ uint32_t h[kRsMaxPasses * kRsBins];
+  const int npass = (end_bit - begin_bit + 7) / 8;
+  for (int i = threadIdx.x; i < npass * kRsBins; i += kRsThreads) h[i] = 0;
   __syncthreads();
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRsTile;
   const int lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kRsTile; i += kRsThreads) {
-    int64_t g = base + i;
-    bool valid = g < n;
-    uint32_t dig = valid ? (static_cast<uint32_t>(keys[g] >> shift) & mask) : (kRsBins + lane);
-    unsigned peers = __match_any_sync(0xffffffffu, dig);
-    if (valid && (__ffs(peers) - 1) == lane) atomicAdd(&h[dig], static_cast<uint32_t>(__popc(peers)));
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRsThreads;
+  // every lane of a warp runs the same number of iterations (the votes need them all)
+  const int64_t n_pad = (n + 31) & ~static_cast<int64_t>(31);
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(kRsThreads) + threadIdx.x; g < n_pad; g += stride) {
+    const bool valid = g < n;
+    const K k = valid ? keys[g] : K(0);
+    for (int p = 0; p < npass; ++p) {
+      const int shift = begin_bit + 8 * p;
+      const int nb = end_bit - shift < 8 ? end_bit - shift : 8;
+      const uint32_t dig = static_cast<uint32_t>(k >> shift) & ((1u << nb) - 1u);
+      const uint32_t d0 = __shfl_sync(0xffffffffu, dig, 0);
+      const unsigned vb = __ballot_sync(0xffffffffu, valid);
+      if (__all_sync(0xffffffffu, !valid || dig == d0)) {
+        if (lane == 0 && vb) atomicAdd(&h[p * kRsBins + d0], static_cast<uint32_t>(__popc(vb)));
+      } else if (valid) {
+        atomicAdd(&h[p * kRsBins + dig], 1u);
+      }
+    }
   }
   __syncthreads();
-  for (int d = threadIdx.x; d < kRsBins; d += kRsThreads) hist[static_cast<int64_t>(d) * num_tiles + blockIdx.x] = h[d];
+  for (int i = threadIdx.x; i < npass * kRsBins; i += kRsThreads)
+    if (h[i]) atomicAdd(&ghist[i], h[i]);
 }
 
 template <typename K>
-__global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restrict__ keys_in,
-                                                                const uint32_t* __restrict__ vals_in,
-                                                                K* __restrict__ keys_out,
-                                                                uint32_t* __restrict__ vals_out, int64_t n,
-                                                                int shift, uint32_t mask,
-                                                                const uint32_t* __restrict__ offsets,
-                                                                int64_t num_tiles) {
+__global__ void __launch_bounds__(kRsThreads, 3) rs_onesweep_kernel(const K* __restrict__ keys_in,
+                                                                 const uint32_t* __restrict__ vals_in,
+                                                                 K* __restrict__ keys_out,
+                                                                 uint32_t* __restrict__ vals_out, int64_t n, int shift,
+                                                                 uint32_t mask, int pass,
+                                                                 const uint32_t* __restrict__ ghist_pass,
+                                                                 uint64_t* __restrict__ status,
+                                                                 uint32_t* __restrict__ next_tile, int32_t* err) {
   extern __shared__ __align__(16) unsigned char rs_smem[];
   K* skeys = reinterpret_cast<K*>(rs_smem);
   uint32_t* svals = reinterpret_cast<uint32_t*>(skeys + kRsTile);
@@ -55,26 +108,35 @@ __global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restr
   uint32_t* bstart = wcnt + kRsWarps * kRsBins;
   uint32_t* goff = bstart + kRsBins;
   __shared__ uint32_t wtot[kRsWarps];
+  __shared__ uint32_t tile_sh;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t base = static_cast<int64_t>(blockIdx.x) * kRsTile;
+  const int nbits = __popc(mask);
+  if (tid == 0) tile_sh = atomicAdd(next_tile, 1u);
   for (int i = tid; i < kRsWarps * kRsBins; i += kRsThreads) wcnt[i] = 0;
-  for (int d = tid; d < kRsBins; d += kRsThreads) goff[d] = offsets[static_cast<int64_t>(d) * num_tiles + blockIdx.x];
   __syncthreads();
+  const int64_t tile = tile_sh;
+  const int64_t base = tile * kRsTile;
 
+  // keys and ranks stay in registers; payloads are read again at the scatter
+  // (three CTAs per SM fit that way)
   K k[kRsChunks];
-  uint32_t v[kRsChunks];
   uint32_t rank[kRsChunks];
   const unsigned lt = (1u << lane) - 1u;
   uint32_t* my = wcnt + warp * kRsBins;
+  const int64_t wbase = base + warp * (kRsChunks * 32) + lane;
+#pragma unroll
+  for (int c = 0; c < kRsChunks; ++c) {  // all loads in flight before the ranking
+    const int64_t g = wbase + c * 32;
+    k[c] = g < n ? keys_in[g] : K(0);
+  }
 #pragma unroll
   for (int c = 0; c < kRsChunks; ++c) {
-    int64_t g = base + warp * (kRsChunks * 32) + c * 32 + lane;
-    bool valid = g < n;
-    k[c] = valid ? keys_in[g] : K(0);
-    v[c] = valid ? vals_in[g] : 0u;
-    uint32_t dig = valid ? (static_cast<uint32_t>(k[c] >> shift) & mask) : (kRsBins + lane);
-    unsigned peers = __match_any_sync(0xffffffffu, dig);
+    const bool valid = wbase + c * 32 < n;
+    uint32_t dig = static_cast<uint32_t>(k[c] >> shift) & mask;
+    const uint32_t d0 = __shfl_sync(0xffffffffu, dig, 0);
+    unsigned peers = __all_sync(0xffffffffu, !valid || dig == d0) ? __ballot_sync(0xffffffffu, valid)
+                                                                   : warp_peers(dig, nbits, valid);
     uint32_t r = __popc(peers & lt);
     uint32_t b = valid ? my[dig] : 0u;
     __syncwarp();
@@ -83,9 +145,11 @@ __global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restr
     rank[c] = b + r;
   }
   __syncthreads();
-  // digit d: exclusive prefix over warps (in place) and the tile total
+  const uint64_t code_agg = static_cast<uint64_t>(2 * pass + 1) << 32;
+  const uint64_t code_inc = static_cast<uint64_t>(2 * pass + 2) << 32;
   {
-    const int d = tid;  // kRsThreads == kRsBins
+    const int d = tid;  // kRsThreads == kRsBins: thread d owns digit d
+    // digit d: exclusive prefix over warps (in place) and the tile's count
     uint32_t run = 0;
 #pragma unroll
     for (int w = 0; w < kRsWarps; ++w) {
@@ -93,6 +157,9 @@ __global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restr
       wcnt[w * kRsBins + d] = run;
       run += t;
     }
+    uint64_t* sw = status + tile * kRsBins + d;
+    st_relaxed_u64(sw, (tile == 0 ? code_inc : code_agg) | run);
+    // the tile-local start of digit d (exclusive scan of the counts over digits)
     uint32_t incl = warp_inclusive_scan(run);
     if (lane == 31) wtot[warp] = incl;
     __syncthreads();
@@ -103,6 +170,63 @@ __global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restr
     }
     __syncthreads();
     bstart[d] = wtot[warp] + incl - run;
+    __syncthreads();
+    // the global start of digit d over the whole pass (same scan over the global histogram)
+    const uint32_t gd = ghist_pass[d];
+    uint32_t gincl = warp_inclusive_scan(gd);
+    if (lane == 31) wtot[warp] = gincl;
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t x = lane < kRsWarps ? wtot[lane] : 0u;
+      uint32_t xi = warp_inclusive_scan(x);
+      if (lane < kRsWarps) wtot[lane] = xi - x;
+    }
+    __syncthreads();
+    uint32_t before = wtot[warp] + gincl - gd;
+    // look back over earlier tiles' counts of digit d, kRsLook status words
+    // per step (independent loads in flight; each word carries its own count,
+    // so relaxed loads suffice)
+    if (tile > 0) {
+      uint32_t excl = 0;
+      int64_t j = tile - 1;
+      int spins = 0;
+      bool timed_out = false;
+      while (true) {
+        uint64_t w[kRsLook];
+#pragma unroll
+        for (int q = 0; q < kRsLook; ++q)
+          w[q] = j - q >= 0 ? ld_relaxed_u64(status + (j - q) * kRsBins + d) : code_inc;
+        int q = 0;  // words consumed, in order from tile j down
+        bool done = false, stalled = false;
+#pragma unroll
+        for (int qq = 0; qq < kRsLook; ++qq) {
+          const uint64_t code = w[qq] & 0xFFFFFFFF00000000ull;
+          if (code < code_agg) {  // not published yet: wait for it below
+            stalled = true;
+            break;
+          }
+          excl += static_cast<uint32_t>(w[qq]);
+          q = qq + 1;
+          if (code == code_inc) {
+            done = true;
+            break;
+          }
+        }
+        if (done) break;
+        j -= q;
+        if (stalled) {  // tile j has not published for this pass
+          if (++spins > kScanSpin) {
+            timed_out = true;
+            break;
+          }
+          if (spins > 64) __nanosleep(64);
+        }
+      }
+      if (timed_out) atomicExch(err ? err : &g_scan_timeout, ES_ERR_TIMEOUT);
+      st_relaxed_u64(sw, code_inc | (excl + run));
+      before += excl;
+    }
+    goff[d] = before;
   }
   __syncthreads();
 #pragma unroll
@@ -112,7 +236,7 @@ __global__ void __launch_bounds__(kRsThreads) rs_scatter_kernel(const K* __restr
       uint32_t dig = static_cast<uint32_t>(k[c] >> shift) & mask;
       uint32_t pos = bstart[dig] + my[dig] + rank[c];
       skeys[pos] = k[c];
-      svals[pos] = v[c];
+      svals[pos] = vals_in[g];
     }
   }
   __syncthreads();
@@ -131,10 +255,15 @@ constexpr size_t rs_scatter_smem() {
   return kRsTile * sizeof(K) + kRsTile * sizeof(uint32_t) + (kRsWarps * kRsBins + 2 * kRsBins) * sizeof(uint32_t);
 }
 
+// Scratch of a sort of n pairs, carved by callers as uint32 elements:
+// hist = the per-(tile, digit) status words (2 uint32 each), then the
+// per-pass tile counters and global histograms; scan = unused (1 element,
+// kept so callers' workspace layouts stay put).
 struct RadixScratchSize {
   static int64_t tiles(int64_t n) { return (n + kRsTile - 1) / kRsTile; }
-  static int64_t hist_elems(int64_t n) { return kRsBins * (tiles(n) > 0 ? tiles(n) : 1); }
-  static int64_t scan_elems(int64_t n) { return scan_scratch_elems(hist_elems(n)); }
+  static int64_t status_words(int64_t n) { return kRsBins * (tiles(n) > 0 ? tiles(n) : 1); }
+  static int64_t hist_elems(int64_t n) { return 2 * status_words(n) + kRsMaxPasses + kRsMaxPasses * kRsBins; }
+  static int64_t scan_elems(int64_t) { return 1; }
 };
 
 // Workspace slices a radix sort of n pairs needs (besides the input arrays).
@@ -161,27 +290,39 @@ struct RadixBuffers {
 };
 
 // Sorts bits [begin_bit, end_bit) of the keys, stable. On return *keys/*vals
-// point at whichever buffer holds the sorted data.
+// point at whichever buffer holds the sorted data (the alternate buffers when
+// the number of 8-bit passes is odd). Launches: one clear of the scratch, the
+// upsweep, one kernel per pass. A look-back timeout is recorded in *err when
+// given.
 template <typename K>
 int radix_sort_pairs(K** keys, uint32_t** vals, RadixBuffers<K>& rb, int64_t n, int begin_bit, int end_bit,
-                     cudaStream_t st) {
+                     cudaStream_t st, int32_t* err = nullptr) {
   if (n <= 1 || begin_bit >= end_bit) return ES_OK;
+  if (n >= static_cast<int64_t>(UINT32_MAX)) return ES_ERR_UNSUPPORTED;
+  const int npass = (end_bit - begin_bit + 7) / 8;
+  if (npass > kRsMaxPasses) return ES_ERR_UNSUPPORTED;
   // The attribute is per device; setting it is a cheap host call.
-  if (cudaFuncSetAttribute(rs_scatter_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(rs_onesweep_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(rs_scatter_smem<K>())) != cudaSuccess)
     return ES_ERR_CUDA;
   const int64_t tiles = RadixScratchSize::tiles(n);
+  uint64_t* status = reinterpret_cast<uint64_t*>(rb.hist);
+  uint32_t* counters = rb.hist + 2 * RadixScratchSize::status_words(n);
+  uint32_t* ghist = counters + kRsMaxPasses;
+  const size_t clear = (2 * RadixScratchSize::status_words(n) + kRsMaxPasses + npass * kRsBins) * sizeof(uint32_t);
+  if (cudaMemsetAsync(rb.hist, 0, clear, st) != cudaSuccess) return ES_ERR_CUDA;
+  const int up_grid = static_cast<int>(tiles < 148 * 8 ? tiles : 148 * 8);
+  ES_LAUNCH(rs_upsweep_kernel<K>, up_grid, kRsThreads, 0, st, *keys, n, begin_bit, end_bit, ghist);
   K* kin = *keys;
   uint32_t* vin = *vals;
   K* kout = rb.keys_alt;
   uint32_t* vout = rb.vals_alt;
-  for (int shift = begin_bit; shift < end_bit; shift += 8) {
-    int nbits = end_bit - shift < 8 ? end_bit - shift : 8;
-    uint32_t mask = (1u << nbits) - 1u;
-    ES_LAUNCH(rs_hist_kernel<K>, (int)tiles, kRsThreads, 0, st, kin, n, shift, mask, rb.hist, tiles);
-    ES_TRY(exclusive_scan<uint32_t>(rb.hist, rb.hist, kRsBins * tiles, (uint32_t*)nullptr, rb.scan, st));
-    ES_LAUNCH(rs_scatter_kernel<K>, (int)tiles, kRsThreads, rs_scatter_smem<K>(), st, kin, vin, kout, vout, n, shift,
-              mask, rb.hist, tiles);
+  for (int p = 0; p < npass; ++p) {
+    const int shift = begin_bit + 8 * p;
+    const int nbits = end_bit - shift < 8 ? end_bit - shift : 8;
+    const uint32_t mask = (1u << nbits) - 1u;
+    ES_LAUNCH(rs_onesweep_kernel<K>, (int)tiles, kRsThreads, rs_scatter_smem<K>(), st, kin, vin, kout, vout, n, shift,
+              mask, p, ghist + p * kRsBins, status, counters + p, err);
     K* tk = kin; kin = kout; kout = tk;
     uint32_t* tv = vin; vin = vout; vout = tv;
   }

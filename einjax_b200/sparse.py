@@ -187,13 +187,14 @@ def as_device_tensor(x, device=None) -> torch.Tensor:
     return t if device is None else t.to(device)
 
 
-def coalesce_coo(indices, values, shape, duplicates="sum", out_dtype=torch.float64):
+def coalesce_coo(indices, values, shape, duplicates="sum", out_dtype=torch.float64, marks=None):
     """One entry per distinct coordinate holding a non-zero value, in row-major
     coordinate order, on the GPU (``es_coo_coalesce``): ``duplicates="sum"``
     adds repeated coordinates (float64, input order; scipy / torch sparse
     semantics), ``"last"`` keeps the last in input order (the reference's
     tiling, ``tensor/sparse.py:211-212``). Zero entries are dropped first.
-    Returns ``(indices int32 (n, ndim), values (n,), nonzero_inputs)``."""
+    Returns ``(indices int32 (n, ndim), values (n,), nonzero_inputs)``.
+    ``marks``: see ``mark`` (coalesce0/coalesce1 around the launches)."""
     if duplicates not in ("sum", "last"):
         raise ValueError(f"duplicates must be 'sum' or 'last', got {duplicates!r}")
     shape = tuple(int(s) for s in shape)
@@ -214,10 +215,12 @@ def coalesce_coo(indices, values, shape, duplicates="sum", out_dtype=torch.float
     oi = torch.empty((max(n, 1), nd), dtype=torch.int32, device=dev)
     ov = torch.empty(max(n, 1), dtype=out_dtype, device=dev)
     cnt = torch.zeros(3, dtype=torch.int64, device=dev)
+    mark(marks, "coalesce0")
     L.check("es_coo_coalesce", lib.es_coo_coalesce(
         idx.data_ptr(), vals.data_ptr(), es_dtype(vals), n, nd, sh,
         L.ES_DUP_SUM if duplicates == "sum" else L.ES_DUP_LAST, ws.data_ptr(), ws.numel(), oi.data_ptr(),
         ov.data_ptr(), es_dtype(ov), cnt.data_ptr(), cnt[2:].data_ptr(), stream_ptr(dev)))
+    mark(marks, "coalesce1")
     u, nz, err = read_counts(cnt)
     if err & 0xFFFFFFFF:
         raise ValueError("COO index outside the tensor shape")
