@@ -24,7 +24,26 @@ struct TileGeom {
   int64_t tile_elems;
   int64_t grid_tiles;
   int64_t total_elems;
+  // log2 of tile[d], grid[d], tile_elems when a power of two, else -1
+  int tile_sh[ES_MAX_DIMS];
+  int grid_sh[ES_MAX_DIMS];
+  int te_sh;
 };
+
+static int pow2_shift(int64_t v) {
+  if (v <= 0 || (v & (v - 1)) != 0) return -1;
+  int s = 0;
+  while ((int64_t{1} << s) != v) ++s;
+  return s;
+}
+
+// x / d: a shift for powers of two, 32-bit division when both fit (the
+// common case: tile and grid extents, tile-linear indices), else 64-bit.
+__device__ __forceinline__ uint64_t udiv(uint64_t x, uint64_t d, int sh) {
+  if (sh >= 0) return x >> sh;
+  if ((x >> 32) == 0 && (d >> 32) == 0) return static_cast<uint32_t>(x) / static_cast<uint32_t>(d);
+  return x / d;
+}
 
 static int make_geom(int ndim, const int64_t* shape, const int64_t* tile, TileGeom* g) {
   if (ndim < 1 || ndim > ES_MAX_DIMS || !shape || !tile) return ES_ERR_INVALID;
@@ -44,6 +63,11 @@ static int make_geom(int ndim, const int64_t* shape, const int64_t* tile, TileGe
     g->total_elems *= shape[d];
   }
   for (int d = ndim; d < ES_MAX_DIMS; ++d) g->shape[d] = g->tile[d] = g->grid[d] = 1;
+  for (int d = 0; d < ES_MAX_DIMS; ++d) {
+    g->tile_sh[d] = pow2_shift(g->tile[d]);
+    g->grid_sh[d] = pow2_shift(g->grid[d]);
+  }
+  g->te_sh = pow2_shift(g->tile_elems);
   return ES_OK;
 }
 
@@ -98,8 +122,9 @@ __global__ void coo_keys_kernel(const int32_t* __restrict__ idx, const void* __r
       for (int d = 0; d < g.ndim; ++d) {
         int64_t x = idx[e * g.ndim + d];
         if (x < 0 || x >= g.shape[d]) ok = false;
-        tl = tl * g.grid[d] + static_cast<uint64_t>(x / g.tile[d]);
-        w = w * g.tile[d] + static_cast<uint64_t>(x % g.tile[d]);
+        const uint64_t q = udiv(static_cast<uint64_t>(x), static_cast<uint64_t>(g.tile[d]), g.tile_sh[d]);
+        tl = tl * g.grid[d] + q;
+        w = w * g.tile[d] + (static_cast<uint64_t>(x) - q * static_cast<uint64_t>(g.tile[d]));
       }
       if (ok) {
         key = tl * static_cast<uint64_t>(g.tile_elems) + w;
@@ -114,12 +139,13 @@ __global__ void coo_keys_kernel(const int32_t* __restrict__ idx, const void* __r
 
 // flags[s] = 1 where entry s starts a new tile (valid entries only).
 __global__ void tile_heads_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
-                                  uint64_t tile_elems, uint64_t sentinel, uint32_t* __restrict__ flags) {
+                                  uint64_t tile_elems, int te_sh, uint64_t sentinel, uint32_t* __restrict__ flags) {
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x) {
     uint64_t k = keys[s];
     uint32_t f = 0;
-    if (k != sentinel) f = (s == 0 || (keys[s - 1] / tile_elems) != (k / tile_elems)) ? 1u : 0u;
+    if (k != sentinel)
+      f = (s == 0 || udiv(keys[s - 1], tile_elems, te_sh) != udiv(k, tile_elems, te_sh)) ? 1u : 0u;
     flags[s] = f;
   }
 }
@@ -130,11 +156,12 @@ __global__ void tile_coords_kernel(const TileHeader* hdr, const uint64_t* k0, co
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x) {
     if (!flags[s]) continue;
-    uint64_t tl = keys[s] / static_cast<uint64_t>(g.tile_elems);
+    uint64_t tl = udiv(keys[s], static_cast<uint64_t>(g.tile_elems), g.te_sh);
     int64_t t = excl[s];
     for (int d = g.ndim - 1; d >= 0; --d) {
-      coords[t * g.ndim + d] = static_cast<int32_t>(tl % static_cast<uint64_t>(g.grid[d]));
-      tl /= static_cast<uint64_t>(g.grid[d]);
+      const uint64_t q = udiv(tl, static_cast<uint64_t>(g.grid[d]), g.grid_sh[d]);
+      coords[t * g.ndim + d] = static_cast<int32_t>(tl - q * static_cast<uint64_t>(g.grid[d]));
+      tl = q;
     }
   }
 }
@@ -143,7 +170,7 @@ __global__ void tile_coords_kernel(const TileHeader* hdr, const uint64_t* k0, co
 // chunk_start[num_chunks] = number of valid entries.
 __global__ void chunk_bounds_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
                                     const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
-                                    uint64_t tile_elems, uint64_t sentinel, int64_t num_chunks,
+                                    uint64_t tile_elems, int te_sh, uint64_t sentinel, int64_t num_chunks,
                                     int64_t* __restrict__ chunk_start) {
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s <= n; s += (int64_t)gridDim.x * blockDim.x) {
@@ -151,7 +178,8 @@ __global__ void chunk_bounds_kernel(const TileHeader* hdr, const uint64_t* k0, c
       uint64_t k = keys[i];
       if (k == sentinel) return num_chunks;
       int64_t tid = static_cast<int64_t>(excl[i]) + flags[i] - 1;
-      int64_t f = tid * static_cast<int64_t>(tile_elems) + static_cast<int64_t>(k % tile_elems);
+      int64_t f = tid * static_cast<int64_t>(tile_elems) +
+                  static_cast<int64_t>(k - udiv(k, tile_elems, te_sh) * tile_elems);
       return f / kChunk;
     };
     int64_t prev = s == 0 ? -1 : chunk_of(s - 1);
@@ -179,7 +207,8 @@ __global__ void __launch_bounds__(256) densify_kernel(const TileHeader* hdr, con
                                                       const uint32_t* __restrict__ excl,
                                                       const int64_t* __restrict__ chunk_start,
                                                       const void* __restrict__ vals, int vdtype, uint64_t tile_elems,
-                                                      int64_t total_out, int vec_ok, OutT* __restrict__ out) {
+                                                      int te_sh, int64_t total_out, int vec_ok,
+                                                      OutT* __restrict__ out) {
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
   const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
   const int64_t c = blockIdx.x;
@@ -202,7 +231,8 @@ __global__ void __launch_bounds__(256) densify_kernel(const TileHeader* hdr, con
     const bool last = (s + 1 >= n) || keys[s + 1] != k;
     if (!last) continue;
     const int64_t tid = static_cast<int64_t>(excl[s]) + flags[s] - 1;
-    const int64_t f = tid * static_cast<int64_t>(tile_elems) + static_cast<int64_t>(k % tile_elems);
+    const int64_t f = tid * static_cast<int64_t>(tile_elems) +
+                      static_cast<int64_t>(k - udiv(k, tile_elems, te_sh) * tile_elems);
     out[f] = cvt_out<OutT>(load_as_f32(vals, vdtype, perm[s]));
   }
 }
@@ -226,10 +256,12 @@ __device__ __forceinline__ int64_t dense_offset(const TileGeom& g, int64_t tile_
   // element e of grid tile tile_lin -> row-major offset in the dense array
   int64_t off = 0, stride = 1;
   for (int d = g.ndim - 1; d >= 0; --d) {
-    int64_t td = tile_lin % g.grid[d];
-    tile_lin /= g.grid[d];
-    int64_t wd = e % g.tile[d];
-    e /= g.tile[d];
+    const int64_t tq = static_cast<int64_t>(udiv(tile_lin, g.grid[d], g.grid_sh[d]));
+    const int64_t td = tile_lin - tq * g.grid[d];
+    tile_lin = tq;
+    const int64_t eq = static_cast<int64_t>(udiv(e, g.tile[d], g.tile_sh[d]));
+    const int64_t wd = e - eq * g.tile[d];
+    e = eq;
     off += (td * g.tile[d] + wd) * stride;
     stride *= g.shape[d];
   }
@@ -327,7 +359,7 @@ extern "C" int es_tile_coo_plan(const int32_t* indices, const void* values, int 
   const int alt = (k != w.keys) ? 1 : 0;
   ES_LAUNCH(set_flag_kernel, 1, 32, 0, st, &w.hdr->sorted_in_alt, alt);
   ES_LAUNCH(tile_heads_kernel, grid_for(nnz, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz,
-            static_cast<uint64_t>(g.tile_elems), sentinel, w.flags);
+            static_cast<uint64_t>(g.tile_elems), g.te_sh, sentinel, w.flags);
   // T (uint32) is accumulated into the low word of *num_tiles_dev.
   if (cudaMemsetAsync(num_tiles_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
   ES_TRY(exclusive_scan<uint32_t>(w.flags, w.excl, nnz, reinterpret_cast<uint32_t*>(num_tiles_dev), w.scan, st));
@@ -351,16 +383,17 @@ extern "C" int es_tile_coo_fill(const void* values, int values_dtype, int64_t nn
   ES_LAUNCH(tile_coords_kernel, grid_for(nnz, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz, w.flags, w.excl, g,
             coords_out);
   ES_LAUNCH(chunk_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz, w.flags,
-            w.excl, static_cast<uint64_t>(g.tile_elems), sentinel, num_chunks, w.chunk_start);
+            w.excl, static_cast<uint64_t>(g.tile_elems), g.te_sh, sentinel, num_chunks, w.chunk_start);
   const int vec_ok = (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0 ? 1 : 0;
   if (out_dtype == ES_F32) {
     ES_LAUNCH(densify_kernel<float>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
               w.rb.vals_alt, nnz, w.flags, w.excl, w.chunk_start, values, values_dtype,
-              static_cast<uint64_t>(g.tile_elems), total_out, vec_ok, static_cast<float*>(values_out));
+              static_cast<uint64_t>(g.tile_elems), g.te_sh, total_out, vec_ok, static_cast<float*>(values_out));
   } else {
     ES_LAUNCH(densify_kernel<__nv_bfloat16>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
               w.rb.vals_alt, nnz, w.flags, w.excl, w.chunk_start, values, values_dtype,
-              static_cast<uint64_t>(g.tile_elems), total_out, vec_ok, static_cast<__nv_bfloat16*>(values_out));
+              static_cast<uint64_t>(g.tile_elems), g.te_sh, total_out, vec_ok,
+              static_cast<__nv_bfloat16*>(values_out));
   }
   return ES_OK;
 }
