@@ -59,15 +59,19 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms from before the
+    warm-up to after the timed regions; the summary keeps the samples whose
+    timestamps fall inside a timed region (``window_start``/``window_end``),
+    or, for a region shorter than the sampling period, the nearest one."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.windows = []
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{gpu_index}.csv")
 
     def __enter__(self):
@@ -75,11 +79,17 @@ class ClockSampler:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
+
+    def window_start(self):
+        self.windows.append([time.time(), None])
+
+    def window_end(self):
+        self.windows[-1][1] = time.time()
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -93,22 +103,32 @@ class ClockSampler:
     def summary(self):
         if self.proc is None or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons = [], [], set()
+        import datetime
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in open(self.path):
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                t = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((t, float(parts[2]), float(parts[3]),
+                             {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        wins = [(a, b) for a, b in self.windows if b is not None]
+        inside = [r for r in rows if any(a - 0.05 <= r[0] <= b + 0.05 for a, b in wins)]
+        nearest = False
+        if not inside and rows and wins:
+            inside = [min(rows, key=lambda r: min(abs(r[0] - (a + b) / 2) for a, b in wins))]
+            nearest = True
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        out = {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+               "reasons": sorted(set().union(*[r[3] for r in inside])), "samples": len(inside)}
+        if nearest:
+            out["nearest_sample"] = True
+        return out
 
 
 def run_ours(args):
@@ -154,6 +174,7 @@ def run_ours(args):
             ev["h"][-1].record()
         return A, B, plan, vals
 
+    clk = ClockSampler(local).__enter__()
     for _ in range(args.warmup):
         A, B, plan, vals = step(idx_d, val_d, b_d)
     torch.cuda.synchronize()
@@ -168,18 +189,19 @@ def run_ours(args):
 
     # ---- device-resident timing
     ev.clear()
-    with ClockSampler(local) as clk:
-        barrier()
-        torch.cuda.synchronize()
-        n0 = _lib.lib().es_launch_count()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(args.steps):
-            A, B, plan, vals = step(idx_d, val_d, b_d, timing=True)
-        e.record()
-        torch.cuda.synchronize()
-        barrier()
-        launches = _lib.lib().es_launch_count() - n0
+    barrier()
+    torch.cuda.synchronize()
+    n0 = _lib.lib().es_launch_count()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk.window_start()
+    s.record()
+    for _ in range(args.steps):
+        A, B, plan, vals = step(idx_d, val_d, b_d, timing=True)
+    e.record()
+    torch.cuda.synchronize()
+    clk.window_end()
+    barrier()
+    launches = _lib.lib().es_launch_count() - n0
     ms = s.elapsed_time(e)
     gemm_ms = [a.elapsed_time(b) for a, b in zip(ev["g"], ev["h"])]
     del A, B, plan, vals
@@ -237,10 +259,13 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk.window_start()
     s2.record()
     outs = e2e_run(args.steps, outs, s2)
     e2.record()
     torch.cuda.synchronize()
+    clk.window_end()
+    clk.__exit__(None, None, None)
     barrier()
     e2e_ms = s2.elapsed_time(e2)
     out_h, oc_h = outs[0]

@@ -23,8 +23,16 @@ namespace es {
 struct CooGeom {
   int ndim;
   int64_t shape[ES_MAX_DIMS];
+  int shape_sh[ES_MAX_DIMS];  // log2(shape[d]) for a power of two, else -1
   int64_t total;
 };
+
+// x / d: a shift for powers of two, 32-bit division when both fit, else 64-bit.
+__device__ __forceinline__ uint64_t coo_udiv(uint64_t x, uint64_t d, int sh) {
+  if (sh >= 0) return x >> sh;
+  if ((x >> 32) == 0 && (d >> 32) == 0) return static_cast<uint32_t>(x) / static_cast<uint32_t>(d);
+  return x / d;
+}
 
 struct CoalesceWs {
   uint64_t* keys;
@@ -70,6 +78,14 @@ static int make_coo_geom(int ndim, const int64_t* shape, CooGeom* g) {
     g->total *= shape[d];
   }
   for (int d = ndim; d < ES_MAX_DIMS; ++d) g->shape[d] = 1;
+  for (int d = 0; d < ES_MAX_DIMS; ++d) {
+    const int64_t v = g->shape[d];
+    int sh = -1;
+    if ((v & (v - 1)) == 0)
+      for (sh = 0; (int64_t{1} << sh) != v; ++sh) {
+      }
+    g->shape_sh[d] = sh;
+  }
   return ES_OK;
 }
 
@@ -142,8 +158,9 @@ __global__ void coalesce_write_kernel(const int32_t* alt, const uint64_t* k0, co
     const int64_t o = excl[s];
     uint64_t lin = k;
     for (int d = g.ndim - 1; d >= 0; --d) {
-      idx_out[o * g.ndim + d] = static_cast<int32_t>(lin % static_cast<uint64_t>(g.shape[d]));
-      lin /= static_cast<uint64_t>(g.shape[d]);
+      const uint64_t q = coo_udiv(lin, static_cast<uint64_t>(g.shape[d]), g.shape_sh[d]);
+      idx_out[o * g.ndim + d] = static_cast<int32_t>(lin - q * static_cast<uint64_t>(g.shape[d]));
+      lin = q;
     }
     double v;
     if (policy == ES_DUP_SUM) {
