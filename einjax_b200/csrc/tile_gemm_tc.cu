@@ -1489,11 +1489,20 @@ __global__ void item_rec_kernel(const uint32_t* __restrict__ off, const uint32_t
   }
 }
 
-// Key chunks of the merge pass: a multiple of the key blocks, about 256 keys
-// each (1 without keys).
+// Key chunks of the merge pass: a multiple of the key blocks, about
+// kMergeChunkKeys keys each (1 without keys). Smaller chunks measured slower
+// on C2 (fill pass 342 us with 256 keys per chunk, 414 us with 32).
+constexpr int64_t kMergeChunkKeys = 256;
+
 int merge_chunks(int nblocks, bool have_key, int64_t key_extent) {
   if (!have_key || key_extent <= 1) return 1;
-  int64_t m = key_extent / (256ll * nblocks);
+  int64_t keys = kMergeChunkKeys;
+  // EINSPARSE_MERGE_KEYS overrides the keys per chunk (tuning, tests)
+  if (const char* e = std::getenv("EINSPARSE_MERGE_KEYS")) {
+    const long long v = std::atoll(e);
+    if (v > 0) keys = v;
+  }
+  int64_t m = key_extent / (keys * nblocks);
   if (m < 1) m = 1;
   while (nblocks * m > kMaxMergeChunks) --m;
   if (m < 1) m = 1;
@@ -1811,8 +1820,11 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     const int C = merge_chunks(nblocks, pair_key != nullptr, key_extent);
     const int32_t* keys = (c.slots > 1 || C > 1) ? pair_key : nullptr;
     const int64_t nw = nslots * C;
+    // grid-stride: nw counts a slot per possible item (most are past the real
+    // items and only write a zero count), so a grid of a few blocks per SM
+    // walks them instead of launching one mostly empty block per 4 slots
     int64_t nb = (nw + kMergeWarps - 1) / kMergeWarps;
-    const int blocks = static_cast<int>(nb < 65536 ? nb : 65536);  // grid-stride beyond
+    const int blocks = static_cast<int>(nb < 148 * 8 ? nb : 148 * 8);
     ES_LAUNCH(tc_merge_kernel<true>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
               w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
               (const uint32_t*)nullptr, w.recs, err);
