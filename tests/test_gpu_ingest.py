@@ -148,3 +148,21 @@ def test_dlpack_and_pydata_inputs():
     c3, v3 = E.SparseTensor("t", _DLPackOnly(dense)).to_relation((8, 8, 8)).to_numpy()
     np.testing.assert_array_equal(c3, ref.coords)
     np.testing.assert_array_equal(v3, v)
+
+
+@pytest.mark.parametrize("n", [1, 2, 31, 4095, 4096, 4097, 3 * 4096 + 5, 70_001])
+@pytest.mark.parametrize("shape", [(7, 3), (1 << 20, 1 << 20, 1 << 20), (3, 1 << 30, 5), (1 << 16, 1 << 16)])
+def test_coalesce_sort_sizes_and_key_widths(n, shape):
+    """The radix sort under coalescing at tile-boundary sizes (4096 keys per
+    tile) and key widths from 5 to 61 bits (1 to 8 passes), heavy repeats."""
+    rng = np.random.default_rng(n + len(shape))
+    idx = np.stack([rng.integers(0, s, n) for s in shape], 1).astype(np.int32)
+    rep = rng.choice(n, n // 2, replace=False) if n > 1 else np.zeros(0, np.int64)
+    idx[rep] = idx[rng.choice(n, len(rep))]
+    val = rng.standard_normal(n)
+    for pol in ("sum", "last"):
+        gi, gv, nz = E.coalesce_coo(torch.from_numpy(idx).cuda(), torch.from_numpy(val).cuda(), shape, pol)
+        ri, rv, rnz = O.coalesce_coo(idx, val, shape, pol)
+        assert nz == rnz
+        np.testing.assert_array_equal(gi.cpu().numpy(), ri)
+        np.testing.assert_array_equal(gv.cpu().numpy(), rv)
