@@ -302,6 +302,44 @@ __global__ void dense_fill_kernel(const void* __restrict__ dense, int dtype, Til
   }
 }
 
+// fp32 -> fp32 with tile rows and dense rows in whole 16-byte pieces (both
+// arrays 16-byte aligned): four consecutive elements of a tile row are four
+// consecutive floats of the dense array, so each thread moves 16-byte pieces,
+// all of a tile's loads issued before its stores.
+__global__ void __launch_bounds__(256) dense_fill_vec_kernel(const float* __restrict__ dense, TileGeom g,
+                                                             const uint32_t* __restrict__ flags,
+                                                             const uint32_t* __restrict__ excl,
+                                                             int32_t* __restrict__ coords, float* __restrict__ out) {
+  constexpr int kPer = 4;  // 16-byte pieces per thread in flight
+  const int64_t pieces = g.tile_elems / 4;
+  for (int64_t t = blockIdx.x; t < g.grid_tiles; t += gridDim.x) {
+    if (!flags[t]) continue;
+    const int64_t r = excl[t];
+    if (threadIdx.x < g.ndim) {
+      int64_t tl = t;
+      for (int d = g.ndim - 1; d >= 0; --d) {
+        const int64_t q = static_cast<int64_t>(udiv(tl, g.grid[d], g.grid_sh[d]));
+        if (d == (int)threadIdx.x) coords[r * g.ndim + d] = static_cast<int32_t>(tl - q * g.grid[d]);
+        tl = q;
+      }
+    }
+    float4* o = reinterpret_cast<float4*>(out + r * g.tile_elems);
+    for (int64_t p0 = threadIdx.x; p0 < pieces; p0 += static_cast<int64_t>(blockDim.x) * kPer) {
+      float4 v[kPer];
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int64_t p = p0 + static_cast<int64_t>(j) * blockDim.x;
+        if (p < pieces) v[j] = *reinterpret_cast<const float4*>(dense + dense_offset(g, t, 4 * p));
+      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int64_t p = p0 + static_cast<int64_t>(j) * blockDim.x;
+        if (p < pieces) o[p] = v[j];
+      }
+    }
+  }
+}
+
 }  // namespace es
 
 using namespace es;
@@ -438,7 +476,13 @@ extern "C" int es_tile_dense_fill(const void* dense, int dtype, int ndim, const 
   dense_layout(c, w, g.grid_tiles);
   if (c.overflow) return ES_ERR_WORKSPACE;
   const int grid = static_cast<int>(g.grid_tiles < 148 * 16 ? g.grid_tiles : 148 * 16);
-  if (out_dtype == ES_F32)
+  const bool vec = dtype == ES_F32 && out_dtype == ES_F32 && g.tile[ndim - 1] % 4 == 0 &&
+                   g.shape[ndim - 1] % 4 == 0 && (reinterpret_cast<uintptr_t>(dense) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0;
+  if (vec)
+    ES_LAUNCH(dense_fill_vec_kernel, grid, 256, 0, st, static_cast<const float*>(dense), g, w.flags, w.excl,
+              coords_out, static_cast<float*>(values_out));
+  else if (out_dtype == ES_F32)
     ES_LAUNCH(dense_fill_kernel<float>, grid, 256, 0, st, dense, dtype, g, w.flags, w.excl, coords_out,
               static_cast<float*>(values_out));
   else
