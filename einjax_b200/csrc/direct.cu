@@ -362,14 +362,26 @@ __global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, 
 #pragma unroll
     for (int j = 0; j < kDirCols; ++j)
       r[j] = c0 + j < C ? direct_lookup(g, table, key, colids[c0 + j]) : -1;
+    // the (strip, column) bases of every hit first, all loads in flight together
+    int64_t pb[kDirCols];
+    uint32_t gb[kDirCols];
+#pragma unroll
+    for (int j = 0; j < kDirCols; ++j) {
+      pb[j] = 0;
+      gb[j] = 0;
+      if (r[j] >= 0) {
+        const int64_t c = c0 + j;
+        const int64_t e = s * C + c;
+        pb[j] = static_cast<int64_t>(posw[e] & 0xFFFFFFFFull);
+        gb[j] = cscan[c * nchp1 + ch] - gstart[e];
+      }
+    }
 #pragma unroll
     for (int j = 0; j < kDirCols; ++j) {
       const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
       if (r[j] >= 0) {
-        const int64_t c = c0 + j;
-        const int64_t e = s * C + c;
-        const uint32_t gi = cscan[c * nchp1 + ch] + __popc(m & below);
-        const int64_t p = static_cast<int64_t>(posw[e] & 0xFFFFFFFFull) + (gi - gstart[e]);
+        // first(s, c) + G_c(i) - G_c(start s), as uint32 (non-negative for a hit)
+        const int64_t p = pb[j] + static_cast<uint32_t>(gb[j] + __popc(m & below));
         seg_lhs[p] = static_cast<int32_t>(i);
         seg_rhs[p] = r[j];
         if (seg_key) seg_key[p] = k;
