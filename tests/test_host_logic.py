@@ -236,3 +236,21 @@ def test_b200_cost_profile_detection(monkeypatch):
     monkeypatch.setattr(CM, "_torch_device_count", lambda: 2)
     cfg = m.detect_device_config()
     assert cfg.device_type == "gpu:b200" and cfg.num_devices == 2
+
+
+def test_plan_operand_order_prefers_tensor_core_form():
+    """A plan step whose tile product only the swapped operand order puts on the
+    tensor cores runs swapped; natural orders stay (host-side path query)."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from einjax_b200.plan import _operand_order
+    a = SimpleNamespace(tile_shape=(128, 128), values=torch.zeros(1))
+    b = SimpleNamespace(tile_shape=(128, 64), values=torch.zeros(1))
+    f, lhs, rhs = _operand_order("kl,ik->il", b, a, "auto")
+    assert f == "ik,kl->il" and lhs is a and rhs is b
+    f, lhs, rhs = _operand_order("ik,kl->il", a, b, "auto")
+    assert f == "ik,kl->il" and lhs is a and rhs is b
+    t = SimpleNamespace(tile_shape=(1, 32, 32), values=torch.zeros(1))
+    assert _operand_order("bkl,bik->bil", t, t, "auto")[0] == "bik,bkl->bil"
