@@ -150,41 +150,36 @@ __global__ void tile_heads_kernel(const TileHeader* hdr, const uint64_t* k0, con
   }
 }
 
-__global__ void tile_coords_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
-                                   const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
-                                   TileGeom g, int32_t* __restrict__ coords) {
+// One pass over the sorted entries (s = 0 .. n):
+// * a tile's first entry writes the tile's coordinates (coords row excl[s]);
+// * chunk_start[c] = first sorted entry whose output position lies in chunk c,
+//   chunk_start[num_chunks] = number of valid entries.
+__global__ void tile_coords_bounds_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
+                                          const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
+                                          TileGeom g, uint64_t sentinel, int64_t num_chunks,
+                                          int32_t* __restrict__ coords, int64_t* __restrict__ chunk_start) {
   const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
-  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x) {
-    if (!flags[s]) continue;
-    uint64_t tl = udiv(keys[s], static_cast<uint64_t>(g.tile_elems), g.te_sh);
-    int64_t t = excl[s];
-    for (int d = g.ndim - 1; d >= 0; --d) {
-      const uint64_t q = udiv(tl, static_cast<uint64_t>(g.grid[d]), g.grid_sh[d]);
-      coords[t * g.ndim + d] = static_cast<int32_t>(tl - q * static_cast<uint64_t>(g.grid[d]));
-      tl = q;
-    }
-  }
-}
-
-// chunk_start[c] = first sorted entry whose output position lies in chunk c;
-// chunk_start[num_chunks] = number of valid entries.
-__global__ void chunk_bounds_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
-                                    const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
-                                    uint64_t tile_elems, int te_sh, uint64_t sentinel, int64_t num_chunks,
-                                    int64_t* __restrict__ chunk_start) {
-  const uint64_t* keys = hdr->sorted_in_alt ? k1 : k0;
+  const uint64_t te = static_cast<uint64_t>(g.tile_elems);
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s <= n; s += (int64_t)gridDim.x * blockDim.x) {
     auto chunk_of = [&](int64_t i) -> int64_t {
       uint64_t k = keys[i];
       if (k == sentinel) return num_chunks;
       int64_t tid = static_cast<int64_t>(excl[i]) + flags[i] - 1;
-      int64_t f = tid * static_cast<int64_t>(tile_elems) +
-                  static_cast<int64_t>(k - udiv(k, tile_elems, te_sh) * tile_elems);
+      int64_t f = tid * static_cast<int64_t>(te) + static_cast<int64_t>(k - udiv(k, te, g.te_sh) * te);
       return f / kChunk;
     };
     int64_t prev = s == 0 ? -1 : chunk_of(s - 1);
     int64_t cur = s == n ? num_chunks : chunk_of(s);
     for (int64_t c = prev + 1; c <= cur; ++c) chunk_start[c] = s;
+    if (s < n && flags[s]) {
+      uint64_t tl = udiv(keys[s], te, g.te_sh);
+      const int64_t t = excl[s];
+      for (int d = g.ndim - 1; d >= 0; --d) {
+        const uint64_t q = udiv(tl, static_cast<uint64_t>(g.grid[d]), g.grid_sh[d]);
+        coords[t * g.ndim + d] = static_cast<int32_t>(tl - q * static_cast<uint64_t>(g.grid[d]));
+        tl = q;
+      }
+    }
   }
 }
 
@@ -418,10 +413,8 @@ extern "C" int es_tile_coo_fill(const void* values, int values_dtype, int64_t nn
   const int64_t total_out = num_tiles * g.tile_elems;
   const int64_t num_chunks = (total_out + kChunk - 1) / kChunk;
   if (num_chunks > max_chunks_for(nnz, g.tile_elems)) return ES_ERR_INVALID;
-  ES_LAUNCH(tile_coords_kernel, grid_for(nnz, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz, w.flags, w.excl, g,
-            coords_out);
-  ES_LAUNCH(chunk_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz, w.flags,
-            w.excl, static_cast<uint64_t>(g.tile_elems), g.te_sh, sentinel, num_chunks, w.chunk_start);
+  ES_LAUNCH(tile_coords_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz,
+            w.flags, w.excl, g, sentinel, num_chunks, coords_out, w.chunk_start);
   const int vec_ok = (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0 ? 1 : 0;
   if (out_dtype == ES_F32) {
     ES_LAUNCH(densify_kernel<float>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
