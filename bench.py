@@ -1,8 +1,8 @@
 """Benchmark of the sparse-einsum hot path (one JSON line on rank 0).
 
-Workload ("C2"): A = 65536^2 element COO with
-4,294,967 unique entries (Zipf s=1.1 rows, uniform columns, N(0,1)), B =
-dense 65536x256 N(0,1), tile 32, ``ij,jk->ik``. One step = one pass of the
+Headline workload ("C2"): A = 65536^2 element COO
+with 4,294,967 unique entries (Zipf s=1.1 rows, uniform columns, N(0,1)),
+B = dense 65536x256 N(0,1), tile 32, ``ij,jk->ik``. One step = one pass of the
 hot path over it: COO->tile-COO tiling of A, dense->tile-COO of B, the
 coordinate join, output grouping and the fused tile-GEMM + segment-sum
 (``execute_sparse``). Metric: useful TFLOP/s = joined tile pairs x 2*32^3
@@ -16,8 +16,21 @@ per second (joined tile-pairs/s is reported beside it).
   back, all inside the timed region; the copies run on one stream per
   direction, so step k+1's inputs and step k-1's result move while step k
   computes (double-buffered device inputs and pinned results).
-* ``--gpus N`` (torchrun, one rank per GPU): weak scaling, every rank runs its
-  own C2 instance (seed = rank); the path needs no collective.
+* ``--gpus N`` (torchrun, one rank per GPU): strong scaling of the one C2
+  problem through output-strip sharding (``execute_sharded_sparse``): rank r
+  takes a tile-aligned range of A's rows balanced by non-empty tiles
+  (``balanced_row_ranges``), tiles, joins, groups and contracts only those
+  against the replicated B; output strips are disjoint, so no collective
+  touches the data path.
+* ``parity``: after the timed loops every rank compares its output strips
+  with scipy's float64 ``A[rows] @ B`` (all elements), and with a plain fp32
+  SpMM for context.
+* ``configs``: the other BASELINE configurations in the same line -- C1, C3,
+  C4 (forward + gradients of all three operands) and C5 on one GPU at N=1;
+  at N>1, C5 sharded over its contracted (k) tile range with the partial
+  output tiles summed by an NCCL reduce-scatter, as BASELINE specifies.
+  Each entry: ms per step, useful TFLOP/s, roofline fractions, clocks and a
+  parity sample against a float64 computation.
 * ``--impl reference``: the CPU oracle (numpy port of the reference's path)
   on a bounded row-slice sample of the same workload, all host threads.
 """
@@ -30,6 +43,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -43,7 +57,7 @@ FLOPS_PER_PAIR = 2 * TILE ** 3
 # capture of the 1/4-scale C2 case (one key block, 923,064 pairs); the lhs
 # tiles dominate and are read once, so the traffic grows with the pairs.
 TRAFFIC_PER_PAIR = 569.3
-TRAFFIC_SOURCE = "ncu dram bytes of tc_strip_kernel at C2 scale 1/4, scaled by pairs (profiles/tc_strip_kernel_c2_scale4.md)"
+TRAFFIC_SOURCE = "ncu dram__bytes_read+write of the tile GEMM at C2 scale 1/4 per pair, times this run's pairs"
 
 
 def _env_rank():
@@ -60,9 +74,10 @@ def _peaks():
 
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 50 ms from before the
-    warm-up to after the timed regions; the summary keeps the samples whose
-    timestamps fall inside a timed region (``window_start``/``window_end``),
-    or, for a region shorter than the sampling period, the nearest one."""
+    warm-up to after the timed regions (into a temporary file); a summary
+    keeps the samples whose timestamps fall inside the chosen timed regions
+    (``window_start``/``window_end``), or, for a region shorter than the
+    sampling period, the nearest one."""
 
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -72,11 +87,11 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.windows = []
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_bench_{gpu_index}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"einsparse_clocks_{gpu_index}_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
@@ -87,11 +102,12 @@ class ClockSampler:
 
     def window_start(self):
         self.windows.append([time.time(), None])
+        return len(self.windows) - 1
 
     def window_end(self):
         self.windows[-1][1] = time.time()
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -99,9 +115,17 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
             self.f.close()
+            self.proc = None
 
-    def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
+    def __exit__(self, *a):
+        self.stop()
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+
+    def summary(self, which=None):
+        if not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         import datetime
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -116,7 +140,7 @@ class ClockSampler:
                              {n for n, v in zip(names, parts[6:10]) if v.lower() == "active"}))
             except ValueError:
                 continue
-        wins = [(a, b) for a, b in self.windows if b is not None]
+        wins = [w for i, w in enumerate(self.windows) if w[1] is not None and (which is None or i in which)]
         inside = [r for r in rows if any(a - 0.05 <= r[0] <= b + 0.05 for a, b in wins)]
         nearest = False
         if not inside and rows and wins:
@@ -131,12 +155,90 @@ class ClockSampler:
         return out
 
 
+# ------------------------------------------------------------------ parity
+# float64 computations straight from the inputs (numpy / scipy), independent
+# of the library and of the CPU oracle package.
+
+def _err_stats(got, ref, mag, rtol):
+    got = np.asarray(got, dtype=np.float64)
+    err = np.abs(got - ref)
+    aref = np.abs(ref)
+    nz = aref > 0
+    return {
+        "elements": int(ref.size),
+        "max_abs_err": float(err.max()) if err.size else 0.0,
+        "max_rel": float((err[nz] / aref[nz]).max()) if nz.any() else 0.0,
+        "within_rtol": round(float((err <= rtol * aref).mean()), 7) if err.size else 1.0,
+        "rel_fro": float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-300)),
+        "bound_ok": bool(np.all(err <= rtol * (aref + mag))),
+    }
+
+
+def c2_parity(w, rows, coords, vals, rtol=1e-5):
+    """This rank's output strips (rows [r0, r1) of the 65536 x 256 result)
+    against scipy float64 ``A[rows] @ B``; a plain fp32 SpMM of the same
+    inputs (scipy, float32 accumulation) is measured the same way beside it."""
+    import scipy.sparse as sp
+    r0, r1 = rows
+    idx, val = w.lhs.indices, w.lhs.values
+    keep = (idx[:, 0] >= r0) & (idx[:, 0] < r1)
+    n, ncol = w.lhs.shape[1], w.rhs.shape[1]
+    A = sp.csr_matrix((val[keep].astype(np.float64), (idx[keep, 0] - r0, idx[keep, 1])), shape=(r1 - r0, n))
+    B = w.rhs.astype(np.float64)
+    ref = A @ B
+    mag = abs(A) @ np.abs(B)
+    got = np.zeros((r1 - r0, ncol), dtype=np.float64)
+    if len(coords):
+        g4 = got.reshape((r1 - r0) // TILE, TILE, ncol // TILE, TILE)
+        g4[coords[:, 0] - r0 // TILE, :, coords[:, 1], :] = vals
+    out = _err_stats(got, ref, mag, rtol)
+    A32 = sp.csr_matrix((val[keep].astype(np.float32), (idx[keep, 0] - r0, idx[keep, 1])), shape=(r1 - r0, n))
+    f32 = _err_stats(A32 @ w.rhs.astype(np.float32), ref, mag, rtol)
+    out["fp32_spmm_within_rtol"] = f32["within_rtol"]
+    out["fp32_spmm_max_rel"] = f32["max_rel"]
+    out["fp32_spmm_rel_fro"] = f32["rel_fro"]
+    return out
+
+
+def blocksparse_ref(lc, lv, rc, rv, nb, want):
+    """float64 tiles of ``(batch..., i, j) x (batch..., j, k) -> (batch..., i, k)``
+    at the output coordinates ``want`` (rows of (batch..., i, k)), summed over
+    the contracted tile index from the host tile arrays; also the same sums
+    of |a||b| (the magnitude scale of each element)."""
+    from collections import defaultdict
+    strips = defaultdict(list)
+    for t, c in enumerate(map(tuple, lc)):
+        strips[c[:-1]].append((c[-1], t))
+    rmap = {c: t for t, c in enumerate(map(tuple, rc))}
+    te = (lv.shape[-2], rv.shape[-1])
+    ref = np.zeros((len(want), *te))
+    mag = np.zeros((len(want), *te))
+    for q, c in enumerate(map(tuple, want)):
+        for j, li in strips.get(c[:-1], ()):
+            ri = rmap.get(c[:nb] + (j, c[-1]))
+            if ri is None:
+                continue
+            a = lv[li].reshape(te[0], -1).astype(np.float64)
+            b = rv[ri].reshape(-1, te[1]).astype(np.float64)
+            ref[q] += a @ b
+            mag[q] += np.abs(a) @ np.abs(b)
+    return ref, mag
+
+
+def _sample_rows(n, k, seed=0):
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(n, min(n, k), replace=False)) if n else np.zeros(0, dtype=np.int64)
+
+
+# ------------------------------------------------------------------ C2 headline
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     import einjax_b200 as E
     from einjax_b200 import _lib
+    from einjax_b200 import distributed as D
     from einjax_b200 import sparse_dispatch as SD
     from einjax_b200 import workloads as W
 
@@ -148,21 +250,32 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     _lib.load()
 
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
     t0 = time.time()
-    w = W.c2_spmm(seed=args.seed + rank, scale=args.scale)
+    w = W.c2_spmm(seed=args.seed, scale=args.scale)
     gen_s = time.time() - t0
     shape = w.lhs.shape
-    idx_h = torch.from_numpy(w.lhs.indices).pin_memory()
-    val_h = torch.from_numpy(w.lhs.values).pin_memory()
+    # output-strip sharding: this rank's tile-aligned rows of A
+    rows = D.balanced_row_ranges(w.lhs.indices, shape, (TILE, TILE), world)[rank] if world > 1 else (0, shape[0])
+    keep = (w.lhs.indices[:, 0] >= rows[0]) & (w.lhs.indices[:, 0] < rows[1])
+    idx_h = torch.from_numpy(np.ascontiguousarray(w.lhs.indices[keep])).pin_memory()
+    val_h = torch.from_numpy(np.ascontiguousarray(w.lhs.values[keep])).pin_memory()
     b_h = torch.from_numpy(w.rhs).pin_memory()
     idx_d, val_d, b_d = idx_h.to(dev), val_h.to(dev), b_h.to(dev)
     jk, ks, ak = w.join_keys, w.kernel_string, w.agg_keys
     ev = {}
 
-    def step(idx, val, b, timing=False):
+    def step(idx, val, b, timing=False, marks=None):
+        E.sparse.mark(marks, "s0")
         A = E.tile_coo(idx, val, shape, (TILE, TILE))
+        E.sparse.mark(marks, "s1")
         B = E.tile_dense(b, (TILE, TILE))
+        E.sparse.mark(marks, "s2")
         plan = SD.plan_pairs(A, B, jk, ak)
+        E.sparse.mark(marks, "s3")
         if timing:
             ev.setdefault("g", []).append(torch.cuda.Event(enable_timing=True))
             ev["g"][-1].record()
@@ -172,6 +285,7 @@ def run_ours(args):
         if timing:
             ev.setdefault("h", []).append(torch.cuda.Event(enable_timing=True))
             ev["h"][-1].record()
+        E.sparse.mark(marks, "s4")
         return A, B, plan, vals
 
     clk = ClockSampler(local).__enter__()
@@ -183,17 +297,13 @@ def run_ours(args):
     T_A = A.num_tuples
     del A, B, plan, vals
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     # ---- device-resident timing
     ev.clear()
     barrier()
     torch.cuda.synchronize()
     n0 = _lib.lib().es_launch_count()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk.window_start()
+    w_main = clk.window_start()
     s.record()
     for _ in range(args.steps):
         A, B, plan, vals = step(idx_d, val_d, b_d, timing=True)
@@ -230,7 +340,8 @@ def run_ours(args):
         idx, val, b = slots[k % 2]
         A = E.SparseTensor("A", (idx, val, shape)).to_relation((TILE, TILE))
         B = E.SparseTensor("B", b).to_relation((TILE, TILE))
-        return E.execute_sparse(A, B, jk, ks, ak, precision=args.precision)
+        return E.execute_sharded_sparse(A, B, jk, ks, ak, precision=args.precision, lhs_sharded=True,
+                                        gather=False)
 
     def e2e_run(steps, outs, start):
         ev_in, ev_done = [None, None], [None, None]
@@ -259,13 +370,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clk.window_start()
+    w_e2e = clk.window_start()
     s2.record()
     outs = e2e_run(args.steps, outs, s2)
     e2.record()
     torch.cuda.synchronize()
     clk.window_end()
-    clk.__exit__(None, None, None)
     barrier()
     e2e_ms = s2.elapsed_time(e2)
     out_h, oc_h = outs[0]
@@ -274,61 +384,68 @@ def run_ours(args):
     del slots
 
     # ---- per-phase split of one device-resident step (untimed for the metric)
-    phases = {}
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-    evs[0].record()
-    A = E.tile_coo(idx_d, val_d, shape, (TILE, TILE))
-    evs[1].record()
-    B = E.tile_dense(b_d, (TILE, TILE))
-    evs[2].record()
-    plan = SD.plan_pairs(A, B, jk, ak)
-    evs[3].record()
-    SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets, precision=args.precision,
-                   seg_strip=plan.seg_strip, pair_key=plan.seg_key, key_extent=plan.key_extent)
-    evs[4].record()
+    m = []
+    A, B, plan, vals = step(idx_d, val_d, b_d, marks=m)
     torch.cuda.synchronize()
-    for name, i in (("tile_coo_A", 0), ("tile_dense_B", 1), ("join_and_group", 2), ("tile_gemm", 3)):
-        phases[name] = round(evs[i].elapsed_time(evs[i + 1]), 3)
-    del A, B, plan
+    d = dict(m)
+    phases = {name: round(d[a].elapsed_time(d[b]), 3) for name, a, b in
+              (("tile_coo_A", "s0", "s1"), ("tile_dense_B", "s1", "s2"), ("join_and_group", "s2", "s3"),
+               ("tile_gemm", "s3", "s4"))}
+    # ---- parity of this rank's output strips (full, float64)
+    par = c2_parity(w, rows, plan.out_coords.cpu().numpy(), vals.cpu().numpy())
+    del A, B, plan, vals
 
-    tot = torch.tensor([ms, e2e_ms, float(P), float(P * FLOPS_PER_PAIR)], dtype=torch.float64, device=dev)
+    per_rank = torch.tensor([ms / args.steps, e2e_ms / args.steps, statistics.mean(gemm_ms),
+                             *[phases[k] for k in ("tile_coo_A", "tile_dense_B", "join_and_group", "tile_gemm")],
+                             float(P), float(T_A), float(O), par["max_rel"], par["max_abs_err"],
+                             par["within_rtol"], 1.0 if par["bound_ok"] else 0.0, par["rel_fro"],
+                             par["fp32_spmm_within_rtol"], float(launches)], dtype=torch.float64, device=dev)
     if world > 1:
-        mx = tot[:2].clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = tot[2:].clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms, e2e_ms = float(mx[0]), float(mx[1])
-        P_all, flops_all = float(sm[0]), float(sm[1])
+        allr = [torch.zeros_like(per_rank) for _ in range(world)]
+        dist.all_gather(allr, per_rank)
+        table = torch.stack(allr).cpu().numpy()
     else:
-        P_all, flops_all = float(P), float(P * FLOPS_PER_PAIR)
+        table = per_rank.cpu().numpy()[None, :]
+
+    cfgs = {}
+    if not args.no_configs:
+        cfgs = measure_configs(args, dev, rank, world, clk, barrier)
 
     if rank == 0:
         hbm, bf16, src = _peaks()
-        g_ms = statistics.mean(gemm_ms)
+        ms_step = float(table[:, 0].max())
+        e2e_step = float(table[:, 1].max())
+        slow = int(table[:, 0].argmax())
+        P_all = float(table[:, 7].sum())
+        flops_all = P_all * FLOPS_PER_PAIR
+        g_ms = float(table[0, 2])
         # dominant kernel: the fused tile GEMM + segment-sum (one es_tile_einsum
-        # call per step). Algorithmic FLOPs = P * 2*32^3 per call.
+        # call per step), on rank 0. Algorithmic FLOPs = P * 2*32^3 per call.
         achieved = P * FLOPS_PER_PAIR / (g_ms * 1e-3) / 1e12
-        bound = "tensor"
         peak = bf16
         line = {
             "metric": "useful TFLOP/s (sparse einsum, C2 element-sparse SpMM)",
-            "value": round(flops_all * args.steps / (ms * 1e-3) / 1e12, 3),
+            "value": round(flops_all / (ms_step * 1e-3) / 1e12, 3),
             "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded C2 generator, seed=rank)",
+            "ms_per_step": round(ms_step, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded C2 generator; one problem shared by all ranks)",
             "config": {"workload": "C2 ij,jk->ik: A 65536^2 COO 4,294,967 nnz Zipf(1.1) rows, B dense 65536x256, "
                                    "tile 32" + (f" (scale 1/{args.scale})" if args.scale != 1 else ""),
-                       "global_batch": world, "pairs_per_rank": P, "tiles_A": T_A, "out_tiles": O,
+                       "global_batch": 1, "pairs": int(P_all), "tiles_A": int(table[:, 8].sum()),
+                       "out_tiles": int(table[:, 9].sum()),
                        "l2": "inputs >> L2 (8 GB of A tiles per step), no flush",
-                       "parallelism": f"independent instance per rank x{world}", "precision": args.precision},
-            "pairs_per_s": round(P_all * args.steps / (ms * 1e-3), 1),
-            "e2e": {"value": round(flops_all * args.steps / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                    "ms_per_step": round(e2e_ms / args.steps, 3),
+                       "parallelism": (f"output-strip sharding x{world}: each rank tiles, joins and contracts a "
+                                       "tile-row range of A balanced by non-empty tiles against the replicated B; "
+                                       "no data-path collective") if world > 1 else "single GPU",
+                       "precision": args.precision},
+            "pairs_per_s": round(P_all / (ms_step * 1e-3), 1),
+            "e2e": {"value": round(flops_all / (e2e_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_step, 3),
                     "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
                     "copies": "one stream per direction, overlapping the neighbouring steps' compute"},
-            "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": bound,
+            "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": "tensor",
                          "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4),
                          "traffic": int(TRAFFIC_PER_PAIR * P),
@@ -338,19 +455,319 @@ def run_ours(args):
                          "fp32_peak": round(peak / 6, 1),
                          "frac_fp32_peak": round(achieved / (peak / 6), 4),
                          "kernel_ms": round(g_ms, 3)},
-            "gpu_launches": int(launches),
-            "phases_ms": phases,
-            "clocks": clk.summary(),
+            "parity": {"reference": "scipy float64 A @ B, every output element" +
+                                    (" (each rank its own strips)" if world > 1 else ""),
+                       "rtol": 1e-5, "max_rel": float(table[:, 10].max()), "max_abs_err": float(table[:, 11].max()),
+                       "within_rtol": float(table[:, 12].min()), "bound_ok": bool(table[:, 13].min() > 0),
+                       "bound": "|got - ref| <= rtol * (|ref| + sum |a*b|)",
+                       "rel_fro": float(table[:, 14].max()),
+                       "fp32_spmm_within_rtol": float(table[:, 15].min())},
+            "gpu_launches": int(table[0, 16]),
+            "phases_ms": {k: float(table[slow, 3 + i]) for i, k in
+                          enumerate(("tile_coo_A", "tile_dense_B", "join_and_group", "tile_gemm"))},
+            "clocks": clk.summary([w_main, w_e2e]),
             "gen_s": round(gen_s, 1),
         }
-        if world == 1:
+        if world > 1:
+            line["ranks"] = {"ms_per_step": [round(float(x), 3) for x in table[:, 0]],
+                             "tile_gemm_ms": [round(float(x), 3) for x in table[:, 6]],
+                             "pairs": [int(x) for x in table[:, 7]],
+                             "slowest": slow,
+                             "imbalance": round(float(table[:, 0].max() / table[:, 0].mean()), 3),
+                             "limiting": "tile GEMM of the slowest rank (no collective on the data path)"}
+        if world == 1 and not args.no_hbm:
             line["hbm_kernels"] = hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, w)
+        if cfgs:
+            line["configs"] = cfgs
         print(json.dumps(line), flush=True)
+    clk.__exit__(None, None, None)
     if world > 1:
+        barrier()
         dist.destroy_process_group()
 
+
+# ------------------------------------------------------------------ other configs
+
+def _timed_steps(step, steps, warmup, clk, barrier):
+    import torch
+    out = None
+    for _ in range(warmup):
+        out = step()
+    torch.cuda.synchronize()
+    del out
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    win = clk.window_start()
+    s.record()
+    for _ in range(steps):
+        out = step()
+    e.record()
+    torch.cuda.synchronize()
+    clk.window_end()
+    barrier()
+    return s.elapsed_time(e) / steps, out, win
+
+
+def _roof(achieved, dtype_s, bf16, src):
+    r = {"bound": "tensor", "achieved": round(achieved, 3), "unit": "TFLOP/s", "peak": bf16,
+         "frac": round(achieved / bf16, 4), "peak_source": f"{src} bf16 dense (MEASURED_PEAKS.json)"}
+    if dtype_s == "f32":
+        r["fp32_peak"] = round(bf16 / 6, 1)
+        r["frac_fp32_peak"] = round(achieved / (bf16 / 6), 4)
+    return r
+
+
+def measure_configs(args, dev, rank, world, clk, barrier):
+    """C1, C3, C4 and C5 (N=1) or sharded C5 (N>1); entries of ``configs``."""
+    out = {}
+    steps = max(3, min(args.steps, 10))
+    warm = max(3, min(args.warmup, 3))
+    names = ["C1", "C3", "C4", "C5"] if world == 1 else ["C5"]
+    if args.configs:
+        names = [n for n in names if n in args.configs.split(",")]
+    for name in names:
+        fn = {"C1": measure_c1, "C3": measure_c3, "C4": measure_c4, "C5": measure_c5}[name]
+        try:
+            out[name] = fn(args, dev, rank, world, clk, barrier, steps, warm)
+        except Exception as ex:  # a failed config must not hide the headline
+            if world > 1:
+                raise
+            out[name] = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+        import torch
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_c1(args, dev, rank, world, clk, barrier, steps, warm):
+    import torch
+
+    import einjax_b200 as E
+    from einjax_b200 import sparse_dispatch as SD
+    from einjax_b200 import workloads as W
+    w = W.c1_block_sparse(seed=args.seed)
+    lhs = E.SparseTensorRelation.from_arrays(w.lhs.coords, w.lhs.values, w.lhs.shape, w.lhs.tile_shape, device=dev)
+    rhs = E.SparseTensorRelation.from_arrays(w.rhs.coords, w.rhs.values, w.rhs.shape, w.rhs.tile_shape, device=dev)
+    ms, res, win = _timed_steps(lambda: E.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys),
+                                steps, warm, clk, barrier)
+    P = SD.plan_pairs(lhs, rhs, w.join_keys, w.agg_keys).num_pairs
+    flops = P * 2 * 128 ** 3
+    hbm, bf16, src = _peaks()
+    c, v = res.to_numpy()
+    ref, mag = blocksparse_ref(w.lhs.coords, w.lhs.values, w.rhs.coords, w.rhs.values, 0, c)
+    return {"workload": "C1 ij,jk->ik 4096^2 fp32, 128^2 tiles at 10% (102 tiles per operand)",
+            "ms_per_step": round(ms, 4), "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "pairs": P, "roofline": _roof(flops / (ms * 1e-3) / 1e12, "f32", bf16, src),
+            "clocks": clk.summary([win]),
+            "parity": dict(_err_stats(v, ref, mag, 1e-5), reference="float64 per-tile products, every output tile")}
+
+
+def measure_c3(args, dev, rank, world, clk, barrier, steps, warm):
+    import torch
+
+    import einjax_b200 as E
+    from einjax_b200 import sparse_dispatch as SD
+    from einjax_b200 import workloads as W
+    w = W.c3_batched_bf16(seed=args.seed)
+    kw = dict(device=dev, dtype=torch.bfloat16)
+    lhs = E.SparseTensorRelation.from_arrays(w.lhs.coords, w.lhs.values, w.lhs.shape, w.lhs.tile_shape, **kw)
+    rhs = E.SparseTensorRelation.from_arrays(w.rhs.coords, w.rhs.values, w.rhs.shape, w.rhs.tile_shape, **kw)
+    ms, res, win = _timed_steps(lambda: E.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys),
+                                steps, warm, clk, barrier)
+    P = SD.plan_pairs(lhs, rhs, w.join_keys, w.agg_keys).num_pairs
+    flops = P * 2 * 64 ** 3
+    hbm, bf16, src = _peaks()
+    c, v = res.to_numpy()
+    pick = _sample_rows(len(c), 512)
+    ref, mag = blocksparse_ref(w.lhs.coords, w.lhs.values, w.rhs.coords, w.rhs.values, 1, c[pick])
+    return {"workload": "C3 bij,bjk->bik b=16 8192^2 bf16, 64^2 tiles at 5% (band + random)",
+            "ms_per_step": round(ms, 4), "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "pairs": P, "roofline": _roof(flops / (ms * 1e-3) / 1e12, "bf16", bf16, src),
+            "clocks": clk.summary([win]),
+            "parity": dict(_err_stats(v[pick].reshape(ref.shape), ref, mag, 2e-2),
+                           reference=f"float64 per-tile products of the bf16 inputs, {len(pick)} random output tiles")}
+
+
+def measure_c4(args, dev, rank, world, clk, barrier, steps, warm):
+    import torch
+
+    import einjax_b200 as E
+    from einjax_b200 import sparse_dispatch as SD
+    from einjax_b200 import workloads as W
+    w = W.c4_chain(seed=args.seed)
+    plan = E.plan_from_path("ij,jk,kl->il", [(0, 1), (0, 1)])  # (A B) C
+    ops = [E.SparseTensorRelation.from_arrays(w[k].coords, w[k].values, w[k].shape, w[k].tile_shape, device=dev,
+                                              dtype=torch.float32) for k in ("A", "B", "C")]
+
+    def step():
+        rels = [E.SparseTensorRelation(o.coords, o.values.detach().requires_grad_(True), o.shape, o.tile_shape)
+                for o in ops]
+        D = E.execute_sparse_plan(plan, rels, differentiable=True)
+        D.values.sum().backward()
+        return D
+    ms, res, win = _timed_steps(step, steps, warm, clk, barrier)
+    AB = E.execute_sparse(ops[0], ops[1], [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    P1 = SD.plan_pairs(ops[0], ops[1], [(1, 0)], [(0, 0), (1, 1)]).num_pairs
+    P2 = SD.plan_pairs(AB, ops[2], [(1, 0)], [(0, 0), (1, 1)]).num_pairs
+    flops = 3 * (P1 + P2) * 2 * 128 ** 3  # forward + two backward products per pair
+    hbm, bf16, src = _peaks()
+    # forward parity: (A B) C in float64 from the host tiles, sampled output tiles
+    abc = AB.coords.cpu().numpy()
+    ab_ref, ab_mag = blocksparse_ref(w["A"].coords, w["A"].values, w["B"].coords, w["B"].values, 0, abc)
+    c, v = res.coords.cpu().numpy(), res.values.detach().float().cpu().numpy()
+    pick = _sample_rows(len(c), 256)
+    ref, _ = blocksparse_ref(abc, ab_ref, w["C"].coords, w["C"].values, 0, c[pick])
+    mag, _ = blocksparse_ref(abc, ab_mag, w["C"].coords, np.abs(w["C"].values), 0, c[pick])
+    return {"workload": "C4 ij,jk,kl->il (A B) C: 3 x 16384^2 fp32, 128^2 tiles at 2%/5%/2%, forward + "
+                        "gradients of A, B, C (loss = sum of the output)",
+            "ms_per_step": round(ms, 4), "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "pairs": P1 + P2, "roofline": _roof(flops / (ms * 1e-3) / 1e12, "f32", bf16, src),
+            "clocks": clk.summary([win]),
+            "parity": dict(_err_stats(v[pick], ref, mag, 1e-5),
+                           reference=f"float64 (A B) C from the host tiles, {len(pick)} random output tiles "
+                                     "(forward; gradients are checked by the GPU tests)")}
+
+
+def c5_sample_ref(idx, val, W, want_ij, tile=16):
+    """float64 C5 output tiles ``Out[i, j, :] = sum_k X[i, j, k] W[k, :]`` for
+    the (i_tile, j_tile) positions ``want_ij`` (rows of 2), from the element
+    COO; shape (len(want_ij), 16, 16, n_out) and the |X||W| magnitudes."""
+    key = (idx[:, 0].astype(np.int64) // tile) * 1_000_000 + idx[:, 1] // tile
+    wk = want_ij[:, 0].astype(np.int64) * 1_000_000 + want_ij[:, 1]
+    order = np.argsort(wk)
+    pos = np.searchsorted(wk[order], key)
+    pos = np.minimum(pos, len(wk) - 1)
+    hit = wk[order][pos] == key
+    q = order[pos[hit]]
+    i, j, k = idx[hit, 0] % tile, idx[hit, 1] % tile, idx[hit, 2]
+    x = val[hit].astype(np.float64)
+    Wd = W.astype(np.float64)
+    ref = np.zeros((len(want_ij), tile, tile, W.shape[1]))
+    mag = np.zeros_like(ref)
+    np.add.at(ref, (q, i, j), x[:, None] * Wd[k])
+    np.add.at(mag, (q, i, j), np.abs(x)[:, None] * np.abs(Wd[k]))
+    return ref, mag
+
+
+def measure_c5(args, dev, rank, world, clk, barrier, steps, warm):
+    """C5 ``ijk,kl->ijl`` at full size (X drawn on the GPU). N=1: one GPU.
+    N>1: X's contracted k tile range split over the ranks (balanced by X tile
+    count), each rank tiles and contracts its k slice, and the partial output
+    tiles are summed by one NCCL reduce-scatter over the union of output
+    coordinates (``execute_sharded_sparse(shard="contracted")``)."""
+    import torch
+    import torch.distributed as dist
+
+    import einjax_b200 as E
+    from einjax_b200 import distributed as D
+    from einjax_b200 import sparse_dispatch as SD
+    from einjax_b200 import workloads as W
+    t0 = time.time()
+    w = W.c5_order3_device(seed=args.seed, scale=args.c5_scale, device=dev)
+    gen_s = time.time() - t0
+    shape, lt, rt = w.lhs.shape, w.lhs_tile, w.rhs_tile
+    idx, val, Wd = w.lhs.indices, w.lhs.values, w.rhs
+    if world > 1:
+        # k tile range of this rank, balanced by non-empty X tiles per k tile
+        g = [s // t for s, t in zip(shape, lt)]
+        tk = (idx[:, 0].long() // lt[0] * g[1] + idx[:, 1].long() // lt[1]) * g[2] + idx[:, 2].long() // lt[2]
+        kt = torch.unique(tk) % g[2]
+        counts = torch.bincount(kt, minlength=g[2]).cpu().numpy()
+        k0, k1 = D.balanced_key_ranges(counts, world)[rank]
+        sel = (idx[:, 2] >= k0 * lt[2]) & (idx[:, 2] < k1 * lt[2])
+        li, lv = idx[sel].contiguous(), val[sel].contiguous()
+        del tk, kt, sel
+    else:
+        li, lv = idx, val
+    marks = []
+
+    def step():
+        X = E.tile_coo(li, lv, shape, lt)
+        Wt = E.tile_dense(Wd, rt)
+        if world > 1:
+            del marks[:]
+            return E.execute_sharded_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys, shard="contracted",
+                                            lhs_sharded=True, gather=False, timings=marks)
+        return E.execute_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys)
+    ms, res, win = _timed_steps(step, steps, warm, clk, barrier)
+    coll_ms = dict(marks)["collective0"].elapsed_time(dict(marks)["collective1"]) if marks else 0.0
+    X = E.tile_coo(li, lv, shape, lt)
+    Wt = E.tile_dense(Wd, rt)
+    plan = SD.plan_pairs(X, Wt, w.join_keys, w.agg_keys)
+    P, T_X = plan.num_pairs, X.num_tuples
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    SD.tile_einsum(w.kernel_string, X.values, Wt.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
+                   seg_strip=plan.seg_strip, pair_key=plan.seg_key, key_extent=plan.key_extent)
+    e.record()
+    torch.cuda.synchronize()
+    gemm_ms = s.elapsed_time(e)
+    del X, Wt, plan
+    # parity: random (i, j) tile positions of this rank's result, every l
+    c, v = res.coords.cpu().numpy(), res.values.float().cpu().numpy()
+    ij = np.unique(c[:, :2], axis=0)
+    want = ij[_sample_rows(len(ij), 96, seed=rank)]
+    ref, mag = c5_sample_ref(idx.cpu().numpy(), val.cpu().numpy(), Wd.cpu().numpy(), want)
+    # the output tiles of the sampled positions this rank holds (a rank's
+    # union chunk may start or end inside the l tiles of one (i, j))
+    rowmap = {tuple(x): r for r, x in enumerate(c)}
+    got_t, ref_t, mag_t = [], [], []
+    for q, (a, b) in enumerate(want):
+        for lt_ in range(ref.shape[-1] // rt[1]):
+            r = rowmap.get((a, b, lt_))
+            if r is not None:
+                sl = slice(lt_ * rt[1], (lt_ + 1) * rt[1])
+                got_t.append(v[r])
+                ref_t.append(ref[q, :, :, sl])
+                mag_t.append(mag[q, :, :, sl])
+    st = _err_stats(np.stack(got_t), np.stack(ref_t), np.stack(mag_t), 1e-5)
+    flops = P * 2 * 16 ** 4
+    u_rows = int(res.coords.shape[0])
+    vec = torch.tensor([ms, float(P), float(T_X), gemm_ms, coll_ms, st["max_rel"], st["within_rtol"],
+                        1.0 if st["bound_ok"] else 0.0, float(u_rows)], dtype=torch.float64, device=dev)
+    if world > 1:
+        allr = [torch.zeros_like(vec) for _ in range(world)]
+        dist.all_gather(allr, vec)
+        tab = torch.stack(allr).cpu().numpy()
+    else:
+        tab = vec.cpu().numpy()[None, :]
+    hbm, bf16, src = _peaks()
+    ms_step = float(tab[:, 0].max())
+    P_all = float(tab[:, 1].sum())
+    flops_all = P_all * 2 * 16 ** 4
+    tile_bytes = 16 * 16 * 16 * 4
+    entry = {"workload": f"C5 ijk,kl->ijl: X {shape} COO {int(val.numel())} nnz Zipf(1.2) per mode (drawn on the "
+                         f"GPU), W {tuple(Wd.shape)} dense, tiles 16" +
+                         (f" (scale 1/{args.c5_scale})" if args.c5_scale != 1 else ""),
+             "ms_per_step": round(ms_step, 3), "value": round(flops_all / (ms_step * 1e-3) / 1e12, 3),
+             "unit": "TFLOP/s", "pairs": int(P_all), "tiles_X": int(tab[:, 2].sum()),
+             "gen_s": round(gen_s, 1),
+             "roofline": dict(_roof(P * 2 * 16 ** 4 / (gemm_ms * 1e-3) / 1e12, "f32", bf16, src),
+                              kernel="einsum (fused tile GEMM + segment-sum), rank 0", kernel_ms=round(gemm_ms, 3),
+                              lhs_gbs=round(T_X * tile_bytes / (gemm_ms * 1e-3) / 1e9, 1),
+                              frac_hbm_lhs=round(T_X * tile_bytes / (gemm_ms * 1e-3) / 1e9 / hbm, 4)),
+             "clocks": clk.summary([win]),
+             "parity": {"reference": "float64 sum over X entries times W, random (i, j) output tile positions "
+                                     "(all l), full contracted range", "rtol": 1e-5,
+                        "max_rel": float(tab[:, 5].max()), "within_rtol": float(tab[:, 6].min()),
+                        "bound_ok": bool(tab[:, 7].min() > 0),
+                        "bound": "|got - ref| <= rtol * (|ref| + sum |x*w|)"}}
+    if world > 1:
+        U = int(tab[:, 8].sum())
+        per_rank_send = (world - 1) * ((U + world - 1) // world) * tile_bytes
+        entry["parallelism"] = (f"contracted k tile range split x{world} (balanced by X tiles); partial output tiles "
+                                "written by the tile GEMM in union order, summed by one NCCL reduce-scatter")
+        entry["scaling"] = "strong"
+        entry["ranks"] = {"ms_per_step": [round(float(x), 3) for x in tab[:, 0]],
+                          "tile_gemm_ms": [round(float(x), 3) for x in tab[:, 3]],
+                          "reduce_scatter_ms": [round(float(x), 3) for x in tab[:, 4]],
+                          "nvlink_bytes_sent_per_rank": int(per_rank_send),
+                          "limiting": "reduce-scatter" if tab[:, 4].max() > tab[:, 3].max() else "tile GEMM"}
+    return entry
+
+
+# ------------------------------------------------------------------ HBM-bound phases (N=1)
 
 def _marks_ms(marks):
     """Launch time of one call from its plan0/plan1/fill0/fill1 marks (the
@@ -445,6 +862,8 @@ def hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm, reps=3):
     return out
 
 
+# ------------------------------------------------------------------ CPU reference arm
+
 def cpu_baseline(args, w=None, budget_s=15.0):
     """Oracle (numpy port of the reference path) on row-slices of the C2
     workload, growing the slice until ~budget_s of CPU time."""
@@ -493,7 +912,7 @@ def run_reference(args):
     cb["value"] = v
     line = {"metric": "useful TFLOP/s (sparse einsum, C2 element-sparse SpMM)", "value": v, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 generator)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded C2 generator)",
             "config": {"workload": "C2 ij,jk->ik: A 65536^2 COO 4,294,967 nnz Zipf(1.1) rows, B dense 65536x256, "
                                    "tile 32", "sample": cb["sample"]},
             "impl": "reference", "cpu_baseline": cb,
@@ -553,111 +972,34 @@ def run_stats(args):
 
 
 def run_config(args):
-    """The other BASELINE configurations on one GPU, for the results table
-    (the headline line is C2, ``run_ours``). One step = the sparse path on
-    device-resident inputs: C1/C3 ``execute_sparse`` of two tile relations;
-    C4 the plan (A B) C through ``execute_sparse_plan`` (intermediate kept
-    on the GPU), forward and the gradients of all three operands (loss = sum
-    of the output); C5 COO -> tiles of X
-    and W, then ``execute_sparse``."""
+    """One other BASELINE configuration on its own line (``--workload C1`` ...);
+    the same measurement as the headline line's ``configs`` entries."""
     import torch
-
-    import einjax_b200 as E
-    from einjax_b200 import workloads as W
-
-    dev = torch.device("cuda", 0)
+    import torch.distributed as dist
+    rank, world, local = _env_rank()
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    wl = args.workload
-    t0 = time.time()
-    if wl == "C4":
-        w = W.c4_chain(seed=args.seed, scale=args.scale)
-        c4_plan = E.plan_from_path("ij,jk,kl->il", [(0, 1), (0, 1)])  # (A B) C
-        t = w["tile"]
-        ops = [E.SparseTensorRelation.from_arrays(w[k].coords, w[k].values, w[k].shape, w[k].tile_shape,
-                                                  device=dev, dtype=torch.float32) for k in ("A", "B", "C")]
-        desc = (f"C4 ij,jk,kl->il (A B) C: 3 x {ops[0].shape[0]}^2 fp32, {t[0]}^2 tiles at 2%/5%/2% "
-                f"({', '.join(str(o.num_tuples) for o in ops)} tiles), forward + gradients of A, B, C")
-        dtype_s = "f32"
-    elif wl in ("C1", "C3"):
-        w = W.c1_block_sparse(seed=args.seed, scale=args.scale) if wl == "C1" else \
-            W.c3_batched_bf16(seed=args.seed, scale=args.scale)
-        tdt = torch.float32 if wl == "C1" else torch.bfloat16
-        lhs = E.SparseTensorRelation.from_arrays(w.lhs.coords, w.lhs.values, w.lhs.shape, w.lhs.tile_shape,
-                                                 device=dev, dtype=tdt)
-        rhs = E.SparseTensorRelation.from_arrays(w.rhs.coords, w.rhs.values, w.rhs.shape, w.rhs.tile_shape,
-                                                 device=dev, dtype=tdt)
-        desc = (f"{wl} {w.kernel_string}: lhs {w.lhs.shape} {lhs.num_tuples} tiles of {w.lhs_tile}, "
-                f"rhs {w.rhs.shape} {rhs.num_tuples} tiles of {w.rhs_tile}, {'fp32' if wl == 'C1' else 'bf16'}")
-        dtype_s = "f32" if wl == "C1" else "bf16"
-    else:  # C5
-        w = W.c5_order3(seed=args.seed, scale=args.scale)
-        idx = torch.from_numpy(w.lhs.indices).to(dev)
-        val = torch.from_numpy(w.lhs.values).to(dev)
-        wd = torch.from_numpy(w.rhs).to(dev)
-        desc = (f"C5 ijk,kl->ijl: X {w.lhs.shape} COO {len(w.lhs.values)} nnz Zipf(1.2), W {tuple(w.rhs.shape)} "
-                f"dense, tiles 16")
-        dtype_s = "f32"
-    gen_s = time.time() - t0
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    def step():
-        if wl == "C4":
-            rels = [E.SparseTensorRelation(o.coords, o.values.detach().requires_grad_(True), o.shape,
-                                           o.tile_shape) for o in ops]
-            D = E.execute_sparse_plan(c4_plan, rels, differentiable=True)
-            D.values.sum().backward()
-            return D, None
-        if wl in ("C1", "C3"):
-            return E.execute_sparse(lhs, rhs, w.join_keys, w.kernel_string, w.agg_keys), None
-        X = E.tile_coo(idx, val, w.lhs.shape, w.lhs_tile)
-        Wt = E.tile_dense(wd, w.rhs_tile)
-        return E.execute_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys), X
-
-    # useful flops of one step: joined pairs x flops per tile pair
-    from einjax_b200 import sparse_dispatch as SD
-    def pairs(lr, rr, jk, ak):
-        return SD.plan_pairs(lr, rr, jk, ak).num_pairs
-    for _ in range(args.warmup):
-        out, aux = step()
-    torch.cuda.synchronize()
-    if wl == "C4":
-        AB = E.execute_sparse(ops[0], ops[1], [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
-        P1 = pairs(ops[0], ops[1], [(1, 0)], [(0, 0), (1, 1)])
-        P2 = pairs(AB, ops[2], [(1, 0)], [(0, 0), (1, 1)])
-        del AB
-        flops = 3 * (P1 + P2) * 2 * t[0] ** 3  # forward + two backward products per pair
-        P = P1 + P2
-    elif wl in ("C1", "C3"):
-        P = pairs(lhs, rhs, w.join_keys, w.agg_keys)
-        te = int(np.prod(w.lhs_tile)) * w.rhs_tile[-1]
-        flops = P * 2 * te
-    else:
-        P = pairs(aux, E.tile_dense(wd, w.rhs_tile), w.join_keys, w.agg_keys)
-        flops = P * 2 * 16 ** 4
-    del out, aux
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    s.record()
-    for _ in range(args.steps):
-        out, aux = step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / args.steps
-    hbm, bf16, src = _peaks()
-    achieved = flops / (ms * 1e-3) / 1e12
-    peak = bf16 if dtype_s == "bf16" else bf16 / 6
-    line = {"metric": f"useful TFLOP/s (sparse einsum, {wl})", "value": round(achieved, 3), "unit": "TFLOP/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype_s,
-            "data": f"synthetic (seeded {wl} generator)",
-            "config": {"workload": desc + (f" (scale 1/{args.scale})" if args.scale != 1 else ""), "pairs": P,
-                       "l2": "device-resident inputs; no flush"},
-            "pairs_per_s": round(P / (ms * 1e-3), 1),
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 3),
-                         "peak": round(peak, 1), "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{src} bf16 dense" + (" / 6 (fp32 as 3 TF32 passes)" if dtype_s == "f32"
-                                                                 else "")},
-            "gen_s": round(gen_s, 1)}
-    print(json.dumps(line), flush=True)
+    def barrier():
+        if world > 1:
+            dist.barrier()
+    fn = {"C1": measure_c1, "C3": measure_c3, "C4": measure_c4, "C5": measure_c5}[args.workload]
+    with ClockSampler(local) as clk:
+        entry = fn(args, dev, rank, world, clk, barrier, args.steps, max(args.warmup, 3))
+    if rank == 0:
+        line = {"metric": f"useful TFLOP/s (sparse einsum, {args.workload})", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": entry.pop("scaling", "strong"),
+                "vs_baseline": None, "dtype": "bf16" if args.workload == "C3" else "f32",
+                "data": f"synthetic (seeded {args.workload} generator)"}
+        line.update(entry)
+        line["config"] = {"workload": entry["workload"], "l2": "device-resident inputs; no flush"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -667,11 +1009,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scale", type=int, default=1, help="shrink C2 by this factor (testing only)")
+    ap.add_argument("--c5-scale", type=int, default=1, help="shrink C5 by this factor (testing only)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--precision", default="auto", choices=["auto", "exact", "tc"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-hbm", action="store_true", help="skip the HBM-bound phase breakdown")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other configurations")
+    ap.add_argument("--configs", default="", help="comma-separated subset of C1,C3,C4,C5 for the configs entry")
     ap.add_argument("--workload", default="C2", choices=["C1", "C2", "C3", "C4", "C5", "STATS"],
-                    help="C2 is the headline line; the others measure one GPU for the results table")
+                    help="C2 is the headline line (with the others under 'configs'); the others alone")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -74,6 +74,7 @@ SIGNATURES = {
                                   c_vp]),
     "es_segsum_plan": (c_int, [c_vp, c_i64, c_int, c_i64p, c_vp, c_sz, c_vp, c_vp, c_vp]),
     "es_segsum_fill": (c_int, [c_vp, c_int, c_i64, c_i64, c_int, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_int, c_vp]),
+    "es_segsum_groups": (c_int, [c_i64, c_int, c_i64p, c_vp, c_sz, c_i64, c_vp, c_vp, c_vp]),
     "es_scatter_add_workspace_size": (c_sz, [c_i64]),
     "es_scatter_add_rows": (c_int, [c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_sz, c_vp, c_vp, c_vp]),
 }
@@ -126,6 +127,18 @@ def i64arr(vals):
 def i32arr(vals):
     vals = [int(v) for v in vals]
     return (ctypes.c_int32 * max(1, len(vals)))(*vals)
+
+
+def device_error(fn: str, err: int, msg: str):
+    """Raise for a non-zero device-side error slot (read with the counts): a
+    bounded device wait that ran out (ES_ERR_TIMEOUT, outputs invalid) raises
+    EinsparseError; anything else is a bad input and raises ValueError(msg)."""
+    e = int(err) & 0xFFFFFFFF
+    if e == ES_OK:
+        return
+    if e == ES_ERR_TIMEOUT:
+        raise EinsparseError(fn, e, lib().es_status_string(e).decode())
+    raise ValueError(msg)
 
 
 def check(fn: str, status: int):

@@ -53,8 +53,7 @@ def _group_by(index: torch.Tensor, n_rows: int):
         rows.data_ptr(), 1, rows.data_ptr(), 1, idx.data_ptr(), zero.data_ptr(), P, L.i32arr([0, 0]),
         1, ext, ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt[1:].data_ptr(), st))
     G, err = read_counts(cnt)
-    if err:
-        raise ValueError("pair index outside its relation")
+    L.device_error("es_segments_plan", err, "pair index outside its relation")
     oc = torch.empty((G, 1), dtype=torch.int32, device=dev)
     so = torch.empty(G + 1, dtype=torch.int64, device=dev)
     sp = torch.empty(P, dtype=torch.int32, device=dev)

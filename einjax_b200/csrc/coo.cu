@@ -210,7 +210,7 @@ extern "C" int es_coo_coalesce(const int32_t* indices, const void* values, int v
             w.perm, error_dev);
   uint64_t* k = w.keys;
   uint32_t* p = w.perm;
-  ES_TRY(radix_sort_pairs<uint64_t>(&k, &p, w.rb, nnz, 0, bit_length(sentinel), st));
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &p, w.rb, nnz, 0, bit_length(sentinel), st, error_dev));
   // non-zero when the sorted data sits in the radix sort's alternate buffers
   if (cudaMemsetAsync(w.alt, k != w.keys ? 1 : 0, sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
   ES_LAUNCH(coalesce_flags_kernel, grid_for(nnz, 256), 256, 0, st, w.alt, w.keys, w.rb.keys_alt, nnz, sentinel,

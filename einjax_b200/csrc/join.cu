@@ -196,7 +196,7 @@ extern "C" int es_join_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_nd
   ES_LAUNCH(join_lhs_keys_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, jk, w.keys, w.idx, error_dev);
   uint64_t* k = w.keys;
   uint32_t* v = w.idx;
-  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n_lhs, 0, bits, st));
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n_lhs, 0, bits, st, error_dev));
   ES_LAUNCH(join_flag_kernel, 1, 32, 0, st, w.hdr, k != w.keys ? 1 : 0);
   ES_LAUNCH(join_count_kernel, grid_for(n_rhs, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, n_lhs, rhs_coords,
             n_rhs, jk, w.counts, w.lo, error_dev);
@@ -264,23 +264,59 @@ constexpr int64_t kStaticMaxTiles = 65536;
 constexpr size_t kStaticScratchBytes = 3u << 20;
 static __device__ __align__(256) unsigned char g_join_scratch[kStaticScratchBytes];
 
+// Identity of the current device's primary context. A context that is torn
+// down and made again (cudaDeviceReset, then any runtime call) gets a new
+// identity, so an address looked up in the old one is never reused. The
+// driver's cuCtxGetCurrent / cuCtxGetId come through the runtime's entry-point
+// query (no link against the driver library); 0 when they are unavailable.
+unsigned long long current_context_id() {
+  typedef int (*GetCurrentFn)(void**);
+  typedef int (*GetIdFn)(void*, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetIdFn>(f);
+  });
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+  return 0;
+}
+
+// Device address of g_join_scratch in the current device's context, looked up
+// with cudaGetSymbolAddress once per (device, context) and kept. Without a
+// context identity (no context current yet, or the driver query missing) the
+// address is looked up on every call.
 void* static_scratch_ptr(int* status) {
   constexpr int kMaxDevices = 64;
   static void* ptrs[kMaxDevices] = {nullptr};
+  static unsigned long long ctx_ids[kMaxDevices] = {0};
   static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
     *status = ES_ERR_CUDA;
     return nullptr;
   }
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || ctx == 0 || ctx_ids[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_join_scratch) != cudaSuccess || !p) {
+      ptrs[dev] = nullptr;
       *status = ES_ERR_CUDA;
       return nullptr;
     }
     ptrs[dev] = p;
+    ctx_ids[dev] = ctx;
   }
   *status = ES_OK;
   return ptrs[dev];
@@ -369,7 +405,7 @@ extern "C" int es_join_static(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   ES_LAUNCH(join_lhs_keys_kernel, grid_for(n_lhs, 256), 256, 0, st, lhs_coords, n_lhs, jk, w.keys, w.idx, error_dev);
   uint64_t* k = w.keys;
   uint32_t* v = w.idx;
-  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n_lhs, 0, bit_length(prod - 1), st));
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n_lhs, 0, bit_length(prod - 1), st, error_dev));
   ES_LAUNCH(join_flag_kernel, 1, 32, 0, st, w.hdr, k != w.keys ? 1 : 0);
   ES_LAUNCH(join_count_kernel, grid_for(n_rhs, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, n_lhs, rhs_coords,
             n_rhs, jk, w.counts, w.lo, error_dev);

@@ -336,11 +336,12 @@ static int make_agg(const int32_t* agg_keys, int out_nd, int lhs_nd, int rhs_nd,
 }
 
 // Sort keys already in w.keys/w.perm, mark heads, scan them. *count_dev gets
-// the number of groups (low 32 bits of an int64 zeroed first).
-static int sort_and_group(SegWs& w, int64_t n, int bits, int64_t* count_dev, cudaStream_t st) {
+// the number of groups (low 32 bits of an int64 zeroed first); a sort whose
+// bounded wait ran out records ES_ERR_TIMEOUT in *err.
+static int sort_and_group(SegWs& w, int64_t n, int bits, int64_t* count_dev, int32_t* err, cudaStream_t st) {
   uint64_t* k = w.keys;
   uint32_t* v = w.perm;
-  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n, 0, bits, st));
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, n, 0, bits, st, err));
   ES_LAUNCH(seg_flag_kernel, 1, 32, 0, st, w.hdr, k != w.keys ? 1 : 0);
   ES_LAUNCH(heads_kernel, grid_for(n, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, n, w.flags);
   if (count_dev && cudaMemsetAsync(count_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
@@ -378,7 +379,7 @@ extern "C" int es_segments_plan(const int32_t* lhs_coords, int lhs_ndim, const i
   if (c.overflow) return ES_ERR_WORKSPACE;
   ES_LAUNCH(pair_out_keys_kernel, grid_for(num_pairs, 256), 256, 0, st, lhs_coords, rhs_coords, lhs_idx, rhs_idx,
             num_pairs, ak, w.keys, w.perm, error_dev);
-  return sort_and_group(w, num_pairs, bits, num_segments_dev, st);
+  return sort_and_group(w, num_pairs, bits, num_segments_dev, error_dev, st);
 }
 
 extern "C" int es_segments_fill(const int32_t* lhs_idx, const int32_t* rhs_idx, int64_t num_pairs, int out_ndim,
@@ -453,7 +454,7 @@ extern "C" int es_segsum_plan(const int32_t* coords, int64_t num_rows, int nd, c
   seg_layout(c, w, num_rows);
   if (c.overflow) return ES_ERR_WORKSPACE;
   ES_LAUNCH(row_keys_kernel, grid_for(num_rows, 256), 256, 0, st, coords, num_rows, nd, ak, w.keys, w.perm, error_dev);
-  return sort_and_group(w, num_rows, bits, num_segments_dev, st);
+  return sort_and_group(w, num_rows, bits, num_segments_dev, error_dev, st);
 }
 
 extern "C" int es_segsum_fill(const void* values, int values_dtype, int64_t num_rows, int64_t tile_elems, int nd,
@@ -480,6 +481,38 @@ extern "C" int es_segsum_fill(const void* values, int values_dtype, int64_t num_
   return ES_OK;
 }
 
+// Group index of every input row: its sorted position s lies in group
+// excl[s] + flags[s] - 1 (flags mark group heads, excl is their exclusive scan).
+__global__ void row_group_kernel(const SegHeader* hdr, const uint32_t* p0, const uint32_t* p1, int64_t n,
+                                 const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
+                                 int32_t* __restrict__ row_group) {
+  const uint32_t* perm = hdr->sorted_in_alt ? p1 : p0;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n; s += (int64_t)gridDim.x * blockDim.x)
+    row_group[perm[s]] = static_cast<int32_t>(excl[s] + flags[s]) - 1;
+}
+
+extern "C" int es_segsum_groups(int64_t num_rows, int nd, const int64_t* extents, void* workspace,
+                                size_t workspace_bytes, int64_t num_segments, int32_t* out_coords, int32_t* row_group,
+                                void* stream) {
+  cudaStream_t st = as_stream(stream);
+  if (num_rows <= 0 || num_segments <= 0) return ES_OK;
+  if (num_segments > INT32_MAX) return ES_ERR_UNSUPPORTED;
+  AggKeys ak;
+  int bits = 0;
+  ES_TRY(make_agg(nullptr, nd, nd, nd, extents, &ak, &bits));
+  SegWs w;
+  Carver c(workspace, workspace_bytes);
+  seg_layout(c, w, num_rows);
+  if (c.overflow) return ES_ERR_WORKSPACE;
+  if (out_coords)
+    ES_LAUNCH(seg_offsets_kernel, grid_for(num_rows, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_rows,
+              w.flags, w.excl, ak, out_coords, w.seg_off, w.nseg);
+  if (row_group)
+    ES_LAUNCH(row_group_kernel, grid_for(num_rows, 256), 256, 0, st, w.hdr, w.perm, w.rb.vals_alt, num_rows, w.flags,
+              w.excl, row_group);
+  return ES_OK;
+}
+
 extern "C" size_t es_scatter_add_workspace_size(int64_t num_rows) { return es_segments_workspace_size(num_rows); }
 
 extern "C" int es_scatter_add_rows(const void* values, int values_dtype, const int32_t* idx, int64_t num_rows,
@@ -497,7 +530,7 @@ extern "C" int es_scatter_add_rows(const void* values, int values_dtype, const i
   seg_layout(c, w, num_rows);
   if (c.overflow) return ES_ERR_WORKSPACE;
   ES_LAUNCH(row_keys_kernel, grid_for(num_rows, 256), 256, 0, st, idx, num_rows, 1, ak, w.keys, w.perm, error_dev);
-  ES_TRY(sort_and_group(w, num_rows, bits, nullptr, st));
+  ES_TRY(sort_and_group(w, num_rows, bits, nullptr, error_dev, st));
   ES_LAUNCH(seg_offsets_kernel, grid_for(num_rows, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, num_rows, w.flags,
             w.excl, ak, (int32_t*)nullptr, w.seg_off, w.nseg);
   ES_TRY(launch_segment_reduce<float>(w, values, values_dtype, tile_elems, 148 * 8, 1, out, st));

@@ -383,7 +383,7 @@ extern "C" int es_sparsity_stats(const int32_t* indices, const void* values, int
     ES_LAUNCH(stats_keys_kernel, grid, 256, 0, st, indices, values, values_dtype, num_entries, p.g, b, w.keys, w.perm);
     uint64_t* k = w.keys;
     uint32_t* v = w.perm;
-    ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, num_entries, 0, bits, st));
+    ES_TRY(radix_sort_pairs<uint64_t>(&k, &v, w.rb, num_entries, 0, bits, st, error_dev));
     ES_LAUNCH(stats_distinct_kernel, grid_for(num_entries, 256), 256, 0, st, k, num_entries, total,
               num_tuples_dev + s);
   }

@@ -1806,7 +1806,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   {
     uint32_t* k = w.sort_keys;
     uint32_t* v = w.order;
-    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st));
+    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st, err));
     if (v != w.order &&
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;

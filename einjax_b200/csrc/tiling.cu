@@ -388,7 +388,7 @@ extern "C" int es_tile_coo_plan(const int32_t* indices, const void* values, int 
             w.perm, error_dev);
   uint64_t* k = w.keys;
   uint32_t* p = w.perm;
-  ES_TRY(radix_sort_pairs<uint64_t>(&k, &p, w.rb, nnz, 0, bits, st));
+  ES_TRY(radix_sort_pairs<uint64_t>(&k, &p, w.rb, nnz, 0, bits, st, error_dev));
   const int alt = (k != w.keys) ? 1 : 0;
   ES_LAUNCH(set_flag_kernel, 1, 32, 0, st, &w.hdr->sorted_in_alt, alt);
   ES_LAUNCH(tile_heads_kernel, grid_for(nnz, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz,

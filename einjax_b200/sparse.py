@@ -222,8 +222,7 @@ def coalesce_coo(indices, values, shape, duplicates="sum", out_dtype=torch.float
         ov.data_ptr(), es_dtype(ov), cnt.data_ptr(), cnt[2:].data_ptr(), stream_ptr(dev)))
     mark(marks, "coalesce1")
     u, nz, err = read_counts(cnt)
-    if err & 0xFFFFFFFF:
-        raise ValueError("COO index outside the tensor shape")
+    L.device_error("es_coo_coalesce", err, "COO index outside the tensor shape")
     return oi[:u], ov[:u], nz
 
 
@@ -267,8 +266,7 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
         cnt.data_ptr(), cnt[1:].data_ptr(), st))
     mark(marks, "plan1")
     T, err = read_counts(cnt)
-    if err:
-        raise ValueError("COO index outside the tensor shape")
+    L.device_error("es_tile_coo_plan", err, "COO index outside the tensor shape")
     coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
     out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
     mark(marks, "fill0")
@@ -389,8 +387,7 @@ def _sparsity_stats(indices, values, shape, tile_shapes, device):
         es_dtype(vals) if vals is not None else L.ES_F32, n, nd, sh, tl, S, ws.data_ptr(), ws.numel(),
         nt.data_ptr(), vc.data_ptr(), err.data_ptr(), stream_ptr(dev)))
     nt_h, vc_h, e = nt.cpu().tolist(), vc.cpu().tolist(), int(err.item())
-    if e:
-        raise ValueError("COO index outside the tensor shape")
+    L.device_error("es_sparsity_stats", e, "COO index outside the tensor shape")
     return {t: (int(nt_h[i]), tuple(int(v) for v in vc_h[i])) for i, t in enumerate(ts)}
 
 

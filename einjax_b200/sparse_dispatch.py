@@ -92,8 +92,7 @@ def _join_int32(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys)
         lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, L.i32arr(flat), len(keys), L.i64arr(ext),
         ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt[1:].data_ptr(), st))
     P, err = read_counts(cnt)
-    if err:
-        raise ValueError("tile coordinate outside the relation's tile grid")
+    L.device_error("es_join_plan", err, "tile coordinate outside the relation's tile grid")
     li = torch.empty(P, dtype=torch.int32, device=dev)
     ri = torch.empty(P, dtype=torch.int32, device=dev)
     L.check("es_join_fill", lib.es_join_fill(nl, nr, len(keys), ws.data_ptr(), ws.numel(), P, li.data_ptr(),
@@ -252,8 +251,7 @@ def segment_sum(values: torch.Tensor, output_coords: torch.Tensor, marks=None):
                                                  cnt[1:].data_ptr(), st))
     mark(marks, "plan1")
     O, err = read_counts(cnt)
-    if err:
-        raise ValueError("segment_sum: coordinate outside its extent")
+    L.device_error("es_segsum_plan", err, "segment_sum: coordinate outside its extent")
     vals = values.contiguous()
     odt = torch.bfloat16 if vals.dtype == torch.bfloat16 else torch.float32
     uc = torch.empty((O, nd), dtype=torch.int32, device=dev)
@@ -343,8 +341,7 @@ def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None):
         cnt.data_ptr(), cnt[3:].data_ptr(), st))
     mark(marks, "plan1")
     P, O, unordered, err = (int(v) for v in cnt.cpu().tolist())
-    if err:
-        raise ValueError("tile coordinate outside the tensor grid")
+    L.device_error("es_direct_plan", err, "tile coordinate outside the tensor grid")
     if unordered:
         return None
     out_nd = len(agg_keys)
@@ -401,8 +398,7 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
         lhs.coords.contiguous().data_ptr(), lhs.ndim, rhs.coords.contiguous().data_ptr(), rhs.ndim, li.data_ptr(),
         ri.data_ptr(), P, flat, out_nd, ext, ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt[1:].data_ptr(), st))
     O, err = read_counts(cnt)
-    if err:
-        raise ValueError("output tile coordinate outside the output grid")
+    L.device_error("es_segments_plan", err, "output tile coordinate outside the output grid")
     oc = torch.empty((O, out_nd), dtype=torch.int32, device=dev)
     so = torch.empty(O + 1, dtype=torch.int64, device=dev)
     sl = torch.empty(P, dtype=torch.int32, device=dev)
@@ -467,21 +463,24 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
 
 def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=None, output_tile_shape=None,
                            mesh=None, num_devices=None, *, group=None, gather=True, precision="auto",
-                           shard="output"):
+                           shard="output", lhs_sharded=False, timings=None):
     """Multi-GPU ``execute_sparse`` (``execution/sparse_dispatch.py:330-478``).
 
     One process per GPU (``torch.distributed``). With no process group, or a
     single rank, this is ``execute_sparse`` (the reference's fallback at
-    :377-393). ``shard="output"``: every rank plans the (replicated, small)
-    join and output grouping, then computes a contiguous range of output tiles
-    balanced by pair count — output tiles are independent, so no collective
-    touches the data path. ``shard="contracted"``: each rank contracts a
-    contiguous range of the (single) join key and the partial tiles are summed
-    by a sparse reduce-scatter. With ``gather`` every rank returns the full
-    relation, as the reference does.
+    :377-393). ``shard="output"``: each rank takes a contiguous range of
+    output strips (lhs tiles sharing their lhs-derived output coordinates)
+    balanced by join pairs, and joins, groups and contracts only those —
+    output tiles are independent, so no collective touches the data path.
+    ``shard="contracted"``: each rank contracts a contiguous range of the
+    (single) join key and the partial tiles are summed by a reduce-scatter
+    over the union of output coordinates. With ``gather`` every rank returns
+    the full relation, as the reference does; without it, its own share.
+    ``lhs_sharded``: ``lhs`` is already this rank's share (e.g. tiled from its
+    ``distributed.balanced_row_ranges`` rows of an element COO).
     ``mesh`` is accepted for signature compatibility; ranks come from ``group``.
     """
     from . import distributed as D
     return D.execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape, output_tile_shape,
                                     num_devices=num_devices, group=group, gather=gather, precision=precision,
-                                    shard=shard)
+                                    shard=shard, lhs_sharded=lhs_sharded, timings=timings)

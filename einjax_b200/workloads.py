@@ -225,6 +225,50 @@ def c5_order3(seed: int = 0, scale: int = 1, n_out: int = 128) -> Workload:
                     "ijk,kl->ijl", [(0, 0), (0, 1), (1, 1)], (16, 16, 16), (16, 16))
 
 
+def c5_order3_device(seed: int = 0, scale: int = 1, n_out: int = 128, device=None) -> Workload:
+    """C5 drawn on the GPU: the same distributions as ``c5_order3`` (each index
+    bounded-Zipf(s=1.2) by inverse-CDF sampling, the first ``target`` distinct
+    coordinates in draw order, N(0,1) values, dense N(0,1) W), with torch's
+    seeded CUDA generator instead of numpy's, so the 50M-entry tensor takes
+    seconds instead of many minutes. The arrays stay on ``device``
+    (``lhs.indices`` int32 (nnz, 3), ``lhs.values`` float32, ``rhs`` float32);
+    the same seed on the same GPU model and torch build gives the same draw,
+    and checkers read the arrays back instead of redrawing them."""
+    import torch
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(int(seed))
+    n = 4096 // scale
+    target = int(round(50_000_000 / scale ** 3))
+    cdf = torch.from_numpy(_bounded_zipf_cdf(n, 1.2)).to(dev)
+    keys = torch.zeros(0, dtype=torch.int64, device=dev)
+    for _ in range(256):
+        need = target - int(keys.numel())
+        if need <= 0:
+            break
+        k = max(4 * need, 1 << 22)
+        parts = []
+        for _ in range(3):
+            r = torch.searchsorted(cdf, torch.rand(k, generator=g, device=dev, dtype=torch.float64), right=True)
+            parts.append(r.clamp_(max=n - 1))
+        batch = (parts[0] * n + parts[1]) * n + parts[2]
+        allk = torch.cat([keys, batch])
+        uk, inv = torch.unique(allk, return_inverse=True)
+        first = torch.full((uk.numel(),), allk.numel(), dtype=torch.int64, device=dev)
+        first.scatter_reduce_(0, inv, torch.arange(allk.numel(), device=dev), reduce="amin")
+        keys = allk[torch.sort(first).values]
+        del allk, uk, inv, first, batch, parts
+    if keys.numel() < target:
+        raise RuntimeError("could not draw enough distinct coordinates")
+    keys = keys[:target]
+    idx = torch.stack([keys // (n * n), (keys // n) % n, keys % n], dim=1).to(torch.int32)
+    del keys
+    vals = torch.randn(target, generator=g, device=dev, dtype=torch.float32)
+    w = torch.randn((n, n_out), generator=g, device=dev, dtype=torch.float32)
+    return Workload("C5", ElementCOO(idx, vals, (n, n, n)), w, [(2, 0)],
+                    "ijk,kl->ijl", [(0, 0), (0, 1), (1, 1)], (16, 16, 16), (16, 16))
+
+
 def round_to_bf16(x: np.ndarray) -> np.ndarray:
     """Round float32 values to the nearest bf16 (ties to even), kept as float32."""
     u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)

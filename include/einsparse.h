@@ -295,6 +295,17 @@ int es_segsum_fill(const void* values, int values_dtype, int64_t num_rows, int64
                    const int64_t* extents, void* workspace, size_t workspace_bytes, int64_t num_segments,
                    int32_t* out_coords, void* out_values, int out_dtype, void* stream);
 
+/* Groups of an es_segsum_plan without a reduction: unique coordinates
+ * (O, nd) sorted lexicographically into out_coords (may be NULL) and, for
+ * each input row r, its group index into row_group[r] (int32, may be NULL).
+ * This is the grouping half of segment_sum (execution/sparse_dispatch.py:
+ * 154-161: the unique output keys and which key each row belongs to); the
+ * sharded path uses it to lay every rank's partial output tiles out in the
+ * order of the union of all ranks' output coordinates before the
+ * reduce-scatter. Same workspace as the plan, which must have run first. */
+int es_segsum_groups(int64_t num_rows, int nd, const int64_t* extents, void* workspace, size_t workspace_bytes,
+                     int64_t num_segments, int32_t* out_coords, int32_t* row_group, void* stream);
+
 /* out[idx[r]] += values[r] for r in row order, rows of tile_elems
  * (autodiff/custom_vjp.py:272-273). out must be F32. Deterministic: rows
  * are grouped by a stable sort, each group is summed in row order, then

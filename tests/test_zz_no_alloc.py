@@ -39,16 +39,17 @@ def _regular_join(lc, rc, keys, ext):
     return li.cpu().numpy(), ri.cpu().numpy()
 
 
-def _static_join(lc, rc, keys, ext, capacity):
+def _static_join(lc, rc, keys, ext, capacity, index_dtype=torch.int64):
     lib = L.lib()
     dev = lc.device
-    li = torch.full((capacity,), -1, dtype=torch.int64, device=dev)
-    ri = torch.full((capacity,), -1, dtype=torch.int64, device=dev)
+    li = torch.full((capacity,), -1, dtype=index_dtype, device=dev)
+    ri = torch.full((capacity,), -1, dtype=index_dtype, device=dev)
     cnt = torch.zeros(2, dtype=torch.int64, device=dev)
     flat = [v for k in keys for v in k]
+    code = L.ES_I64 if index_dtype == torch.int64 else L.ES_I32
     L.check("es_join_static", lib.es_join_static(
         lc.data_ptr(), lc.shape[0], lc.shape[1], rc.data_ptr(), rc.shape[0], rc.shape[1], L.i32arr(flat), len(keys),
-        L.i64arr(ext), li.data_ptr(), ri.data_ptr(), L.ES_I64, capacity, cnt.data_ptr(), cnt[1:].data_ptr(),
+        L.i64arr(ext), li.data_ptr(), ri.data_ptr(), code, capacity, cnt.data_ptr(), cnt[1:].data_ptr(),
         stream_ptr(dev)))
     P, err = read_counts(cnt)
     return P, err, li.cpu().numpy(), ri.cpu().numpy()
@@ -90,3 +91,37 @@ def test_static_join_limits():
                             out.data_ptr(), out.data_ptr(), L.ES_I64, 4, cnt.data_ptr(), cnt[1:].data_ptr(),
                             stream_ptr(big.device))
     assert st == L.ES_ERR_UNSUPPORTED
+
+
+def test_static_join_at_the_tile_limit():
+    # exactly 65536 tiles per side: the largest input the fixed array serves
+    lc, rc = _case(4, 65536, 65536, 4096)
+    keys, ext = [(1, 0)], [4096]
+    want_l, want_r = _regular_join(lc, rc, keys, ext)
+    P, err, got_l, got_r = _static_join(lc, rc, keys, ext, capacity=want_l.size)
+    assert err == 0 and P == want_l.size
+    np.testing.assert_array_equal(got_l, want_l)
+    np.testing.assert_array_equal(got_r, want_r)
+
+
+def test_static_join_int32_outputs():
+    lc, rc = _case(5, 5000, 7000, 300)
+    keys, ext = [(1, 0), (0, 1)], [300, 300]
+    want_l, want_r = _regular_join(lc, rc, keys, ext)
+    P, err, got_l, got_r = _static_join(lc, rc, keys, ext, capacity=want_l.size + 8, index_dtype=torch.int32)
+    assert err == 0 and P == want_l.size
+    np.testing.assert_array_equal(got_l[:P].astype(np.int64), want_l)
+    np.testing.assert_array_equal(got_r[:P].astype(np.int64), want_r)
+    assert np.all(got_l[P:] == -1)
+
+
+def test_static_join_capped_cross_product():
+    # no join keys: the lhs-major cross product, cut at the capacity
+    lc, rc = _case(6, 300, 200, 10)
+    want_l, want_r = _regular_join(lc, rc, [], [])
+    assert want_l.size == 300 * 200
+    cap = 1000
+    P, err, got_l, got_r = _static_join(lc, rc, [], [], capacity=cap)
+    assert err == L.ES_ERR_WORKSPACE and P == 300 * 200
+    np.testing.assert_array_equal(got_l, want_l[:cap])
+    np.testing.assert_array_equal(got_r, want_r[:cap])
