@@ -85,11 +85,15 @@ constexpr int kRecInts = 16;
 constexpr int kRecAhead = 4;  // records the scheduler has in flight ahead of use
 constexpr int kMaxSplit = 16;  // 16-byte lhs chunks per split thread and stage (lhs operand <= 32 KB)
 
-// A work item: up to S sub-strips (<= G segments of one strip each).
+// A work item: up to S sub-strips (<= G segments of one strip each). The
+// scheduler hands the epilogue one entry per accumulation it drains: a
+// whole item in one key block, or one chain of it (see TcParams::chain_recs).
 struct ItemInfo {
   int s0[kMaxSlots];    // first segment per slot
   int gcnt[kMaxSlots];  // segments per slot (0: empty slot)
-  int nsteps;           // data stages this item produced (0: nothing in this key block)
+  int nsteps;           // records left in this key block (0: nothing in this key block)
+  int blk;              // key block of the item
+  int acc;              // 1: add into the destination (a chain after the item's first)
 };
 
 struct Ctrl {
@@ -127,6 +131,14 @@ struct TcParams {
   const int32_t* order;   // item indices, largest work first
   int* queue;             // next position in `order`, zero at launch
   int accumulate;           // 1: add into the output (key blocks after the first)
+  int fused;                // 1: one launch over every (key block, item) unit; block b > 0
+                            //    writes its sums to part + (b - 1) * part_stride
+  int chain_recs;           // > 0: an item's accumulation restarts every chain_recs
+                            //    records and the epilogue adds each chain into the
+                            //    destination in fp32 (round to nearest), so the tensor
+                            //    core's accumulator never sums a long run
+  float* part;              // fused: per-block partial sums, segment-major rows
+  int64_t part_stride;      // elements of one block's partial
   const int32_t* seg_out;
   void* out;
   int odt;
@@ -570,8 +582,8 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
 // writes its columns into shared memory (stg: 4 KB for fp32 output, 2 KB for
 // bf16) and reads back 16-byte pieces of rows, which it stores (or adds)
 // into the output tile.
-__device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_t (&r)[32], int64_t tile0, int m0,
-                                                bool empty, float* stg, int lane) {
+__device__ __forceinline__ void epi_store_block(const TcParams& p, void* obase, bool accm, const uint32_t (&r)[32],
+                                                int64_t tile0, int m0, bool empty, float* stg, int lane) {
   const TcConfig& c = p.c;
   const int rows = c.Mt - m0 < 32 ? c.Mt - m0 : 32;
   if (p.odt == ES_F32) {
@@ -584,9 +596,9 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_
       if (j < rows) {
         float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
         float4* dst =
-            reinterpret_cast<float4*>(static_cast<float*>(p.out) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt) +
+            reinterpret_cast<float4*>(static_cast<float*>(obase) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt) +
             piece;
-        if (p.accumulate) {
+        if (accm) {
           const float4 o = *dst;
           x.x += o.x;
           x.y += o.y;
@@ -596,7 +608,7 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_
         *dst = x;
       }
     }
-  } else if (p.accumulate) {
+  } else if (accm) {
     // add the old values in fp32 before the one rounding: two passes of 16
     // rows through the 2 KB staging area
 #pragma unroll
@@ -608,7 +620,7 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_
       for (int it = 0; it < 2; ++it) {
         const int j = it * 8 + (lane >> 2), piece = lane & 3;
         if (pass * 16 + j < rows) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 +
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(obase) + tile0 +
                                                 static_cast<int64_t>(m0 + pass * 16 + j) * c.Nt) +
                        piece;
           const uint4 o = *dst;
@@ -636,7 +648,7 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_
     for (int it = 0; it < 4; ++it) {
       const int j = it * 8 + (lane >> 2), piece = lane & 3;
       if (j < rows)
-        reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt)
+        reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(obase) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt)
             [piece] = reinterpret_cast<const uint4*>(sb16 + j * 32)[piece];
     }
   }
@@ -648,8 +660,8 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, const uint32_
 // takes every other block. tacc: the accumulator's first column, in this
 // warp's TMEM lane quadrant. The next block's TMEM load is in flight while
 // a block is stored.
-__device__ void epi_swap_staged(const TcParams& p, const ItemInfo& info, uint32_t tacc, int quad, int lane,
-                                float* stg, bool empty, int t0, int tstep) {
+__device__ void epi_swap_staged(const TcParams& p, const ItemInfo& info, void* obase, const int32_t* oseg, bool accm,
+                                uint32_t tacc, int quad, int lane, float* stg, bool empty, int t0, int tstep) {
   const TcConfig& c = p.c;
   const int s0 = info.s0[0], gcnt = info.gcnt[0];
   const int nmb = (c.Mt + 31) / 32;
@@ -662,7 +674,7 @@ __device__ void epi_swap_staged(const TcParams& p, const ItemInfo& info, uint32_
     const int r0 = h * 128 + quad * 32;
     const int g0 = r0 / c.Nt;
     if (g0 < gcnt) {
-      const int64_t row = p.seg_out ? p.seg_out[s0 + g0] : static_cast<int64_t>(s0 + g0);
+      const int64_t row = oseg ? oseg[s0 + g0] : static_cast<int64_t>(s0 + g0);
       (h == 0 ? t0a : t0b) = row * c.Mt * c.Nt + r0 % c.Nt;
     }
   }
@@ -676,11 +688,11 @@ __device__ void epi_swap_staged(const TcParams& p, const ItemInfo& info, uint32_
   for (int t = t0; t < nblk; t += 2 * tstep) {
     const int u = t + tstep;
     if (u < nblk) tmem_ld32_async(addr(u), rb);
-    if (tile_of(t) >= 0) epi_store_block(p, ra, tile_of(t), (t % nmb) * 32, empty, stg, lane);
+    if (tile_of(t) >= 0) epi_store_block(p, obase, accm, ra, tile_of(t), (t % nmb) * 32, empty, stg, lane);
     if (u < nblk) {
       tmem_wait32(rb);
       if (u + tstep < nblk) tmem_ld32_async(addr(u + tstep), ra);
-      if (tile_of(u) >= 0) epi_store_block(p, rb, tile_of(u), (u % nmb) * 32, empty, stg, lane);
+      if (tile_of(u) >= 0) epi_store_block(p, obase, accm, rb, tile_of(u), (u % nmb) * 32, empty, stg, lane);
       if (u + tstep < nblk) tmem_wait32(ra);
     }
   }
@@ -750,6 +762,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     const int S = c.slots, G = c.G;
     const int64_t W1 = W;                      // sub-strips
     const int64_t nitems = (W1 + S - 1) / S;  // work items of S sub-strips
+    // units handed out by the queue: the items of this launch's key block, or
+    // (fused) every (key block, item) pair, block-major so that the CTAs in
+    // flight share one or two blocks' rhs panel in L2
+    const int64_t nunits = p.fused ? nitems * p.nblocks : nitems;
     uint32_t it = 0;
     int stage = 0;
     uint32_t ph = 0;
@@ -764,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     // claim held that long unbalances the largest-first queue, so the next
     // item is claimed during the current item's last kRecAhead steps and its
     // metadata and records are loaded at the item's end.
-    const bool deep = nitems >= 16 * static_cast<int64_t>(gridDim.x);
+    const bool deep = nunits >= 16 * static_cast<int64_t>(gridDim.x);
     int nq_raw = 0;  // lane 0: raw atomic result
     int nq = 0, n_ss = -1, n_s0 = 0, n_gcnt = 0, pf = 0;  // next item (A)
     int64_t n_rb = 0, n_re = 0;
@@ -772,16 +788,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     int bq = 0, b_ss = -1;  // deep: the item after next (B)
     int64_t b_rb = 0, b_re = 0;
     auto load_meta = [&](int q_, int64_t& rb_, int64_t& re_, int& ss_) {
-      if (q_ < nitems) {
-        const int64_t* ib = p.item_rec + static_cast<int64_t>(q_) * (p.nblocks + 1) + p.blk;
+      if (q_ < nunits) {
+        const int64_t qi = p.fused ? q_ % nitems : q_;
+        const int blk_ = p.fused ? static_cast<int>(q_ / nitems) : p.blk;
+        const int64_t* ib = p.item_rec + qi * (p.nblocks + 1) + blk_;
         rb_ = ib[0];
         re_ = ib[1];
-        const int64_t sub = static_cast<int64_t>(q_) * S + lane;
+        const int64_t sub = qi * S + lane;
         ss_ = (lane < S && sub < W1) ? p.order[sub] : -1;
       }
     };
     auto load_info = [&]() {
-      if (nq < nitems) {
+      if (nq < nunits) {
         n_s0 = n_ss >= 0 ? p.item_first[n_ss] : 0;
         n_gcnt = n_ss >= 0 ? p.item_count[n_ss] : 0;
 #pragma unroll
@@ -832,14 +850,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         n_re = b_re;
         n_ss = b_ss;
         bq = __shfl_sync(0xffffffffu, nq_raw, 0);
-        if (lane == 0 && bq < nitems) nq_raw = atomicAdd(p.queue, 1);
+        if (lane == 0 && bq < nunits) nq_raw = atomicAdd(p.queue, 1);
         load_meta(bq, b_rb, b_re, b_ss);
         load_info();
         pf = 3;
       } else {
         pf = 0;
       }
-      if (q >= nitems) {
+      if (q >= nunits) {
         // no more items: exit marker
         if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
           aborted = true;
@@ -852,17 +870,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         __syncwarp();
         break;
       }
-      if (p.accumulate && re == rb) {
+      const int cur_blk = p.fused ? static_cast<int>(q / nitems) : p.blk;
+      if ((p.accumulate || cur_blk > 0) && re == rb) {
         // nothing to add from this key block: the item is not handed on
         while (pf < 3) pf_advance();
         continue;
       }
-      if (lane < kMaxSlots) {
-        ItemInfo& info = ctl->item_log[item_iter % kItemLog];
-        info.s0[lane] = s0_cur;
-        info.gcnt[lane] = gcnt_cur;
-        if (lane == 0) info.nsteps = static_cast<int>(re - rb);
-      }
+      auto log_item = [&](int64_t left, int acc) {
+        if (lane < kMaxSlots) {
+          ItemInfo& info = ctl->item_log[item_iter % kItemLog];
+          info.s0[lane] = s0_cur;
+          info.gcnt[lane] = gcnt_cur;
+          if (lane == 0) {
+            info.nsteps = static_cast<int>(left);
+            info.blk = cur_blk;
+            info.acc = acc;
+          }
+        }
+        __syncwarp();
+      };
+      log_item(re - rb, 0);
+      int since = 0;  // records of the current chain
       // ahead[] is a ring indexed at compile time (the loop below is
       // unrolled by kRecAhead): record r sits in ahead[r % kRecAhead] and is
       // replaced by record r + kRecAhead as soon as it is read, so no step
@@ -902,6 +930,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
           }
           const int k0 = chunk * c.KC;
           uint8_t* sbase = smem + stage * c.stage_bytes;
+          if (!F32 && !zfill) {
+            // the copy below overwrites every panel slot of this stage
+            zmask &= ~(0xFFull << (stage * kMaxG));
+          }
           if (zfill) {
             const int sh = stage * kMaxG;
             uint32_t need = absent & ~static_cast<uint32_t>((zmask >> sh) & 0xFFull);
@@ -949,6 +981,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             stage = 0;
             ph ^= 1u;
           }
+        }
+        if (p.chain_recs > 0 && ++since == p.chain_recs && r < re && !aborted) {
+          // end of a chain: the MMA warp commits this accumulation and starts
+          // the rest of the item in a fresh accumulator; the epilogue adds
+          // each chain into the destination
+          since = 0;
+          if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
+            aborted = true;
+            break;
+          }
+          if (lane == 0) {
+            ctl->ring[stage].done = 1;
+            mbar_arrive_expect_tx(&ctl->copy[stage], 0);
+          }
+          __syncwarp();
+          ++it;
+          ++item_iter;
+          if (++stage == c.stages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+          log_item(re - r, 1);
         }
         }
       }
@@ -1024,8 +1078,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       if (*reinterpret_cast<volatile int*>(&ctl->exit_at) == static_cast<int>(item_iter)) break;
       const ItemInfo& info = ctl->item_log[item_iter % kItemLog];
       const bool empty = info.nsteps == 0;  // zeros: written by the first key block only
+      // destination: the output (rows through seg_out), or in a fused launch
+      // block b's partial sums (segment rows); chains after an item's first
+      // and key blocks after the first of sequential launches add into it
+      const bool accm = p.accumulate || info.acc;
+      void* obase = p.out;
+      const int32_t* oseg = p.seg_out;
+      if (p.fused && info.blk > 0) {
+        obase = p.part + static_cast<int64_t>(info.blk - 1) * p.part_stride;
+        oseg = nullptr;
+      }
       tc_fence_after();
-      for (int h = 0; h < c.halves && !(empty && p.accumulate); ++h) {
+      for (int h = 0; h < c.halves && !(empty && accm); ++h) {
         const uint32_t tbase =
             tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride + h * col_per_half;
         if (!c.swap) {
@@ -1047,22 +1111,22 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                 const int col = c0 + j;
                 const int g = col / c.Nt, n = col % c.Nt;
                 if (col >= c.n_mma || g >= gcnt) continue;
-                const int64_t row = p.seg_out ? p.seg_out[s0 + g] : static_cast<int64_t>(s0 + g);
+                const int64_t row = oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g);
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m) * c.Nt + n;
                 if (p.odt == ES_F32) {
-                  float4* of = reinterpret_cast<float4*>(static_cast<float*>(p.out) + o);
+                  float4* of = reinterpret_cast<float4*>(static_cast<float*>(obase) + o);
                   float4 r4 = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                  if (p.accumulate) {
+                  if (accm) {
                     const float4 old = *of;
                     r4.x += old.x; r4.y += old.y; r4.z += old.z; r4.w += old.w;
                   }
                   *of = r4;
                 } else {
-                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + o;
+                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(obase) + o;
 #pragma unroll
                   for (int q = 0; q < 4; ++q) {
                     float x = v[j + q];
-                    if (p.accumulate) x += __bfloat162float(ob[q]);
+                    if (accm) x += __bfloat162float(ob[q]);
                     ob[q] = __float2bfloat16_rn(x);
                   }
                 }
@@ -1072,14 +1136,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         } else if (c.epi_stage) {
           // all halves at once (see epi_swap_staged)
           if (h == 0)
-            epi_swap_staged(p, info, tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride, quad, lane,
-                            stg, empty, grp, dual ? 2 : 1);
+            epi_swap_staged(p, info, obase, oseg, accm, tmem + (static_cast<uint32_t>(quad * 32) << 16) + b * acc_stride,
+                            quad, lane, stg, empty, grp, dual ? 2 : 1);
         } else {
           const int s0 = info.s0[0], gcnt = info.gcnt[0];
           const int r = h * 128 + quad * 32 + lane;  // panel row = (g, n)
           const int g = r / c.Nt, n = r % c.Nt;
           const bool live = g < gcnt;
-          const int64_t row = live ? (p.seg_out ? p.seg_out[s0 + g] : static_cast<int64_t>(s0 + g)) : 0;
+          const int64_t row = live ? (oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g)) : 0;
           for (int m0 = 0; m0 < c.Mt; m0 += 32) {
             float v[32];
             tmem_ld32(tbase + m0, v);
@@ -1097,12 +1161,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m0 + j) * c.Nt + n;
                 float x = empty ? 0.f : v[j];
                 if (p.odt == ES_F32) {
-                  float* of = static_cast<float*>(p.out) + o;
-                  if (p.accumulate) x += *of;
+                  float* of = static_cast<float*>(obase) + o;
+                  if (accm) x += *of;
                   *of = x;
                 } else {
-                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + o;
-                  if (p.accumulate) x += __bfloat162float(*ob);
+                  __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(obase) + o;
+                  if (accm) x += __bfloat162float(*ob);
                   *ob = __float2bfloat16_rn(x);
                 }
               }
@@ -1509,7 +1573,58 @@ int merge_chunks(int nblocks, bool have_key, int64_t key_extent) {
   return static_cast<int>(nblocks * m);
 }
 
+// Fused key blocks: one launch takes every (key block, item) unit; blocks
+// after the first write partial sums (fp32, one row per segment) that a last
+// pass adds into the output in block order. Used when the partials fit in
+// this budget (and the output is fp32); else one launch per block.
+constexpr int64_t kMaxPartialBytes = 4ll << 30;
+
+bool fused_blocks_possible(const TcConfig& c, int nblocks, int64_t nseg) {
+  if (nblocks <= 1) return false;
+  const int64_t bytes = static_cast<int64_t>(nblocks - 1) * nseg * c.Mt * c.Nt * 4;
+  return bytes <= kMaxPartialBytes;
+}
+
+// Accumulation chains (fp32): the tensor core adds each MMA's products into
+// its fp32 accumulator with truncation, a bias that grows with the number of
+// MMAs summed into one accumulator. Restarting the accumulator every
+// kChainKsteps k-steps (K = 8 each) and adding the chains in fp32 with
+// round-to-nearest keeps a long contraction within plain fp32 accuracy.
+constexpr int kChainKsteps = 64;
+
+int chain_records(const TcConfig& c) {
+  if (!c.fp32) return 0;
+  int64_t ks = kChainKsteps;
+  // EINSPARSE_CHAIN_KSTEPS overrides the chain length (0: no chains; tuning, tests)
+  if (const char* e = std::getenv("EINSPARSE_CHAIN_KSTEPS")) ks = std::atoll(e);
+  if (ks <= 0) return 0;
+  const int per = c.Kt / 8 > 0 ? c.Kt / 8 : 1;  // k-steps per record
+  const int64_t r = ks / per;
+  return static_cast<int>(r < 1 ? 1 : r);
+}
+
+// out[row(s)] += part[0][s] + part[1][s] + ... in block order (float4 pieces).
+__global__ void add_partials_kernel(float* __restrict__ out, const float* __restrict__ part, int64_t nseg, int64_t te4,
+                                    int nparts, int64_t stride, const int32_t* __restrict__ seg_out) {
+  const int64_t nv = nseg * te4;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sg = v / te4, e = v - sg * te4;
+    const int64_t row = seg_out ? static_cast<int64_t>(seg_out[sg]) : sg;
+    float4* o = reinterpret_cast<float4*>(out) + row * te4 + e;
+    float4 a = *o;
+    for (int b = 0; b < nparts; ++b) {
+      const float4 x = __ldcs(reinterpret_cast<const float4*>(part + b * stride) + v);
+      a.x += x.x;
+      a.y += x.y;
+      a.z += x.z;
+      a.w += x.w;
+    }
+    *o = a;
+  }
+}
+
 struct TcWs {
+  float* part;
   uint8_t* pan_hi;
   uint8_t* pan_lo;
   uint8_t* zeros;
@@ -1566,6 +1681,9 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npai
   w.rb.hist = cv.template take<uint32_t>(RadixScratchSize::hist_elems(nseg));
   w.rb.scan = cv.template take<uint32_t>(RadixScratchSize::scan_elems(nseg));
   w.queue = cv.template take<int>(1);
+  w.part = fused_blocks_possible(c, nblocks, nseg)
+               ? cv.template take<float>(static_cast<int64_t>(nblocks - 1) * nseg * c.Mt * c.Nt)
+               : nullptr;
 }
 
 struct SizeOnly {
@@ -1863,6 +1981,14 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.out = out;
   prm.odt = odt;
   prm.err = err;
+  prm.chain_recs = chain_records(c);
+  prm.part = w.part;
+  prm.part_stride = nseg * c.Mt * c.Nt;
+  // EINSPARSE_NO_FUSED_BLOCKS: one launch per key block (tuning, tests)
+  prm.fused = (w.part != nullptr && odt == ES_F32 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+               !std::getenv("EINSPARSE_NO_FUSED_BLOCKS"))
+                  ? 1
+                  : 0;
   // 2-D view of the lhs values for the TMA: (k, row over all tiles); a box
   // of (KC, Mt) lands one tile's k-chunk in shared memory as Mt swizzled
   // rows of W bytes, the operand layout of the MMA.
@@ -1900,6 +2026,22 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     if (cudaFuncSetAttribute(tc_strip_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
         cudaSuccess)
       return ES_ERR_CUDA;
+  }
+  if (prm.fused) {
+    const size_t pbytes = static_cast<size_t>(nblocks - 1) * prm.part_stride * sizeof(float);
+    if (cudaMemsetAsync(w.part, 0, pbytes, st) != cudaSuccess) return ES_ERR_CUDA;
+    prm.blk = 0;
+    prm.accumulate = 0;
+    if (c.fp32)
+      ES_LAUNCH(tc_strip_kernel<true>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+    else
+      ES_LAUNCH(tc_strip_kernel<false>, (int)grid, kThreads, c.smem_bytes, st, prm, lhs_map);
+    const int64_t te4 = static_cast<int64_t>(c.Mt) * c.Nt / 4;
+    const int64_t nv = nseg * te4;
+    const int pg = static_cast<int>(nv / 256 + 1 < 148 * 8 ? nv / 256 + 1 : 148 * 8);
+    ES_LAUNCH(add_partials_kernel, pg, 256, 0, st, static_cast<float*>(out), w.part, nseg, te4, nblocks - 1,
+              prm.part_stride, seg_out);
+    return ES_OK;
   }
   for (int b = 0; b < nblocks; ++b) {
     prm.blk = b;
