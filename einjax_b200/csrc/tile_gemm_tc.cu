@@ -137,6 +137,7 @@ struct TcParams {
                             //    records and the epilogue adds each chain into the
                             //    destination in fp32 (round to nearest), so the tensor
                             //    core's accumulator never sums a long run
+  int rn_split;             // fp32: 1 = rounded hi/lo split (tf32_split), 0 = truncating
   float* part;              // fused: per-block partial sums, segment-major rows
   int64_t part_stride;      // elements of one block's partial
   const int32_t* seg_out;
@@ -370,6 +371,35 @@ __device__ __forceinline__ float tf32_rem(float x) {
   return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
+// x rounded to TF32 (cvt.rna: to nearest, ties away from zero), in an fp32
+// container the tensor core reads exactly.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Rounded split: hi = rna(x), lo = rna(x - hi) (x - hi is exact, |x - hi| <=
+// 2^-11 |x|). Both parts round to nearest, so the 3-pass product's error
+// (the dropped lo*lo term and lo's rounding, ~2^-22 |ab|) has no sign bias;
+// the truncating split (hi = x, lo = x - trunc(x)) errs toward zero.
+__device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
+  hi = tf32_rna(x);
+  lo = tf32_rna(x - hi);
+}
+
+__device__ __forceinline__ void tf32_split4(const float4& x, bool rn, float4& hi, float4& lo) {
+  if (rn) {
+    tf32_split(x.x, hi.x, lo.x);
+    tf32_split(x.y, hi.y, lo.y);
+    tf32_split(x.z, hi.z, lo.z);
+    tf32_split(x.w, hi.w, lo.w);
+  } else {
+    hi = x;
+    lo = make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
+  }
+}
+
 // Operand layout of one stage as the MMA warp sees it.
 struct MmaArgs {
   uint32_t smem0, tmem;
@@ -560,9 +590,11 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
       for (int j = 0; j < PER; ++j) {
         const int f = tid + j * kProducers;
         if (f < nf) {
-          const float4 lo = make_float4(tf32_rem(x[j].x), tf32_rem(x[j].y), tf32_rem(x[j].z), tf32_rem(x[j].w));
+          float4 hi, lo;
+          tf32_split4(x[j], p.rn_split != 0, hi, lo);
           *reinterpret_cast<float4*>(sbase + off_lhs + c.lhs_bytes + f * 16) = lo;
-          if (!on[j]) *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = x[j];  // absent slot: zero hi too
+          // the rounded hi replaces the raw chunk; absent slots become zeros
+          if (!on[j] || p.rn_split) *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
         }
       }
       fence_proxy_async();
@@ -590,6 +622,18 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, void* obase, 
 #pragma unroll
     for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = empty ? 0.f : __uint_as_float(r[j]);
     __syncwarp();
+    // old values of all 8 pieces are loaded before any store (one memory
+    // round trip per block when accumulating)
+    float4 old[8];
+    if (accm) {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int j = it * 4 + (lane >> 3), piece = lane & 7;
+        old[it] = j < rows ? reinterpret_cast<const float4*>(static_cast<float*>(obase) + tile0 +
+                                                             static_cast<int64_t>(m0 + j) * c.Nt)[piece]
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int j = it * 4 + (lane >> 3), piece = lane & 7;
@@ -599,11 +643,10 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, void* obase, 
             reinterpret_cast<float4*>(static_cast<float*>(obase) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt) +
             piece;
         if (accm) {
-          const float4 o = *dst;
-          x.x += o.x;
-          x.y += o.y;
-          x.z += o.z;
-          x.w += o.w;
+          x.x += old[it].x;
+          x.y += old[it].y;
+          x.z += old[it].z;
+          x.w += old[it].w;
         }
         *dst = x;
       }
@@ -1105,7 +1148,40 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            if (gcnt > 0) {
+            if (gcnt > 0 && p.odt == ES_F32) {
+              // the 8 pieces' old values are all loaded before any store, so
+              // an accumulating epilogue waits one memory round trip per 32
+              // columns instead of one per piece
+              float4* dst[8];
+              float4 old[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const int col = c0 + 4 * q;
+                const int g = col / c.Nt, n = col % c.Nt;
+                dst[q] = nullptr;
+                if (col < c.n_mma && g < gcnt) {
+                  const int64_t row = oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g);
+                  dst[q] = reinterpret_cast<float4*>(static_cast<float*>(obase) + row * c.Mt * c.Nt +
+                                                     static_cast<int64_t>(m) * c.Nt + n);
+                }
+              }
+              if (accm) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) old[q] = dst[q] ? *dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                if (!dst[q]) continue;
+                float4 r4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (accm) {
+                  r4.x += old[q].x;
+                  r4.y += old[q].y;
+                  r4.z += old[q].z;
+                  r4.w += old[q].w;
+                }
+                *dst[q] = r4;
+              }
+            } else if (gcnt > 0) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 const int col = c0 + j;
@@ -1113,15 +1189,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
                 if (col >= c.n_mma || g >= gcnt) continue;
                 const int64_t row = oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g);
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m) * c.Nt + n;
-                if (p.odt == ES_F32) {
-                  float4* of = reinterpret_cast<float4*>(static_cast<float*>(obase) + o);
-                  float4 r4 = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                  if (accm) {
-                    const float4 old = *of;
-                    r4.x += old.x; r4.y += old.y; r4.z += old.z; r4.w += old.w;
-                  }
-                  *of = r4;
-                } else {
+                {
                   __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(obase) + o;
 #pragma unroll
                   for (int q = 0; q < 4; ++q) {
@@ -1154,17 +1222,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += w[j];
             }
-            if (live) {
+            if (live && p.odt == ES_F32) {
+              float* ob = static_cast<float*>(obase) + row * c.Mt * c.Nt + n;
+              float old[32];
+              if (accm) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) old[j] = m0 + j < c.Mt ? ob[static_cast<int64_t>(m0 + j) * c.Nt] : 0.f;
+              }
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (m0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
+                float x = empty ? 0.f : v[j];
+                if (accm) x += old[j];
+                ob[static_cast<int64_t>(m0 + j) * c.Nt] = x;
+              }
+            } else if (live) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 if (m0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
                 const int64_t o = row * c.Mt * c.Nt + static_cast<int64_t>(m0 + j) * c.Nt + n;
                 float x = empty ? 0.f : v[j];
-                if (p.odt == ES_F32) {
-                  float* of = static_cast<float*>(obase) + o;
-                  if (accm) x += *of;
-                  *of = x;
-                } else {
+                {
                   __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(obase) + o;
                   if (accm) x += __bfloat162float(*ob);
                   *ob = __float2bfloat16_rn(x);
@@ -1201,7 +1279,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 // value (read as TF32 by the tensor core) to hi and x - trunc_tf32(x) to lo.
 template <bool F32, bool KMAJOR>
 __global__ void __launch_bounds__(256) layout_rhs_kernel(const void* __restrict__ rhs, int64_t rows, int Kt, int Nt,
-                                                         int KC, void* __restrict__ hi, void* __restrict__ lo) {
+                                                         int KC, void* __restrict__ hi, void* __restrict__ lo, int rn) {
   using E = typename std::conditional<F32, float, __nv_bfloat16>::type;
   constexpr int ESZ = F32 ? 4 : 2;
   constexpr int EPU = 16 / ESZ;  // elements per 16-byte piece
@@ -1211,10 +1289,10 @@ __global__ void __launch_bounds__(256) layout_rhs_kernel(const void* __restrict_
   const E* src = static_cast<const E*>(rhs);
   auto put = [&](int64_t dst, const E (&v)[EPU]) {
     if constexpr (F32) {
-      const float4 x = make_float4(v[0], v[1], v[2], v[3]);
-      *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;
-      *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) =
-          make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
+      float4 h, l;
+      tf32_split4(make_float4(v[0], v[1], v[2], v[3]), rn != 0, h, l);
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = h;
+      *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) = l;
     } else {
       *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
     }
@@ -1267,7 +1345,7 @@ constexpr int kLayoutCols = 32;
 template <bool F32>
 __global__ void __launch_bounds__(256) layout_rhs_wide_kernel(const void* __restrict__ rhs, int64_t rows, int Kt,
                                                               int Nt, int KC, void* __restrict__ hi,
-                                                              void* __restrict__ lo) {
+                                                              void* __restrict__ lo, int rn) {
   using E = typename std::conditional<F32, float, __nv_bfloat16>::type;
   constexpr int ESZ = F32 ? 4 : 2;
   constexpr int EPU = 16 / ESZ;
@@ -1300,10 +1378,10 @@ __global__ void __launch_bounds__(256) layout_rhs_wide_kernel(const void* __rest
       const int sw = ((n * W) >> 7) & (pieces - 1);
       const int64_t dst = ((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16);
       if constexpr (F32) {
-        const float4 x = make_float4(v[0], v[1], v[2], v[3]);
-        *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = x;
-        *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) =
-            make_float4(tf32_rem(x.x), tf32_rem(x.y), tf32_rem(x.z), tf32_rem(x.w));
+        float4 h, l;
+        tf32_split4(make_float4(v[0], v[1], v[2], v[3]), rn != 0, h, l);
+        *reinterpret_cast<float4*>(static_cast<uint8_t*>(hi) + dst) = h;
+        *reinterpret_cast<float4*>(static_cast<uint8_t*>(lo) + dst) = l;
       } else {
         *reinterpret_cast<uint4*>(static_cast<uint8_t*>(hi) + dst) = *reinterpret_cast<const uint4*>(v);
       }
@@ -1885,26 +1963,29 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   if (cv.overflow) return ES_ERR_WORKSPACE;
   if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
   // 1. rhs tiles into the shared-memory image (split for fp32)
+  // EINSPARSE_TF32_SPLIT=trunc: the truncating split (comparisons, tests)
+  const char* split_env = std::getenv("EINSPARSE_TF32_SPLIT");
+  const int rn = (split_env && std::strcmp(split_env, "trunc") == 0) ? 0 : 1;
   const int64_t pe = rhs_rows * c.Kt * c.Nt / (c.fp32 ? 4 : 8);  // 16-byte pieces of the image
   if (pe > 0) {
     if (c.rhs_kmajor) {
       if (c.fp32)
         ES_LAUNCH((layout_rhs_kernel<true, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, w.pan_lo);
+                  w.pan_hi, w.pan_lo, rn);
       else
         ES_LAUNCH((layout_rhs_kernel<false, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, (void*)nullptr);
+                  w.pan_hi, (void*)nullptr, rn);
     } else if (c.fp32 && c.Nt >= 128) {
       const int64_t nblk = rhs_rows * (c.Kt / c.KC) * ((c.Nt + kLayoutCols - 1) / kLayoutCols);
       const int g = static_cast<int>(nblk < 148 * 16 ? nblk : 148 * 16);
-      ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo);
+      ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo, rn);
     } else {
       if (c.fp32)
         ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, w.pan_lo);
+                  w.pan_hi, w.pan_lo, rn);
       else
         ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, (void*)nullptr);
+                  w.pan_hi, (void*)nullptr, rn);
     }
   }
   // 2. work items
@@ -1982,6 +2063,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.odt = odt;
   prm.err = err;
   prm.chain_recs = chain_records(c);
+  prm.rn_split = rn;
   prm.part = w.part;
   prm.part_stride = nseg * c.Mt * c.Nt;
   // EINSPARSE_NO_FUSED_BLOCKS: one launch per key block (tuning, tests)
