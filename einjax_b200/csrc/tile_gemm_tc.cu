@@ -93,7 +93,9 @@ struct ItemInfo {
   int gcnt[kMaxSlots];  // segments per slot (0: empty slot)
   int nsteps;           // records left in this key block (0: nothing in this key block)
   int blk;              // key block of the item
-  int acc;              // 1: add into the destination (a chain after the item's first)
+  int acc;              // 1: a chain after the item's first (its earlier chains are summed
+                        //    in TMEM, or, without tmem_chain, in the destination)
+  int last;             // 1: this accumulation ends the item (written with its end marker)
 };
 
 struct Ctrl {
@@ -284,6 +286,27 @@ __device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
                  "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
                :
                : "memory");
+}
+
+// tcgen05.st of 32 consecutive columns of this warp's TMEM lane quadrant
+// (one register per column), then the wait for its completion.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])),
+      "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])),
+      "r"(__float_as_uint(v[23])), "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])),
+      "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])),
+      "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major operand in a swizzled layout
@@ -622,33 +645,30 @@ __device__ __forceinline__ void epi_store_block(const TcParams& p, void* obase, 
 #pragma unroll
     for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = empty ? 0.f : __uint_as_float(r[j]);
     __syncwarp();
-    // old values of all 8 pieces are loaded before any store (one memory
-    // round trip per block when accumulating)
-    float4 old[8];
-    if (accm) {
+    // old values are loaded four pieces at a time before their stores (the
+    // caller holds two 32-register TMEM blocks, so not all eight)
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int j = it * 4 + (lane >> 3), piece = lane & 7;
-        old[it] = j < rows ? reinterpret_cast<const float4*>(static_cast<float*>(obase) + tile0 +
-                                                             static_cast<int64_t>(m0 + j) * c.Nt)[piece]
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = 0; i0 < 8; i0 += 4) {
+      float4 old[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = (i0 + q) * 4 + (lane >> 3), piece = lane & 7;
+        old[q] = (accm && j < rows) ? reinterpret_cast<const float4*>(static_cast<float*>(obase) + tile0 +
+                                                                      static_cast<int64_t>(m0 + j) * c.Nt)[piece]
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    }
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int j = it * 4 + (lane >> 3), piece = lane & 7;
-      if (j < rows) {
-        float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
-        float4* dst =
-            reinterpret_cast<float4*>(static_cast<float*>(obase) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt) +
-            piece;
-        if (accm) {
-          x.x += old[it].x;
-          x.y += old[it].y;
-          x.z += old[it].z;
-          x.w += old[it].w;
+      for (int q = 0; q < 4; ++q) {
+        const int j = (i0 + q) * 4 + (lane >> 3), piece = lane & 7;
+        if (j < rows) {
+          float4 x = reinterpret_cast<const float4*>(stg + j * 32)[piece];
+          x.x += old[q].x;
+          x.y += old[q].y;
+          x.z += old[q].z;
+          x.w += old[q].w;
+          reinterpret_cast<float4*>(static_cast<float*>(obase) + tile0 + static_cast<int64_t>(m0 + j) * c.Nt)[piece] =
+              x;
         }
-        *dst = x;
       }
     }
   } else if (accm) {
@@ -1035,6 +1055,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             break;
           }
           if (lane == 0) {
+            ctl->item_log[item_iter % kItemLog].last = 0;
             ctl->ring[stage].done = 1;
             mbar_arrive_expect_tx(&ctl->copy[stage], 0);
           }
@@ -1057,6 +1078,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         break;
       }
       if (lane == 0) {
+        ctl->item_log[item_iter % kItemLog].last = 1;
         ctl->ring[stage].done = 1;
         mbar_arrive_expect_tx(&ctl->copy[stage], 0);
       }
@@ -1124,7 +1146,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       // destination: the output (rows through seg_out), or in a fused launch
       // block b's partial sums (segment rows); chains after an item's first
       // and key blocks after the first of sequential launches add into it
-      const bool accm = p.accumulate || info.acc;
+      // chains summed in TMEM (tmem_chain): an accumulation that does not end
+      // its item is added into the running sum S at column acc_stride and
+      // released; the last one adds S and goes out
+      const bool tchain = c.tmem_chain != 0;
+      const bool accm = p.accumulate || (info.acc && !tchain);
+      const bool flush = tchain && !info.last;
+      const bool add_s = tchain && info.acc;
       void* obase = p.out;
       const int32_t* oseg = p.seg_out;
       if (p.fused && info.blk > 0) {
@@ -1148,38 +1176,49 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
+            if (add_s) {
+              uint32_t sv[32];
+              tmem_ld32_async(tbase + acc_stride + c0, sv);
+              tmem_wait32(sv);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(sv[j]);
+            }
+            if (flush) {
+              tmem_st32(tbase + acc_stride + c0, v);
+              continue;
+            }
             if (gcnt > 0 && p.odt == ES_F32) {
               // the 8 pieces' old values are all loaded before any store, so
               // an accumulating epilogue waits one memory round trip per 32
               // columns instead of one per piece
-              float4* dst[8];
-              float4 old[8];
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
+              auto piece = [&](int q) -> float4* {
                 const int col = c0 + 4 * q;
                 const int g = col / c.Nt, n = col % c.Nt;
-                dst[q] = nullptr;
-                if (col < c.n_mma && g < gcnt) {
-                  const int64_t row = oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g);
-                  dst[q] = reinterpret_cast<float4*>(static_cast<float*>(obase) + row * c.Mt * c.Nt +
-                                                     static_cast<int64_t>(m) * c.Nt + n);
-                }
-              }
+                if (col >= c.n_mma || g >= gcnt) return nullptr;
+                const int64_t row = oseg ? oseg[s0 + g] : static_cast<int64_t>(s0 + g);
+                return reinterpret_cast<float4*>(static_cast<float*>(obase) + row * c.Mt * c.Nt +
+                                                 static_cast<int64_t>(m) * c.Nt + n);
+              };
               if (accm) {
+                float4 old[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) old[q] = dst[q] ? *dst[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                if (!dst[q]) continue;
-                float4 r4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                if (accm) {
-                  r4.x += old[q].x;
-                  r4.y += old[q].y;
-                  r4.z += old[q].z;
-                  r4.w += old[q].w;
+                for (int q = 0; q < 8; ++q) {
+                  const float4* d = piece(q);
+                  old[q] = d ? *d : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
-                *dst[q] = r4;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  float4* d = piece(q);
+                  if (d)
+                    *d = make_float4(v[4 * q] + old[q].x, v[4 * q + 1] + old[q].y, v[4 * q + 2] + old[q].z,
+                                     v[4 * q + 3] + old[q].w);
+                }
+              } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  float4* d = piece(q);
+                  if (d) *d = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                }
               }
             } else if (gcnt > 0) {
 #pragma unroll
@@ -1223,18 +1262,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
               for (int j = 0; j < 32; ++j) v[j] += w[j];
             }
             if (live && p.odt == ES_F32) {
+              // old values in groups of 8 loads before their stores
               float* ob = static_cast<float*>(obase) + row * c.Mt * c.Nt + n;
-              float old[32];
-              if (accm) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) old[j] = m0 + j < c.Mt ? ob[static_cast<int64_t>(m0 + j) * c.Nt] : 0.f;
-              }
+              for (int j0 = 0; j0 < 32; j0 += 8) {
+                float old[8];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (m0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
-                float x = empty ? 0.f : v[j];
-                if (accm) x += old[j];
-                ob[static_cast<int64_t>(m0 + j) * c.Nt] = x;
+                for (int j = 0; j < 8; ++j)
+                  old[j] = (accm && m0 + j0 + j < c.Mt) ? ob[static_cast<int64_t>(m0 + j0 + j) * c.Nt] : 0.f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  if (m0 + j0 + j >= c.Mt) break;  // Mt < 32: the tail columns are not part of the tile
+                  const float x = (empty ? 0.f : v[j0 + j]) + old[j];
+                  ob[static_cast<int64_t>(m0 + j0 + j) * c.Nt] = x;
+                }
               }
             } else if (live) {
 #pragma unroll
@@ -2064,6 +2105,19 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.err = err;
   prm.chain_recs = chain_records(c);
   prm.rn_split = rn;
+  if (prm.chain_recs > 0) {
+    // chains only pay for long items: records per item, estimated from the
+    // pairs per segment (stacked steps carry about S / 2 lhs tiles)
+    const double spp = c.slots > 1 ? c.slots / 2.0 : 1.0;
+    const double recs_per_unit = static_cast<double>(npairs) * spp / static_cast<double>(nseg) / nblocks;
+    if (recs_per_unit < 2.0 * prm.chain_recs) {
+      prm.chain_recs = 0;
+    } else if (c.fp32 && !c.swap && c.halves * c.col_per_half <= 256) {
+      // the running sum of the chains lives in the second half of TMEM
+      prm.c.tmem_chain = 1;
+      prm.c.acc_bufs = 1;
+    }
+  }
   prm.part = w.part;
   prm.part_stride = nseg * c.Mt * c.Nt;
   // EINSPARSE_NO_FUSED_BLOCKS: one launch per key block (tuning, tests)

@@ -37,6 +37,8 @@ struct TcConfig {
                    // split) form a second epilogue group; the groups take alternate blocks
   int epi_warp_bytes;  // staging bytes per epilogue warp (2 KB for bf16 output, 4 KB for fp32)
   int smem_bytes;  // dynamic shared memory per CTA
+  int tmem_chain;  // set at launch: fp32 accumulation chains summed in TMEM (one accumulator
+                   // at column 0, the running sum at column acc_stride; acc_bufs = 1)
   int rhs_kmajor;  // set by the caller: rhs tiles are stored Nt x Kt (k contiguous), the
                    // transposed form of the contraction's rhs
 };
