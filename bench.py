@@ -197,6 +197,7 @@ def c2_parity(w, rows, coords, vals, rtol=1e-5):
     out["fp32_spmm_within_rtol"] = f32["within_rtol"]
     out["fp32_spmm_max_rel"] = f32["max_rel"]
     out["fp32_spmm_rel_fro"] = f32["rel_fro"]
+    out["fp32_spmm_max_abs_err"] = f32["max_abs_err"]
     return out
 
 
@@ -399,7 +400,8 @@ def run_ours(args):
                              *[phases[k] for k in ("tile_coo_A", "tile_dense_B", "join_and_group", "tile_gemm")],
                              float(P), float(T_A), float(O), par["max_rel"], par["max_abs_err"],
                              par["within_rtol"], 1.0 if par["bound_ok"] else 0.0, par["rel_fro"],
-                             par["fp32_spmm_within_rtol"], float(launches)], dtype=torch.float64, device=dev)
+                             par["fp32_spmm_within_rtol"], float(launches), par["fp32_spmm_rel_fro"],
+                             par["fp32_spmm_max_abs_err"]], dtype=torch.float64, device=dev)
     if world > 1:
         allr = [torch.zeros_like(per_rank) for _ in range(world)]
         dist.all_gather(allr, per_rank)
@@ -461,7 +463,10 @@ def run_ours(args):
                        "within_rtol": float(table[:, 12].min()), "bound_ok": bool(table[:, 13].min() > 0),
                        "bound": "|got - ref| <= rtol * (|ref| + sum |a*b|)",
                        "rel_fro": float(table[:, 14].max()),
-                       "fp32_spmm_within_rtol": float(table[:, 15].min())},
+                       "fp32_spmm": {"what": "scipy float32 A @ B (row-order fp32 accumulation) against the same "
+                                             "float64 reference", "within_rtol": float(table[:, 15].min()),
+                                     "rel_fro": float(table[:, 17].max()),
+                                     "max_abs_err": float(table[:, 18].max())}},
             "gpu_launches": int(table[0, 16]),
             "phases_ms": {k: float(table[slow, 3 + i]) for i, k in
                           enumerate(("tile_coo_A", "tile_dense_B", "join_and_group", "tile_gemm"))},

@@ -13,7 +13,7 @@ from .kernels import (block_sparse_matmul, block_sparse_matmul_generic, coordina
                       coordinate_join_sorted)
 from .partition import tile_shape_to_partition_spec  # noqa: F401
 from .plan import PlanStep, execute_sparse_plan, plan_from_path, reduction_keys  # noqa: F401
-from .registry import KernelInfo, KernelRegistry, register_b200_kernels  # noqa: F401
+from .registry import register_b200_kernels  # noqa: F401
 from .sparse import (DUPLICATE_POLICIES, SparseTensor, SparseTensorRelation, as_device_tensor,  # noqa: F401
                      coalesce_coo, compute_sparsity_stats_coo, compute_sparsity_stats_dense, factor_tile_shapes,
                      find_all_factors, tile_coo, tile_dense)

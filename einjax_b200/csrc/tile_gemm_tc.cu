@@ -1709,7 +1709,7 @@ bool fused_blocks_possible(const TcConfig& c, int nblocks, int64_t nseg) {
 // MMAs summed into one accumulator. Restarting the accumulator every
 // kChainKsteps k-steps (K = 8 each) and adding the chains in fp32 with
 // round-to-nearest keeps a long contraction within plain fp32 accuracy.
-constexpr int kChainKsteps = 64;
+constexpr int kChainKsteps = 128;
 
 int chain_records(const TcConfig& c) {
   if (!c.fp32) return 0;

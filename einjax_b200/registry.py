@@ -1,109 +1,32 @@
-"""Kernel registry; mirrors einjax ``kernels/registry.py`` and registers the
-B200 kernels into it.
+"""Registration of the B200 kernels into einjax's own ``KernelRegistry``.
 
-``KernelRegistry``/``KernelInfo`` keep the reference's lookup rules
-(``kernels/registry.py:27-273``): highest priority wins, ``"*"`` matches any
-pattern, ``"generic"`` any backend, ``"gpu"`` also matches ``"gpu:<x>"``.
-``register_b200_kernels(registry)`` adds, to this registry or to the
-reference's own (duck-typed: anything with ``register(KernelInfo-like)``),
+The reference dispatches sparse contractions through
+``KernelRegistry.lookup(pattern, backend, sparsity)`` (``kernels/registry.py:107-140``),
+whose built-ins are registered in ``KernelRegistry.__init__``
+(``kernels/registry.py:63-97``). ``register_b200_kernels(registry)`` adds to
+that registry (or to any object with a ``register(info)`` method and the same
+``KernelInfo`` fields):
 
 * ``b200_block_sparse_matmul`` — pattern ``"ij,jk->ik"``, backend ``"gpu"``,
-  sparsity ``"sparse"``, priority 10, signature of
+  sparsity ``"sparse"``, priority 10, the signature of
   ``block_sparse_matmul_generic(lhs, rhs, block_shape=None)``;
-* ``b200_sparse_einsum`` — pattern ``"*"``, same backend/sparsity,
-  priority 10, signature of ``execute_sparse``.
+* ``b200_sparse_einsum`` — pattern ``"*"``, same backend / sparsity /
+  priority, the signature of ``execute_sparse``.
 
-Both accept the reference's numpy relations and, with ``host_result=True``
-(the default for the adapters registered into a foreign registry), return a
-relation of numpy arrays, so callers written against the reference keep
-working unchanged.
+The registry's own matching rules then pick them over the generic JAX
+kernels for ``backend="gpu"`` (and ``"gpu:<x>"``) lookups. Both accept the
+reference's numpy relations and, with ``host_result=True``, return the
+reference's ``SparseTensorRelation`` (numpy arrays, values float32), so
+callers written against the reference keep working unchanged.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Any, Callable
-
-
-@dataclass
-class KernelInfo:
-    """``kernels/registry.py:27-45``."""
-
-    name: str
-    pattern: str
-    backend: str
-    sparsity: str
-    priority: int
-    kernel_fn: Callable[..., Any]
-
-
-def _pattern_matches(registered: str, query: str) -> bool:
-    return registered == "*" or registered == query
-
-
-def _backend_matches(registered: str, query: str) -> bool:
-    return registered == "generic" or registered == query or query.startswith(registered + ":")
-
-
-def _sparsity_matches(registered: str, query: str) -> bool:
-    return registered == "any" or registered == query
-
-
-def _detect_backend() -> str:
-    """"gpu" when a CUDA device is visible, else "cpu" (``kernels/registry.py:226-242``)."""
-    try:
-        import torch
-        if torch.cuda.is_available():
-            return "gpu"
-    except Exception:  # pragma: no cover
-        pass
-    return "cpu"
-
-
-class KernelRegistry:
-    """Pattern/backend/sparsity dispatch table (``kernels/registry.py:48-223``).
-
-    Built with the B200 kernels registered (the reference registers its
-    generic JAX fallbacks here; this package has no CPU fallback).
-    """
-
-    def __init__(self, register_builtins: bool = True) -> None:
-        self._kernels: list[KernelInfo] = []
-        if register_builtins:
-            register_b200_kernels(self, host_result=False)
-
-    def register(self, kernel) -> None:
-        self._kernels.append(kernel)
-
-    def _find_candidates(self, pattern, backend, sparsity):
-        return [k for k in self._kernels if _pattern_matches(k.pattern, pattern)
-                and _backend_matches(k.backend, backend) and _sparsity_matches(k.sparsity, sparsity)]
-
-    def lookup_info(self, pattern: str, backend: str | None = None, sparsity: str = "dense") -> KernelInfo:
-        backend = backend or _detect_backend()
-        c = self._find_candidates(pattern, backend, sparsity)
-        if not c:
-            raise ValueError(f"No kernel found for pattern={pattern!r}, backend={backend!r}, "
-                             f"sparsity={sparsity!r}")
-        c.sort(key=lambda k: k.priority, reverse=True)
-        return c[0]
-
-    def lookup(self, pattern: str, backend: str | None = None, sparsity: str = "dense"):
-        return self.lookup_info(pattern, backend, sparsity).kernel_fn
-
-    def list_kernels(self, pattern=None, backend=None, sparsity=None) -> list:
-        r = list(self._kernels)
-        if pattern is not None:
-            r = [k for k in r if k.pattern == pattern or k.pattern == "*"]
-        if backend is not None:
-            r = [k for k in r if _backend_matches(k.backend, backend)]
-        if sparsity is not None:
-            r = [k for k in r if k.sparsity == sparsity or k.sparsity == "any"]
-        return r
+from typing import Any
 
 
 class _HostRelation:
-    """Plain relation of numpy arrays returned to reference-side callers."""
+    """Plain relation of numpy arrays, for callers without einjax installed."""
 
     def __init__(self, coords, values, shape, tile_shape):
         self.coords, self.values, self.shape, self.tile_shape = coords, values, tuple(shape), tuple(tile_shape)
@@ -115,6 +38,15 @@ class _HostRelation:
     @property
     def ndim(self):
         return len(self.shape)
+
+
+def _reference_attr(module: str, name: str):
+    """``einjax.<module>.<name>`` when einjax is importable, else None."""
+    try:
+        import importlib
+        return getattr(importlib.import_module(f"einjax.{module}"), name)
+    except Exception:  # einjax (or jax) not installed
+        return None
 
 
 def _to_host(rel, relation_cls=None):
@@ -141,14 +73,25 @@ def make_sparse_einsum_kernel(host_result=True, relation_cls=None):
     return b200_sparse_einsum
 
 
-def register_b200_kernels(registry, info_cls=None, host_result=True, relation_cls=None, priority=10):
-    """Register the B200 kernels into ``registry`` (ours or the reference's).
+def register_b200_kernels(registry=None, info_cls=None, host_result=True, relation_cls=None, priority=10) -> Any:
+    """Register the B200 kernels into ``registry`` and return it.
 
-    ``info_cls``: the registry's KernelInfo class (defaults to this module's);
-    ``relation_cls``: class used for host results (e.g. the reference's
-    ``SparseTensorRelation``), defaults to a plain numpy-holding relation.
+    ``registry``: einjax's ``KernelRegistry`` instance (default: a new one,
+    ``einjax.kernels.registry.KernelRegistry()``) or any object with
+    ``register(info)``. ``info_cls``: the registry's ``KernelInfo`` class
+    (default: einjax's). ``relation_cls``: class of host results (default:
+    einjax's ``SparseTensorRelation``, else a plain numpy-holding relation).
     """
-    info_cls = info_cls or KernelInfo
+    if registry is None:
+        cls = _reference_attr("kernels.registry", "KernelRegistry")
+        if cls is None:
+            raise ImportError("einjax is not importable: pass the registry to register into")
+        registry = cls()
+    info_cls = info_cls or _reference_attr("kernels.registry", "KernelInfo")
+    if info_cls is None:
+        raise ImportError("einjax is not importable: pass the registry's KernelInfo class as info_cls")
+    if relation_cls is None and host_result:
+        relation_cls = _reference_attr("tensor.sparse", "SparseTensorRelation")
     registry.register(info_cls(name="b200_block_sparse_matmul", pattern="ij,jk->ik", backend="gpu",
                                sparsity="sparse", priority=priority,
                                kernel_fn=make_block_sparse_matmul_kernel(host_result, relation_cls)))

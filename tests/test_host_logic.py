@@ -7,7 +7,6 @@ import pytest
 
 import einjax_b200 as E
 from einjax_b200 import distributed as D
-from einjax_b200.registry import _backend_matches, _pattern_matches, _sparsity_matches
 from golden_io import load_cases
 
 H = load_cases()["helpers"].meta
@@ -33,30 +32,6 @@ def test_partition_spec_matches_reference():
                 E.tile_shape_to_partition_spec(tuple(shape), tuple(tile))
         else:
             assert list(E.tile_shape_to_partition_spec(tuple(shape), tuple(tile))) == want
-
-
-def test_matchers():
-    assert _pattern_matches("*", "anything") and not _pattern_matches("ij,jk->ik", "ij,kj->ik")
-    assert _backend_matches("generic", "gpu") and _backend_matches("gpu", "gpu:triton")
-    assert not _backend_matches("gpu", "tpu")
-    assert _sparsity_matches("any", "dense") and not _sparsity_matches("sparse", "dense")
-
-
-def test_registry_dispatch():
-    reg = E.KernelRegistry()
-    info = reg.lookup_info("ij,jk->ik", backend="gpu", sparsity="sparse")
-    assert info.name == "b200_block_sparse_matmul" and info.priority > 0
-    assert reg.lookup_info("bij,bjk->bik", backend="gpu:anything", sparsity="sparse").name == "b200_sparse_einsum"
-    with pytest.raises(ValueError):
-        reg.lookup("ij,jk->ik", backend="gpu", sparsity="dense")
-    with pytest.raises(ValueError):
-        reg.lookup("ij,jk->ik", backend="tpu", sparsity="sparse")
-
-    def custom(*a, **k):
-        return "custom"
-    reg.register(E.KernelInfo("custom", "ij,jk->ik", "generic", "sparse", 99, custom))
-    assert reg.lookup("ij,jk->ik", backend="cpu", sparsity="sparse") is custom
-    assert len(reg.list_kernels(sparsity="sparse")) == 3
 
 
 def test_register_into_foreign_registry():
