@@ -282,7 +282,7 @@ def run_ours(args):
             ev["g"][-1].record()
         vals = SD.tile_einsum(ks, A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
                               precision=args.precision, seg_strip=plan.seg_strip, pair_key=plan.seg_key,
-                              key_extent=plan.key_extent)
+                              key_extent=plan.key_extent, check="defer")
         if timing:
             ev.setdefault("h", []).append(torch.cuda.Event(enable_timing=True))
             ev["h"][-1].record()
@@ -384,6 +384,7 @@ def run_ours(args):
     d2h_bytes = out_h.numel() * out_h.element_size() + oc_h.numel() * 4
     del slots
 
+    E.check_device_errors()
     # ---- per-phase split of one device-resident step (untimed for the metric)
     m = []
     A, B, plan, vals = step(idx_d, val_d, b_d, marks=m)

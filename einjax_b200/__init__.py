@@ -15,8 +15,8 @@ from .partition import tile_shape_to_partition_spec  # noqa: F401
 from .plan import PlanStep, execute_sparse_plan, plan_from_path, reduction_keys  # noqa: F401
 from .registry import register_b200_kernels  # noqa: F401
 from .sparse import (DUPLICATE_POLICIES, SparseTensor, SparseTensorRelation, as_device_tensor,  # noqa: F401
-                     coalesce_coo, compute_sparsity_stats_coo, compute_sparsity_stats_dense, factor_tile_shapes,
-                     find_all_factors, tile_coo, tile_dense)
+                     check_device_errors, coalesce_coo, compute_sparsity_stats_coo, compute_sparsity_stats_dense,
+                     factor_tile_shapes, find_all_factors, tile_coo, tile_dense)
 from .sparse_dispatch import (_add_batch_dim, _compute_output_coords, _infer_output_tile_shape,  # noqa: F401
                               _partition_matched_pairs, coordinate_join, execute_sharded_sparse, execute_sparse,
                               kernel_einsum, plan_pairs, segment_sum, tile_einsum)

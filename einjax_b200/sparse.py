@@ -54,9 +54,70 @@ def mark(marks, label: str) -> None:
         marks.append((label, ev))
 
 
+class _DeferredErrors:
+    """Device error slots read back later, without a sync of their own.
+
+    ``defer`` queues an asynchronous copy of a call's int32 error slot into a
+    pinned host ring and records an event; ``flush`` (run after every host
+    read of counts, which waits on the stream anyway, and by
+    ``check_device_errors``) reads the copies that have landed and raises for
+    the first non-zero one. A failure of a call is then reported by the next
+    call that reads counts back, as CUDA reports asynchronous errors."""
+
+    SLOTS = 256
+
+    def __init__(self):
+        self.host = None
+        self.next = 0
+        self.pending = []  # (function name, slot, event)
+
+    def defer(self, fn: str, err: torch.Tensor) -> None:
+        if self.host is None:
+            self.host = torch.zeros(self.SLOTS, dtype=torch.int32, pin_memory=True)
+        if len(self.pending) >= self.SLOTS - 1:
+            self.flush()
+        slot = self.next
+        self.next = (self.next + 1) % self.SLOTS
+        self.host[slot:slot + 1].copy_(err.reshape(1), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.pending.append((fn, slot, ev))
+
+    def flush(self) -> None:
+        pending, self.pending = self.pending, []
+        first = None
+        for fn, slot, ev in pending:
+            ev.synchronize()
+            e = int(self.host[slot])
+            if e and first is None:
+                first = (fn, e)
+        if first is not None:
+            L.check(first[0] + " (device)", first[1])
+
+
+_DEFERRED = _DeferredErrors()
+
+
+def defer_device_error(fn: str, err: torch.Tensor) -> None:
+    """Check ``err`` (device int32 status) at the next count read or
+    ``check_device_errors`` instead of now."""
+    _DEFERRED.defer(fn, err)
+
+
+def check_device_errors() -> None:
+    """Wait for the deferred device error slots of earlier calls and raise
+    for the first failure (``ValueError`` for bad input, ``EinsparseError``
+    otherwise, e.g. a bounded wait that ran out)."""
+    _DEFERRED.flush()
+
+
 def read_counts(t: torch.Tensor):
-    """Read a small device int64 tensor (count, error, ...) with one sync."""
-    return [int(v) for v in t.tolist()]
+    """Read a small device int64 tensor (count, error, ...) with one sync;
+    deferred error slots of earlier calls are checked at the same time."""
+    vals = [int(v) for v in t.tolist()]
+    if _DEFERRED.pending:
+        _DEFERRED.flush()
+    return vals
 
 
 def value_dtype_for(dtype) -> torch.dtype:

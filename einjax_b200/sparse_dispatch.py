@@ -21,8 +21,8 @@ from math import prod
 import torch
 
 from . import _lib as L
-from .sparse import (SparseTensorRelation, as_relation, empty_relation, es_dtype, mark, read_counts, stream_ptr,
-                     workspace)
+from .sparse import (SparseTensorRelation, as_relation, defer_device_error, empty_relation, es_dtype, mark,
+                     read_counts, stream_ptr, workspace)
 
 _PREC = {"auto": L.ES_PREC_AUTO, "exact": L.ES_PREC_EXACT, "tc": L.ES_PREC_TC}
 
@@ -132,7 +132,9 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     tensor-core path batch the segments of one output strip; ``pair_key`` (the
     contracted tile coordinate of each pair, in ``[0, key_extent)``) lets it
     block the contracted range so the re-read operand stays in L2. With
-    ``check`` the device error flag is read back (one 4-byte copy).
+    ``check`` the device error flag is read back (one 4-byte copy and a wait);
+    ``check="defer"`` queues it for the next count read or
+    ``check_device_errors()`` (no wait here); False skips it.
     """
     lib = L.lib()
     dev = lhs_values.device
@@ -173,7 +175,9 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
         pk.data_ptr() if pk is not None else None, kext, out.data_ptr(),
         _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         err.data_ptr(), stream_ptr(dev)))
-    if check:
+    if check == "defer":
+        defer_device_error("es_tile_einsum", err)
+    elif check:
         e = int(err.item())
         if e:
             L.check("es_tile_einsum (device)", e)
@@ -455,9 +459,10 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
     plan = plan or plan_pairs(lhs, rhs, join_keys, agg_keys)
     if plan.num_pairs == 0:
         return empty_relation(output_shape, output_tile_shape, lhs.values.dtype, lhs.device)
+    # the GEMM's device status is read at the next count read (no wait here)
     vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
                        precision=precision, seg_strip=plan.seg_strip, pair_key=plan.seg_key,
-                       key_extent=plan.key_extent)
+                       key_extent=plan.key_extent, check="defer")
     return SparseTensorRelation(plan.out_coords, vals, output_shape, output_tile_shape)
 
 

@@ -148,3 +148,26 @@ def test_bf16_sparse_rhs_panel_slots(dens):
     c, v = res.to_numpy()
     np.testing.assert_array_equal(c, ref.coords)
     assert np.all(np.abs(v.astype(np.float64) - ref.values) <= 2e-2 * (np.abs(ref.values) + mag.values))
+
+
+def test_deferred_device_error_reported_later():
+    """A device-side error of a call made with check="defer" (here a pair
+    index past the lhs rows, which the kernel reports and reads as a zero
+    tile) is raised by the next count read or by check_device_errors, not
+    by the call itself."""
+    n = 2048
+    idx, val, b = _c2_like(7, n, nnz=8000)
+    A, B, plan = _run(idx, val, b, n)
+    bad = plan.seg_lhs.clone()
+    bad[0] = A.num_tuples + 5
+    out = SD.tile_einsum(MM[1], A.values, B.values, bad, plan.seg_rhs, plan.seg_offsets, precision="tc",
+                         seg_strip=plan.seg_strip, pair_key=plan.seg_key, key_extent=plan.key_extent,
+                         check="defer")
+    assert out.shape[0] == plan.num_segments
+    with pytest.raises(ValueError):
+        E.check_device_errors()
+    E.check_device_errors()  # reported once
+    # a good call afterwards is unaffected
+    SD.tile_einsum(MM[1], A.values, B.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets, precision="tc",
+                   seg_strip=plan.seg_strip, pair_key=plan.seg_key, key_extent=plan.key_extent, check="defer")
+    E.check_device_errors()
