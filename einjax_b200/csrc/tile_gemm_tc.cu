@@ -1045,10 +1045,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             ph ^= 1u;
           }
         }
-        if (p.chain_recs > 0 && ++since == p.chain_recs && r < re && !aborted) {
+        }
+        // chains end on a multiple of kRecAhead records, outside the unrolled
+        // loop above (ahead[] is a ring indexed at compile time, and the
+        // scheduler's per-record path stays as short as without chains)
+        if (p.chain_recs > 0 && r < re && !aborted && (since += kRecAhead) >= p.chain_recs) {
           // end of a chain: the MMA warp commits this accumulation and starts
           // the rest of the item in a fresh accumulator; the epilogue adds
-          // each chain into the destination
+          // each chain into the running sum
           since = 0;
           if (!wait_bar(&ctl->empty[stage], ph ^ 1u, ctl, p.err)) {
             aborted = true;
@@ -1067,7 +1071,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
             ph ^= 1u;
           }
           log_item(re - r, 1);
-        }
         }
       }
       if (aborted) break;
@@ -1718,8 +1721,9 @@ int chain_records(const TcConfig& c) {
   if (const char* e = std::getenv("EINSPARSE_CHAIN_KSTEPS")) ks = std::atoll(e);
   if (ks <= 0) return 0;
   const int per = c.Kt / 8 > 0 ? c.Kt / 8 : 1;  // k-steps per record
-  const int64_t r = ks / per;
-  return static_cast<int>(r < 1 ? 1 : r);
+  int64_t r = ks / per;
+  r = (r + kRecAhead - 1) / kRecAhead * kRecAhead;  // the scheduler ends chains every kRecAhead records
+  return static_cast<int>(r < kRecAhead ? kRecAhead : r);
 }
 
 // out[row(s)] += part[0][s] + part[1][s] + ... in block order (float4 pieces).
