@@ -139,7 +139,8 @@ struct TcParams {
                             //    records and the epilogue adds each chain into the
                             //    destination in fp32 (round to nearest), so the tensor
                             //    core's accumulator never sums a long run
-  int rn_split;             // fp32: 1 = rounded hi/lo split (tf32_split), 0 = truncating
+  int rn_split;             // fp32: 1 = lo parts rounded to nearest TF32 (lhs: x - trunc(x);
+                            //    rhs panel: the tf32_split of x), 0 = truncating split
   float* part;              // fused: per-block partial sums, segment-major rows
   int64_t part_stride;      // elements of one block's partial
   const int32_t* seg_out;
@@ -584,7 +585,7 @@ __device__ void mma_dispatch(const TcParams& p, Ctrl* ctl, const MmaArgs& m, int
 // is) gets its lo copy, x - trunc_tf32(x); slots absent from the step
 // (stacked mode) become zeros in both copies. PER bounds the 16-byte chunks
 // per thread at compile time, so the loads are all issued before the stores.
-template <int PER>
+template <int PER, bool RNLO>
 __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_lhs, int slot_bytes, int tid) {
   const TcConfig& c = p.c;
   const int nf = c.lhs_bytes / 16;
@@ -613,11 +614,12 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
       for (int j = 0; j < PER; ++j) {
         const int f = tid + j * kProducers;
         if (f < nf) {
-          float4 hi, lo;
-          tf32_split4(x[j], p.rn_split != 0, hi, lo);
+          // hi stays the raw chunk (read truncated to TF32 by the tensor
+          // core); lo = x - trunc(x), rounded to nearest TF32 with RNLO
+          float4 lo = make_float4(tf32_rem(x[j].x), tf32_rem(x[j].y), tf32_rem(x[j].z), tf32_rem(x[j].w));
+          if (RNLO) lo = make_float4(tf32_rna(lo.x), tf32_rna(lo.y), tf32_rna(lo.z), tf32_rna(lo.w));
           *reinterpret_cast<float4*>(sbase + off_lhs + c.lhs_bytes + f * 16) = lo;
-          // the rounded hi replaces the raw chunk; absent slots become zeros
-          if (!on[j] || p.rn_split) *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = hi;
+          if (!on[j]) *reinterpret_cast<float4*>(sbase + off_lhs + f * 16) = x[j];  // absent slot: zero hi too
         }
       }
       fence_proxy_async();
@@ -629,6 +631,16 @@ __device__ void split_role(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_
     }
     if (d == 2) break;
   }
+}
+
+template <bool RNLO>
+__device__ void split_dispatch(const TcParams& p, Ctrl* ctl, uint8_t* smem, int off_lhs, int slot_bytes, int tid,
+                               int per) {
+  if (per <= 1) split_role<1, RNLO>(p, ctl, smem, off_lhs, slot_bytes, tid);
+  else if (per <= 2) split_role<2, RNLO>(p, ctl, smem, off_lhs, slot_bytes, tid);
+  else if (per <= 4) split_role<4, RNLO>(p, ctl, smem, off_lhs, slot_bytes, tid);
+  else if (per <= 8) split_role<8, RNLO>(p, ctl, smem, off_lhs, slot_bytes, tid);
+  else split_role<16, RNLO>(p, ctl, smem, off_lhs, slot_bytes, tid);
 }
 
 // Swapped epilogue through shared memory (TcConfig::epi_stage): accumulator
@@ -1104,11 +1116,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
     if constexpr (F32) {
       const int nf = c.lhs_bytes / 16;  // 16-byte chunks of the lhs operand (all slots)
       const int per = (nf + kProducers - 1) / kProducers;
-      if (per <= 1) split_role<1>(p, ctl, smem, off_lhs, slot_bytes, tid);
-      else if (per <= 2) split_role<2>(p, ctl, smem, off_lhs, slot_bytes, tid);
-      else if (per <= 4) split_role<4>(p, ctl, smem, off_lhs, slot_bytes, tid);
-      else if (per <= 8) split_role<8>(p, ctl, smem, off_lhs, slot_bytes, tid);
-      else split_role<16>(p, ctl, smem, off_lhs, slot_bytes, tid);
+      if (p.rn_split) split_dispatch<true>(p, ctl, smem, off_lhs, slot_bytes, tid, per);
+      else split_dispatch<false>(p, ctl, smem, off_lhs, slot_bytes, tid, per);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA warp
