@@ -28,7 +28,8 @@ per second (joined tile-pairs/s is reported beside it).
 * ``configs``: the other BASELINE configurations in the same line -- C1, C3,
   C4 (forward + gradients of all three operands) and C5 on one GPU at N=1;
   at N>1, C5 sharded over its contracted (k) tile range with the partial
-  output tiles summed by an NCCL reduce-scatter, as BASELINE specifies.
+  output tiles summed by an NCCL reduce-scatter, as BASELINE specifies, and
+  (``C5_output``) over X's i rows with no collective, for comparison.
   Each entry: ms per step, useful TFLOP/s, roofline fractions, clocks and a
   parity sample against a float64 computation.
 * ``--impl reference``: the CPU oracle (numpy port of the reference's path)
@@ -541,11 +542,12 @@ def measure_configs(args, dev, rank, world, clk, barrier):
     out = {}
     steps = max(3, min(args.steps, 10))
     warm = max(3, min(args.warmup, 3))
-    names = ["C1", "C3", "C4", "C5"] if world == 1 else ["C5"]
+    names = ["C1", "C3", "C4", "C5"] if world == 1 else ["C5", "C5_output"]
     if args.configs:
         names = [n for n in names if n in args.configs.split(",")]
     for name in names:
-        fn = {"C1": measure_c1, "C3": measure_c3, "C4": measure_c4, "C5": measure_c5}[name]
+        fn = {"C1": measure_c1, "C3": measure_c3, "C4": measure_c4, "C5": measure_c5,
+              "C5_output": lambda *a: measure_c5(*a, shard="output")}[name]
         try:
             out[name] = fn(args, dev, rank, world, clk, barrier, steps, warm)
         except Exception as ex:  # a failed config must not hide the headline
@@ -667,12 +669,14 @@ def c5_sample_ref(idx, val, W, want_ij, tile=16):
     return ref, mag
 
 
-def measure_c5(args, dev, rank, world, clk, barrier, steps, warm):
+def measure_c5(args, dev, rank, world, clk, barrier, steps, warm, shard="contracted"):
     """C5 ``ijk,kl->ijl`` at full size (X drawn on the GPU). N=1: one GPU.
-    N>1: X's contracted k tile range split over the ranks (balanced by X tile
-    count), each rank tiles and contracts its k slice, and the partial output
-    tiles are summed by one NCCL reduce-scatter over the union of output
-    coordinates (``execute_sharded_sparse(shard="contracted")``)."""
+    N>1, ``shard="contracted"`` (the BASELINE configuration): X's contracted
+    k tile range split over the ranks (balanced by X tile count), each rank
+    tiles and contracts its k slice, and the partial output tiles are summed
+    by one NCCL reduce-scatter over the union of output coordinates
+    (``execute_sharded_sparse(shard="contracted")``). ``shard="output"``, for
+    comparison: X's i rows split (``balanced_row_ranges``), no collective."""
     import torch
     import torch.distributed as dist
 
@@ -685,7 +689,13 @@ def measure_c5(args, dev, rank, world, clk, barrier, steps, warm):
     gen_s = time.time() - t0
     shape, lt, rt = w.lhs.shape, w.lhs_tile, w.rhs_tile
     idx, val, Wd = w.lhs.indices, w.lhs.values, w.rhs
-    if world > 1:
+    if world > 1 and shard == "output":
+        i_np = idx[:, 0].cpu().numpy()
+        r0, r1 = D.balanced_row_ranges(idx.cpu().numpy(), shape, lt, world)[rank]
+        sel = (idx[:, 0] >= r0) & (idx[:, 0] < r1)
+        li, lv = idx[sel].contiguous(), val[sel].contiguous()
+        del sel, i_np
+    elif world > 1:
         # k tile range of this rank, balanced by non-empty X tiles per k tile
         g = [s // t for s, t in zip(shape, lt)]
         tk = (idx[:, 0].long() // lt[0] * g[1] + idx[:, 1].long() // lt[1]) * g[2] + idx[:, 2].long() // lt[2]
@@ -704,7 +714,7 @@ def measure_c5(args, dev, rank, world, clk, barrier, steps, warm):
         Wt = E.tile_dense(Wd, rt)
         if world > 1:
             del marks[:]
-            return E.execute_sharded_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys, shard="contracted",
+            return E.execute_sharded_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys, shard=shard,
                                             lhs_sharded=True, gather=False, timings=marks)
         return E.execute_sparse(X, Wt, w.join_keys, w.kernel_string, w.agg_keys)
     ms, res, win = _timed_steps(step, steps, warm, clk, barrier)
@@ -770,7 +780,13 @@ def measure_c5(args, dev, rank, world, clk, barrier, steps, warm):
                         "max_rel": float(tab[:, 5].max()), "within_rtol": float(tab[:, 6].min()),
                         "bound_ok": bool(tab[:, 7].min() > 0),
                         "bound": "|got - ref| <= rtol * (|ref| + sum |x*w|)"}}
-    if world > 1:
+    if world > 1 and shard == "output":
+        entry["parallelism"] = (f"output sharding x{world}: X's i rows split (balanced by X tiles), W replicated, "
+                                "no collective (a comparison for the contracted split BASELINE specifies)")
+        entry["scaling"] = "strong"
+        entry["ranks"] = {"ms_per_step": [round(float(x), 3) for x in tab[:, 0]],
+                          "tile_gemm_ms": [round(float(x), 3) for x in tab[:, 3]]}
+    elif world > 1:
         U = int(tab[:, 8].sum())
         per_rank_send = (world - 1) * ((U + world - 1) // world) * tile_bytes
         entry["parallelism"] = (f"contracted k tile range split x{world} (balanced by X tiles); partial output tiles "
