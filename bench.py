@@ -57,7 +57,7 @@ FLOPS_PER_PAIR = 2 * TILE ** 3
 # DRAM bytes (read + write) of the tile GEMM per joined pair, from the ncu
 # capture of the 1/4-scale C2 case (one key block, 923,064 pairs); the lhs
 # tiles dominate and are read once, so the traffic grows with the pairs.
-TRAFFIC_PER_PAIR = 569.3
+TRAFFIC_PER_PAIR = 571.9
 TRAFFIC_SOURCE = "ncu dram__bytes_read+write of the tile GEMM at C2 scale 1/4 per pair, times this run's pairs"
 
 
