@@ -389,7 +389,7 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
         continue;
       const int64_t ke = keys ? key_extent : 0;
       size_t sz = tc_workspace_size(c, rhs_rows, num_pairs, num_segments,
-                                    tc_key_blocks(c, rhs_rows, keys != 0, ke), ke);
+                                    tc_key_blocks(c, rhs_rows, keys != 0, ke, num_segments), ke);
       if (v.tl) sz += round256(static_cast<size_t>(lhs_rows) * d.lhs_te * dtype_size(lhs_dtype)) + 256;
       if (sz > best) best = sz;
     }

@@ -67,6 +67,7 @@ constexpr uint64_t kDrainNs = 100000000ull;   // 100 ms to drain own copies / MM
 constexpr uint32_t kEpiSleepNs = EXP_EPI_SLEEP;
 constexpr int64_t kPanelL2Budget = 40ll << 20;  // rhs panel bytes per key block
 constexpr int kMaxKeyBlocks = 16;
+constexpr int kUnitsPerSm = 4;  // fused launch: (key block, item) units per SM at least
 constexpr int kMaxMergeChunks = 64;
 
 // done: 0 data stage, 1 end of a work item, 2 no more items; mask: lhs
@@ -1686,22 +1687,40 @@ __global__ void item_rec_kernel(const uint32_t* __restrict__ off, const uint32_t
 
 // Key chunks of the merge pass: a multiple of the key blocks, about
 // kMergeChunkKeys keys each (1 without keys). Smaller chunks measured slower
-// on C2 (fill pass 342 us with 256 keys per chunk, 414 us with 32).
+// on C2 (fill pass 342 us with 256 keys per chunk, 414 us with 32). A
+// chunk's merge is one warp's serial loop, so with few items (one rank's
+// share of the strips) the chunks are cut finer until about
+// kMergeTargetWarps warps run: the pass then takes the longest chunk's
+// time, not the longest item's.
 constexpr int64_t kMergeChunkKeys = 256;
+constexpr int64_t kMergeTargetWarps = 148 * 16;
 
-int merge_chunks(int nblocks, bool have_key, int64_t key_extent) {
+int merge_chunks(int nblocks, bool have_key, int64_t key_extent, int64_t items) {
   if (!have_key || key_extent <= 1) return 1;
   int64_t keys = kMergeChunkKeys;
   // EINSPARSE_MERGE_KEYS overrides the keys per chunk (tuning, tests)
-  if (const char* e = std::getenv("EINSPARSE_MERGE_KEYS")) {
-    const long long v = std::atoll(e);
+  const char* env = std::getenv("EINSPARSE_MERGE_KEYS");
+  if (env) {
+    const long long v = std::atoll(env);
     if (v > 0) keys = v;
   }
   int64_t m = key_extent / (keys * nblocks);
+  if (!env && items > 0) {
+    const int64_t want = (kMergeTargetWarps + items * nblocks - 1) / (items * nblocks);
+    if (want > m) m = want;
+  }
+  if (m > key_extent / nblocks) m = key_extent / nblocks;  // at least one key per chunk
   if (m < 1) m = 1;
   while (nblocks * m > kMaxMergeChunks) --m;
   if (m < 1) m = 1;
   return static_cast<int>(nblocks * m);
+}
+
+// Work items a launch forms from nseg segments (upper estimate: every strip
+// fills its G segment slots).
+int64_t items_estimate(const TcConfig& c, int64_t nseg) {
+  const int64_t per_item = static_cast<int64_t>(c.G > 0 ? c.G : 1) * (c.slots > 0 ? c.slots : 1);
+  return (nseg + per_item - 1) / per_item;
 }
 
 // Fused key blocks: one launch takes every (key block, item) unit; blocks
@@ -1794,7 +1813,7 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npai
   w.zeros = cv.template take<uint8_t>(zero_bytes(c));
   w.recs = cv.template take<int32_t>(npairs * kRecInts);
   w.item_rec = cv.template take<int64_t>(nseg * (nblocks + 1));
-  const int nck = merge_chunks(nblocks, key_extent > 0, key_extent);
+  const int nck = merge_chunks(nblocks, key_extent > 0, key_extent, items_estimate(c, nseg));
   w.ipairs = cv.template take<uint32_t>(nseg * nck);    // steps per (item, key chunk)
   w.rec_base = cv.template take<uint32_t>(nseg * nck);  // their record offsets
   w.rec_total = cv.template take<uint32_t>(1);
@@ -1981,7 +2000,9 @@ bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips,
 // Key blocks: the rhs operand re-read by every strip is split along the
 // contracted range into slices that fit in L2; one launch per slice, in
 // order, later slices adding into the output.
-int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent) {
+int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent, int64_t nseg,
+                  int* l2_blocks) {
+  if (l2_blocks) *l2_blocks = 1;
   if (!have_key || key_extent <= 1) return 1;
   const int64_t panel_bytes = rhs_rows * c.Kt * c.Nt * (c.fp32 ? 8 : 2);
   // EINSPARSE_KBLOCK_BYTES overrides the per-block panel budget (tuning, tests)
@@ -1993,7 +2014,21 @@ int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t ke
   int64_t nb = (panel_bytes + budget - 1) / budget;
   if (nb > key_extent) nb = key_extent;
   if (nb > kMaxKeyBlocks) nb = kMaxKeyBlocks;
-  return nb < 1 ? 1 : static_cast<int>(nb);
+  if (nb < 1) nb = 1;
+  if (l2_blocks) *l2_blocks = static_cast<int>(nb);
+  // the fused launch hands out (key block, item) units; with few items (e.g.
+  // one rank's share of the strips) split the contracted range further so
+  // that every SM gets several units and the launch does not end in a tail
+  if (nb > 1 && nseg > 0) {
+    int dev = 0, sms = kSMs;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t items = items_estimate(c, nseg);
+    const int64_t want = (kUnitsPerSm * sms + items - 1) / items;
+    if (want > nb) nb = want;
+    if (nb > key_extent) nb = key_extent;
+    if (nb > kMaxKeyBlocks) nb = kMaxKeyBlocks;
+  }
+  return static_cast<int>(nb);
 }
 
 size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks,
@@ -2010,7 +2045,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
               int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st) {
   if (nseg <= 0) return ES_OK;
   if (nseg >= INT32_MAX || rhs_rows >= INT32_MAX || lhs_rows >= INT32_MAX) return ES_ERR_UNSUPPORTED;
-  const int nblocks = tc_key_blocks(c, rhs_rows, pair_key != nullptr, key_extent);
+  int l2_blocks = 1;
+  const int nblocks = tc_key_blocks(c, rhs_rows, pair_key != nullptr, key_extent, nseg, &l2_blocks);
   Carver cv(ws, ws_bytes);
   TcWs w;
   tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks, pair_key ? key_extent : 0);
@@ -2070,7 +2106,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   {
     const int S = c.slots;
     const int64_t nslots = (nseg + S - 1) / S;
-    const int C = merge_chunks(nblocks, pair_key != nullptr, key_extent);
+    const int C = merge_chunks(nblocks, pair_key != nullptr, key_extent, items_estimate(c, nseg));
     const int32_t* keys = (c.slots > 1 || C > 1) ? pair_key : nullptr;
     const int64_t nw = nslots * C;
     // grid-stride: nw counts a slot per possible item (most are past the real
@@ -2122,7 +2158,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     // chains only pay for long items: records per item, estimated from the
     // pairs per segment (stacked steps carry about S / 2 lhs tiles)
     const double spp = c.slots > 1 ? c.slots / 2.0 : 1.0;
-    const double recs_per_unit = static_cast<double>(npairs) * spp / static_cast<double>(nseg) / nblocks;
+    const double recs_per_unit = static_cast<double>(npairs) * spp / static_cast<double>(nseg) / l2_blocks;
     if (recs_per_unit < 2.0 * prm.chain_recs) {
       prm.chain_recs = 0;
     } else if (c.fp32 && !c.swap && c.halves * c.col_per_half <= 256) {

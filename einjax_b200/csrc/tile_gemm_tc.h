@@ -49,8 +49,11 @@ struct TcConfig {
 // have_keys: pair_key is available (required for stacked mode).
 bool tc_config(const EinsumDesc& d, int ldt, int rdt, int odt, bool have_strips, bool have_keys, TcConfig* c);
 
-// Launches over the contracted range (one per key block) for these operands.
-int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent);
+// Key blocks of the contracted range for these operands: enough that each
+// block's rhs panel fits in L2 (*l2_blocks), and, for few work items, more so
+// that a fused launch has several (block, item) units per SM.
+int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t key_extent, int64_t nseg,
+                  int* l2_blocks = nullptr);
 
 size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, int64_t nseg, int nblocks,
                          int64_t key_extent);
