@@ -140,10 +140,6 @@ struct TcParams {
                             //    records and the epilogue adds each chain into the
                             //    destination in fp32 (round to nearest), so the tensor
                             //    core's accumulator never sums a long run
-  int l2_prefetch;          // > 0 (a multiple of kRecAhead): the scheduler prefetches the lhs
-                            //    tiles of the record this many records ahead into L2, so
-                            //    the stage's TMA load finds them there (shapes whose record
-                            //    is one short stage, where HBM latency bounds the ring)
   int rn_split;             // fp32: 1 = lo parts rounded to nearest TF32 (lhs: x - trunc(x);
                             //    rhs panel: the tf32_split of x), 0 = truncating split
   float* part;              // fused: per-block partial sums, segment-major rows
@@ -203,11 +199,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -976,23 +967,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
       };
       log_item(re - rb, 0);
       int since = 0;  // records of the current chain
-      // L2 prefetch of lhs tiles: records [rb + kRecAhead, rb + D) now, then
-      // record r + D while record r is issued, its tile index loaded
-      // kRecAhead records earlier (pfv ring, indexed like ahead[])
-      const int D = p.l2_prefetch;
-      const uint32_t tile_bytes = static_cast<uint32_t>(c.Mt) * c.Kt * (F32 ? 4u : 2u);
-      int pfv[kRecAhead];
-      if (D > 0) {
-        if (lane < S) {
-          for (int64_t q = rb + kRecAhead; q < rb + D && q < re; ++q) {
-            const int t = __ldg(p.recs + q * kRecInts + lane);
-            if (t >= 0 && t < p.lhs_rows) prefetch_l2(p.lhs + static_cast<int64_t>(t) * tile_bytes, tile_bytes);
-          }
-        }
-#pragma unroll
-        for (int a = 0; a < kRecAhead; ++a)
-          pfv[a] = (lane < S && rb + D + a < re) ? __ldg(p.recs + (rb + D + a) * kRecInts + lane) : -1;
-      }
       // ahead[] is a ring indexed at compile time (the loop below is
       // unrolled by kRecAhead): record r sits in ahead[r % kRecAhead] and is
       // replaced by record r + kRecAhead as soon as it is read, so no step
@@ -1004,12 +978,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         if (r >= re || aborted) break;
         const int cur = ahead[a];
         ahead[a] = (lane < kRecInts && r + kRecAhead < re) ? __ldg(p.recs + (r + kRecAhead) * kRecInts + lane) : 0;
-        if (D > 0) {
-          const int t = pfv[a];
-          if (lane < S && t >= 0 && t < p.lhs_rows)
-            prefetch_l2(p.lhs + static_cast<int64_t>(t) * tile_bytes, tile_bytes);
-          pfv[a] = (lane < S && r + D + kRecAhead < re) ? __ldg(p.recs + (r + D + kRecAhead) * kRecInts + lane) : -1;
-        }
         ++r;
         const int my_lhs = __shfl_sync(0xffffffffu, cur, lane & (kMaxSlots - 1));  // lanes < S: slot lane
         const int flags = __shfl_sync(0xffffffffu, cur, S + G);
@@ -1774,9 +1742,6 @@ bool fused_blocks_possible(const TcConfig& c, int nblocks, int64_t nseg) {
 // round-to-nearest keeps a long contraction within plain fp32 accuracy.
 constexpr int kChainKsteps = 128;
 
-// Records the scheduler prefetches ahead into L2 when a record is one stage.
-constexpr int kL2PrefetchRecs = 12;
-
 int chain_records(const TcConfig& c) {
   if (!c.fp32) return 0;
   int64_t ks = kChainKsteps;
@@ -2189,10 +2154,6 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.err = err;
   prm.chain_recs = chain_records(c);
   prm.rn_split = rn;
-  // EINSPARSE_L2_PREFETCH=<records> overrides the prefetch distance (0: off)
-  prm.l2_prefetch = c.Kt == c.KC ? kL2PrefetchRecs : 0;
-  if (const char* e = std::getenv("EINSPARSE_L2_PREFETCH")) prm.l2_prefetch = std::atoi(e);
-  prm.l2_prefetch = prm.l2_prefetch <= 0 ? 0 : (prm.l2_prefetch + kRecAhead - 1) / kRecAhead * kRecAhead;
   if (prm.chain_recs > 0) {
     // chains only pay for long items: records per item, estimated from the
     // pairs per segment (stacked steps carry about S / 2 lhs tiles)
