@@ -14,8 +14,9 @@ per second (joined tile-pairs/s is reported beside it).
 * ``e2e``: the same step through the public API with host buffers: pinned
   host -> device copies of the COO arrays and B, and the result tiles copied
   back, all inside the timed region; the copies run on one stream per
-  direction, so step k+1's inputs and step k-1's result move while step k
-  computes (double-buffered device inputs and pinned results).
+  direction and are enqueued while step k's tile GEMM runs (step k+1's
+  inputs, step k-1's result), so they neither wait for nor delay the step's
+  reads of counts (double-buffered device inputs and pinned results).
 * ``--gpus N`` (torchrun, one rank per GPU): strong scaling of the one C2
   problem through output-strip sharding (``execute_sharded_sparse``): rank r
   takes a tile-aligned range of A's rows balanced by non-empty tiles
@@ -354,26 +355,40 @@ def run_ours(args):
         return E.execute_sharded_sparse(A, B, jk, ks, ak, precision=args.precision, lhs_sharded=True,
                                         gather=False)
 
+    def d2h(k, res, done, outs):
+        if outs[k % 2] is None:
+            outs[k % 2] = (torch.empty(res.values.shape, dtype=res.values.dtype, pin_memory=True),
+                           torch.empty(res.coords.shape, dtype=res.coords.dtype, pin_memory=True))
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done)
+            outs[k % 2][0].copy_(res.values, non_blocking=True)
+            outs[k % 2][1].copy_(res.coords, non_blocking=True)
+            res.values.record_stream(s_out)
+            res.coords.record_stream(s_out)
+
     def e2e_run(steps, outs, start):
+        # The step reads counts back from the device a few times before its
+        # tile GEMM and none after it. Copies are enqueued right after a step's
+        # GEMM, so they run under it: the next step's inputs, and the
+        # previous step's result (done long before). A result copy that became
+        # runnable together with the next step's first count read would hold
+        # that 16-byte read behind it on the device-to-host copy engine.
         ev_in, ev_done = [None, None], [None, None]
         ev_in[0] = h2d(0, start)
+        prev = None
         for k in range(steps):
-            if k + 1 < steps:
-                ev_in[(k + 1) % 2] = h2d(k + 1, ev_done[(k + 1) % 2] or start)
             comp.wait_event(ev_in[k % 2])
             res = compute(k)
             done = torch.cuda.Event()
             done.record(comp)
             ev_done[k % 2] = done
-            if outs[k % 2] is None:
-                outs[k % 2] = (torch.empty(res.values.shape, dtype=res.values.dtype, pin_memory=True),
-                               torch.empty(res.coords.shape, dtype=res.coords.dtype, pin_memory=True))
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(done)
-                outs[k % 2][0].copy_(res.values, non_blocking=True)
-                outs[k % 2][1].copy_(res.coords, non_blocking=True)
-                res.values.record_stream(s_out)
-                res.coords.record_stream(s_out)
+            if k + 1 < steps:
+                ev_in[(k + 1) % 2] = h2d(k + 1, ev_done[(k + 1) % 2] if k >= 1 else start)
+            if prev is not None:
+                d2h(k - 1, *prev, outs)
+            prev = (res, done)
+        if prev is not None:
+            d2h(steps - 1, *prev, outs)
         comp.wait_stream(s_out)
         return outs
 
@@ -457,7 +472,8 @@ def run_ours(args):
             "e2e": {"value": round(flops_all / (e2e_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_step, 3),
                     "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
-                    "copies": "one stream per direction, overlapping the neighbouring steps' compute" +
+                    "copies": "one stream per direction, enqueued under each step's tile GEMM (next inputs, "
+                              "previous result)" +
                               ("; each rank copies its A rows and 1/N of B's rows, B is all-gathered over "
                                "NVLink (NCCL) inside the step" if world > 1 else "")},
             "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": "tensor",
