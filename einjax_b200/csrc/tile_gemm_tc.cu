@@ -1711,7 +1711,13 @@ int merge_chunks(int nblocks, bool have_key, int64_t key_extent, int64_t items) 
   }
   if (m > key_extent / nblocks) m = key_extent / nblocks;  // at least one key per chunk
   if (m < 1) m = 1;
-  while (nblocks * m > kMaxMergeChunks) --m;
+  // EINSPARSE_MERGE_MAXCHUNKS overrides the cap on chunks (tuning, tests)
+  int64_t cap = kMaxMergeChunks;
+  if (const char* e = std::getenv("EINSPARSE_MERGE_MAXCHUNKS")) {
+    const long long v = std::atoll(e);
+    if (v > 0) cap = v;
+  }
+  while (nblocks * m > cap) --m;
   if (m < 1) m = 1;
   return static_cast<int>(nblocks * m);
 }
@@ -2023,7 +2029,13 @@ int tc_key_blocks(const TcConfig& c, int64_t rhs_rows, bool have_key, int64_t ke
     int dev = 0, sms = kSMs;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int64_t items = items_estimate(c, nseg);
-    const int64_t want = (kUnitsPerSm * sms + items - 1) / items;
+    // EINSPARSE_UNITS_PER_SM overrides the units per SM (tuning, tests)
+    int64_t per_sm = kUnitsPerSm;
+    if (const char* e = std::getenv("EINSPARSE_UNITS_PER_SM")) {
+      const long long v = std::atoll(e);
+      if (v > 0) per_sm = v;
+    }
+    const int64_t want = (per_sm * sms + items - 1) / items;
     if (want > nb) nb = want;
     if (nb > key_extent) nb = key_extent;
     if (nb > kMaxKeyBlocks) nb = kMaxKeyBlocks;
