@@ -274,8 +274,12 @@ def run_ours(args):
     def step(idx, val, b, timing=False, marks=None):
         E.sparse.mark(marks, "s0")
         A = E.tile_coo(idx, val, shape, (TILE, TILE))
+        if marks is not None:
+            A.materialize()  # the phase split times each tiling with its value fill
         E.sparse.mark(marks, "s1")
         B = E.tile_dense(b, (TILE, TILE))
+        if marks is not None:
+            B.materialize()
         E.sparse.mark(marks, "s2")
         plan = SD.plan_pairs(A, B, jk, ak)
         E.sparse.mark(marks, "s3")
@@ -868,7 +872,7 @@ def hbm_kernels(idx_d, val_d, b_d, shape, jk, ak, hbm, reps=3):
     del ci, cv
     out["coo_coalesce"] = entry(statistics.median(t), nnz * (2 * 4 + 4) + U * (2 * 4 + 8),
                                 "nnz x 12 read + U x (8 + 8) written (float64 sums); one 64-bit key sort between")
-    B = E.tile_dense(b_d, (TILE, TILE))
+    B = E.tile_dense(b_d, (TILE, TILE)).materialize()
     t = []
     for _ in range(reps):
         m = []

@@ -151,14 +151,18 @@ __device__ __forceinline__ int lex_cmp(const int32_t* a, const int32_t* b, int n
   return 0;
 }
 
-// Clears the table (-1), the column flags and the order flag.
+// Clears the table (-1), the column flags, the order flag and the caller's
+// status slot.
 __global__ void direct_init_kernel(int32_t* __restrict__ table, int64_t tn, uint32_t* __restrict__ colflag,
-                                   int64_t cext, int32_t* __restrict__ bad) {
+                                   int64_t cext, int32_t* __restrict__ bad, int32_t* __restrict__ err) {
   const int64_t n = tn > cext ? tn : cext;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     if (i < tn) table[i] = -1;
     if (i < cext) colflag[i] = 0u;
-    if (i == 0) *bad = 0;
+    if (i == 0) {
+      *bad = 0;
+      if (err) *err = 0;
+    }
   }
 }
 
@@ -449,7 +453,7 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   if (cv.overflow) return ES_ERR_WORKSPACE;
   const int64_t tn = g.kext * g.cext;
   ES_LAUNCH(direct_init_kernel, grid_for(tn > g.cext ? tn : g.cext, 256), 256, 0, st, w.table, tn, w.colflag, g.cext,
-            w.bad);
+            w.bad, error_dev);
   ES_LAUNCH(direct_inputs_kernel, grid_for(n_rhs + n_lhs, 256), 256, 0, st, rhs_coords, n_rhs, lhs_coords, n_lhs, g,
             w.table, w.colflag, w.sflag, w.bad, error_dev);
   ES_TRY(exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, w.scan, st));

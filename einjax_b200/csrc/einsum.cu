@@ -410,9 +410,11 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
   if (out_dtype != ES_F32 && out_dtype != ES_BF16) return ES_ERR_UNSUPPORTED;
   auto ok_in = [](int t) { return t == ES_F32 || t == ES_BF16 || t == ES_F64; };
   if (!ok_in(lhs_dtype) || !ok_in(rhs_dtype)) return ES_ERR_UNSUPPORTED;
+  cudaStream_t st = as_stream(stream);
+  // the status slot needs no initialisation by the caller
+  if (error_dev && cudaMemsetAsync(error_dev, 0, sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
   const int64_t nseg = seg_offsets ? num_segments : num_pairs;
   if (nseg <= 0 || num_pairs <= 0) return ES_OK;
-  cudaStream_t st = as_stream(stream);
   if (want_tc(precision)) {
     TcConfig c;
     TcVariant v;

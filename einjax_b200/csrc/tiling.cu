@@ -151,7 +151,8 @@ __global__ void tile_heads_kernel(const TileHeader* hdr, const uint64_t* k0, con
 }
 
 // One pass over the sorted entries (s = 0 .. n):
-// * a tile's first entry writes the tile's coordinates (coords row excl[s]);
+// * a tile's first entry writes the tile's coordinates (coords row excl[s];
+//   skipped when coords is null);
 // * chunk_start[c] = first sorted entry whose output position lies in chunk c,
 //   chunk_start[num_chunks] = number of valid entries.
 __global__ void tile_coords_bounds_kernel(const TileHeader* hdr, const uint64_t* k0, const uint64_t* k1, int64_t n,
@@ -171,7 +172,7 @@ __global__ void tile_coords_bounds_kernel(const TileHeader* hdr, const uint64_t*
     int64_t prev = s == 0 ? -1 : chunk_of(s - 1);
     int64_t cur = s == n ? num_chunks : chunk_of(s);
     for (int64_t c = prev + 1; c <= cur; ++c) chunk_start[c] = s;
-    if (s < n && flags[s]) {
+    if (coords && s < n && flags[s]) {
       uint64_t tl = udiv(keys[s], te, g.te_sh);
       const int64_t t = excl[s];
       for (int d = g.ndim - 1; d >= 0; --d) {
@@ -278,59 +279,72 @@ __global__ void dense_flags_kernel(const void* __restrict__ dense, int dtype, Ti
   }
 }
 
+// Coordinates of the non-zero tiles: thread t writes grid tile t's row
+// excl[t] when flags[t] is set.
+__global__ void dense_coords_kernel(TileGeom g, const uint32_t* __restrict__ flags,
+                                    const uint32_t* __restrict__ excl, int32_t* __restrict__ coords) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < g.grid_tiles;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    if (!flags[t]) continue;
+    const int64_t r = excl[t];
+    int64_t tl = t;
+    for (int d = g.ndim - 1; d >= 0; --d) {
+      const int64_t q = static_cast<int64_t>(udiv(tl, g.grid[d], g.grid_sh[d]));
+      coords[r * g.ndim + d] = static_cast<int32_t>(tl - q * g.grid[d]);
+      tl = q;
+    }
+  }
+}
+
+// Values of the non-zero tiles, any input dtype: one block per grid tile at a
+// time, row excl[t] of out.
 template <typename OutT>
 __global__ void dense_fill_kernel(const void* __restrict__ dense, int dtype, TileGeom g,
                                   const uint32_t* __restrict__ flags, const uint32_t* __restrict__ excl,
-                                  int32_t* __restrict__ coords, OutT* __restrict__ out) {
+                                  OutT* __restrict__ out) {
   for (int64_t t = blockIdx.x; t < g.grid_tiles; t += gridDim.x) {
     if (!flags[t]) continue;
     const int64_t r = excl[t];
-    if (threadIdx.x < g.ndim) {
-      int64_t tl = t;
-      for (int d = g.ndim - 1; d >= 0; --d) {
-        if (d == (int)threadIdx.x) coords[r * g.ndim + d] = static_cast<int32_t>(tl % g.grid[d]);
-        tl /= g.grid[d];
-      }
-    }
     for (int64_t e = threadIdx.x; e < g.tile_elems; e += blockDim.x)
       out[r * g.tile_elems + e] = cvt_out<OutT>(load_as_f32(dense, dtype, dense_offset(g, t, e)));
   }
 }
 
-// fp32 -> fp32 with tile rows and dense rows in whole 16-byte pieces (both
-// arrays 16-byte aligned): four consecutive elements of a tile row are four
-// consecutive floats of the dense array, so each thread moves 16-byte pieces,
-// all of a tile's loads issued before its stores.
+// fp32 -> fp32 in whole 16-byte pieces (both arrays 16-byte aligned, tile
+// rows a multiple of four floats, so four consecutive elements of a tile row
+// are four consecutive floats of the dense array). A block takes
+// kDenseBatch consecutive grid tiles at a time; each thread keeps kPer
+// pieces of them in flight, all loads of a round issued before its stores.
+constexpr int kDenseBatch = 4;
+
 __global__ void __launch_bounds__(256) dense_fill_vec_kernel(const float* __restrict__ dense, TileGeom g,
                                                              const uint32_t* __restrict__ flags,
                                                              const uint32_t* __restrict__ excl,
-                                                             int32_t* __restrict__ coords, float* __restrict__ out) {
-  constexpr int kPer = 4;  // 16-byte pieces per thread in flight
-  const int64_t pieces = g.tile_elems / 4;
-  for (int64_t t = blockIdx.x; t < g.grid_tiles; t += gridDim.x) {
-    if (!flags[t]) continue;
-    const int64_t r = excl[t];
-    if (threadIdx.x < g.ndim) {
-      int64_t tl = t;
-      for (int d = g.ndim - 1; d >= 0; --d) {
-        const int64_t q = static_cast<int64_t>(udiv(tl, g.grid[d], g.grid_sh[d]));
-        if (d == (int)threadIdx.x) coords[r * g.ndim + d] = static_cast<int32_t>(tl - q * g.grid[d]);
-        tl = q;
-      }
-    }
-    float4* o = reinterpret_cast<float4*>(out + r * g.tile_elems);
-    for (int64_t p0 = threadIdx.x; p0 < pieces; p0 += static_cast<int64_t>(blockDim.x) * kPer) {
+                                                             float* __restrict__ out) {
+  constexpr int kPer = 4;
+  const uint32_t pieces = static_cast<uint32_t>(g.tile_elems / 4);
+  const uint32_t span = pieces * kDenseBatch;
+  for (int64_t t0 = blockIdx.x * static_cast<int64_t>(kDenseBatch); t0 < g.grid_tiles;
+       t0 += static_cast<int64_t>(gridDim.x) * kDenseBatch) {
+    for (uint32_t q0 = threadIdx.x; q0 < span; q0 += blockDim.x * kPer) {
       float4 v[kPer];
+      int64_t dst[kPer];
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
-        const int64_t p = p0 + static_cast<int64_t>(j) * blockDim.x;
-        if (p < pieces) v[j] = *reinterpret_cast<const float4*>(dense + dense_offset(g, t, 4 * p));
+        dst[j] = -1;
+        const uint32_t q = q0 + j * blockDim.x;
+        if (q < span) {
+          const uint32_t bt = q / pieces, p = q - bt * pieces;
+          const int64_t t = t0 + bt;
+          if (t < g.grid_tiles && flags[t]) {
+            v[j] = *reinterpret_cast<const float4*>(dense + dense_offset(g, t, 4 * static_cast<int64_t>(p)));
+            dst[j] = static_cast<int64_t>(excl[t]) * pieces + p;
+          }
+        }
       }
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int64_t p = p0 + static_cast<int64_t>(j) * blockDim.x;
-        if (p < pieces) o[p] = v[j];
-      }
+      for (int j = 0; j < kPer; ++j)
+        if (dst[j] >= 0) reinterpret_cast<float4*>(out)[dst[j]] = v[j];
     }
   }
 }
@@ -376,6 +390,8 @@ extern "C" int es_tile_coo_plan(const int32_t* indices, const void* values, int 
   if (nnz < 0 || nnz >= (int64_t)UINT32_MAX) return ES_ERR_UNSUPPORTED;
   if (values_dtype != ES_F32 && values_dtype != ES_F64 && values_dtype != ES_BF16) return ES_ERR_UNSUPPORTED;
   cudaStream_t st = as_stream(stream);
+  // the status slot needs no initialisation by the caller
+  if (error_dev && cudaMemsetAsync(error_dev, 0, sizeof(int32_t), st) != cudaSuccess) return ES_ERR_CUDA;
   if (nnz == 0) {
     if (cudaMemsetAsync(num_tiles_dev, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
     return ES_OK;
@@ -413,8 +429,13 @@ extern "C" int es_tile_coo_fill(const void* values, int values_dtype, int64_t nn
   const int64_t total_out = num_tiles * g.tile_elems;
   const int64_t num_chunks = (total_out + kChunk - 1) / kChunk;
   if (num_chunks > max_chunks_for(nnz, g.tile_elems)) return ES_ERR_INVALID;
-  ES_LAUNCH(tile_coords_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz,
-            w.flags, w.excl, g, sentinel, num_chunks, coords_out, w.chunk_start);
+  // coords_out null: the values alone, from the chunk bounds an earlier call
+  // with coords_out left in this workspace; values_out null: coords (and the
+  // bounds) alone
+  if (coords_out)
+    ES_LAUNCH(tile_coords_bounds_kernel, grid_for(nnz + 1, 256), 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, nnz,
+              w.flags, w.excl, g, sentinel, num_chunks, coords_out, w.chunk_start);
+  if (!values_out) return ES_OK;
   const int vec_ok = (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0 ? 1 : 0;
   if (out_dtype == ES_F32) {
     ES_LAUNCH(densify_kernel<float>, (int)num_chunks, 256, 0, st, w.hdr, w.keys, w.rb.keys_alt, w.perm,
@@ -468,18 +489,25 @@ extern "C" int es_tile_dense_fill(const void* dense, int dtype, int ndim, const 
   DenseWs w;
   dense_layout(c, w, g.grid_tiles);
   if (c.overflow) return ES_ERR_WORKSPACE;
+  // coords_out / values_out null: that output is not written
+  if (coords_out)
+    ES_LAUNCH(dense_coords_kernel, grid_for(g.grid_tiles, 256), 256, 0, st, g, w.flags, w.excl, coords_out);
+  if (!values_out) return ES_OK;
   const int grid = static_cast<int>(g.grid_tiles < 148 * 16 ? g.grid_tiles : 148 * 16);
   const bool vec = dtype == ES_F32 && out_dtype == ES_F32 && g.tile[ndim - 1] % 4 == 0 &&
-                   g.shape[ndim - 1] % 4 == 0 && (reinterpret_cast<uintptr_t>(dense) & 15u) == 0 &&
+                   g.shape[ndim - 1] % 4 == 0 && g.tile_elems < (1LL << 28) &&
+                   (reinterpret_cast<uintptr_t>(dense) & 15u) == 0 &&
                    (reinterpret_cast<uintptr_t>(values_out) & 15u) == 0;
-  if (vec)
-    ES_LAUNCH(dense_fill_vec_kernel, grid, 256, 0, st, static_cast<const float*>(dense), g, w.flags, w.excl,
-              coords_out, static_cast<float*>(values_out));
-  else if (out_dtype == ES_F32)
-    ES_LAUNCH(dense_fill_kernel<float>, grid, 256, 0, st, dense, dtype, g, w.flags, w.excl, coords_out,
+  if (vec) {
+    const int64_t nb = (g.grid_tiles + kDenseBatch - 1) / kDenseBatch;
+    ES_LAUNCH(dense_fill_vec_kernel, static_cast<int>(nb < 148 * 16 ? nb : 148 * 16), 256, 0, st,
+              static_cast<const float*>(dense), g, w.flags, w.excl, static_cast<float*>(values_out));
+  } else if (out_dtype == ES_F32) {
+    ES_LAUNCH(dense_fill_kernel<float>, grid, 256, 0, st, dense, dtype, g, w.flags, w.excl,
               static_cast<float*>(values_out));
-  else
-    ES_LAUNCH(dense_fill_kernel<__nv_bfloat16>, grid, 256, 0, st, dense, dtype, g, w.flags, w.excl, coords_out,
+  } else {
+    ES_LAUNCH(dense_fill_kernel<__nv_bfloat16>, grid, 256, 0, st, dense, dtype, g, w.flags, w.excl,
               static_cast<__nv_bfloat16*>(values_out));
+  }
   return ES_OK;
 }

@@ -10,7 +10,6 @@ GPU through ``es_tile_coo_*`` / ``es_tile_dense_*``.
 
 from __future__ import annotations
 
-from dataclasses import dataclass
 from math import prod
 from typing import Any
 
@@ -36,8 +35,19 @@ def default_device() -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def _device_index(device) -> int:
+    if isinstance(device, torch.device):
+        return device.index if device.index is not None else torch.cuda.current_device()
+    return torch.cuda.current_device() if device is None else int(device)
+
+
 def stream_ptr(device=None) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """cudaStream_t of the current stream of ``device``."""
+    return _raw_stream(_device_index(device))
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or (
+    lambda i: torch.cuda.current_stream(i).cuda_stream)
 
 
 def workspace(nbytes: int, device) -> torch.Tensor:
@@ -111,10 +121,130 @@ def check_device_errors() -> None:
     _DEFERRED.flush()
 
 
-def read_counts(t: torch.Tensor):
-    """Read a small device int64 tensor (count, error, ...) with one sync;
-    deferred error slots of earlier calls are checked at the same time."""
-    vals = [int(v) for v in t.tolist()]
+class _PendingFills:
+    """Relations whose tile values are not written yet, oldest first.
+
+    The tiling calls write a relation's coordinates at once and queue the
+    launch of its value fill here. The pair plan's count reads launch the
+    queued fills between the copy of their counts and their wait, so the GPU
+    fills tiles (the largest writes of a step) while the host waits for the
+    counts and then sizes and launches what follows; a relation's first
+    ``values`` access launches its own fill."""
+
+    def __init__(self):
+        self.rels = []  # weak references, creation order
+
+    def add(self, rel) -> None:
+        import weakref
+        self.rels.append(weakref.ref(rel))
+
+    def __bool__(self) -> bool:
+        return bool(self.rels)
+
+    def flush(self) -> None:
+        rels, self.rels = self.rels, []
+        for r in rels:
+            rel = r()
+            if rel is not None:
+                rel.materialize()
+
+
+_PENDING = _PendingFills()
+
+
+class _PendingTilings:
+    """Tile counts of tiling calls not read yet. Each call copies its counts
+    into a slot of a pinned ring right after its plan launches and records
+    an event (no wait); the first use of any such relation waits for the
+    copies and resolves every pending tiling in call order."""
+
+    SLOTS = 1024
+
+    def __init__(self):
+        self.host = None
+        self.next = 0
+        self.items = []  # (weak relation, slot, n, event)
+
+    def add(self, rel, counts: torch.Tensor) -> None:
+        import weakref
+        n = int(counts.numel())
+        if self.host is None:
+            self.host = torch.empty(self.SLOTS, dtype=torch.int64, pin_memory=True)
+        if self.next + n > self.SLOTS:
+            self.resolve_all()
+            self.next = 0
+        slot = self.next
+        self.next += n
+        self.host[slot:slot + n].copy_(counts, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.items.append((weakref.ref(rel), slot, n, ev))
+
+    def __bool__(self) -> bool:
+        return bool(self.items)
+
+    def resolve_all(self) -> None:
+        items, self.items = self.items, []
+        if not items:
+            return
+        for _, _, _, ev in items:
+            ev.synchronize()
+        vals = self.host[:max(slot + n for _, slot, n, _ in items)].tolist()
+        self.next = 0
+        for r, slot, n, _ in items:
+            rel = r()
+            if rel is not None and rel._finish is not None:
+                rel._complete(vals[slot:slot + n])
+
+
+_TILINGS = _PendingTilings()
+
+
+def resolve_tilings() -> None:
+    """Read the tile counts of every unresolved relation (one wait) and
+    launch their coordinate writes."""
+    _TILINGS.resolve_all()
+
+
+def launch_pending_fills() -> None:
+    """Launch the value fills of every relation whose values are pending
+    (stream-ordered like any launch; nothing waits)."""
+    _PENDING.flush()
+
+
+class _CountReader:
+    """Pinned host buffer for count reads: the copy goes in asynchronously,
+    pending fills are launched behind it, and the host waits on an event
+    recorded right after the copy, not on the whole stream."""
+
+    def __init__(self):
+        self.host = None
+
+    def read(self, t: torch.Tensor, launch_pending: bool):
+        n = int(t.numel())
+        if self.host is None or self.host.numel() < n:
+            self.host = torch.empty(max(n, 16), dtype=torch.int64, pin_memory=True)
+        h = self.host[:n]
+        h.copy_(t.reshape(-1).to(torch.int64), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        if launch_pending and _PENDING:
+            _PENDING.flush()
+        ev.synchronize()
+        return [int(v) for v in h.tolist()]
+
+
+_COUNTS = _CountReader()
+
+
+def read_counts(t: torch.Tensor, launch_pending: bool = False):
+    """Read a small device int64 tensor (count, error, ...): one wait, on the
+    copy alone; deferred error slots of earlier calls are checked after it.
+    ``launch_pending``: launch the pending value fills behind the copy first
+    (the pair plan's reads do, since the most host work of a contraction --
+    sizing the pairs and launching the tile einsum -- follows them, and the
+    fills keep the GPU busy meanwhile)."""
+    vals = _COUNTS.read(t, launch_pending)
     if _DEFERRED.pending:
         _DEFERRED.flush()
     return vals
@@ -127,18 +257,115 @@ def value_dtype_for(dtype) -> torch.dtype:
     return torch.float32
 
 
-@dataclass
 class SparseTensorRelation:
-    """Tile-COO relation held on the GPU (``tensor/sparse.py:27-90``)."""
+    """Tile-COO relation held on the GPU (``tensor/sparse.py:27-90``).
 
-    coords: torch.Tensor
-    values: torch.Tensor
-    shape: tuple
-    tile_shape: tuple
+    ``tile_coo`` and ``tile_dense`` return relations in two deferred states.
+    Unresolved: the tile count is still on its way to the host; the first
+    use of ``coords``, ``values`` or ``num_tuples`` of any unresolved
+    relation waits once and resolves all of them (allocation and coordinate
+    launch), so the operands of a contraction share one host wait; a bad
+    input (e.g. a COO index outside the shape) raises there. Pending
+    values: the value fill is launched by the first read of ``values``, by
+    ``materialize()``, or by the next count read of a pair plan
+    (``plan_pairs``), whichever comes first; it reads the tiling's input
+    until then, and raises if that input was changed in place meanwhile."""
 
-    def __post_init__(self):
-        self.shape = tuple(int(s) for s in self.shape)
-        self.tile_shape = tuple(int(t) for t in self.tile_shape)
+    __slots__ = ("_coords", "_values", "shape", "tile_shape", "_pending", "_finish", "_failed", "_dev",
+                 "__weakref__")
+
+    def __init__(self, coords: torch.Tensor, values: torch.Tensor, shape, tile_shape, pending=None):
+        self._coords = coords
+        self._values = values
+        self.shape = tuple(int(s) for s in shape)
+        self.tile_shape = tuple(int(t) for t in tile_shape)
+        self._pending = pending
+        self._finish = None
+        self._failed = None
+        self._dev = None
+        if pending is not None:
+            _PENDING.add(self)
+
+    @classmethod
+    def _unresolved(cls, shape, tile_shape, device, counts: torch.Tensor, finish) -> "SparseTensorRelation":
+        """A relation whose tile count is on the device (``counts``):
+        ``finish(host_counts)`` returns ``(coords, values, pending_fill)``."""
+        rel = cls(None, None, shape, tile_shape)
+        rel._finish = finish
+        rel._dev = device
+        _TILINGS.add(rel, counts)
+        return rel
+
+    def _resolve(self) -> None:
+        if self._finish is not None:
+            _TILINGS.resolve_all()
+        if self._failed is not None:
+            raise self._failed
+
+    def _complete(self, host_counts) -> None:
+        finish, self._finish = self._finish, None
+        try:
+            coords, values, pending = finish(host_counts)
+        except Exception as e:  # kept: every later use raises it again
+            self._failed = e
+            return
+        self._coords, self._values = coords, values
+        if pending is not None:
+            self._pending = pending
+            _PENDING.add(self)
+
+    @property
+    def coords(self) -> torch.Tensor:
+        if self._finish is not None or self._failed is not None:
+            self._resolve()
+        return self._coords
+
+    @coords.setter
+    def coords(self, c: torch.Tensor) -> None:
+        self._finish = self._failed = None
+        self._coords = c
+
+    @property
+    def values(self) -> torch.Tensor:
+        if self._finish is not None or self._failed is not None:
+            self._resolve()
+        if self._pending is not None:
+            self.materialize()
+        return self._values
+
+    @values.setter
+    def values(self, v: torch.Tensor) -> None:
+        self._pending = None
+        self._values = v
+
+    @property
+    def pending(self) -> bool:
+        """True while the tile count is unread or the value fill has not been
+        launched."""
+        return self._finish is not None or self._pending is not None
+
+    def materialize_count(self) -> "SparseTensorRelation":
+        """Resolve the tile count (and with it every unresolved relation);
+        the value fill stays pending."""
+        if self._finish is not None or self._failed is not None:
+            self._resolve()
+        return self
+
+    def materialize(self) -> "SparseTensorRelation":
+        """Resolve the tile count and launch the pending value fill (no-op
+        when neither is pending)."""
+        if self._finish is not None or self._failed is not None:
+            self._resolve()
+        fill, self._pending = self._pending, None
+        if fill is not None:
+            fill()
+        return self
+
+    def __repr__(self) -> str:
+        if self._finish is not None:
+            return f"SparseTensorRelation(unresolved, shape={self.shape}, tile_shape={self.tile_shape})"
+        return (f"SparseTensorRelation(tuples={self.num_tuples}, shape={self.shape}, "
+                f"tile_shape={self.tile_shape}, dtype={self._values.dtype}, pending={self.pending})")
 
     @property
     def num_tuples(self) -> int:
@@ -163,7 +390,7 @@ class SparseTensorRelation:
 
     @property
     def device(self) -> torch.device:
-        return self.values.device
+        return self._dev if self._finish is not None else self.coords.device
 
     def grid(self) -> tuple:
         """Tile-grid extent per dimension (ceil(shape / tile), at least 1)."""
@@ -297,6 +524,14 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
     (``coalesce_coo`` first), ``"error"`` raises ``ValueError``. ``marks``:
     see ``mark`` (plan0/plan1 around the plan launches, fill0/fill1 around the
     fill).
+
+    The relation comes back unresolved (``SparseTensorRelation``): the tile
+    count is read, and an index outside ``shape`` raises ``ValueError``, at
+    its first use, together with every other unresolved relation; the tile
+    values are then a pending fill launched at the first use of ``values``
+    or the next pair plan's count read. ``values`` (the input) must stay
+    unchanged until then (``materialize()`` does both now). With ``marks``
+    the tiling is complete before returning.
     """
     if duplicates not in DUPLICATE_POLICIES:
         raise ValueError(f"duplicates must be one of {DUPLICATE_POLICIES}, got {duplicates!r}")
@@ -319,28 +554,67 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
     nd = len(shape)
     wsb = lib.es_tile_coo_workspace_size(nnz, nd, sh, tl)
     ws = workspace(wsb, dev)
-    cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+    cnt = torch.empty(2, dtype=torch.int64, device=dev)  # cleared by the plan call
     st = stream_ptr(dev)
     mark(marks, "plan0")
     L.check("es_tile_coo_plan", lib.es_tile_coo_plan(
         idx.data_ptr(), vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(),
         cnt.data_ptr(), cnt[1:].data_ptr(), st))
     mark(marks, "plan1")
-    T, err = read_counts(cnt)
-    L.device_error("es_tile_coo_plan", err, "COO index outside the tensor shape")
-    coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
-    out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+    oc = L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16
+    vd = es_dtype(vals)
+    stream = torch.cuda.current_stream(dev)
+    version = vals._version
+
+    def finish(counts):
+        T, err = counts
+        L.device_error("es_tile_coo_plan", err, "COO index outside the tensor shape")
+        with _on(stream):
+            coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
+            out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+            L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
+                vals.data_ptr(), vd, nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), None, oc,
+                stream.cuda_stream))
+
+        def launch(sp):
+            L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
+                vals.data_ptr(), vd, nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T, None, out.data_ptr(), oc, sp))
+        return coords, out, (_deferred_fill(dev, vals, launch, "tile_coo", stream, version) if T > 0 else None)
+
+    if marks is None:
+        return SparseTensorRelation._unresolved(shape, tile_shape, dev, cnt, finish)
+    # timed callers get the tiling done now, between their marks
+    coords, out, fill = finish(read_counts(cnt))
     mark(marks, "fill0")
-    L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
-        vals.data_ptr(), es_dtype(vals), nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T,
-        coords.data_ptr(), out.data_ptr(), L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16, st))
+    if fill is not None:
+        fill()
     mark(marks, "fill1")
     return SparseTensorRelation(coords, out, shape, tile_shape)
 
 
+class _on:
+    """``torch.cuda.stream(s)`` when ``s`` is not already current (entering
+    the context costs a few microseconds)."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self.ctx = None
+
+    def __enter__(self):
+        if _raw_stream(self.stream.device_index) != self.stream.cuda_stream:
+            self.ctx = torch.cuda.stream(self.stream)
+            self.ctx.__enter__()
+
+    def __exit__(self, *a):
+        if self.ctx is not None:
+            self.ctx.__exit__(*a)
+
+
 def tile_dense(dense: torch.Tensor, tile_shape, out_dtype=torch.float32) -> SparseTensorRelation:
     """Dense device array -> tile-COO of its non-zero tiles (``to_relation`` of a
-    dense ``SparseTensor``, ``tensor/sparse.py:104-117,160-219``)."""
+    dense ``SparseTensor``, ``tensor/sparse.py:104-117,160-219``). As with
+    ``tile_coo``, the relation comes back unresolved and its values are a
+    pending fill that reads ``dense`` when it runs."""
     shape = tuple(int(s) for s in dense.shape)
     tile_shape = tuple(int(t) for t in tile_shape)
     _check_divisible(shape, tile_shape)
@@ -350,17 +624,47 @@ def tile_dense(dense: torch.Tensor, tile_shape, out_dtype=torch.float32) -> Spar
     sh, tl = L.i64arr(shape), L.i64arr(tile_shape)
     nd = len(shape)
     ws = workspace(lib.es_tile_dense_workspace_size(nd, sh, tl), dev)
-    cnt = torch.zeros(1, dtype=torch.int64, device=dev)
+    cnt = torch.empty(1, dtype=torch.int64, device=dev)  # cleared by the plan call
     st = stream_ptr(dev)
     L.check("es_tile_dense_plan", lib.es_tile_dense_plan(
         d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), cnt.data_ptr(), st))
-    T = read_counts(cnt)[0]
-    coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
-    out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
-    L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
-        d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), out.data_ptr(),
-        L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16, st))
-    return SparseTensorRelation(coords, out, shape, tile_shape)
+    oc = L.ES_F32 if out_dtype == torch.float32 else L.ES_BF16
+    stream = torch.cuda.current_stream(dev)
+    version = d._version
+
+    def finish(counts):
+        T = counts[0]
+        with _on(stream):
+            coords = torch.empty((T, nd), dtype=torch.int32, device=dev)
+            out = torch.empty((T, *tile_shape), dtype=out_dtype, device=dev)
+            L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
+                d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), None, oc,
+                stream.cuda_stream))
+
+        def launch(sp):
+            L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
+                d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, None, out.data_ptr(), oc, sp))
+        return coords, out, (_deferred_fill(dev, d, launch, "tile_dense", stream, version) if T > 0 else None)
+
+    return SparseTensorRelation._unresolved(shape, tile_shape, dev, cnt, finish)
+
+
+def _deferred_fill(dev, source: torch.Tensor, launch, name: str, stream, version: int):
+    """Pending value fill of a tiling call: ``launch(stream)`` runs on the
+    tiling's stream (the one its coordinates went out on), and a caller on
+    another stream then waits for it. ``source``, the tiling's input, must
+    not be changed in place before the fill runs (checked through its
+    version counter against ``version``, taken when the tiling was called)."""
+
+    def fill():
+        if source._version != version:
+            raise RuntimeError(f"{name}: the input was changed in place before the tile values were filled; "
+                               "call materialize() on the relation before changing it")
+        launch(stream.cuda_stream)
+        cur = torch.cuda.current_stream(dev)
+        if cur != stream:
+            cur.wait_stream(stream)
+    return fill
 
 
 def _extract_coo(data: Any):
@@ -520,6 +824,9 @@ class SparseTensor:
             val = as_device_tensor(self._b).to(self.device, non_blocking=True)
             if val.dtype not in _TORCH_TO_ES:
                 val = val.to(torch.float64)
-            return tile_coo(idx, val, self.shape, tile_shape, self._out_dtype, duplicates=self.duplicates)
+            # resolved here, so that bad input raises from to_relation as in
+            # the reference; the values stay a pending fill
+            return tile_coo(idx, val, self.shape, tile_shape, self._out_dtype,
+                            duplicates=self.duplicates).materialize_count()
         dense = self._a if torch.is_tensor(self._a) else torch.from_numpy(np.ascontiguousarray(self._a))
-        return tile_dense(dense.to(self.device, non_blocking=True), tile_shape, self._out_dtype)
+        return tile_dense(dense.to(self.device, non_blocking=True), tile_shape, self._out_dtype).materialize_count()

@@ -91,7 +91,7 @@ def _join_int32(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys)
     L.check("es_join_plan", lib.es_join_plan(
         lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, L.i32arr(flat), len(keys), L.i64arr(ext),
         ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt[1:].data_ptr(), st))
-    P, err = read_counts(cnt)
+    P, err = read_counts(cnt, launch_pending=True)
     L.device_error("es_join_plan", err, "tile coordinate outside the relation's tile grid")
     li = torch.empty(P, dtype=torch.int32, device=dev)
     ri = torch.empty(P, dtype=torch.int32, device=dev)
@@ -120,6 +120,25 @@ def _es_out(dt):
     return L.ES_BF16 if dt == torch.bfloat16 else L.ES_F32
 
 
+_OUT_TILES = {}
+
+
+def _out_tile(kernel_string, lt, rt):
+    """(encoded kernel string, output tile shape) of a tile einsum, cached."""
+    key = (kernel_string, lt, rt)
+    hit = _OUT_TILES.get(key)
+    if hit is None:
+        ks = kernel_string.replace(" ", "").encode()
+        ot = L.i64arr([0] * 8)
+        nd = L.lib().es_out_tile_shape(ks, L.i64arr(lt), len(lt), L.i64arr(rt), len(rt), ot)
+        if nd < 0:
+            raise ValueError(f"invalid kernel string {kernel_string!r} for tiles {lt} and {rt}")
+        hit = (ks, tuple(int(ot[i]) for i in range(nd)))
+        if len(_OUT_TILES) < 4096:
+            _OUT_TILES[key] = hit
+    return hit
+
+
 def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_offsets=None, seg_out_index=None,
                 out=None, num_out_rows=None, out_dtype=None, precision="auto", seg_strip=None, pair_key=None,
                 key_extent=0, check=True):
@@ -140,12 +159,7 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     dev = lhs_values.device
     lt = tuple(lhs_values.shape[1:])
     rt = tuple(rhs_values.shape[1:])
-    ks = kernel_string.replace(" ", "").encode()
-    ot = L.i64arr([0] * 8)
-    nd = lib.es_out_tile_shape(ks, L.i64arr(lt), len(lt), L.i64arr(rt), len(rt), ot)
-    if nd < 0:
-        raise ValueError(f"invalid kernel string {kernel_string!r} for tiles {lt} and {rt}")
-    out_tile = tuple(int(ot[i]) for i in range(nd))
+    ks, out_tile = _out_tile(kernel_string, lt, rt)
     P = int(pair_lhs.shape[0])
     nseg = int(seg_offsets.shape[0]) - 1 if seg_offsets is not None else P
     odt = out_dtype or _out_dtype(lhs_values.dtype, rhs_values.dtype)
@@ -167,7 +181,7 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     wsb = lib.es_tile_einsum_workspace_size(ks, lti, len(lt), rti, len(rt), es_dtype(lv), es_dtype(rv),
                                             int(lv.shape[0]), int(rv.shape[0]), P, nseg, kext, prec)
     ws = workspace(wsb, dev) if wsb else None
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.empty(1, dtype=torch.int32, device=dev)  # cleared by the call
     L.check("es_tile_einsum", lib.es_tile_einsum(
         ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
         int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
@@ -326,17 +340,19 @@ def _direct_shape(lhs, rhs, join_keys, agg_keys) -> bool:
     return _direct_batch_dims(lhs, rhs, join_keys, agg_keys) is not None
 
 
-def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None):
+def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None, nb=None):
     """Join + grouping without sorts (``es_direct_*``); None when a relation
     is not in lexicographic order (the general path then runs). ``marks``:
-    see ``sparse.mark``."""
+    see ``sparse.mark``; ``nb``: ``_direct_batch_dims`` when known."""
     dev = lhs.device
     lib = L.lib()
-    nb = _direct_batch_dims(lhs, rhs, join_keys, agg_keys)
+    if nb is None:
+        nb = _direct_batch_dims(lhs, rhs, join_keys, agg_keys)
     lg, rg = L.i64arr(lhs.grid()), L.i64arr(rhs.grid())
     nl, nr = lhs.num_tuples, rhs.num_tuples
     ws = workspace(lib.es_direct_workspace_size(nl, lhs.ndim, nr, rhs.ndim, nb, lg, rg), dev)
-    cnt = torch.zeros(4, dtype=torch.int64, device=dev)  # P, O, out of order, error
+    # P, O, out of order (all written by the plan), status (cleared by it)
+    cnt = torch.empty(4, dtype=torch.int64, device=dev)
     st = stream_ptr(dev)
     lc, rc = lhs.coords.contiguous(), rhs.coords.contiguous()
     mark(marks, "plan0")
@@ -344,7 +360,7 @@ def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None):
         lc.data_ptr(), nl, lhs.ndim, rc.data_ptr(), nr, rhs.ndim, nb, lg, rg, ws.data_ptr(), ws.numel(),
         cnt.data_ptr(), cnt[3:].data_ptr(), st))
     mark(marks, "plan1")
-    P, O, unordered, err = (int(v) for v in cnt.cpu().tolist())
+    P, O, unordered, err = read_counts(cnt, launch_pending=True)
     L.device_error("es_direct_plan", err, "tile coordinate outside the tensor grid")
     if unordered:
         return None
@@ -378,8 +394,9 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     each output tile are in join order either way, and ``lhs_idx``/``rhs_idx``
     then hold the grouped order."""
     dev = lhs.device
-    if lhs.num_tuples > 0 and rhs.num_tuples > 0 and _direct_shape(lhs, rhs, join_keys, agg_keys):
-        plan = _plan_direct(lhs, rhs, join_keys, agg_keys, marks)
+    nb = _direct_batch_dims(lhs, rhs, join_keys, agg_keys) if lhs.num_tuples > 0 and rhs.num_tuples > 0 else None
+    if nb is not None:
+        plan = _plan_direct(lhs, rhs, join_keys, agg_keys, marks, nb)
         if plan is not None:
             return plan
     li, ri = _join_int32(lhs, rhs, join_keys)
@@ -401,7 +418,7 @@ def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, 
     L.check("es_segments_plan", lib.es_segments_plan(
         lhs.coords.contiguous().data_ptr(), lhs.ndim, rhs.coords.contiguous().data_ptr(), rhs.ndim, li.data_ptr(),
         ri.data_ptr(), P, flat, out_nd, ext, ws.data_ptr(), ws.numel(), cnt.data_ptr(), cnt[1:].data_ptr(), st))
-    O, err = read_counts(cnt)
+    O, err = read_counts(cnt, launch_pending=True)
     L.device_error("es_segments_plan", err, "output tile coordinate outside the output grid")
     oc = torch.empty((O, out_nd), dtype=torch.int32, device=dev)
     so = torch.empty(O + 1, dtype=torch.int64, device=dev)

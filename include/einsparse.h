@@ -10,7 +10,10 @@
  * query reports, and data-dependent output sizes are written to a device
  * int64 that the caller reads before allocating the outputs of the *_fill
  * phase. Device-side checks (an index outside its grid) set *error_dev to a
- * non-zero es_status; the caller reads it together with the size.
+ * non-zero es_status; the caller reads it together with the size. The
+ * caller clears *error_dev (and the counts) before a call, except for
+ * es_tile_coo_plan, es_tile_dense_plan, es_direct_plan and es_tile_einsum,
+ * which clear their own count and status outputs first.
  *
  * Threading: calls on different streams may run concurrently as long as
  * they do not share a workspace. The library holds no global mutable state
@@ -63,6 +66,11 @@ const char* es_status_string(int status);
  * wins (NumPy fancy assignment, :211-212). shape[d] % tile[d] != 0 gives
  * ES_ERR_INVALID (:174-179). Plan writes the tile count T to *num_tiles_dev;
  * fill writes coords int32 (T, ndim) and values (T, prod(tile)) of out_dtype.
+ * Either fill output may be NULL: with values_out NULL the call writes the
+ * coords (and keeps the value bounds in the workspace); with coords_out NULL
+ * it writes the values from the bounds that an earlier coords call left in
+ * the same workspace (so the values can be filled later, e.g. while the host
+ * waits for other counts).
  * ------------------------------------------------------------------------- */
 size_t es_tile_coo_workspace_size(int64_t nnz, int ndim, const int64_t* shape, const int64_t* tile);
 int es_tile_coo_plan(const int32_t* indices, const void* values, int values_dtype, int64_t nnz,
@@ -103,7 +111,9 @@ int es_coo_coalesce(const int32_t* indices, const void* values, int values_dtype
 
 /* Dense array (row-major `shape`) -> tile-COO of the tiles holding any
  * non-zero. Same result as SparseTensor(dense).to_relation(tile)
- * (tensor/sparse.py:104-117,160-219, via np.nonzero at :260-268). */
+ * (tensor/sparse.py:104-117,160-219, via np.nonzero at :260-268). Fill:
+ * coords_out or values_out may be NULL (that output is not written; the
+ * other one only needs the plan's workspace and the dense array). */
 size_t es_tile_dense_workspace_size(int ndim, const int64_t* shape, const int64_t* tile);
 int es_tile_dense_plan(const void* dense, int dtype, int ndim, const int64_t* shape,
                        const int64_t* tile, void* workspace, size_t workspace_bytes,

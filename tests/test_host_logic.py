@@ -229,3 +229,40 @@ def test_plan_operand_order_prefers_tensor_core_form():
     assert f == "ik,kl->il" and lhs is a and rhs is b
     t = SimpleNamespace(tile_shape=(1, 32, 32), values=torch.zeros(1))
     assert _operand_order("bkl,bik->bil", t, t, "auto")[0] == "bik,bkl->bil"
+
+
+def test_pending_fill_runs_once_in_creation_order():
+    """A relation's pending value fill runs at the first ``values`` access or
+    at ``launch_pending_fills`` (oldest first), once; assigning ``values``
+    drops it."""
+    import torch
+    from einjax_b200 import sparse as S
+
+    S.launch_pending_fills()  # nothing left from other tests
+    ran = []
+
+    def fake(tag, rel_box):
+        def fill():
+            ran.append(tag)
+            rel_box[0]._values.fill_(1.0)
+        return fill
+
+    boxes = [[None], [None], [None]]
+    rels = []
+    for i, box in enumerate(boxes):
+        r = S.SparseTensorRelation(torch.zeros((1, 2), dtype=torch.int32), torch.zeros((1, 2, 2)), (4, 4), (2, 2),
+                                   pending=fake(i, box))
+        box[0] = r
+        rels.append(r)
+    assert all(r.pending for r in rels)
+    assert rels[1].device == torch.device("cpu")  # from the coords: no fill
+    assert float(rels[1].values.sum()) == 4.0 and ran == [1]
+    assert not rels[1].pending
+    rels[2].values = torch.full((1, 2, 2), 7.0)  # replaced: its fill is dropped
+    assert not rels[2].pending
+    S.launch_pending_fills()
+    assert ran == [1, 0]
+    assert float(rels[0].values.sum()) == 4.0 and float(rels[2].values.sum()) == 28.0
+    rels[0].materialize()
+    assert ran == [1, 0]
+    assert "pending=False" in repr(rels[0])
