@@ -1538,9 +1538,11 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
     const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub, int S, int G, int64_t lhs_rows,
     int64_t rhs_rows, int C, int64_t key_extent, int64_t nw, uint32_t* __restrict__ cnt,
     const uint32_t* __restrict__ off, int32_t* __restrict__ recs, int32_t* __restrict__ err) {
-  __shared__ int win_l[kMergeWarps][32][kWin];
-  __shared__ int win_r[kMergeWarps][32][kWin];
-  __shared__ int win_k[kMergeWarps][32][kWin];
+  // [entry][lane]: a step's reads (one entry per lane) and a refill's
+  // stores (entry qq of every refilling lane) touch 32 distinct banks
+  __shared__ int win_l[kMergeWarps][kWin][32];
+  __shared__ int win_r[kMergeWarps][kWin][32];
+  __shared__ int win_k[kMergeWarps][kWin][32];
   const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t W1 = *num_sub;
   const int64_t nitems = (W1 + S - 1) / S;
@@ -1599,21 +1601,21 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
         }
 #pragma unroll
         for (int qq = 0; qq < kWin; ++qq) {
-          win_l[wib][lane][qq] = tl[qq];
-          win_r[wib][lane][qq] = tr[qq];
-          win_k[wib][lane][qq] = tk[qq];
+          win_l[wib][qq][lane] = tl[qq];
+          win_r[wib][qq][lane] = tr[qq];
+          win_k[wib][qq][lane] = tk[qq];
         }
         wpos = 0;
       }
       __syncwarp();
       const bool live = cur < end;
-      const int hl = live ? win_l[wib][lane][wpos] : INT_MAX;
-      const int hk = live ? win_k[wib][lane][wpos] : INT_MAX;
+      const int hl = live ? win_l[wib][wpos][lane] : INT_MAX;
+      const int hk = live ? win_k[wib][wpos][lane] : INT_MAX;
       const int v = S > 1 ? hk : hl;
       const int vmin = __reduce_min_sync(0xffffffffu, v);
       if (vmin == INT_MAX) break;
       const bool matched = live && v == vmin;
-      const int hr = matched ? win_r[wib][lane][wpos] : -1;
+      const int hr = matched ? win_r[wib][wpos][lane] : -1;
       // the first sub-strip holding vmin sets the rhs tiles of the step
       const uint32_t mm = __ballot_sync(0xffffffffu, matched);
       const int ref = (__ffs(mm) - 1) / G;
