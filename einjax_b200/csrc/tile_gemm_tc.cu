@@ -144,6 +144,8 @@ struct TcParams {
                             //    rhs panel: the tf32_split of x), 0 = truncating split
   float* part;              // fused: per-block partial sums, segment-major rows
   int64_t part_stride;      // elements of one block's partial
+  uint8_t* pwritten;        // fused: per (block b > 0, segment) 1 when its partial row was written
+  int64_t nseg;             // segments (row stride of pwritten)
   const int32_t* seg_out;
   void* out;
   int odt;
@@ -947,6 +949,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_strip_kernel(const TcParams p,
         break;
       }
       const int cur_blk = p.fused ? static_cast<int>(q / nitems) : p.blk;
+      if (p.fused && cur_blk > 0) {
+        // every unit is visited once: its segments' partial rows are marked
+        // written (it has records, so its epilogue writes them) or not, and
+        // the ordered addition skips the unwritten ones
+        uint8_t* wr = p.pwritten + static_cast<int64_t>(cur_blk - 1) * p.nseg + s0_cur;
+        const uint8_t v = re > rb ? 1 : 0;
+        for (int g = 0; g < gcnt_cur; ++g) wr[g] = v;
+      }
       if ((p.accumulate || cur_blk > 0) && re == rb) {
         // nothing to add from this key block: the item is not handed on
         while (pf < 3) pf_advance();
@@ -1369,22 +1379,31 @@ __global__ void __launch_bounds__(256) layout_rhs_kernel(const void* __restrict_
       put(((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16), v);
     }
   } else {
-    // one thread per 16-byte piece of the image: (tile t, k-chunk c, piece j
-    // of row n); n varies fastest, so the column reads of a warp are coalesced
-    const int64_t total = rows * nck * pieces * static_cast<int64_t>(Nt);
+    // one thread per image row (tile t, k-chunk c, row n): the row's pieces
+    // are W contiguous bytes, so a warp (32 consecutive n) stores 32 * W
+    // contiguous bytes; n varies fastest, so every column read of a warp is
+    // one coalesced row segment of the source tile
+    const int64_t total = rows * nck * static_cast<int64_t>(Nt);
     for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
       const int n = static_cast<int>(q % Nt);
-      int64_t r = q / Nt;
-      const int j = static_cast<int>(r % pieces);
-      r /= pieces;
+      const int64_t r = q / Nt;
       const int c = static_cast<int>(r % nck);
       const int64_t t = r / nck;
-      const E* col = src + t * static_cast<int64_t>(Kt) * Nt + (static_cast<int64_t>(c) * KC + j * EPU) * Nt + n;
-      __align__(16) E v[EPU];
-#pragma unroll
-      for (int e = 0; e < EPU; ++e) v[e] = col[static_cast<int64_t>(e) * Nt];
+      const E* col = src + t * static_cast<int64_t>(Kt) * Nt + static_cast<int64_t>(c) * KC * Nt + n;
       const int sw = ((n * W) >> 7) & (pieces - 1);
-      put(((static_cast<int64_t>(c) * rows + t) * Nt + n) * W + ((j ^ sw) * 16), v);
+      const int64_t row = ((static_cast<int64_t>(c) * rows + t) * Nt + n) * W;
+      constexpr int kBatch = 4;  // pieces with loads in flight together
+      for (int j0 = 0; j0 < pieces; j0 += kBatch) {
+        __align__(16) E v[kBatch][EPU];
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj)
+#pragma unroll
+          for (int e = 0; e < EPU; ++e)
+            if (j0 + jj < pieces) v[jj][e] = col[static_cast<int64_t>((j0 + jj) * EPU + e) * Nt];
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj)
+          if (j0 + jj < pieces) put(row + (((j0 + jj) ^ sw) * 16), v[jj]);
+      }
     }
   }
 }
@@ -1762,9 +1781,11 @@ int chain_records(const TcConfig& c) {
   return static_cast<int>(r < kRecAhead ? kRecAhead : r);
 }
 
-// out[row(s)] += part[0][s] + part[1][s] + ... in block order (float4 pieces).
-__global__ void add_partials_kernel(float* __restrict__ out, const float* __restrict__ part, int64_t nseg, int64_t te4,
-                                    int nparts, int64_t stride, const int32_t* __restrict__ seg_out) {
+// out[row(s)] += part[0][s] + part[1][s] + ... in block order (float4 pieces),
+// over the partial rows marked written.
+__global__ void add_partials_kernel(float* __restrict__ out, const float* __restrict__ part,
+                                    const uint8_t* __restrict__ written, int64_t nseg, int64_t te4, int nparts,
+                                    int64_t stride, const int32_t* __restrict__ seg_out) {
   const int64_t nv = nseg * te4;
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
     const int64_t sg = v / te4, e = v - sg * te4;
@@ -1772,6 +1793,7 @@ __global__ void add_partials_kernel(float* __restrict__ out, const float* __rest
     float4* o = reinterpret_cast<float4*>(out) + row * te4 + e;
     float4 a = *o;
     for (int b = 0; b < nparts; ++b) {
+      if (!written[b * nseg + sg]) continue;
       const float4 x = __ldcs(reinterpret_cast<const float4*>(part + b * stride) + v);
       a.x += x.x;
       a.y += x.y;
@@ -1784,6 +1806,7 @@ __global__ void add_partials_kernel(float* __restrict__ out, const float* __rest
 
 struct TcWs {
   float* part;
+  uint8_t* pwritten;
   uint8_t* pan_hi;
   uint8_t* pan_lo;
   uint8_t* zeros;
@@ -1840,9 +1863,9 @@ void tc_layout(C& cv, TcWs& w, const TcConfig& c, int64_t rhs_rows, int64_t npai
   w.rb.hist = cv.template take<uint32_t>(RadixScratchSize::hist_elems(nseg));
   w.rb.scan = cv.template take<uint32_t>(RadixScratchSize::scan_elems(nseg));
   w.queue = cv.template take<int>(1);
-  w.part = fused_blocks_possible(c, nblocks, nseg)
-               ? cv.template take<float>(static_cast<int64_t>(nblocks - 1) * nseg * c.Mt * c.Nt)
-               : nullptr;
+  const bool fb = fused_blocks_possible(c, nblocks, nseg);
+  w.part = fb ? cv.template take<float>(static_cast<int64_t>(nblocks - 1) * nseg * c.Mt * c.Nt) : nullptr;
+  w.pwritten = fb ? cv.template take<uint8_t>(static_cast<int64_t>(nblocks - 1) * nseg) : nullptr;
 }
 
 struct SizeOnly {
@@ -2084,12 +2107,13 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
       const int g = static_cast<int>(nblk < 148 * 16 ? nblk : 148 * 16);
       ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo, rn);
     } else {
+      const int64_t prow = rhs_rows * (c.Kt / c.KC) * c.Nt;  // image rows, one thread each
       if (c.fp32)
-        ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+        ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
                   w.pan_hi, w.pan_lo, rn);
       else
-        ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, (void*)nullptr, rn);
+        ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt,
+                  c.KC, w.pan_hi, (void*)nullptr, rn);
     }
   }
   // 2. work items
@@ -2183,6 +2207,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   }
   prm.part = w.part;
   prm.part_stride = nseg * c.Mt * c.Nt;
+  prm.pwritten = w.pwritten;
+  prm.nseg = nseg;
   // EINSPARSE_NO_FUSED_BLOCKS: one launch per key block (tuning, tests)
   prm.fused = (w.part != nullptr && odt == ES_F32 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                !std::getenv("EINSPARSE_NO_FUSED_BLOCKS"))
@@ -2227,8 +2253,6 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
       return ES_ERR_CUDA;
   }
   if (prm.fused) {
-    const size_t pbytes = static_cast<size_t>(nblocks - 1) * prm.part_stride * sizeof(float);
-    if (cudaMemsetAsync(w.part, 0, pbytes, st) != cudaSuccess) return ES_ERR_CUDA;
     prm.blk = 0;
     prm.accumulate = 0;
     if (c.fp32)
@@ -2238,8 +2262,8 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     const int64_t te4 = static_cast<int64_t>(c.Mt) * c.Nt / 4;
     const int64_t nv = nseg * te4;
     const int pg = static_cast<int>(nv / 256 + 1 < 148 * 8 ? nv / 256 + 1 : 148 * 8);
-    ES_LAUNCH(add_partials_kernel, pg, 256, 0, st, static_cast<float*>(out), w.part, nseg, te4, nblocks - 1,
-              prm.part_stride, seg_out);
+    ES_LAUNCH(add_partials_kernel, pg, 256, 0, st, static_cast<float*>(out), w.part, w.pwritten, nseg, te4,
+              nblocks - 1, prm.part_stride, seg_out);
     return ES_OK;
   }
   for (int b = 0; b < nblocks; ++b) {
