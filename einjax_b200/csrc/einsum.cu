@@ -397,14 +397,15 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
   return best;
 }
 
-extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
-                              int rhs_nd, const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
-                              const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
-                              const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
-                              int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
-                              const int32_t* pair_key, int64_t key_extent, void* out_values, int out_dtype,
-                              int precision, void* workspace,
-                              size_t workspace_bytes, int32_t* error_dev, void* stream) {
+extern "C" int es_tile_einsum_ev(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
+                                 const int64_t* rhs_tile, int rhs_nd, const void* lhs_values, int lhs_dtype,
+                                 int64_t lhs_rows, const void* rhs_values, int rhs_dtype, int64_t rhs_rows,
+                                 const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
+                                 const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
+                                 const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
+                                 void* out_values, int out_dtype, int precision, void* workspace,
+                                 size_t workspace_bytes, int32_t* error_dev, void* stream, void* values_ready) {
+  cudaEvent_t ready = static_cast<cudaEvent_t>(values_ready);
   EinsumDesc d;
   ES_TRY(parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d));
   if (out_dtype != ES_F32 && out_dtype != ES_BF16) return ES_ERR_UNSUPPORTED;
@@ -437,6 +438,7 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
       if (v.tl) {
         void* t = take(static_cast<size_t>(lhs_rows) * d.lhs_te * dtype_size(lhs_dtype));
         if (!t) return ES_ERR_WORKSPACE;
+        if (ready && cudaStreamWaitEvent(st, ready, 0) != cudaSuccess) return ES_ERR_CUDA;
         ES_TRY(transpose_tiles(lhs_values, t, lhs_dtype, lhs_rows, lhs_tile, lhs_nd, st));
         lv = t;
       }
@@ -445,11 +447,26 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
       if (v.tr) c.rhs_kmajor = 1;
       const int r = tc_launch(c, lv, lhs_rows, rv, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets, nseg,
                               seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, ws, left,
-                              error_dev, st);
+                              error_dev, st, ready);
       if (r != ES_ERR_UNSUPPORTED || precision == ES_PREC_TC) return r;
     }
     if (precision == ES_PREC_TC) return ES_ERR_UNSUPPORTED;
   }
+  if (ready && cudaStreamWaitEvent(st, ready, 0) != cudaSuccess) return ES_ERR_CUDA;
   return launch_simt(d, lhs_values, lhs_dtype, rhs_values, rhs_dtype, pair_lhs, pair_rhs, seg_offsets, nseg,
                      seg_out_index, out_values, out_dtype, st);
+}
+
+extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
+                              int rhs_nd, const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                              const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
+                              const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
+                              int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
+                              const int32_t* pair_key, int64_t key_extent, void* out_values, int out_dtype,
+                              int precision, void* workspace, size_t workspace_bytes, int32_t* error_dev,
+                              void* stream) {
+  return es_tile_einsum_ev(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_values, lhs_dtype, lhs_rows,
+                           rhs_values, rhs_dtype, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets, num_segments,
+                           seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, precision, workspace,
+                           workspace_bytes, error_dev, stream, nullptr);
 }

@@ -2079,7 +2079,7 @@ size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, in
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
               const int32_t* pl, const int32_t* pr, int64_t npairs, const int64_t* seg_off, int64_t nseg,
               const int32_t* seg_out, const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out,
-              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st) {
+              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st, cudaEvent_t values_ready) {
   if (nseg <= 0) return ES_OK;
   if (nseg >= INT32_MAX || rhs_rows >= INT32_MAX || lhs_rows >= INT32_MAX) return ES_ERR_UNSUPPORTED;
   int l2_blocks = 1;
@@ -2089,33 +2089,6 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks, pair_key ? key_extent : 0);
   if (cv.overflow) return ES_ERR_WORKSPACE;
   if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
-  // 1. rhs tiles into the shared-memory image (split for fp32)
-  // EINSPARSE_TF32_SPLIT=trunc: the truncating split (comparisons, tests)
-  const char* split_env = std::getenv("EINSPARSE_TF32_SPLIT");
-  const int rn = (split_env && std::strcmp(split_env, "trunc") == 0) ? 0 : 1;
-  const int64_t pe = rhs_rows * c.Kt * c.Nt / (c.fp32 ? 4 : 8);  // 16-byte pieces of the image
-  if (pe > 0) {
-    if (c.rhs_kmajor) {
-      if (c.fp32)
-        ES_LAUNCH((layout_rhs_kernel<true, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, w.pan_lo, rn);
-      else
-        ES_LAUNCH((layout_rhs_kernel<false, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, (void*)nullptr, rn);
-    } else if (c.fp32 && c.Nt >= 128) {
-      const int64_t nblk = rhs_rows * (c.Kt / c.KC) * ((c.Nt + kLayoutCols - 1) / kLayoutCols);
-      const int g = static_cast<int>(nblk < 148 * 16 ? nblk : 148 * 16);
-      ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo, rn);
-    } else {
-      const int64_t prow = rhs_rows * (c.Kt / c.KC) * c.Nt;  // image rows, one thread each
-      if (c.fp32)
-        ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
-                  w.pan_hi, w.pan_lo, rn);
-      else
-        ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt,
-                  c.KC, w.pan_hi, (void*)nullptr, rn);
-    }
-  }
   // 2. work items
   if (seg_strip && c.G > 1) {
     ES_LAUNCH(item_heads_kernel, grid_for(nseg, 256), 256, 0, st, seg_strip, nseg, c.G, w.flags, w.cnt);
@@ -2162,8 +2135,38 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     ES_LAUNCH(item_rec_kernel, grid_for(nslots, 256), 256, 0, st, (const uint32_t*)w.rec_base,
               (const uint32_t*)w.rec_total, w.num_items, S, C, nblocks, nw, w.item_rec);
   }
+  // the steps above read only the pair lists; the values may still be in
+  // flight (values_ready: e.g. a tiling's fill on another stream)
+  if (values_ready && cudaStreamWaitEvent(st, values_ready, 0) != cudaSuccess) return ES_ERR_CUDA;
+  // 5. rhs tiles into the shared-memory image (split for fp32)
+  // EINSPARSE_TF32_SPLIT=trunc: the truncating split (comparisons, tests)
+  const char* split_env = std::getenv("EINSPARSE_TF32_SPLIT");
+  const int rn = (split_env && std::strcmp(split_env, "trunc") == 0) ? 0 : 1;
+  const int64_t pe = rhs_rows * c.Kt * c.Nt / (c.fp32 ? 4 : 8);  // 16-byte pieces of the image
+  if (pe > 0) {
+    if (c.rhs_kmajor) {
+      if (c.fp32)
+        ES_LAUNCH((layout_rhs_kernel<true, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, w.pan_lo, rn);
+      else
+        ES_LAUNCH((layout_rhs_kernel<false, true>), grid_for(pe, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, (void*)nullptr, rn);
+    } else if (c.fp32 && c.Nt >= 128) {
+      const int64_t nblk = rhs_rows * (c.Kt / c.KC) * ((c.Nt + kLayoutCols - 1) / kLayoutCols);
+      const int g = static_cast<int>(nblk < 148 * 16 ? nblk : 148 * 16);
+      ES_LAUNCH(layout_rhs_wide_kernel<true>, g, 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC, w.pan_hi, w.pan_lo, rn);
+    } else {
+      const int64_t prow = rhs_rows * (c.Kt / c.KC) * c.Nt;  // image rows, one thread each
+      if (c.fp32)
+        ES_LAUNCH((layout_rhs_kernel<true, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt, c.KC,
+                  w.pan_hi, w.pan_lo, rn);
+      else
+        ES_LAUNCH((layout_rhs_kernel<false, false>), grid_for(prow, 256), 256, 0, st, rhs, rhs_rows, c.Kt, c.Nt,
+                  c.KC, w.pan_hi, (void*)nullptr, rn);
+    }
+  }
   if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
-  // 5. persistent tensor-core kernel, one CTA per SM
+  // 6. persistent tensor-core kernel, one CTA per SM
   TcParams prm;
   prm.c = c;
   // the staged epilogue stores 16-byte pieces (its shared memory stays reserved)

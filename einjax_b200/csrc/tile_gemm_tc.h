@@ -61,6 +61,6 @@ size_t tc_workspace_size(const TcConfig& c, int64_t rhs_rows, int64_t npairs, in
 int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* rhs, int64_t rhs_rows,
               const int32_t* pl, const int32_t* pr, int64_t npairs, const int64_t* seg_off, int64_t nseg,
               const int32_t* seg_out, const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent, void* out,
-              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st);
+              int odt, void* ws, size_t ws_bytes, int32_t* err, cudaStream_t st, cudaEvent_t values_ready = nullptr);
 
 }  // namespace es

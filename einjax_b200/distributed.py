@@ -304,7 +304,7 @@ def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_
     strips for ``shard="output"``, e.g. the tiles of its ``balanced_row_ranges``
     rows; its contracted key range for ``"contracted"``). ``timings``: a list
     that receives ``(label, CUDA event)`` marks around the collective."""
-    from .sparse import SparseTensorRelation, as_relation, empty_relation, mark
+    from .sparse import SparseTensorRelation, as_relation, empty_relation, latest_ready, mark
     from .sparse_dispatch import _out_extents, _resolve_shapes, execute_sparse, plan_pairs, tile_einsum
 
     rank, n = world(group)
@@ -340,9 +340,11 @@ def execute_sharded_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_
         buf = torch.zeros((per * n, *output_tile_shape), dtype=odt, device=lhs.device)
         if plan is not None and plan.num_pairs:
             # the fused GEMM writes each partial output tile at its union row
-            tile_einsum(kernel_string, local.values, rhs.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
+            lv, lr = local.values_and_ready()
+            rv, rr = rhs.values_and_ready()
+            tile_einsum(kernel_string, lv, rv, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
                         seg_out_index=pos, out=buf, precision=precision, seg_strip=plan.seg_strip,
-                        pair_key=plan.seg_key, key_extent=plan.key_extent)
+                        pair_key=plan.seg_key, key_extent=plan.key_extent, ready=latest_ready(lr, rr))
         mark(timings, "collective0")
         c, v = _scatter_partials(buf, ucoords, per, group, gather)
         mark(timings, "collective1")
@@ -375,7 +377,7 @@ def _replicated_plan_shard(lhs, rhs, join_keys, kernel_string, agg_keys, output_
     """Output sharding for outputs without a strip layout: every rank plans
     the whole join and grouping, then contracts a contiguous range of output
     tiles balanced by pair count."""
-    from .sparse import SparseTensorRelation, empty_relation
+    from .sparse import SparseTensorRelation, empty_relation, latest_ready
     from .sparse_dispatch import plan_pairs, tile_einsum
     rank, n = world(group)
     plan = plan_pairs(lhs, rhs, join_keys, agg_keys)
@@ -383,10 +385,12 @@ def _replicated_plan_shard(lhs, rhs, join_keys, kernel_string, agg_keys, output_
         return empty_relation(output_shape, output_tile_shape, lhs.values.dtype, lhs.device)
     s0, s1 = balanced_segment_ranges(plan.seg_offsets.cpu().numpy(), n)[rank]
     if s1 > s0:
-        vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs,
+        lv, lr = lhs.values_and_ready()
+        rv, rr = rhs.values_and_ready()
+        vals = tile_einsum(kernel_string, lv, rv, plan.seg_lhs, plan.seg_rhs,
                            plan.seg_offsets[s0:s1 + 1], precision=precision,
                            seg_strip=plan.seg_strip[s0:s1] if plan.seg_strip is not None else None,
-                           pair_key=plan.seg_key, key_extent=plan.key_extent)
+                           pair_key=plan.seg_key, key_extent=plan.key_extent, ready=latest_ready(lr, rr))
     else:
         vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs[:0], plan.seg_rhs[:0],
                            None, num_out_rows=0, precision=precision)

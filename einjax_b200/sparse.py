@@ -206,6 +206,13 @@ def resolve_tilings() -> None:
     _TILINGS.resolve_all()
 
 
+def latest_ready(*readies):
+    """The newest of ``(sequence, event)`` pairs (None entries skipped): the
+    fill stream runs in order, so its event covers the older ones."""
+    rs = [r for r in readies if r is not None]
+    return max(rs, key=lambda r: r[0]) if rs else None
+
+
 def launch_pending_fills() -> None:
     """Launch the value fills of every relation whose values are pending
     (stream-ordered like any launch; nothing waits)."""
@@ -271,7 +278,7 @@ class SparseTensorRelation:
     (``plan_pairs``), whichever comes first; it reads the tiling's input
     until then, and raises if that input was changed in place meanwhile."""
 
-    __slots__ = ("_coords", "_values", "shape", "tile_shape", "_pending", "_finish", "_failed", "_dev",
+    __slots__ = ("_coords", "_values", "shape", "tile_shape", "_pending", "_finish", "_failed", "_dev", "_ready",
                  "__weakref__")
 
     def __init__(self, coords: torch.Tensor, values: torch.Tensor, shape, tile_shape, pending=None):
@@ -283,6 +290,7 @@ class SparseTensorRelation:
         self._finish = None
         self._failed = None
         self._dev = None
+        self._ready = None  # (sequence, event) behind the value fill on the fill stream
         if pending is not None:
             _PENDING.add(self)
 
@@ -327,16 +335,30 @@ class SparseTensorRelation:
 
     @property
     def values(self) -> torch.Tensor:
-        if self._finish is not None or self._failed is not None:
-            self._resolve()
-        if self._pending is not None:
-            self.materialize()
-        return self._values
+        """The tile values; the current stream waits for a deferred fill."""
+        v, ready = self.values_and_ready()
+        if ready is not None:
+            torch.cuda.current_stream(v.device).wait_event(ready[1])
+        return v
 
     @values.setter
     def values(self, v: torch.Tensor) -> None:
         self._pending = None
+        self._ready = None
         self._values = v
+
+    def values_and_ready(self):
+        """``(values, ready)`` without waiting: ``ready`` is ``(sequence,
+        event)`` behind the value fill on the device's fill stream, or None
+        when the values are written in stream order. A caller that reads the
+        values on a stream must make it wait for the event first (e.g.
+        ``tile_einsum(..., ready=...)``, which waits just before the launch
+        that reads them)."""
+        if self._finish is not None or self._failed is not None:
+            self._resolve()
+        if self._pending is not None:
+            self.materialize()
+        return self._values, self._ready
 
     @property
     def pending(self) -> bool:
@@ -358,7 +380,7 @@ class SparseTensorRelation:
             self._resolve()
         fill, self._pending = self._pending, None
         if fill is not None:
-            fill()
+            self._ready = fill()
         return self
 
     def __repr__(self) -> str:
@@ -575,11 +597,15 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
             L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
                 vals.data_ptr(), vd, nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), None, oc,
                 stream.cuda_stream))
+        if T == 0:
+            return coords, out, None
+        after = torch.cuda.Event()
+        after.record(stream)
 
         def launch(sp):
             L.check("es_tile_coo_fill", lib.es_tile_coo_fill(
                 vals.data_ptr(), vd, nnz, nd, sh, tl, ws.data_ptr(), ws.numel(), T, None, out.data_ptr(), oc, sp))
-        return coords, out, (_deferred_fill(dev, vals, launch, "tile_coo", stream, version) if T > 0 else None)
+        return coords, out, _deferred_fill(dev, vals, launch, "tile_coo", after, version, (out, ws, vals))
 
     if marks is None:
         return SparseTensorRelation._unresolved(shape, tile_shape, dev, cnt, finish)
@@ -587,7 +613,7 @@ def tile_coo(indices: torch.Tensor, values: torch.Tensor, shape, tile_shape,
     coords, out, fill = finish(read_counts(cnt))
     mark(marks, "fill0")
     if fill is not None:
-        fill()
+        torch.cuda.current_stream(dev).wait_event(fill()[1])
     mark(marks, "fill1")
     return SparseTensorRelation(coords, out, shape, tile_shape)
 
@@ -640,30 +666,60 @@ def tile_dense(dense: torch.Tensor, tile_shape, out_dtype=torch.float32) -> Spar
             L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
                 d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, coords.data_ptr(), None, oc,
                 stream.cuda_stream))
+        if T == 0:
+            return coords, out, None
+        after = torch.cuda.Event()
+        after.record(stream)
 
         def launch(sp):
             L.check("es_tile_dense_fill", lib.es_tile_dense_fill(
                 d.data_ptr(), es_dtype(d), nd, sh, tl, ws.data_ptr(), ws.numel(), T, None, out.data_ptr(), oc, sp))
-        return coords, out, (_deferred_fill(dev, d, launch, "tile_dense", stream, version) if T > 0 else None)
+        return coords, out, _deferred_fill(dev, d, launch, "tile_dense", after, version, (out, ws, d))
 
     return SparseTensorRelation._unresolved(shape, tile_shape, dev, cnt, finish)
 
 
-def _deferred_fill(dev, source: torch.Tensor, launch, name: str, stream, version: int):
-    """Pending value fill of a tiling call: ``launch(stream)`` runs on the
-    tiling's stream (the one its coordinates went out on), and a caller on
-    another stream then waits for it. ``source``, the tiling's input, must
-    not be changed in place before the fill runs (checked through its
-    version counter against ``version``, taken when the tiling was called)."""
+_FILL_STREAMS = {}
+_FILL_SEQ = [0]
+
+
+def _fill_stream(dev) -> torch.cuda.Stream:
+    """The device's stream for deferred value fills (one per device), at the
+    lowest priority: a caller on a higher-priority stream gets its kernels
+    scheduled ahead of a running fill's remaining CTAs, so the two overlap
+    (on a default-priority stream the fill's CTAs go first)."""
+    i = _device_index(dev)
+    st = _FILL_STREAMS.get(i)
+    if st is None:
+        st = _FILL_STREAMS[i] = torch.cuda.Stream(device=i, priority=torch.cuda.Stream.priority_range()[0])
+    return st
+
+
+def _deferred_fill(dev, source: torch.Tensor, launch, name: str, after: torch.cuda.Event, version: int, keep):
+    """Pending value fill of a tiling call. ``launch(stream)`` runs on the
+    device's fill stream once ``after`` (recorded behind the tiling's
+    coordinate write) has passed, so the fill overlaps whatever the tiling's
+    stream does next; the returned callable launches it and gives back
+    ``(sequence, event)``, the event recorded behind it. The tensors in
+    ``keep`` (output, workspace, input) are marked used on the fill stream
+    so their memory is not reused before the fill ends. ``source``, the
+    tiling's input, must not be changed in place before the fill runs
+    (checked through its version counter against ``version``, taken when the
+    tiling was called)."""
 
     def fill():
         if source._version != version:
             raise RuntimeError(f"{name}: the input was changed in place before the tile values were filled; "
                                "call materialize() on the relation before changing it")
-        launch(stream.cuda_stream)
-        cur = torch.cuda.current_stream(dev)
-        if cur != stream:
-            cur.wait_stream(stream)
+        side = _fill_stream(dev)
+        side.wait_event(after)
+        launch(side.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        for t in keep:
+            t.record_stream(side)
+        _FILL_SEQ[0] += 1
+        return (_FILL_SEQ[0], ev)
     return fill
 
 

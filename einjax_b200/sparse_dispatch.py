@@ -21,8 +21,8 @@ from math import prod
 import torch
 
 from . import _lib as L
-from .sparse import (SparseTensorRelation, as_relation, defer_device_error, empty_relation, es_dtype, mark,
-                     read_counts, stream_ptr, workspace)
+from .sparse import (SparseTensorRelation, as_relation, defer_device_error, empty_relation, es_dtype, latest_ready,
+                     mark, read_counts, stream_ptr, workspace)
 
 _PREC = {"auto": L.ES_PREC_AUTO, "exact": L.ES_PREC_EXACT, "tc": L.ES_PREC_TC}
 
@@ -141,7 +141,7 @@ def _out_tile(kernel_string, lt, rt):
 
 def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_offsets=None, seg_out_index=None,
                 out=None, num_out_rows=None, out_dtype=None, precision="auto", seg_strip=None, pair_key=None,
-                key_extent=0, check=True):
+                key_extent=0, check=True, ready=None):
     """Segmented tile einsum through ``es_tile_einsum``.
 
     Without ``seg_offsets`` every pair is its own segment (per-pair output,
@@ -153,7 +153,10 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
     block the contracted range so the re-read operand stays in L2. With
     ``check`` the device error flag is read back (one 4-byte copy and a wait);
     ``check="defer"`` queues it for the next count read or
-    ``check_device_errors()`` (no wait here); False skips it.
+    ``check_device_errors()`` (no wait here); False skips it. ``ready``: a
+    ``(sequence, event)`` from ``SparseTensorRelation.values_and_ready``
+    that the call waits for right before its first launch reading the
+    values (its pair grouping runs before that, overlapping the fill).
     """
     lib = L.lib()
     dev = lhs_values.device
@@ -168,6 +171,10 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
         out = (torch.zeros if seg_out_index is not None else torch.empty)((rows, *out_tile), dtype=odt, device=dev)
     if P == 0 or nseg == 0:
         return out
+    if ready is not None and not (lhs_values.is_contiguous() and rhs_values.is_contiguous()):
+        # a copy would read the values now: wait here instead
+        torch.cuda.current_stream(dev).wait_event(ready[1])
+        ready = None
     lv, rv = lhs_values.contiguous(), rhs_values.contiguous()
     pl = pair_lhs.to(torch.int32).contiguous()
     pr = pair_rhs.to(torch.int32).contiguous()
@@ -182,13 +189,13 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
                                             int(lv.shape[0]), int(rv.shape[0]), P, nseg, kext, prec)
     ws = workspace(wsb, dev) if wsb else None
     err = torch.empty(1, dtype=torch.int32, device=dev)  # cleared by the call
-    L.check("es_tile_einsum", lib.es_tile_einsum(
+    L.check("es_tile_einsum", lib.es_tile_einsum_ev(
         ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
         int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
         sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None,
         pk.data_ptr() if pk is not None else None, kext, out.data_ptr(),
         _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-        err.data_ptr(), stream_ptr(dev)))
+        err.data_ptr(), stream_ptr(dev), ready[1].cuda_event if ready is not None else None))
     if check == "defer":
         defer_device_error("es_tile_einsum", err)
     elif check:
@@ -476,10 +483,13 @@ def execute_sparse(lhs, rhs, join_keys, kernel_string, agg_keys, output_shape=No
     plan = plan or plan_pairs(lhs, rhs, join_keys, agg_keys)
     if plan.num_pairs == 0:
         return empty_relation(output_shape, output_tile_shape, lhs.values.dtype, lhs.device)
-    # the GEMM's device status is read at the next count read (no wait here)
-    vals = tile_einsum(kernel_string, lhs.values, rhs.values, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
+    # deferred tile fills finish under the GEMM's pair grouping; the GEMM's
+    # device status is read at the next count read (no wait here)
+    lv, lr = lhs.values_and_ready()
+    rv, rr = rhs.values_and_ready()
+    vals = tile_einsum(kernel_string, lv, rv, plan.seg_lhs, plan.seg_rhs, plan.seg_offsets,
                        precision=precision, seg_strip=plan.seg_strip, pair_key=plan.seg_key,
-                       key_extent=plan.key_extent, check="defer")
+                       key_extent=plan.key_extent, check="defer", ready=latest_ready(lr, rr))
     return SparseTensorRelation(plan.out_coords, vals, output_shape, output_tile_shape)
 
 

@@ -12,7 +12,7 @@
  * phase. Device-side checks (an index outside its grid) set *error_dev to a
  * non-zero es_status; the caller reads it together with the size. The
  * caller clears *error_dev (and the counts) before a call, except for
- * es_tile_coo_plan, es_tile_dense_plan, es_direct_plan and es_tile_einsum,
+ * es_tile_coo_plan, es_tile_dense_plan, es_direct_plan and es_tile_einsum(_ev),
  * which clear their own count and status outputs first.
  *
  * Threading: calls on different streams may run concurrently as long as
@@ -243,6 +243,22 @@ int es_tile_einsum(const char* kernel_string,
                    const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
                    void* out_values, int out_dtype, int precision,
                    void* workspace, size_t workspace_bytes, int32_t* error_dev, void* stream);
+
+/* es_tile_einsum that waits for the cudaEvent_t values_ready (NULL: no
+ * wait) on `stream` right before its first launch that reads lhs_values or
+ * rhs_values: the grouping of the pairs into work items and step records
+ * runs first, so values written on another stream (e.g. a tiling's value
+ * fill) overlap it. */
+int es_tile_einsum_ev(const char* kernel_string,
+                      const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
+                      const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                      const void* rhs_values, int rhs_dtype, int64_t rhs_rows,
+                      const int32_t* pair_lhs, const int32_t* pair_rhs, int64_t num_pairs,
+                      const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
+                      const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
+                      void* out_values, int out_dtype, int precision,
+                      void* workspace, size_t workspace_bytes, int32_t* error_dev, void* stream,
+                      void* values_ready);
 
 /* Which path es_tile_einsum takes for these arguments: 1 tensor cores,
  * 0 SIMT, negative es_status if the call would be rejected. Host-side. */

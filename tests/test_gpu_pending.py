@@ -90,3 +90,21 @@ def test_unresolved_tilings_resolve_together_and_raise_late():
         _ = R.values
     with pytest.raises(ValueError):  # the reference-facing call raises at once
         E.SparseTensor("t", (bad.cpu().numpy(), np.ones(2), (4, 4))).to_relation((2, 2))
+
+
+def test_fill_overlaps_gemm_grouping_and_matches_eager():
+    """execute_sparse with the tile fill on the fill stream (the GEMM waits
+    for it inside the call) equals the same call on filled operands."""
+    idx, val = _coo(4, shape=(512, 1024), nnz=20000)
+    b = torch.randn(1024, 128, device="cuda")
+    A = E.tile_coo(idx, val, (512, 1024), (32, 32))
+    B = E.tile_dense(b, (32, 32))
+    got = E.execute_sparse(A, B, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    A2 = E.tile_coo(idx, val, (512, 1024), (32, 32)).materialize()
+    B2 = E.tile_dense(b, (32, 32)).materialize()
+    torch.cuda.synchronize()
+    want = E.execute_sparse(A2, B2, [(1, 0)], "ij,jk->ik", [(0, 0), (1, 1)])
+    assert torch.equal(got.coords, want.coords)
+    assert torch.equal(got.values, want.values)
+    lv, ready = A.values_and_ready()
+    assert ready is not None and ready[1].query() in (True, False)
