@@ -340,10 +340,12 @@ def run_ours(args):
     slots = [tuple(torch.empty(h.shape, dtype=h.dtype, device=dev) for h in hosts) for _ in range(2)]
     b_full = torch.empty(b_h.shape, dtype=b_h.dtype, device=dev) if world > 1 else None
 
-    def h2d(k, after):
+    def h2d(k, after, gemm=None):
         with torch.cuda.stream(s_in):
             if after is not None:
                 s_in.wait_event(after)
+            if gemm is not None:
+                s_in.wait_event(gemm)
             for d, h in zip(slots[k % 2], hosts):
                 d.copy_(h, non_blocking=True)
             ev_h = torch.cuda.Event()
@@ -355,42 +357,50 @@ def run_ours(args):
         if world > 1:
             dist.all_gather_into_tensor(b_full, b)
             b = b_full
-        A = E.SparseTensor("A", (idx, val, shape)).to_relation((TILE, TILE))
-        B = E.SparseTensor("B", b).to_relation((TILE, TILE))
-        return E.execute_sharded_sparse(A, B, jk, ks, ak, precision=args.precision, lhs_sharded=True,
-                                        gather=False)
+        # the public device-tensor tilings (their counts resolve together at
+        # the plan, their value fills overlap the GEMM's pair grouping)
+        A = E.tile_coo(idx, val, shape, (TILE, TILE))
+        B = E.tile_dense(b, (TILE, TILE))
+        res = E.execute_sharded_sparse(A, B, jk, ks, ak, precision=args.precision, lhs_sharded=True,
+                                       gather=False)
+        # the event behind the step's tile fills: the tile GEMM starts when
+        # it has passed, so copies issued behind it run under the GEMM
+        ready = E.sparse.latest_ready(A.values_and_ready()[1], B.values_and_ready()[1])
+        return res, (ready[1] if ready is not None else None)
 
-    def d2h(k, res, done, outs):
+    def d2h(k, res, done, outs, gemm=None):
         if outs[k % 2] is None:
             outs[k % 2] = (torch.empty(res.values.shape, dtype=res.values.dtype, pin_memory=True),
                            torch.empty(res.coords.shape, dtype=res.coords.dtype, pin_memory=True))
         with torch.cuda.stream(s_out):
             s_out.wait_event(done)
+            if gemm is not None:
+                s_out.wait_event(gemm)
             outs[k % 2][0].copy_(res.values, non_blocking=True)
             outs[k % 2][1].copy_(res.coords, non_blocking=True)
             res.values.record_stream(s_out)
             res.coords.record_stream(s_out)
 
     def e2e_run(steps, outs, start):
-        # The step reads counts back from the device a few times before its
-        # tile GEMM and none after it. Copies are enqueued right after a step's
-        # GEMM, so they run under it: the next step's inputs, and the
-        # previous step's result (done long before). A result copy that became
-        # runnable together with the next step's first count read would hold
-        # that 16-byte read behind it on the device-to-host copy engine.
+        # The step reads counts back from the device before its tile GEMM and
+        # none after it. The next step's inputs and the previous step's result
+        # are copied while step k's GEMM runs: issued behind the event of step
+        # k's tile fills, which the GEMM waits for, so they neither contend
+        # with the fills and the pair grouping for HBM nor hold a count read
+        # of the next step behind them on a copy engine.
         ev_in, ev_done = [None, None], [None, None]
         ev_in[0] = h2d(0, start)
         prev = None
         for k in range(steps):
             comp.wait_event(ev_in[k % 2])
-            res = compute(k)
+            res, gemm = compute(k)
             done = torch.cuda.Event()
             done.record(comp)
             ev_done[k % 2] = done
             if k + 1 < steps:
-                ev_in[(k + 1) % 2] = h2d(k + 1, ev_done[(k + 1) % 2] if k >= 1 else start)
+                ev_in[(k + 1) % 2] = h2d(k + 1, ev_done[(k + 1) % 2] if k >= 1 else start, gemm)
             if prev is not None:
-                d2h(k - 1, *prev, outs)
+                d2h(k - 1, *prev, outs, gemm)
             prev = (res, done)
         if prev is not None:
             d2h(steps - 1, *prev, outs)
@@ -489,8 +499,8 @@ def run_ours(args):
             "e2e": {"value": round(flops_all / (e2e_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                     "ms_per_step": round(e2e_step, 3),
                     "h2d_bytes_per_step": int(h2d_bytes), "d2h_bytes_per_step": int(d2h_bytes),
-                    "copies": "one stream per direction, enqueued under each step's tile GEMM (next inputs, "
-                              "previous result)" +
+                    "copies": "one stream per direction, issued behind each step's tile fills so they run "
+                              "under its tile GEMM (next inputs, previous result)" +
                               ("; each rank copies its A rows and 1/N of B's rows, B is all-gathered over "
                                "NVLink (NCCL) inside the step" if world > 1 else "")},
             "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": "tensor",
@@ -971,10 +981,12 @@ def run_reference(args):
     from einjax_b200 import workloads as W
     w = W.c2_spmm(seed=args.seed, scale=args.scale)
     vals = []
+    # each step a bounded sample: about a minute of CPU work over the run
+    per = max(1.0, min(8.0, 60.0 / max(1, args.steps)))
     for _ in range(max(0, args.warmup)):
-        cpu_baseline(args, w, budget_s=4.0)
+        cpu_baseline(args, w, budget_s=min(4.0, per))
     for _ in range(args.steps):
-        vals.append(cpu_baseline(args, w, budget_s=8.0))
+        vals.append(cpu_baseline(args, w, budget_s=per))
     v = statistics.median(x["value"] for x in vals)
     cb = dict(vals[-1])
     cb["value"] = v
@@ -1073,7 +1085,7 @@ def run_config(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--scale", type=int, default=1, help="shrink C2 by this factor (testing only)")
