@@ -68,7 +68,7 @@ SIGNATURES = {
                                c_sz, c_vp, c_vp]),
     "es_tile_einsum_ev": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_vp, c_int, c_i64, c_vp, c_int,
                                   c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_int,
-                                  c_vp, c_sz, c_vp, c_vp, c_vp]),
+                                  c_vp, c_sz, c_vp, c_vp, c_vp, c_vp]),
     "es_tile_einsum_path": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_int, c_int, c_int]),
     "es_out_tile_shape": (c_int, [ctypes.c_char_p, c_i64p, c_int, c_i64p, c_int, c_i64p]),
     "es_segsum_workspace_size": (c_sz, [c_i64]),

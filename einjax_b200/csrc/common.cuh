@@ -38,6 +38,45 @@ inline int check_launch() {
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 constexpr int kSMs = 148;
+constexpr int kMaxAttrDevices = 64;  // devices whose once-per-device kernel attributes are tracked
+
+// Up to four device ranges of 32-bit words that a kernel clears for the
+// launches after it: folds a cudaMemsetAsync (an API call and a device
+// operation of its own) into a launch that is already there.
+struct ZeroSpans {
+  uint32_t* p[4];
+  int64_t words[4];
+};
+
+inline ZeroSpans no_zero_spans() {
+  ZeroSpans z;
+  for (int i = 0; i < 4; ++i) {
+    z.p[i] = nullptr;
+    z.words[i] = 0;
+  }
+  return z;
+}
+
+// Adds a range (nothing for nwords <= 0); false when all four are taken.
+inline bool add_zero_span(ZeroSpans& z, void* ptr, int64_t nwords) {
+  if (nwords <= 0) return true;
+  for (int i = 0; i < 4; ++i)
+    if (!z.p[i]) {
+      z.p[i] = static_cast<uint32_t*>(ptr);
+      z.words[i] = nwords;
+      return true;
+    }
+  return false;
+}
+
+__device__ __forceinline__ void zero_spans(const ZeroSpans& z) {
+  const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (z.p[i])
+      for (int64_t j = t; j < z.words[i]; j += nt) z.p[i][j] = 0u;
+}
 
 inline int grid_for(int64_t n, int threads, int64_t cap = 148LL * 32) {
   int64_t g = (n + threads - 1) / threads;

@@ -55,7 +55,10 @@ struct DirectWs {
   uint64_t* cnz;       // (SC) per (strip, present column), strip-major: pairs | (pairs > 0) << 32
   uint64_t* pos;       // (SC) exclusive scan of cnz: first pair | output tile index << 32
   uint32_t* gstart;    // (SC) G_c(first tile of the strip)
-  uint32_t* scan;      // scan scratch (largest length, also used as 64-bit words)
+  uint32_t* scan_c;    // scratch of the column-flag scan
+  uint32_t* scan_s;    // scratch of the strip-head scan
+  uint32_t* scan_m;    // scratch of the mask-count scan
+  uint32_t* scan_p;    // scratch of the pair-count scan (64-bit values)
   uint32_t* ncols;     // (1) present columns
   uint32_t* nstrips;   // (1)
   uint32_t* total;     // (1) scratch totals
@@ -93,11 +96,11 @@ static void direct_layout(C& c, DirectWs& w, int64_t nl, int64_t nr, const Direc
   w.cnz = c.template take<uint64_t>(sc);
   w.pos = c.template take<uint64_t>(sc);
   w.gstart = c.template take<uint32_t>(sc);
-  int64_t mx = sc + 1;
-  if (hm > mx) mx = hm;
-  if (g.cext > mx) mx = g.cext;
-  if (nl > mx) mx = nl;
-  w.scan = c.template take<uint32_t>(scan_scratch_elems(mx));
+  // one scratch per scan, so the init launch clears all four up front
+  w.scan_c = c.template take<uint32_t>(scan_scratch_elems(g.cext));
+  w.scan_s = c.template take<uint32_t>(scan_scratch_elems(nl));
+  w.scan_m = c.template take<uint32_t>(scan_scratch_elems(hm));
+  w.scan_p = c.template take<uint32_t>(2 * scan_scratch_elems(sc));
   w.ncols = c.template take<uint32_t>(1);
   w.nstrips = c.template take<uint32_t>(1);
   w.total = c.template take<uint32_t>(1);
@@ -154,7 +157,9 @@ __device__ __forceinline__ int lex_cmp(const int32_t* a, const int32_t* b, int n
 // Clears the table (-1), the column flags, the order flag and the caller's
 // status slot.
 __global__ void direct_init_kernel(int32_t* __restrict__ table, int64_t tn, uint32_t* __restrict__ colflag,
-                                   int64_t cext, int32_t* __restrict__ bad, int32_t* __restrict__ err) {
+                                   int64_t cext, int32_t* __restrict__ bad, int32_t* __restrict__ err,
+                                   ZeroSpans zs) {
+  zero_spans(zs);
   const int64_t n = tn > cext ? tn : cext;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     if (i < tn) table[i] = -1;
@@ -452,31 +457,37 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   direct_layout(cv, w, n_lhs, n_rhs, g);
   if (cv.overflow) return ES_ERR_WORKSPACE;
   const int64_t tn = g.kext * g.cext;
+  const int64_t nchp1 = direct_chunks(n_lhs);
+  const int64_t cb = direct_col_bound(g, n_rhs);
+  const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
+  ZeroSpans zs = no_zero_spans();
+  add_zero_span(zs, w.scan_c, scan_clear_words(g.cext));
+  add_zero_span(zs, w.scan_s, scan_clear_words(n_lhs));
+  add_zero_span(zs, w.scan_m, scan_clear_words(cb * nchp1));
+  add_zero_span(zs, w.scan_p, 2 * scan_clear_words(sc));
   ES_LAUNCH(direct_init_kernel, grid_for(tn > g.cext ? tn : g.cext, 256), 256, 0, st, w.table, tn, w.colflag, g.cext,
-            w.bad, error_dev);
+            w.bad, error_dev, zs);
   ES_LAUNCH(direct_inputs_kernel, grid_for(n_rhs + n_lhs, 256), 256, 0, st, rhs_coords, n_rhs, lhs_coords, n_lhs, g,
             w.table, w.colflag, w.sflag, w.bad, error_dev);
-  ES_TRY(exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, w.scan, st));
-  ES_TRY(exclusive_scan<uint32_t>(w.sflag, w.sexcl, n_lhs, w.nstrips, w.scan, st));
+  ES_TRY(exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, w.scan_c, st, nullptr, true));
+  ES_TRY(exclusive_scan<uint32_t>(w.sflag, w.sexcl, n_lhs, w.nstrips, w.scan_s, st, nullptr, true));
   ES_LAUNCH(direct_index_kernel, grid_for(n_lhs > g.cext ? n_lhs : g.cext, 256), 256, 0, st, w.colflag, w.colrank,
             g.cext, w.colids, w.sflag, w.sexcl, n_lhs, w.nstrips, w.sstart);
   // hit masks per (present column, chunk), their scan, then the per-(strip,
   // column) counts; the column count lives on the device, so grids cover the
   // upper bound and stride over the used part
-  const int64_t nchp1 = direct_chunks(n_lhs);
-  const int64_t cb = direct_col_bound(g, n_rhs);
-  const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
   ES_LAUNCH(direct_masks_kernel, grid_for(nchp1 * ((cb + kDirCols - 1) / kDirCols) * 32, 256), 256, 0, st,
             lhs_coords, n_lhs, g, w.table, w.colids, w.ncols, nchp1, w.mask, w.ccnt);
   // column-major: entries of columns past ncols are not written and only
   // ever enter prefixes past the used part
-  ES_TRY(exclusive_scan<uint32_t>(w.ccnt, w.cscan, cb * nchp1, w.total, w.scan, st));
+  ES_TRY(exclusive_scan<uint32_t>(w.ccnt, w.cscan, cb * nchp1, w.total, w.scan_m, st, nullptr, true));
   ES_LAUNCH(direct_counts_kernel, grid_for(sc, 256), 256, 0, st, w.mask, w.cscan, nchp1, w.ncols, w.nstrips,
             w.sstart, w.cnz, w.gstart);
   // one scan gives first pairs (low word) and output tile indices (high);
   // it runs over the upper bound: entries past nstrips * ncols are not
   // written and only ever enter prefixes past the used length
-  ES_TRY(exclusive_scan<uint64_t>(w.cnz, w.pos, sc, w.total64, reinterpret_cast<uint64_t*>(w.scan), st));
+  ES_TRY(exclusive_scan<uint64_t>(w.cnz, w.pos, sc, w.total64, reinterpret_cast<uint64_t*>(w.scan_p), st, nullptr,
+                                  true));
   ES_LAUNCH(direct_totals_kernel, 1, 32, 0, st, w.pos, w.cnz, w.nstrips, w.ncols, w.bad, counts_dev);
   return ES_OK;
 }

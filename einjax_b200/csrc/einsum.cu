@@ -239,8 +239,18 @@ static int launch_simt(const EinsumDesc& d, const void* lhs, int ldt, const void
   const int64_t tab_ints = 3LL * d.B.total + 2LL * d.M.total + 2LL * d.N.total + 2LL * d.K.total;
   const size_t smem = static_cast<size_t>(tab_ints) * sizeof(int);
   if (smem > 160 * 1024) return ES_ERR_UNSUPPORTED;
-  if (cudaFuncSetAttribute(einsum_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return ES_ERR_CUDA;
+  {
+    // raised once per device to the largest size asked for
+    static int attr_bytes[kMaxAttrDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ES_ERR_CUDA;
+    if (dev < 0 || dev >= kMaxAttrDevices || attr_bytes[dev] < static_cast<int>(smem)) {
+      if (cudaFuncSetAttribute(einsum_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+        return ES_ERR_CUDA;
+      if (dev >= 0 && dev < kMaxAttrDevices) attr_bytes[dev] = static_cast<int>(smem);
+    }
+  }
   const int64_t mb = (d.M.total + kBM - 1) / kBM, nb = (d.N.total + kBN - 1) / kBN;
   const int64_t items = nseg * d.B.total * mb * nb;
   if (items <= 0) return ES_OK;
@@ -397,6 +407,15 @@ extern "C" size_t es_tile_einsum_workspace_size(const char* kernel_string, const
   return best;
 }
 
+static int tile_einsum_impl(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
+                            int rhs_nd, const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                            const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
+                            const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
+                            int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
+                            const int32_t* pair_key, int64_t key_extent, void* out_values, int out_dtype,
+                            int precision, void* workspace, size_t workspace_bytes, int32_t* error_dev,
+                            void* stream, void* values_ready);
+
 extern "C" int es_tile_einsum_ev(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd,
                                  const int64_t* rhs_tile, int rhs_nd, const void* lhs_values, int lhs_dtype,
                                  int64_t lhs_rows, const void* rhs_values, int rhs_dtype, int64_t rhs_rows,
@@ -404,7 +423,28 @@ extern "C" int es_tile_einsum_ev(const char* kernel_string, const int64_t* lhs_t
                                  const int64_t* seg_offsets, int64_t num_segments, const int32_t* seg_out_index,
                                  const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
                                  void* out_values, int out_dtype, int precision, void* workspace,
-                                 size_t workspace_bytes, int32_t* error_dev, void* stream, void* values_ready) {
+                                 size_t workspace_bytes, int32_t* error_dev, void* stream, void* values_ready,
+                                 int32_t* status_host) {
+  const int r = tile_einsum_impl(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_values, lhs_dtype, lhs_rows,
+                                 rhs_values, rhs_dtype, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets,
+                                 num_segments, seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype,
+                                 precision, workspace, workspace_bytes, error_dev, stream, values_ready);
+  // the device status follows into pinned host memory behind the launches
+  if (r == ES_OK && status_host && error_dev &&
+      cudaMemcpyAsync(status_host, error_dev, sizeof(int32_t), cudaMemcpyDeviceToHost, as_stream(stream)) !=
+          cudaSuccess)
+    return ES_ERR_CUDA;
+  return r;
+}
+
+static int tile_einsum_impl(const char* kernel_string, const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile,
+                            int rhs_nd, const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
+                            const void* rhs_values, int rhs_dtype, int64_t rhs_rows, const int32_t* pair_lhs,
+                            const int32_t* pair_rhs, int64_t num_pairs, const int64_t* seg_offsets,
+                            int64_t num_segments, const int32_t* seg_out_index, const int64_t* seg_strip,
+                            const int32_t* pair_key, int64_t key_extent, void* out_values, int out_dtype,
+                            int precision, void* workspace, size_t workspace_bytes, int32_t* error_dev,
+                            void* stream, void* values_ready) {
   cudaEvent_t ready = static_cast<cudaEvent_t>(values_ready);
   EinsumDesc d;
   ES_TRY(parse_einsum(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, &d));
@@ -468,5 +508,5 @@ extern "C" int es_tile_einsum(const char* kernel_string, const int64_t* lhs_tile
   return es_tile_einsum_ev(kernel_string, lhs_tile, lhs_nd, rhs_tile, rhs_nd, lhs_values, lhs_dtype, lhs_rows,
                            rhs_values, rhs_dtype, rhs_rows, pair_lhs, pair_rhs, num_pairs, seg_offsets, num_segments,
                            seg_out_index, seg_strip, pair_key, key_extent, out_values, out_dtype, precision, workspace,
-                           workspace_bytes, error_dev, stream, nullptr);
+                           workspace_bytes, error_dev, stream, nullptr, nullptr);
 }

@@ -289,28 +289,38 @@ struct RadixBuffers {
   }
 };
 
+// 32-bit words of rb.hist that a sort of n keys needs cleared before it runs.
+inline int64_t radix_clear_words(int64_t n) { return RadixScratchSize::hist_elems(n); }
+
 // Sorts bits [begin_bit, end_bit) of the keys, stable. On return *keys/*vals
 // point at whichever buffer holds the sorted data (the alternate buffers when
-// the number of 8-bit passes is odd). Launches: one clear of the scratch, the
-// upsweep, one kernel per pass. A look-back timeout is recorded in *err when
-// given.
+// the number of 8-bit passes is odd). Launches: one clear of the scratch
+// (none when precleared: an earlier launch on the stream cleared
+// radix_clear_words(n) words of rb.hist), the upsweep, one kernel per pass.
+// A look-back timeout is recorded in *err when given.
 template <typename K>
 int radix_sort_pairs(K** keys, uint32_t** vals, RadixBuffers<K>& rb, int64_t n, int begin_bit, int end_bit,
-                     cudaStream_t st, int32_t* err = nullptr) {
+                     cudaStream_t st, int32_t* err = nullptr, bool precleared = false) {
   if (n <= 1 || begin_bit >= end_bit) return ES_OK;
   if (n >= static_cast<int64_t>(UINT32_MAX)) return ES_ERR_UNSUPPORTED;
   const int npass = (end_bit - begin_bit + 7) / 8;
   if (npass > kRsMaxPasses) return ES_ERR_UNSUPPORTED;
-  // The attribute is per device; setting it is a cheap host call.
-  if (cudaFuncSetAttribute(rs_onesweep_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(rs_scatter_smem<K>())) != cudaSuccess)
-    return ES_ERR_CUDA;
+  // the attribute is per device: set once on each
+  static bool attr_set[kMaxAttrDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return ES_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxAttrDevices || !attr_set[dev]) {
+    if (cudaFuncSetAttribute(rs_onesweep_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(rs_scatter_smem<K>())) != cudaSuccess)
+      return ES_ERR_CUDA;
+    if (dev >= 0 && dev < kMaxAttrDevices) attr_set[dev] = true;
+  }
   const int64_t tiles = RadixScratchSize::tiles(n);
   uint64_t* status = reinterpret_cast<uint64_t*>(rb.hist);
   uint32_t* counters = rb.hist + 2 * RadixScratchSize::status_words(n);
   uint32_t* ghist = counters + kRsMaxPasses;
   const size_t clear = (2 * RadixScratchSize::status_words(n) + kRsMaxPasses + npass * kRsBins) * sizeof(uint32_t);
-  if (cudaMemsetAsync(rb.hist, 0, clear, st) != cudaSuccess) return ES_ERR_CUDA;
+  if (!precleared && cudaMemsetAsync(rb.hist, 0, clear, st) != cudaSuccess) return ES_ERR_CUDA;
   const int up_grid = static_cast<int>(tiles < 148 * 8 ? tiles : 148 * 8);
   ES_LAUNCH(rs_upsweep_kernel<K>, up_grid, kRsThreads, 0, st, *keys, n, begin_bit, end_bit, ghist);
   K* kin = *keys;

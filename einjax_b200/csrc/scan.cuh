@@ -181,8 +181,19 @@ inline int64_t scan_scratch_elems(int64_t n) {
 // out[i] = sum(in[0..i)); *total (device, optional) = sum(in). In-place
 // allowed. Inputs are non-negative. One launch (plus a clear of the tile
 // status) at any size; a look-back timeout is recorded in *err when given.
+// 32-bit words of `scratch` that a scan of n inputs needs cleared before it
+// runs (0: the single-tile scan needs none).
+inline int64_t scan_clear_words(int64_t n) {
+  if (n <= kScanTile) return 0;
+  const int64_t nb = (n + kScanTile - 1) / kScanTile;
+  return 2 * nb + 1;
+}
+
+// precleared: an earlier launch on the stream cleared scan_clear_words(n)
+// words of scratch (no clear of its own here).
 template <typename T>
-int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStream_t st, int32_t* err = nullptr) {
+int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStream_t st, int32_t* err = nullptr,
+                   bool precleared = false) {
   if (n <= 0) {
     if (total) {
       if (cudaMemsetAsync(total, 0, sizeof(T), st) != cudaSuccess) return ES_ERR_CUDA;
@@ -196,7 +207,8 @@ int exclusive_scan(const T* in, T* out, int64_t n, T* total, T* scratch, cudaStr
   const int64_t nb = (n + kScanTile - 1) / kScanTile;
   uint64_t* status = reinterpret_cast<uint64_t*>(scratch);
   uint32_t* next_tile = reinterpret_cast<uint32_t*>(status + nb);
-  if (cudaMemsetAsync(status, 0, nb * sizeof(uint64_t) + sizeof(uint32_t), st) != cudaSuccess) return ES_ERR_CUDA;
+  if (!precleared && cudaMemsetAsync(status, 0, nb * sizeof(uint64_t) + sizeof(uint32_t), st) != cudaSuccess)
+    return ES_ERR_CUDA;
   ES_LAUNCH(scan_lookback_kernel<T>, static_cast<int>(nb), kScanThreads, 0, st, in, out, n, status, next_tile, total,
             err);
   return ES_OK;

@@ -1464,7 +1464,8 @@ __global__ void __launch_bounds__(256) layout_rhs_wide_kernel(const void* __rest
 }
 
 __global__ void item_heads_kernel(const int64_t* __restrict__ strip, int64_t nseg, int G, uint32_t* __restrict__ flags,
-                                  int32_t* __restrict__ cnt) {
+                                  int32_t* __restrict__ cnt, ZeroSpans zs) {
+  zero_spans(zs);
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg; s += (int64_t)gridDim.x * blockDim.x) {
     const int64_t key = strip[s];
     int64_t lo = 0, hi = s;  // first index with strip >= key
@@ -1497,7 +1498,8 @@ __global__ void item_place_kernel(const uint32_t* __restrict__ flags, const uint
 }
 
 __global__ void item_identity_kernel(int64_t nseg, int32_t* __restrict__ first, int32_t* __restrict__ count,
-                                     int64_t* __restrict__ num) {
+                                     int64_t* __restrict__ num, ZeroSpans zs) {
+  zero_spans(zs);
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < nseg; s += (int64_t)gridDim.x * blockDim.x) {
     first[s] = static_cast<int32_t>(s);
     count[s] = 1;
@@ -1556,7 +1558,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
     const int64_t* __restrict__ seg_off, const int32_t* __restrict__ item_first, const int32_t* __restrict__ item_count,
     const uint32_t* __restrict__ order, const int64_t* __restrict__ num_sub, int S, int G, int64_t lhs_rows,
     int64_t rhs_rows, int C, int64_t key_extent, int64_t nw, uint32_t* __restrict__ cnt,
-    const uint32_t* __restrict__ off, int32_t* __restrict__ recs, int32_t* __restrict__ err) {
+    const uint32_t* __restrict__ off, int32_t* __restrict__ recs, int32_t* __restrict__ err, ZeroSpans zs) {
+  zero_spans(zs);
   // [entry][lane]: a step's reads (one entry per lane) and a refill's
   // stores (entry qq of every refilling lane) touch 32 distinct banks
   __shared__ int win_l[kMergeWarps][kWin][32];
@@ -1694,7 +1697,8 @@ __global__ void __launch_bounds__(kMergeWarps * 32) tc_merge_kernel(
 // next item's first record (or the total).
 __global__ void item_rec_kernel(const uint32_t* __restrict__ off, const uint32_t* __restrict__ total,
                                 const int64_t* __restrict__ num_sub, int S, int C, int nblocks, int64_t nw,
-                                int64_t* __restrict__ item_rec) {
+                                int64_t* __restrict__ item_rec, ZeroSpans zs) {
+  zero_spans(zs);
   const int64_t W1 = *num_sub;
   const int64_t nitems = (W1 + S - 1) / S;
   const int m = C / nblocks;
@@ -2088,17 +2092,26 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   TcWs w;
   tc_layout(cv, w, c, rhs_rows, npairs, nseg, nblocks, pair_key ? key_extent : 0);
   if (cv.overflow) return ES_ERR_WORKSPACE;
-  if (cudaMemsetAsync(w.zeros, 0, zero_bytes(c), st) != cudaSuccess) return ES_ERR_CUDA;
+  // the clears the steps below need ride on launches that are there anyway:
+  // the first item kernel clears the zero tile, the item count and the item
+  // scan's and item sort's scratch; the merge count pass the record scan's
+  // scratch; item_rec the work queue
+  const bool grouped = seg_strip && c.G > 1;
+  ZeroSpans z0 = no_zero_spans();
+  if (!add_zero_span(z0, w.zeros, zero_bytes(c) / 4) || !add_zero_span(z0, w.rb.hist, radix_clear_words(nseg)) ||
+      (grouped && (!add_zero_span(z0, w.num_items, 2) || !add_zero_span(z0, w.scan, scan_clear_words(nseg)))))
+    return ES_ERR_INVALID;
   // 2. work items
-  if (seg_strip && c.G > 1) {
-    ES_LAUNCH(item_heads_kernel, grid_for(nseg, 256), 256, 0, st, seg_strip, nseg, c.G, w.flags, w.cnt);
-    if (cudaMemsetAsync(w.num_items, 0, sizeof(int64_t), st) != cudaSuccess) return ES_ERR_CUDA;
-    ES_TRY(exclusive_scan<uint32_t>(w.flags, w.excl, nseg, reinterpret_cast<uint32_t*>(w.num_items), w.scan, st));
+  if (grouped) {
+    ES_LAUNCH(item_heads_kernel, grid_for(nseg, 256), 256, 0, st, seg_strip, nseg, c.G, w.flags, w.cnt, z0);
+    ES_TRY(exclusive_scan<uint32_t>(w.flags, w.excl, nseg, reinterpret_cast<uint32_t*>(w.num_items), w.scan, st,
+                                    nullptr, true));
     ES_LAUNCH(item_place_kernel, grid_for(nseg, 256), 256, 0, st, w.flags, w.excl, w.cnt, nseg, w.item_first,
               w.item_count);
   } else {
     if (c.G != 1) return ES_ERR_INVALID;
-    ES_LAUNCH(item_identity_kernel, grid_for(nseg, 256), 256, 0, st, nseg, w.item_first, w.item_count, w.num_items);
+    ES_LAUNCH(item_identity_kernel, grid_for(nseg, 256), 256, 0, st, nseg, w.item_first, w.item_count, w.num_items,
+              z0);
   }
   // 3. largest items first, handed out by a device-wide queue
   ES_LAUNCH(item_work_keys_kernel, grid_for(nseg, 256), 256, 0, st, w.item_first, w.item_count, seg_off, w.num_items,
@@ -2106,7 +2119,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   {
     uint32_t* k = w.sort_keys;
     uint32_t* v = w.order;
-    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st, err));
+    ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st, err, true));
     if (v != w.order &&
         cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return ES_ERR_CUDA;
@@ -2125,15 +2138,18 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     // walks them instead of launching one mostly empty block per 4 slots
     int64_t nb = (nw + kMergeWarps - 1) / kMergeWarps;
     const int blocks = static_cast<int>(nb < 148 * 8 ? nb : 148 * 8);
+    ZeroSpans z1 = no_zero_spans(), z2 = no_zero_spans();
+    add_zero_span(z1, w.scan2, scan_clear_words(nw));
+    add_zero_span(z2, w.queue, 1);
     ES_LAUNCH(tc_merge_kernel<true>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
               w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
-              (const uint32_t*)nullptr, w.recs, err);
-    ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nw, w.rec_total, w.scan2, st));
+              (const uint32_t*)nullptr, w.recs, err, z1);
+    ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nw, w.rec_total, w.scan2, st, nullptr, true));
     ES_LAUNCH(tc_merge_kernel<false>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
               w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
-              (const uint32_t*)w.rec_base, w.recs, err);
+              (const uint32_t*)w.rec_base, w.recs, err, no_zero_spans());
     ES_LAUNCH(item_rec_kernel, grid_for(nslots, 256), 256, 0, st, (const uint32_t*)w.rec_base,
-              (const uint32_t*)w.rec_total, w.num_items, S, C, nblocks, nw, w.item_rec);
+              (const uint32_t*)w.rec_total, w.num_items, S, C, nblocks, nw, w.item_rec, z2);
   }
   // the steps above read only the pair lists; the values may still be in
   // flight (values_ready: e.g. a tiling's fill on another stream)
@@ -2165,7 +2181,6 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
                   c.KC, w.pan_hi, (void*)nullptr, rn);
     }
   }
-  if (cudaMemsetAsync(w.queue, 0, sizeof(int), st) != cudaSuccess) return ES_ERR_CUDA;
   // 6. persistent tensor-core kernel, one CTA per SM
   TcParams prm;
   prm.c = c;
@@ -2246,14 +2261,20 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   int dev = 0, sms = kSMs;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t grid = nseg < sms ? nseg : sms;
-  if (c.fp32) {
-    if (cudaFuncSetAttribute(tc_strip_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
-        cudaSuccess)
-      return ES_ERR_CUDA;
-  } else {
-    if (cudaFuncSetAttribute(tc_strip_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem_bytes) !=
-        cudaSuccess)
-      return ES_ERR_CUDA;
+  {
+    // the kernel's dynamic shared memory limit: per device, raised once to
+    // the largest configuration (any smaller one then fits)
+    static int attr_bytes[2][kMaxAttrDevices] = {};
+    const int fi = c.fp32 ? 1 : 0;
+    if (dev < 0 || dev >= kMaxAttrDevices || attr_bytes[fi][dev] < c.smem_bytes) {
+      const cudaError_t e =
+          c.fp32 ? cudaFuncSetAttribute(tc_strip_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        c.smem_bytes)
+                 : cudaFuncSetAttribute(tc_strip_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        c.smem_bytes);
+      if (e != cudaSuccess) return ES_ERR_CUDA;
+      if (dev >= 0 && dev < kMaxAttrDevices) attr_bytes[fi][dev] = c.smem_bytes;
+    }
   }
   if (prm.fused) {
     prm.blk = 0;

@@ -81,17 +81,36 @@ class _DeferredErrors:
         self.next = 0
         self.pending = []  # (function name, slot, event)
 
-    def defer(self, fn: str, err: torch.Tensor) -> None:
+    def _slot(self) -> int:
         if self.host is None:
             self.host = torch.zeros(self.SLOTS, dtype=torch.int32, pin_memory=True)
+            self.events = [None] * self.SLOTS
+        # a slot (and its event) is reused SLOTS allocations later, always
+        # after a flush has consumed its previous entry
         if len(self.pending) >= self.SLOTS - 1:
             self.flush()
         slot = self.next
         self.next = (self.next + 1) % self.SLOTS
-        self.host[slot:slot + 1].copy_(err.reshape(1), non_blocking=True)
-        ev = torch.cuda.Event()
+        return slot
+
+    def _commit(self, fn: str, slot: int) -> None:
+        ev = self.events[slot]
+        if ev is None:
+            ev = self.events[slot] = torch.cuda.Event()
         ev.record()
         self.pending.append((fn, slot, ev))
+
+    def defer(self, fn: str, err: torch.Tensor) -> None:
+        slot = self._slot()
+        self.host[slot:slot + 1].copy_(err.reshape(1), non_blocking=True)
+        self._commit(fn, slot)
+
+    def reserve(self, fn: str):
+        """``(host_address, commit)`` for a call that copies its own status
+        into the pinned slot (``es_tile_einsum_ev``'s ``status_host``);
+        ``commit()`` after the call queues the slot for the next flush."""
+        slot = self._slot()
+        return self.host.data_ptr() + 4 * slot, (lambda: self._commit(fn, slot))
 
     def flush(self) -> None:
         pending, self.pending = self.pending, []

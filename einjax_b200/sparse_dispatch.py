@@ -21,8 +21,8 @@ from math import prod
 import torch
 
 from . import _lib as L
-from .sparse import (SparseTensorRelation, as_relation, defer_device_error, empty_relation, es_dtype, latest_ready,
-                     mark, read_counts, stream_ptr, workspace)
+from .sparse import (_DEFERRED, SparseTensorRelation, as_relation, empty_relation, es_dtype, latest_ready, mark,
+                     read_counts, stream_ptr, workspace)
 
 _PREC = {"auto": L.ES_PREC_AUTO, "exact": L.ES_PREC_EXACT, "tc": L.ES_PREC_TC}
 
@@ -189,15 +189,17 @@ def tile_einsum(kernel_string, lhs_values, rhs_values, pair_lhs, pair_rhs, seg_o
                                             int(lv.shape[0]), int(rv.shape[0]), P, nseg, kext, prec)
     ws = workspace(wsb, dev) if wsb else None
     err = torch.empty(1, dtype=torch.int32, device=dev)  # cleared by the call
+    # deferred check: the call copies its status into a pinned slot itself
+    status_host, commit = _DEFERRED.reserve("es_tile_einsum") if check == "defer" else (None, None)
     L.check("es_tile_einsum", lib.es_tile_einsum_ev(
         ks, lti, len(lt), rti, len(rt), lv.data_ptr(), es_dtype(lv), int(lv.shape[0]), rv.data_ptr(), es_dtype(rv),
         int(rv.shape[0]), pl.data_ptr(), pr.data_ptr(), P, so.data_ptr() if so is not None else None, nseg,
         sx.data_ptr() if sx is not None else None, sg.data_ptr() if sg is not None else None,
         pk.data_ptr() if pk is not None else None, kext, out.data_ptr(),
         _es_out(out.dtype), prec, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-        err.data_ptr(), stream_ptr(dev), ready[1].cuda_event if ready is not None else None))
+        err.data_ptr(), stream_ptr(dev), ready[1].cuda_event if ready is not None else None, status_host))
     if check == "defer":
-        defer_device_error("es_tile_einsum", err)
+        commit()
     elif check:
         e = int(err.item())
         if e:

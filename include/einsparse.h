@@ -248,7 +248,9 @@ int es_tile_einsum(const char* kernel_string,
  * wait) on `stream` right before its first launch that reads lhs_values or
  * rhs_values: the grouping of the pairs into work items and step records
  * runs first, so values written on another stream (e.g. a tiling's value
- * fill) overlap it. */
+ * fill) overlap it. status_host (NULL: none): pinned host int32 that
+ * receives *error_dev by an asynchronous copy behind the call's launches,
+ * so a caller can check the status later without a copy of its own. */
 int es_tile_einsum_ev(const char* kernel_string,
                       const int64_t* lhs_tile, int lhs_nd, const int64_t* rhs_tile, int rhs_nd,
                       const void* lhs_values, int lhs_dtype, int64_t lhs_rows,
@@ -258,7 +260,7 @@ int es_tile_einsum_ev(const char* kernel_string,
                       const int64_t* seg_strip, const int32_t* pair_key, int64_t key_extent,
                       void* out_values, int out_dtype, int precision,
                       void* workspace, size_t workspace_bytes, int32_t* error_dev, void* stream,
-                      void* values_ready);
+                      void* values_ready, int32_t* status_host);
 
 /* Which path es_tile_einsum takes for these arguments: 1 tensor cores,
  * 0 SIMT, negative es_status if the call would be rejected. Host-side. */
