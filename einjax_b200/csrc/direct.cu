@@ -26,6 +26,8 @@
 // goes to offset(s, c) + G_c(i) - G_c(start s). Nothing of size pairs or
 // (columns x lhs tiles) is materialised besides the pair arrays themselves:
 // the masks are (columns x tiles / 32) words.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -175,11 +177,15 @@ __global__ void direct_init_kernel(int32_t* __restrict__ table, int64_t tn, uint
 // lexicographic order). Threads [nr, nr + nl): strip head flag of lhs tile
 // i (flags lhs tiles out of lexicographic order or repeated, and keys
 // outside the table).
-__global__ void direct_inputs_kernel(const int32_t* __restrict__ rc, int64_t nr, const int32_t* __restrict__ lc,
-                                     int64_t nl, DirectGeom g, int32_t* __restrict__ table,
-                                     uint32_t* __restrict__ colflag, uint32_t* __restrict__ sflag,
-                                     int32_t* __restrict__ bad, int32_t* err) {
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nr + nl; q += (int64_t)gridDim.x * blockDim.x) {
+// (Each phase below is a device function over threads t0, t0 + nt, ...: the
+// multi-CTA kernels call it with the grid's threads, the one-CTA plan for
+// small inputs with the block's.)
+__device__ __forceinline__ void direct_inputs_body(const int32_t* __restrict__ rc, int64_t nr,
+                                                   const int32_t* __restrict__ lc, int64_t nl, const DirectGeom& g,
+                                                   int32_t* __restrict__ table, uint32_t* __restrict__ colflag,
+                                                   uint32_t* __restrict__ sflag, int32_t* __restrict__ bad,
+                                                   int32_t* err, int64_t t0, int64_t nt) {
+  for (int64_t q = t0; q < nr + nl; q += nt) {
     if (q < nr) {
       const int64_t j = q;
       const int32_t* row = rc + j * g.rhs_nd;
@@ -212,14 +218,24 @@ __global__ void direct_inputs_kernel(const int32_t* __restrict__ rc, int64_t nr,
   }
 }
 
+__global__ void direct_inputs_kernel(const int32_t* __restrict__ rc, int64_t nr, const int32_t* __restrict__ lc,
+                                     int64_t nl, DirectGeom g, int32_t* __restrict__ table,
+                                     uint32_t* __restrict__ colflag, uint32_t* __restrict__ sflag,
+                                     int32_t* __restrict__ bad, int32_t* err) {
+  direct_inputs_body(rc, nr, lc, nl, g, table, colflag, sflag, bad, err, blockIdx.x * (int64_t)blockDim.x + threadIdx.x,
+                     (int64_t)gridDim.x * blockDim.x);
+}
+
 // Threads [0, cext): present column ids in order; threads [0, nl): first lhs
 // tile of each strip, then sstart[nstrips] = nl.
-__global__ void direct_index_kernel(const uint32_t* __restrict__ colflag, const uint32_t* __restrict__ colrank,
-                                    int64_t cext, uint32_t* __restrict__ colids, const uint32_t* __restrict__ sflag,
-                                    const uint32_t* __restrict__ sexcl, int64_t nl,
-                                    const uint32_t* __restrict__ nstrips, uint32_t* __restrict__ sstart) {
+__device__ __forceinline__ void direct_index_body(const uint32_t* __restrict__ colflag,
+                                                  const uint32_t* __restrict__ colrank, int64_t cext,
+                                                  uint32_t* __restrict__ colids, const uint32_t* __restrict__ sflag,
+                                                  const uint32_t* __restrict__ sexcl, int64_t nl,
+                                                  const uint32_t* __restrict__ nstrips, uint32_t* __restrict__ sstart,
+                                                  int64_t t0, int64_t nt) {
   const int64_t n = nl > cext ? nl : cext;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = t0; i < n; i += nt) {
     if (i < cext && colflag[i]) colids[colrank[i]] = static_cast<uint32_t>(i);
     if (i < nl) {
       if (sflag[i]) sstart[sexcl[i]] = static_cast<uint32_t>(i);
@@ -228,10 +244,22 @@ __global__ void direct_index_kernel(const uint32_t* __restrict__ colflag, const 
   }
 }
 
-// Table lookup of a tile's key for column col: the rhs tile or -1.
+__global__ void direct_index_kernel(const uint32_t* __restrict__ colflag, const uint32_t* __restrict__ colrank,
+                                    int64_t cext, uint32_t* __restrict__ colids, const uint32_t* __restrict__ sflag,
+                                    const uint32_t* __restrict__ sexcl, int64_t nl,
+                                    const uint32_t* __restrict__ nstrips, uint32_t* __restrict__ sstart) {
+  direct_index_body(colflag, colrank, cext, colids, sflag, sexcl, nl, nstrips, sstart,
+                    blockIdx.x * (int64_t)blockDim.x + threadIdx.x, (int64_t)gridDim.x * blockDim.x);
+}
+
+// Table lookup of a tile's key for column col: the rhs tile or -1. NC: read
+// through the read-only path, valid when an earlier launch wrote the table
+// (not within the kernel that writes it).
+template <bool NC = true>
 __device__ __forceinline__ int32_t direct_lookup(const DirectGeom& g, const int32_t* __restrict__ table, int64_t key,
                                                  int64_t col) {
-  return key >= 0 ? __ldg(table + key * g.cext + col) : -1;
+  if (key < 0) return -1;
+  return NC ? __ldg(table + key * g.cext + col) : table[key * g.cext + col];
 }
 
 // Table row of lhs tile i (-1 out of range); *k = its contracted coordinate.
@@ -249,16 +277,18 @@ constexpr int kDirCols = 8;
 
 // Hit masks: one warp per (32-tile chunk, group of kDirCols present
 // columns); chunks run to nch inclusive, the last one past every tile.
-__global__ void direct_masks_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
-                                    const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
-                                    const uint32_t* __restrict__ ncols, int64_t nchp1, uint32_t* __restrict__ mask,
-                                    uint32_t* __restrict__ ccnt) {
+template <bool NC>
+__device__ __forceinline__ void direct_masks_body(const int32_t* __restrict__ lc, int64_t nl, const DirectGeom& g,
+                                                  const int32_t* __restrict__ table,
+                                                  const uint32_t* __restrict__ colids,
+                                                  const uint32_t* __restrict__ ncols, int64_t nchp1,
+                                                  uint32_t* __restrict__ mask, uint32_t* __restrict__ ccnt, int64_t t0,
+                                                  int64_t nt) {
   const int64_t C = *ncols;
   const int64_t groups = (C + kDirCols - 1) / kDirCols;
   const int lane = threadIdx.x & 31;
-  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t u = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5; u < nchp1 * groups;
-       u += nw) {
+  const int64_t nw = nt >> 5;
+  for (int64_t u = t0 >> 5; u < nchp1 * groups; u += nw) {
     const int64_t ch = u / groups, c0 = (u - ch * groups) * kDirCols;
     const int64_t i = ch * 32 + lane;
     int32_t k;
@@ -266,7 +296,7 @@ __global__ void direct_masks_kernel(const int32_t* __restrict__ lc, int64_t nl, 
     int32_t r[kDirCols];
 #pragma unroll
     for (int j = 0; j < kDirCols; ++j)
-      r[j] = c0 + j < C ? direct_lookup(g, table, key, colids[c0 + j]) : -1;
+      r[j] = c0 + j < C ? direct_lookup<NC>(g, table, key, colids[c0 + j]) : -1;
 #pragma unroll
     for (int j = 0; j < kDirCols; ++j) {
       const uint32_t m = __ballot_sync(0xffffffffu, r[j] >= 0);
@@ -278,6 +308,15 @@ __global__ void direct_masks_kernel(const int32_t* __restrict__ lc, int64_t nl, 
   }
 }
 
+__global__ void direct_masks_kernel(const int32_t* __restrict__ lc, int64_t nl, DirectGeom g,
+                                    const int32_t* __restrict__ table, const uint32_t* __restrict__ colids,
+                                    const uint32_t* __restrict__ ncols, int64_t nchp1, uint32_t* __restrict__ mask,
+                                    uint32_t* __restrict__ ccnt) {
+  direct_masks_body<true>(lc, nl, g, table, colids, ncols, nchp1, mask, ccnt,
+                          blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
+                          static_cast<int64_t>(gridDim.x) * blockDim.x);
+}
+
 // G_c(t): hits of present column c among lhs tiles [0, t), plus a constant
 // per column.
 __device__ __forceinline__ uint32_t direct_g(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
@@ -287,13 +326,14 @@ __device__ __forceinline__ uint32_t direct_g(const uint32_t* __restrict__ mask, 
 }
 
 // Pairs per (strip, present column), strip-major, one thread per entry.
-__global__ void direct_counts_kernel(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
-                                     int64_t nchp1, const uint32_t* __restrict__ ncols,
-                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
-                                     uint64_t* __restrict__ cnz, uint32_t* __restrict__ gstart) {
+__device__ __forceinline__ void direct_counts_body(const uint32_t* __restrict__ mask,
+                                                   const uint32_t* __restrict__ cscan, int64_t nchp1,
+                                                   const uint32_t* __restrict__ ncols,
+                                                   const uint32_t* __restrict__ nstrips,
+                                                   const uint32_t* __restrict__ sstart, uint64_t* __restrict__ cnz,
+                                                   uint32_t* __restrict__ gstart, int64_t t0, int64_t nt) {
   const int64_t S = *nstrips, C = *ncols;
-  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < S * C;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  for (int64_t e = t0; e < S * C; e += nt) {
     const int64_t s = e / C, c = e - s * C;
     const uint32_t ga = direct_g(mask, cscan, nchp1, c, sstart[s]);
     const uint32_t n = direct_g(mask, cscan, nchp1, c, sstart[s + 1]) - ga;
@@ -302,16 +342,33 @@ __global__ void direct_counts_kernel(const uint32_t* __restrict__ mask, const ui
   }
 }
 
+__global__ void direct_counts_kernel(const uint32_t* __restrict__ mask, const uint32_t* __restrict__ cscan,
+                                     int64_t nchp1, const uint32_t* __restrict__ ncols,
+                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ sstart,
+                                     uint64_t* __restrict__ cnz, uint32_t* __restrict__ gstart) {
+  direct_counts_body(mask, cscan, nchp1, ncols, nstrips, sstart, cnz, gstart,
+                     blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x,
+                     static_cast<int64_t>(gridDim.x) * blockDim.x);
+}
+
 // Counts of the host's sizes: [0] pairs, [1] output tiles, [2] out of order.
-__global__ void direct_totals_kernel(const uint64_t* __restrict__ pos, const uint64_t* __restrict__ cnz,
-                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ ncols,
-                                     const int32_t* __restrict__ bad, int64_t* __restrict__ out) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+__device__ __forceinline__ void direct_totals_body(const uint64_t* __restrict__ pos,
+                                                   const uint64_t* __restrict__ cnz,
+                                                   const uint32_t* __restrict__ nstrips,
+                                                   const uint32_t* __restrict__ ncols, const int32_t* __restrict__ bad,
+                                                   int64_t* __restrict__ out) {
   const int64_t n = static_cast<int64_t>(*nstrips) * (*ncols);
   const uint64_t t = n == 0 ? 0ull : pos[n - 1] + cnz[n - 1];
   out[0] = static_cast<int64_t>(t & 0xFFFFFFFFull);
   out[1] = static_cast<int64_t>(t >> 32);
   out[2] = *bad;
+}
+
+__global__ void direct_totals_kernel(const uint64_t* __restrict__ pos, const uint64_t* __restrict__ cnz,
+                                     const uint32_t* __restrict__ nstrips, const uint32_t* __restrict__ ncols,
+                                     const int32_t* __restrict__ bad, int64_t* __restrict__ out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  direct_totals_body(pos, cnz, nstrips, ncols, bad, out);
 }
 
 // Fill. Threads first write the output-tile records of the (strip, present
@@ -399,6 +456,86 @@ __global__ void direct_pairs_kernel(const int32_t* __restrict__ lc, int64_t nl, 
   }
 }
 
+// Exclusive scan of n values by one CTA (every thread of the block calls
+// it): thread t sums a contiguous run, the runs' sums are scanned across the
+// block, then each run is written. In place allowed; *total gets the sum.
+template <typename T>
+__device__ void block_exclusive_scan(const T* in, T* out, int64_t n, T* total, T* sh) {
+  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarp = nth >> 5;
+  const int64_t per = (n + nth - 1) / nth;
+  const int64_t b = min(n, static_cast<int64_t>(tid) * per), e = min(n, b + per);
+  T s = 0;
+  for (int64_t i = b; i < e; ++i) s += in[i];
+  T incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sh[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const T v = lane < nwarp ? sh[lane] : T(0);
+    T iv = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T u = __shfl_up_sync(0xffffffffu, iv, o);
+      if (lane >= o) iv += u;
+    }
+    if (lane < nwarp) sh[lane] = iv - v;
+  }
+  __syncthreads();
+  T run = sh[warp] + incl - s;
+  if (tid == nth - 1 && total) *total = run + s;
+  for (int64_t i = b; i < e; ++i) {
+    const T v = in[i];
+    out[i] = run;
+    run += v;
+  }
+  __syncthreads();
+}
+
+// The whole plan in one CTA for small inputs: the phases of the multi-CTA
+// launches, separated by block barriers (which order the global writes of
+// one phase before the next phase's reads), with block scans. The table is
+// written inside this kernel, so its lookups use plain loads.
+constexpr int kDirSmallThreads = 1024;
+constexpr int64_t kDirSmallTiles = 8192;   // n_lhs + n_rhs at most
+constexpr int64_t kDirSmallTable = 65536;  // table, mask and (strip, column) entries at most
+
+__global__ void __launch_bounds__(kDirSmallThreads) direct_plan_small_kernel(
+    const int32_t* __restrict__ rc, int64_t nr, const int32_t* __restrict__ lc, int64_t nl, DirectGeom g, DirectWs w,
+    int64_t tn, int64_t nchp1, int64_t* __restrict__ counts, int32_t* err) {
+  __shared__ uint32_t sh32[32];
+  __shared__ uint64_t sh64[32];
+  const int64_t t0 = threadIdx.x, nt = blockDim.x;
+  const int64_t ni = tn > g.cext ? tn : g.cext;
+  for (int64_t i = t0; i < ni; i += nt) {
+    if (i < tn) w.table[i] = -1;
+    if (i < g.cext) w.colflag[i] = 0u;
+  }
+  if (t0 == 0) {
+    *w.bad = 0;
+    if (err) *err = 0;
+  }
+  __syncthreads();
+  direct_inputs_body(rc, nr, lc, nl, g, w.table, w.colflag, w.sflag, w.bad, err, t0, nt);
+  __syncthreads();
+  block_exclusive_scan<uint32_t>(w.colflag, w.colrank, g.cext, w.ncols, sh32);
+  block_exclusive_scan<uint32_t>(w.sflag, w.sexcl, nl, w.nstrips, sh32);
+  direct_index_body(w.colflag, w.colrank, g.cext, w.colids, w.sflag, w.sexcl, nl, w.nstrips, w.sstart, t0, nt);
+  __syncthreads();
+  direct_masks_body<false>(lc, nl, g, w.table, w.colids, w.ncols, nchp1, w.mask, w.ccnt, t0, nt);
+  __syncthreads();
+  // only the present columns' masks (column-major) and the (strip, present
+  // column) entries are scanned
+  block_exclusive_scan<uint32_t>(w.ccnt, w.cscan, static_cast<int64_t>(*w.ncols) * nchp1, w.total, sh32);
+  direct_counts_body(w.mask, w.cscan, nchp1, w.ncols, w.nstrips, w.sstart, w.cnz, w.gstart, t0, nt);
+  __syncthreads();
+  block_exclusive_scan<uint64_t>(w.cnz, w.pos, static_cast<int64_t>(*w.nstrips) * (*w.ncols), w.total64, sh64);
+  if (t0 == 0) direct_totals_body(w.pos, w.cnz, w.nstrips, w.ncols, w.bad, counts);
+}
+
 static int make_direct_geom(int lhs_nd, int rhs_nd, int nb, const int64_t* lhs_grid, const int64_t* rhs_grid,
                             DirectGeom* g) {
   if (lhs_nd < 1 || rhs_nd < 1 || lhs_nd > ES_MAX_DIMS || rhs_nd > ES_MAX_DIMS) return ES_ERR_INVALID;
@@ -460,6 +597,14 @@ extern "C" int es_direct_plan(const int32_t* lhs_coords, int64_t n_lhs, int lhs_
   const int64_t nchp1 = direct_chunks(n_lhs);
   const int64_t cb = direct_col_bound(g, n_rhs);
   const int64_t sc = direct_sc_bound(g, n_lhs, n_rhs);
+  // EINSPARSE_NO_SMALL_PLAN: always the multi-launch plan (tests)
+  if (n_lhs + n_rhs <= kDirSmallTiles && tn <= kDirSmallTable && cb * nchp1 <= kDirSmallTable &&
+      sc <= kDirSmallTable && !std::getenv("EINSPARSE_NO_SMALL_PLAN")) {
+    // small inputs: one launch instead of about ten
+    ES_LAUNCH(direct_plan_small_kernel, 1, kDirSmallThreads, 0, st, rhs_coords, n_rhs, lhs_coords, n_lhs, g, w, tn,
+              nchp1, counts_dev, error_dev);
+    return ES_OK;
+  }
   ZeroSpans zs = no_zero_spans();
   add_zero_span(zs, w.scan_c, scan_clear_words(g.cext));
   add_zero_span(zs, w.scan_s, scan_clear_words(n_lhs));

@@ -2116,13 +2116,13 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   // 3. largest items first, handed out by a device-wide queue
   ES_LAUNCH(item_work_keys_kernel, grid_for(nseg, 256), 256, 0, st, w.item_first, w.item_count, seg_off, w.num_items,
             nseg, w.sort_keys, w.order);
+  // the sorted order stays in whichever buffer the sort left it
+  const uint32_t* order = w.order;
   {
     uint32_t* k = w.sort_keys;
     uint32_t* v = w.order;
     ES_TRY(radix_sort_pairs<uint32_t>(&k, &v, w.rb, nseg, 0, 8, st, err, true));
-    if (v != w.order &&
-        cudaMemcpyAsync(w.order, v, nseg * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-      return ES_ERR_CUDA;
+    order = v;
   }
   // 4. merge steps of every item (all items and key chunks in parallel);
   //    item q takes the sub-strips order[q*S .. q*S+S-1], so items come
@@ -2142,11 +2142,11 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
     add_zero_span(z1, w.scan2, scan_clear_words(nw));
     add_zero_span(z2, w.queue, 1);
     ES_LAUNCH(tc_merge_kernel<true>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
-              w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
+              w.item_count, order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
               (const uint32_t*)nullptr, w.recs, err, z1);
     ES_TRY(exclusive_scan<uint32_t>(w.ipairs, w.rec_base, nw, w.rec_total, w.scan2, st, nullptr, true));
     ES_LAUNCH(tc_merge_kernel<false>, blocks, kMergeWarps * 32, 0, st, pl, pr, keys, seg_off, w.item_first,
-              w.item_count, w.order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
+              w.item_count, order, w.num_items, S, c.G, lhs_rows, rhs_rows, C, key_extent, nw, w.ipairs,
               (const uint32_t*)w.rec_base, w.recs, err, no_zero_spans());
     ES_LAUNCH(item_rec_kernel, grid_for(nslots, 256), 256, 0, st, (const uint32_t*)w.rec_base,
               (const uint32_t*)w.rec_total, w.num_items, S, C, nblocks, nw, w.item_rec, z2);
@@ -2202,7 +2202,7 @@ int tc_launch(const TcConfig& c, const void* lhs, int64_t lhs_rows, const void* 
   prm.item_first = w.item_first;
   prm.item_count = w.item_count;
   prm.num_items = w.num_items;
-  prm.order = reinterpret_cast<const int32_t*>(w.order);
+  prm.order = reinterpret_cast<const int32_t*>(order);
   prm.queue = w.queue;
   prm.seg_out = seg_out;
   prm.out = out;
