@@ -338,7 +338,10 @@ def run_ours(args):
     b_part_h = b_h[rank * nb:(rank + 1) * nb] if world > 1 else b_h
     hosts = (idx_h, val_h, b_part_h)
     slots = [tuple(torch.empty(h.shape, dtype=h.dtype, device=dev) for h in hosts) for _ in range(2)]
-    b_full = torch.empty(b_h.shape, dtype=b_h.dtype, device=dev) if world > 1 else None
+    # B's full rows, double-buffered: step k gathers into b_full[k % 2] on
+    # its own stream while step k-1's deferred B fill may still read the other
+    b_full = [torch.empty(b_h.shape, dtype=b_h.dtype, device=dev) for _ in range(2)] if world > 1 else None
+    s_ag = torch.cuda.Stream(dev) if world > 1 else None
 
     def h2d(k, after, gemm=None):
         with torch.cuda.stream(s_in):
@@ -352,14 +355,24 @@ def run_ours(args):
             ev_h.record(s_in)
         return ev_h
 
-    def compute(k):
+    def compute(k, inputs_ready):
         idx, val, b = slots[k % 2]
         if world > 1:
-            dist.all_gather_into_tensor(b_full, b)
-            b = b_full
+            # the other ranks' rows of B come over NVLink on a stream of their
+            # own as soon as this step's slice has landed, beside A's tiling,
+            # which needs none of B
+            bf = b_full[k % 2]
+            s_ag.wait_event(inputs_ready)
+            with torch.cuda.stream(s_ag):
+                dist.all_gather_into_tensor(bf, b)
+            gathered = torch.cuda.Event()
+            gathered.record(s_ag)
         # the public device-tensor tilings (their counts resolve together at
         # the plan, their value fills overlap the GEMM's pair grouping)
         A = E.tile_coo(idx, val, shape, (TILE, TILE))
+        if world > 1:
+            comp.wait_event(gathered)
+            b = bf
         B = E.tile_dense(b, (TILE, TILE))
         res = E.execute_sharded_sparse(A, B, jk, ks, ak, precision=args.precision, lhs_sharded=True,
                                        gather=False)
@@ -393,7 +406,7 @@ def run_ours(args):
         prev = None
         for k in range(steps):
             comp.wait_event(ev_in[k % 2])
-            res, gemm = compute(k)
+            res, gemm = compute(k, ev_in[k % 2])
             done = torch.cuda.Event()
             done.record(comp)
             ev_done[k % 2] = done
@@ -502,7 +515,8 @@ def run_ours(args):
                     "copies": "one stream per direction, issued behind each step's tile fills so they run "
                               "under its tile GEMM (next inputs, previous result)" +
                               ("; each rank copies its A rows and 1/N of B's rows, B is all-gathered over "
-                               "NVLink (NCCL) inside the step" if world > 1 else "")},
+                               "NVLink (NCCL) inside the step, on its own stream beside A's tiling"
+                               if world > 1 else "")},
             "roofline": {"kernel": "einsum (fused tile GEMM + segment-sum)", "bound": "tensor",
                          "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4),
