@@ -396,8 +396,14 @@ def _plan_direct(lhs, rhs, join_keys, agg_keys, marks=None, nb=None):
 
 def plan_pairs(lhs: SparseTensorRelation, rhs: SparseTensorRelation, join_keys, agg_keys,
                marks=None) -> PairPlan:
-    """Join the relations and group the pairs by output tile (two host syncs:
-    the pair count and the output-tile count).
+    """Join the relations and group the pairs by output tile.
+
+    Host waits: one for the operands' tile counts when they come unresolved
+    from ``tile_coo`` / ``tile_dense`` (both resolved together), and one for
+    the pair and output-tile counts (matmul-like shapes; the general path
+    reads them one after the other). The operands' pending value fills are
+    launched behind that count copy, so they run while the host sizes the
+    pair arrays and launches what follows.
 
     Matmul-like shapes (``_direct_shape``) group without sorting; the pairs of
     each output tile are in join order either way, and ``lhs_idx``/``rhs_idx``
